@@ -1,0 +1,119 @@
+/*
+ * miag.h -- C ABI of the B200 (sm_100a) MoE FFN block for the motorIa engine.
+ *
+ * libmiag.so replaces, for one layer's MoE feed-forward block, the body of
+ * motorIa's static `moe()` (src/model/forward.c:167-197) and the Q8_0 /
+ * f32 `mia_matvec` it calls (src/tensor/matmul.c:91-106).  The expert
+ * weights live in HBM for the lifetime of the context, so the reference's
+ * disk-streamed LRU cache (src/storage/expert_cache.c:59-85) is not needed;
+ * its loader port (include/mia/expert_cache.h:8) is still how blobs arrive.
+ *
+ * Conventions follow the reference: functions return 0 on success and -1 on
+ * failure, writing a message into err[errlen] (mia_file_open,
+ * include/mia/mia_file.h:40).  Nothing here calls exit() or prints.  No CPU
+ * fallback exists: without an sm_100a GPU every compute entry point fails.
+ * A context is used by one host thread at a time (like mia_model).
+ */
+#ifndef MIAG_H
+#define MIAG_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct miag_ctx miag_ctx;
+
+/* The mia_header fields the MoE block reads (include/mia/mia_file.h:10-19).
+ * dim and expert_hidden are multiples of 32; n_active <= 64 (forward.c:172). */
+typedef struct {
+    int32_t dim;           /* d, 2048 for Qwen3-30B-A3B */
+    int32_t n_layers;      /* layers whose experts are kept resident */
+    int32_t n_experts;     /* E <= 1024 */
+    int32_t n_active;      /* K, top-k per token */
+    int32_t expert_hidden; /* eh */
+    int32_t norm_topk;     /* renormalise the top-k weights (forward.c:180) */
+    float norm_eps;        /* rmsnorm epsilon */
+} miag_shape;
+
+/* The reference loader port, include/mia/expert_cache.h:8: fills dst with the
+ * expert blob (layer, expert) in .mia layout (gate | up | down, Q8_0 rows,
+ * offsets as src/storage/mia_file.c:275-278).  mia_file_read_expert
+ * (include/mia/mia_file.h:44) has this signature. */
+typedef int (*miag_expert_loader)(void *ctx, int layer, int expert, void *dst);
+
+/* Byte size of one expert blob in .mia layout for this shape
+ * (tools/internal/mia/format.go:160-163, 16 KiB aligned). */
+size_t miag_blob_bytes(const miag_shape *shape);
+
+/* Creates a context on CUDA device `device`: validates the shape, allocates
+ * HBM for every layer's experts and dense router tensors.  Replaces
+ * mia_cache_init (include/mia/expert_cache.h:28-30) for the MoE path. */
+int miag_open(miag_ctx **out, const miag_shape *shape, int device, char *err,
+              size_t errlen);
+void miag_close(miag_ctx *c);
+
+/* Per-layer dense tensors of the block: ffn_norm [dim] and router
+ * [n_experts][dim] f32 (src/storage/mia_file.c:265-266).  bias [n_experts]
+ * is an optional logit offset added after the router matvec (NULL for the
+ * reference's behaviour). */
+int miag_set_layer(miag_ctx *c, int layer, const float *ffn_norm,
+                   const float *router, const float *bias, char *err,
+                   size_t errlen);
+
+/* Uploads n expert blobs of one layer from host memory (blob e at
+ * blobs + (e - first) * stride) into the resident HBM store. */
+int miag_upload_experts(miag_ctx *c, int layer, int first, int n,
+                        const void *blobs, size_t stride, char *err,
+                        size_t errlen);
+
+/* Uploads every (layer, expert) through the reference loader port, the way
+ * mia_cache_get fills a slot on a miss (src/storage/expert_cache.c:78).  A
+ * loader failure aborts with -1 and leaves the store unchanged for that
+ * expert. */
+int miag_load_experts(miag_ctx *c, miag_expert_loader load, void *load_ctx,
+                      char *err, size_t errlen);
+
+/* The MoE block, replacing forward.c:167-197 for n_tokens independent
+ * tokens: x [n_tokens][dim] f32 is the residual stream, read and updated in
+ * place (x += sum_j w_j * down_j(silu(gate_j xn) * up_j xn)).
+ * miag_moe takes a HOST pointer and returns when x holds the result.
+ * miag_moe_async takes a DEVICE pointer and only enqueues on `stream`
+ * (a cudaStream_t; NULL = the context's own stream). */
+int miag_moe(miag_ctx *c, int layer, float *x, int n_tokens, char *err,
+             size_t errlen);
+int miag_moe_async(miag_ctx *c, int layer, float *x_dev, int n_tokens,
+                   void *stream, char *err, size_t errlen);
+
+/* Waits for the context's work on `stream` (NULL = own stream) and reports
+ * any device-side error (a bounded wait that gave up, a bad index). */
+int miag_sync(miag_ctx *c, void *stream, char *err, size_t errlen);
+
+/* Routing of the most recent miag_moe / miag_moe_async call, copied to host
+ * (any pointer may be NULL): idx, w [n_tokens][n_active]; counts [E];
+ * offsets [E+1]; perm [n_tokens*n_active] (pair id t*K+j at each position of
+ * the canonical expert-sorted order). */
+int miag_routing(miag_ctx *c, int32_t *idx, float *w, int32_t *counts,
+                 int32_t *offsets, int32_t *perm, char *err, size_t errlen);
+
+/* Device kernels behind the reference's public math ABI, on device pointers
+ * and a stream (NULL = legacy default stream):
+ *   miag_quantize_row_q8  <- mia_quantize_row_q8 (include/mia/quant.h:18,
+ *                            src/tensor/quant.c:11-27); y holds n/32 36-byte
+ *                            mia_block_q8 records.
+ *   miag_matvec           <- mia_matvec (include/mia/matmul.h:11-12); w is
+ *                            row-major f32 (wtype 0) or Q8_0 blocks (wtype 1);
+ *                            xq is scratch for cols/32 blocks (Q8_0 only). */
+int miag_quantize_row_q8(const float *x, void *y, int n, void *stream);
+int miag_matvec(float *out, const void *w, int wtype, const float *x,
+                void *xq, int rows, int cols, void *stream);
+
+/* Number of kernels the most recent miag_moe / miag_moe_async launched. */
+int miag_last_launch_count(const miag_ctx *c);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,85 @@
+"""ctypes binding of libmiag.so (include/miag/miag.h).
+
+The library is the product: a C ABI over hand-written sm_100a kernels.  This
+module only declares its signatures.  It never substitutes anything for a
+missing library -- import fails loudly instead.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "lib" / "libmiag.so"
+
+
+class Shape(C.Structure):
+    """miag_shape (include/miag/miag.h)."""
+
+    _fields_ = [
+        ("dim", C.c_int32),
+        ("n_layers", C.c_int32),
+        ("n_experts", C.c_int32),
+        ("n_active", C.c_int32),
+        ("expert_hidden", C.c_int32),
+        ("norm_topk", C.c_int32),
+        ("norm_eps", C.c_float),
+    ]
+
+
+LOADER = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_void_p)
+
+# Every symbol include/miag/miag.h declares: name -> (restype, argtypes).
+SIGNATURES = {
+    "miag_blob_bytes": (C.c_size_t, [C.POINTER(Shape)]),
+    "miag_open": (C.c_int, [C.POINTER(C.c_void_p), C.POINTER(Shape), C.c_int, C.c_char_p,
+                            C.c_size_t]),
+    "miag_close": (None, [C.c_void_p]),
+    "miag_set_layer": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
+                                 C.c_char_p, C.c_size_t]),
+    "miag_upload_experts": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p,
+                                      C.c_size_t, C.c_char_p, C.c_size_t]),
+    "miag_load_experts": (C.c_int, [C.c_void_p, LOADER, C.c_void_p, C.c_char_p, C.c_size_t]),
+    "miag_moe": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_char_p, C.c_size_t]),
+    "miag_moe_async": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p,
+                                 C.c_char_p, C.c_size_t]),
+    "miag_sync": (C.c_int, [C.c_void_p, C.c_void_p, C.c_char_p, C.c_size_t]),
+    "miag_routing": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                               C.c_void_p, C.c_char_p, C.c_size_t]),
+    "miag_quantize_row_q8": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p]),
+    "miag_matvec": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_int,
+                              C.c_int, C.c_void_p]),
+    "miag_last_launch_count": (C.c_int, [C.c_void_p]),
+}
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    """Loads libmiag.so (raises if it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise ImportError(
+                f"{LIB_PATH} is missing: build it with `python -m motoria_b200.build` "
+                "(libmiag has no CPU fallback)")
+        dll = C.CDLL(str(LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(dll, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = dll
+    return _lib
+
+
+class MiagError(RuntimeError):
+    pass
+
+
+def check(rc: int, err: C.Array, what: str) -> None:
+    if rc != 0:
+        raise MiagError(f"{what}: {err.value.decode(errors='replace') or 'failed'}")
+
+
+def errbuf() -> C.Array:
+    return C.create_string_buffer(512)

@@ -1,0 +1,473 @@
+// api.cu -- the libmiag C ABI (include/miag/miag.h): context, HBM expert
+// store, workspace and the MoE block launch sequence.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <new>
+#include <vector>
+
+#include "../../include/miag/miag.h"
+#include "kernels.cuh"
+
+using namespace miag;
+
+namespace {
+
+struct LayerState {
+    float *ffn_norm = nullptr;
+    float *router_t = nullptr;
+    float *bias = nullptr;
+    bool has_bias = false;
+    bool dense_set = false;
+    uint8_t *experts = nullptr;
+};
+
+}  // namespace
+
+struct miag_ctx {
+    miag_shape shape;
+    Dims dims;
+    StoreLayout lay;
+    int device = 0, num_sms = 0;
+    cudaStream_t stream = nullptr;
+    std::vector<LayerState> layers;
+    size_t blob_bytes = 0;
+    // workspace
+    void *ws_mem = nullptr;
+    size_t ws_bytes = 0;
+    int ws_cap = 0;
+    Work ws{};
+    float *x_dev = nullptr;
+    int *d_err = nullptr;
+    int last_T = 0, last_launches = 0;
+    // upload staging
+    uint8_t *stage_dev = nullptr, *stage_host = nullptr;
+    size_t stage_bytes = 0;
+};
+
+static void set_err(char *err, size_t errlen, const char *fmt, ...) {
+    if (!err || errlen == 0) return;
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(err, errlen, fmt, ap);
+    va_end(ap);
+}
+
+#define CU(call)                                                                          \
+    do {                                                                                  \
+        cudaError_t e_ = (call);                                                          \
+        if (e_ != cudaSuccess) {                                                          \
+            set_err(err, errlen, "%s: %s", #call, cudaGetErrorString(e_));                \
+            return -1;                                                                    \
+        }                                                                                 \
+    } while (0)
+
+// Bytes of a .mia expert blob that hold data: gate and up at 64-byte aligned
+// offsets, then down (src/storage/mia_file.c:275-278).
+static size_t mia_blob_content(const miag_shape *s) {
+    const size_t mat = (size_t)s->expert_hidden * (s->dim / MIAG_QK) * 36;
+    const size_t off_up = round_up_sz(mat, 64);
+    const size_t down = (size_t)s->dim * (s->expert_hidden / MIAG_QK) * 36;
+    return 2 * off_up + down;
+}
+
+// The blob padded to the 16 KiB expert alignment (tools/internal/mia/format.go:164).
+static size_t mia_blob_bytes(const miag_shape *s) {
+    return round_up_sz(mia_blob_content(s), 16384);
+}
+
+extern "C" size_t miag_blob_bytes(const miag_shape *shape) {
+    return shape ? mia_blob_bytes(shape) : 0;
+}
+
+static int check_shape(const miag_shape *s, char *err, size_t errlen) {
+    if (!s) {
+        set_err(err, errlen, "null shape");
+        return -1;
+    }
+    if (s->dim <= 0 || s->dim % MIAG_QK || s->expert_hidden <= 0 ||
+        s->expert_hidden % MIAG_QK || s->n_experts <= 0 || s->n_experts > 1024 ||
+        s->n_active <= 0 || s->n_active > s->n_experts || s->n_active > 64 ||
+        s->n_layers <= 0) {
+        set_err(err, errlen,
+                "unsupported MoE shape (dim %d, expert_hidden %d, experts %d, active %d, layers %d)",
+                s->dim, s->expert_hidden, s->n_experts, s->n_active, s->n_layers);
+        return -1;
+    }
+    return 0;
+}
+
+extern "C" int miag_open(miag_ctx **out, const miag_shape *shape, int device, char *err,
+                         size_t errlen) {
+    if (!out) {
+        set_err(err, errlen, "null output pointer");
+        return -1;
+    }
+    *out = nullptr;
+    if (check_shape(shape, err, errlen)) return -1;
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
+        cudaGetLastError();
+        set_err(err, errlen, "no CUDA device: libmiag has no CPU path");
+        return -1;
+    }
+    if (device < 0 || device >= ndev) {
+        set_err(err, errlen, "device %d out of range (%d devices)", device, ndev);
+        return -1;
+    }
+    CU(cudaSetDevice(device));
+    cudaDeviceProp prop;
+    CU(cudaGetDeviceProperties(&prop, device));
+    if (prop.major != 10) {
+        set_err(err, errlen, "device %d is sm_%d%d; libmiag is built for sm_100a", device,
+                prop.major, prop.minor);
+        return -1;
+    }
+    miag_ctx *c = new (std::nothrow) miag_ctx();
+    if (!c) {
+        set_err(err, errlen, "out of host memory");
+        return -1;
+    }
+    c->shape = *shape;
+    c->dims = Dims{shape->dim, shape->expert_hidden, shape->n_experts, shape->n_active,
+                   shape->norm_topk, shape->norm_eps};
+    c->lay = make_layout(shape->dim, shape->expert_hidden);
+    c->device = device;
+    c->num_sms = prop.multiProcessorCount;
+    c->blob_bytes = mia_blob_bytes(shape);
+    c->layers.resize((size_t)shape->n_layers);
+    auto fail = [&](const char *what, cudaError_t e) {
+        set_err(err, errlen, "%s: %s", what, cudaGetErrorString(e));
+        miag_close(c);
+        return -1;
+    };
+    cudaError_t e;
+    if ((e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking)) != cudaSuccess)
+        return fail("cudaStreamCreate", e);
+    if ((e = cudaMalloc(&c->d_err, sizeof(int))) != cudaSuccess) return fail("cudaMalloc(err)", e);
+    if ((e = cudaMemset(c->d_err, 0, sizeof(int))) != cudaSuccess) return fail("cudaMemset", e);
+    const size_t E = (size_t)shape->n_experts, d = (size_t)shape->dim;
+    for (auto &L : c->layers) {
+        if ((e = cudaMalloc(&L.experts, E * c->lay.expert_bytes)) != cudaSuccess)
+            return fail("cudaMalloc(expert store)", e);
+        if ((e = cudaMemset(L.experts, 0, E * c->lay.expert_bytes)) != cudaSuccess)
+            return fail("cudaMemset(expert store)", e);
+        if ((e = cudaMalloc(&L.ffn_norm, d * 4)) != cudaSuccess) return fail("cudaMalloc", e);
+        if ((e = cudaMalloc(&L.router_t, d * E * 4)) != cudaSuccess) return fail("cudaMalloc", e);
+        if ((e = cudaMalloc(&L.bias, E * 4)) != cudaSuccess) return fail("cudaMalloc", e);
+    }
+    if (gemv_setup_attributes(c->dims, c->lay) != 0) {
+        set_err(err, errlen, "expert GEMV tiles do not fit in shared memory for this shape");
+        miag_close(c);
+        return -1;
+    }
+    *out = c;
+    return 0;
+}
+
+extern "C" void miag_close(miag_ctx *c) {
+    if (!c) return;
+    cudaSetDevice(c->device);
+    if (c->stream) cudaStreamSynchronize(c->stream);
+    for (auto &L : c->layers) {
+        cudaFree(L.experts);
+        cudaFree(L.ffn_norm);
+        cudaFree(L.router_t);
+        cudaFree(L.bias);
+    }
+    cudaFree(c->ws_mem);
+    cudaFree(c->d_err);
+    cudaFree(c->stage_dev);
+    if (c->stage_host) cudaFreeHost(c->stage_host);
+    if (c->stream) cudaStreamDestroy(c->stream);
+    delete c;
+}
+
+static int check_layer(miag_ctx *c, int layer, char *err, size_t errlen) {
+    if (!c) {
+        set_err(err, errlen, "null context");
+        return -1;
+    }
+    if (layer < 0 || layer >= c->shape.n_layers) {
+        set_err(err, errlen, "layer %d out of range (%d layers)", layer, c->shape.n_layers);
+        return -1;
+    }
+    return 0;
+}
+
+extern "C" int miag_set_layer(miag_ctx *c, int layer, const float *ffn_norm, const float *router,
+                              const float *bias, char *err, size_t errlen) {
+    if (check_layer(c, layer, err, errlen)) return -1;
+    if (!ffn_norm || !router) {
+        set_err(err, errlen, "ffn_norm and router are required");
+        return -1;
+    }
+    CU(cudaSetDevice(c->device));
+    LayerState &L = c->layers[(size_t)layer];
+    const size_t E = (size_t)c->shape.n_experts, d = (size_t)c->shape.dim;
+    float *tmp = nullptr;
+    CU(cudaMalloc(&tmp, E * d * 4));
+    cudaError_t e = cudaMemcpyAsync(tmp, router, E * d * 4, cudaMemcpyHostToDevice, c->stream);
+    if (e == cudaSuccess) {
+        launch_transpose_router(tmp, L.router_t, (int)E, (int)d, c->stream);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(L.ffn_norm, ffn_norm, d * 4, cudaMemcpyHostToDevice, c->stream);
+    if (e == cudaSuccess && bias)
+        e = cudaMemcpyAsync(L.bias, bias, E * 4, cudaMemcpyHostToDevice, c->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    cudaFree(tmp);
+    if (e != cudaSuccess) {
+        set_err(err, errlen, "set_layer: %s", cudaGetErrorString(e));
+        return -1;
+    }
+    L.has_bias = bias != nullptr;
+    L.dense_set = true;
+    return 0;
+}
+
+static int ensure_staging(miag_ctx *c, size_t bytes, char *err, size_t errlen) {
+    if (c->stage_bytes >= bytes) return 0;
+    cudaFree(c->stage_dev);
+    if (c->stage_host) cudaFreeHost(c->stage_host);
+    c->stage_dev = nullptr, c->stage_host = nullptr, c->stage_bytes = 0;
+    CU(cudaMalloc(&c->stage_dev, bytes));
+    CU(cudaMallocHost(&c->stage_host, bytes));
+    c->stage_bytes = bytes;
+    return 0;
+}
+
+static const int kUploadBatch = 16;  // experts per staging round
+
+extern "C" int miag_upload_experts(miag_ctx *c, int layer, int first, int n, const void *blobs,
+                                   size_t stride, char *err, size_t errlen) {
+    if (check_layer(c, layer, err, errlen)) return -1;
+    if (!blobs || n < 0 || first < 0 || first + n > c->shape.n_experts) {
+        set_err(err, errlen, "bad expert range [%d, %d)", first, first + n);
+        return -1;
+    }
+    const size_t need = mia_blob_content(&c->shape);
+    if (stride < need) {
+        set_err(err, errlen, "blob stride %zu smaller than the .mia blob (%zu)", stride, need);
+        return -1;
+    }
+    CU(cudaSetDevice(c->device));
+    if (ensure_staging(c, (size_t)kUploadBatch * stride, err, errlen)) return -1;
+    LayerState &L = c->layers[(size_t)layer];
+    for (int e0 = 0; e0 < n; e0 += kUploadBatch) {
+        const int nb = n - e0 < kUploadBatch ? n - e0 : kUploadBatch;
+        const uint8_t *src = (const uint8_t *)blobs + (size_t)e0 * stride;
+        memcpy(c->stage_host, src, (size_t)nb * stride);
+        CU(cudaMemcpyAsync(c->stage_dev, c->stage_host, (size_t)nb * stride, cudaMemcpyHostToDevice,
+                           c->stream));
+        launch_repack(c->dims, c->lay, c->stage_dev, stride, nb,
+                      L.experts + (size_t)(first + e0) * c->lay.expert_bytes, c->stream);
+        CU(cudaGetLastError());
+        CU(cudaStreamSynchronize(c->stream));
+    }
+    return 0;
+}
+
+extern "C" int miag_load_experts(miag_ctx *c, miag_expert_loader load, void *load_ctx, char *err,
+                                 size_t errlen) {
+    if (!c || !load) {
+        set_err(err, errlen, "null context or loader");
+        return -1;
+    }
+    CU(cudaSetDevice(c->device));
+    const size_t stride = c->blob_bytes;
+    if (ensure_staging(c, (size_t)kUploadBatch * stride, err, errlen)) return -1;
+    for (int l = 0; l < c->shape.n_layers; l++) {
+        LayerState &L = c->layers[(size_t)l];
+        for (int e0 = 0; e0 < c->shape.n_experts; e0 += kUploadBatch) {
+            const int nb = c->shape.n_experts - e0 < kUploadBatch ? c->shape.n_experts - e0
+                                                                   : kUploadBatch;
+            // Wait for the previous batch's copy out of the pinned buffer.
+            CU(cudaStreamSynchronize(c->stream));
+            int ok = 0;
+            for (int k = 0; k < nb; k++) {
+                if (load(load_ctx, l, e0 + k, c->stage_host + (size_t)k * stride) != 0) {
+                    set_err(err, errlen, "expert loader failed for layer %d expert %d", l, e0 + k);
+                    break;
+                }
+                ok++;
+            }
+            // Experts that did load in this batch are still stored.
+            if (ok > 0) {
+                CU(cudaMemcpyAsync(c->stage_dev, c->stage_host, (size_t)ok * stride,
+                                   cudaMemcpyHostToDevice, c->stream));
+                launch_repack(c->dims, c->lay, c->stage_dev, stride, ok,
+                              L.experts + (size_t)e0 * c->lay.expert_bytes, c->stream);
+                CU(cudaGetLastError());
+            }
+            if (ok < nb) {
+                cudaStreamSynchronize(c->stream);
+                return -1;
+            }
+        }
+    }
+    CU(cudaStreamSynchronize(c->stream));
+    return 0;
+}
+
+static void *bump(uint8_t *&p, size_t bytes) {
+    void *r = p;
+    p += round_up_sz(bytes, 256);
+    return r;
+}
+
+static size_t ws_layout(miag_ctx *c, int T, uint8_t *base, Work *w, float **x_dev) {
+    const Dims &m = c->dims;
+    const size_t P = (size_t)T * m.K;
+    const int nchunks = (int)((P + kPermChunk - 1) / kPermChunk);
+    const int xs = scale_pad(m.d / MIAG_QK), hs = scale_pad(m.eh / MIAG_QK);
+    uint8_t *p = base;
+    Work v{};
+    v.T = T, v.P = (int)P, v.nchunks = nchunks;
+    v.xq = (int8_t *)bump(p, (size_t)T * m.d);
+    v.dx = (float *)bump(p, (size_t)T * xs * 4);
+    v.logits = (float *)bump(p, (size_t)T * m.E * 4);
+    v.ticket = (int32_t *)bump(p, (size_t)((T + 1) / 2) * 4);
+    v.idx = (int32_t *)bump(p, P * 4);
+    v.w = (float *)bump(p, P * 4);
+    v.rank = (int32_t *)bump(p, P * 4);
+    v.chunk_cnt = (int32_t *)bump(p, (size_t)nchunks * m.E * 4);
+    v.chunk_base = (int32_t *)bump(p, (size_t)nchunks * m.E * 4);
+    v.counts = (int32_t *)bump(p, (size_t)m.E * 4);
+    v.offsets = (int32_t *)bump(p, (size_t)(m.E + 1) * 4);
+    v.active = (int32_t *)bump(p, (size_t)m.E * 4);
+    v.n_active = (int32_t *)bump(p, 4);
+    v.perm = (int32_t *)bump(p, P * 4);
+    v.inv = (int32_t *)bump(p, P * 4);
+    v.h = (float *)bump(p, P * m.eh * 4);
+    v.hq = (int8_t *)bump(p, P * m.eh);
+    v.dh = (float *)bump(p, P * hs * 4);
+    v.y = (float *)bump(p, P * m.d * 4);
+    float *xd = (float *)bump(p, (size_t)T * m.d * 4);
+    if (w) *w = v;
+    if (x_dev) *x_dev = xd;
+    return (size_t)(p - base);
+}
+
+// Sizes the workspace for at least T tokens.  Buffers are laid out for the
+// capacity, so per-call state that must persist (the zeroed route tickets)
+// keeps its address; only the counts change with T.
+static int ensure_ws(miag_ctx *c, int T, char *err, size_t errlen) {
+    if (T > c->ws_cap) {
+        int cap = c->ws_cap ? c->ws_cap : 64;
+        while (cap < T) cap *= 2;
+        const size_t bytes = ws_layout(c, cap, nullptr, nullptr, nullptr);
+        cudaStreamSynchronize(c->stream);
+        cudaFree(c->ws_mem);
+        c->ws_mem = nullptr, c->ws_cap = 0;
+        CU(cudaMalloc(&c->ws_mem, bytes));
+        CU(cudaMemset(c->ws_mem, 0, bytes));
+        c->ws_bytes = bytes;
+        c->ws_cap = cap;
+    }
+    ws_layout(c, c->ws_cap, (uint8_t *)c->ws_mem, &c->ws, &c->x_dev);
+    const int P = T * c->dims.K;
+    c->ws.T = T, c->ws.P = P, c->ws.nchunks = (P + kPermChunk - 1) / kPermChunk;
+    return 0;
+}
+
+static int enqueue_moe(miag_ctx *c, int layer, float *x_dev, int T, cudaStream_t s, char *err,
+                       size_t errlen) {
+    const LayerState &Ls = c->layers[(size_t)layer];
+    if (!Ls.dense_set) {
+        set_err(err, errlen, "layer %d has no router / ffn_norm (miag_set_layer)", layer);
+        return -1;
+    }
+    LayerDev L{Ls.ffn_norm, Ls.router_t, Ls.has_bias ? Ls.bias : nullptr, Ls.experts};
+    const Work &w = c->ws;
+    launch_route(c->dims, L, x_dev, w, c->d_err, s);
+    launch_permute(c->dims, w, c->d_err, s);
+    launch_gateup(c->dims, c->lay, L, w, c->num_sms, c->d_err, s);
+    launch_quant_h(c->dims, w, s);
+    launch_down(c->dims, c->lay, L, w, c->num_sms, c->d_err, s);
+    launch_combine(c->dims, w, x_dev, s);
+    c->last_launches = 8;
+    c->last_T = T;
+    CU(cudaGetLastError());
+    return 0;
+}
+
+extern "C" int miag_moe_async(miag_ctx *c, int layer, float *x_dev, int n_tokens, void *stream,
+                              char *err, size_t errlen) {
+    if (check_layer(c, layer, err, errlen)) return -1;
+    if (n_tokens < 0 || (n_tokens > 0 && !x_dev)) {
+        set_err(err, errlen, "bad token buffer");
+        return -1;
+    }
+    if (n_tokens == 0) {
+        c->last_launches = 0;
+        return 0;
+    }
+    CU(cudaSetDevice(c->device));
+    if (ensure_ws(c, n_tokens, err, errlen)) return -1;
+    return enqueue_moe(c, layer, x_dev, n_tokens, stream ? (cudaStream_t)stream : c->stream, err,
+                       errlen);
+}
+
+static int read_device_error(miag_ctx *c, char *err, size_t errlen) {
+    int code = 0;
+    CU(cudaMemcpy(&code, c->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (code == 0) return 0;
+    CU(cudaMemset(c->d_err, 0, sizeof(int)));
+    const char *what = code == kErrWaitFull    ? "a consumer timed out waiting for a staged tile"
+                       : code == kErrWaitEmpty ? "the producer timed out waiting for a free stage"
+                       : code == kErrBadExpert ? "a routing index was out of range"
+                                               : "unknown device error";
+    set_err(err, errlen, "device error %d: %s", code, what);
+    return -1;
+}
+
+extern "C" int miag_sync(miag_ctx *c, void *stream, char *err, size_t errlen) {
+    if (!c) {
+        set_err(err, errlen, "null context");
+        return -1;
+    }
+    CU(cudaSetDevice(c->device));
+    CU(cudaStreamSynchronize(stream ? (cudaStream_t)stream : c->stream));
+    return read_device_error(c, err, errlen);
+}
+
+extern "C" int miag_moe(miag_ctx *c, int layer, float *x, int n_tokens, char *err, size_t errlen) {
+    if (check_layer(c, layer, err, errlen)) return -1;
+    if (n_tokens < 0 || (n_tokens > 0 && !x)) {
+        set_err(err, errlen, "bad token buffer");
+        return -1;
+    }
+    if (n_tokens == 0) {
+        c->last_launches = 0;
+        return 0;
+    }
+    CU(cudaSetDevice(c->device));
+    if (ensure_ws(c, n_tokens, err, errlen)) return -1;
+    const size_t bytes = (size_t)n_tokens * c->shape.dim * sizeof(float);
+    CU(cudaMemcpyAsync(c->x_dev, x, bytes, cudaMemcpyHostToDevice, c->stream));
+    if (enqueue_moe(c, layer, c->x_dev, n_tokens, c->stream, err, errlen)) return -1;
+    CU(cudaMemcpyAsync(x, c->x_dev, bytes, cudaMemcpyDeviceToHost, c->stream));
+    CU(cudaStreamSynchronize(c->stream));
+    return read_device_error(c, err, errlen);
+}
+
+extern "C" int miag_routing(miag_ctx *c, int32_t *idx, float *w, int32_t *counts, int32_t *offsets,
+                            int32_t *perm, char *err, size_t errlen) {
+    if (!c) {
+        set_err(err, errlen, "null context");
+        return -1;
+    }
+    CU(cudaSetDevice(c->device));
+    CU(cudaStreamSynchronize(c->stream));
+    const size_t P = (size_t)c->last_T * c->dims.K, E = (size_t)c->dims.E;
+    if (idx) CU(cudaMemcpy(idx, c->ws.idx, P * 4, cudaMemcpyDeviceToHost));
+    if (w) CU(cudaMemcpy(w, c->ws.w, P * 4, cudaMemcpyDeviceToHost));
+    if (counts) CU(cudaMemcpy(counts, c->ws.counts, E * 4, cudaMemcpyDeviceToHost));
+    if (offsets) CU(cudaMemcpy(offsets, c->ws.offsets, (E + 1) * 4, cudaMemcpyDeviceToHost));
+    if (perm) CU(cudaMemcpy(perm, c->ws.perm, P * 4, cudaMemcpyDeviceToHost));
+    return 0;
+}
+
+extern "C" int miag_last_launch_count(const miag_ctx *c) { return c ? c->last_launches : 0; }

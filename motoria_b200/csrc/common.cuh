@@ -1,0 +1,174 @@
+// common.cuh -- shared device helpers and layouts of libmiag (sm_100a).
+//
+// Numerics: nothing here is compiled with fast-math.  Every float operation
+// whose rounding the reference fixes is written with an explicit
+// round-to-nearest intrinsic (__fadd_rn, __fmul_rn, __fdiv_rn, ...), which
+// the compiler never contracts into an FMA, so the GPU repeats the
+// reference's x86 scalar arithmetic operation for operation.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#define MIAG_QK 32
+
+namespace miag {
+
+// Device error codes written to the context's error word (first one wins).
+enum : int {
+    kErrNone = 0,
+    kErrWaitFull = 1,     // a consumer gave up waiting for a staged tile
+    kErrWaitEmpty = 2,    // the producer gave up waiting for a free stage
+    kErrBadExpert = 3,    // a routing index outside [0, E)
+};
+
+// Bounded spin: about one second at B200 clocks.
+constexpr long long kWaitCycles = 2000000000LL;
+
+// ---------------------------------------------------------------------------
+// HBM layout of one layer's expert store ("SoA", repacked from the .mia
+// array-of-36-byte-blocks layout at upload).  Per expert, contiguous:
+//   gu_q  int8  [2*eh][d]        row 2i = gate row i, row 2i+1 = up row i
+//   gu_s  f32   [2*eh][gu_srow]  that row's per-32-block scales (16-B rows)
+//   dn_q  int8  [d][eh]          down rows
+//   dn_s  f32   [d][dn_srow]
+// Every row starts 16-byte aligned, so a row is one bulk-copy unit.
+struct StoreLayout {
+    int d, eh;
+    uint32_t gu_q_off, gu_s_off, dn_q_off, dn_s_off;
+    uint32_t gu_s_row, dn_s_row;  // bytes per scale row (multiple of 16)
+    size_t expert_bytes;
+};
+
+inline size_t round_up_sz(size_t n, size_t a) { return (n + a - 1) / a * a; }
+
+inline StoreLayout make_layout(int d, int eh) {
+    StoreLayout L;
+    L.d = d, L.eh = eh;
+    L.gu_s_row = (uint32_t)round_up_sz((size_t)(d / MIAG_QK) * 4, 16);
+    L.dn_s_row = (uint32_t)round_up_sz((size_t)(eh / MIAG_QK) * 4, 16);
+    size_t off = 0;
+    L.gu_q_off = (uint32_t)off;
+    off = round_up_sz(off + (size_t)2 * eh * d, 256);
+    L.gu_s_off = (uint32_t)off;
+    off = round_up_sz(off + (size_t)2 * eh * L.gu_s_row, 256);
+    L.dn_q_off = (uint32_t)off;
+    off = round_up_sz(off + (size_t)d * eh, 256);
+    L.dn_s_off = (uint32_t)off;
+    off = round_up_sz(off + (size_t)d * L.dn_s_row, 256);
+    L.expert_bytes = off;
+    return L;
+}
+
+// Shared-memory row stride for a staged row of `bytes`: a multiple of 16
+// whose 16-byte count is odd, so eight lanes reading 16 bytes at the same
+// column of eight consecutive rows hit 32 distinct banks.
+__host__ __device__ inline uint32_t smem_stride(uint32_t bytes) {
+    uint32_t s = (bytes + 15u) & ~15u;
+    if (((s >> 4) & 1u) == 0u) s += 16u;
+    return s;
+}
+
+// Padded count of f32 scales per activation row (16-byte rows).
+__host__ __device__ inline int scale_pad(int nblocks) { return (nblocks + 3) & ~3; }
+
+// ---------------------------------------------------------------------------
+// Correctly rounded expf: the float nearest CUDA's double-precision exp
+// (documented max error 1 double ulp), i.e. the true e^x rounded to float
+// except within ~2^-29 relative of a float rounding midpoint.
+__device__ __forceinline__ float expf_cr(float x) {
+    return __double2float_rn(exp((double)x));
+}
+
+// Reference SiLU-GLU element (forward.c:189-190): g / (1 + expf(-g)) * u.
+__device__ __forceinline__ float swiglu_ref(float g, float u) {
+    float e = expf_cr(-g);
+    return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, e)), u);
+}
+
+// ---------------------------------------------------------------------------
+// mbarrier / bulk-copy (TMA 1-D) wrappers.  No cluster multicast anywhere.
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
+                 : "memory");
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Waits for the phase of `parity` to complete; false after ~1 s.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity)) {
+        if (clock64() - t0 > kWaitCycles) return false;
+    }
+    return true;
+}
+
+// Global -> shared bulk copy completing on `bar` (16-B aligned, bytes % 16 == 0).
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes,
+                                         uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void set_error(int *err, int code) {
+    if (err) atomicCAS(err, 0, code);
+}
+
+__device__ __forceinline__ int4 ldg_nc_v4(const void *p) {
+    return __ldg(reinterpret_cast<const int4 *>(p));
+}
+
+// Exact int8 dot of one 32-value block held as two 16-byte vectors each.
+__device__ __forceinline__ int dot_block_i8(int4 a0, int4 a1, int4 b0, int4 b1) {
+    int acc = 0;
+    acc = __dp4a(a0.x, b0.x, acc);
+    acc = __dp4a(a0.y, b0.y, acc);
+    acc = __dp4a(a0.z, b0.z, acc);
+    acc = __dp4a(a0.w, b0.w, acc);
+    acc = __dp4a(a1.x, b1.x, acc);
+    acc = __dp4a(a1.y, b1.y, acc);
+    acc = __dp4a(a1.z, b1.z, acc);
+    acc = __dp4a(a1.w, b1.w, acc);
+    return acc;
+}
+
+// One reference Q8_0 step: s += ((float)acc * dw) * dx (matmul.c:25).
+__device__ __forceinline__ float q8_step(float s, int acc, float dw, float dx) {
+    return __fadd_rn(s, __fmul_rn(__fmul_rn(__int2float_rn(acc), dw), dx));
+}
+
+}  // namespace miag

@@ -1,0 +1,65 @@
+// kernels.cuh -- launchers of the MoE block kernels (host-side declarations).
+#pragma once
+
+#include "common.cuh"
+
+namespace miag {
+
+// Device workspace of one MoE call over T tokens, P = T*K pairs.
+struct Work {
+    int T, P, nchunks;
+    int8_t *xq;            // [T][d]        quantized normalised input (Q8_0 values)
+    float *dx;             // [T][xs_pad]   its block scales
+    float *logits;         // [T][E]        router logits (+ bias)
+    int32_t *ticket;       // [ceil(T/2)]   route token-group completion tickets (self-resetting)
+    int32_t *idx;          // [T][K]
+    float *w;              // [T][K]
+    int32_t *rank;         // [P]           stable rank of a pair inside its chunk
+    int32_t *chunk_cnt;    // [nchunks][E]
+    int32_t *chunk_base;   // [nchunks][E]
+    int32_t *counts;       // [E]
+    int32_t *offsets;      // [E+1]
+    int32_t *active;       // [E]           experts with >= 1 pair, ascending
+    int32_t *n_active;     // [1]
+    int32_t *perm;         // [P]           pair id at each sorted position
+    int32_t *inv;          // [P]           sorted position of each pair
+    float *h;              // [P][eh]       silu(gate) * up, sorted order
+    int8_t *hq;            // [P][eh]       Q8_0 values of h
+    float *dh;             // [P][hs_pad]
+    float *y;              // [P][d]        down projections, sorted order
+};
+
+struct LayerDev {
+    const float *ffn_norm;  // [d]
+    const float *router_t;  // [d][E]  router transposed (column e contiguous over d)
+    const float *bias;      // [E] or nullptr
+    const uint8_t *experts; // E * layout.expert_bytes
+};
+
+struct Dims {
+    int d, eh, E, K, norm_topk;
+    float eps;
+};
+
+constexpr int kPermChunk = 1024;
+
+// route.cu
+void launch_route(const Dims &m, const LayerDev &L, const float *x, const Work &w,
+                  int *err, cudaStream_t s);
+// permute.cu
+void launch_permute(const Dims &m, const Work &w, int *err, cudaStream_t s);
+// gemv.cu
+void launch_gateup(const Dims &m, const StoreLayout &lay, const LayerDev &L, const Work &w,
+                   int num_sms, int *err, cudaStream_t s);
+void launch_quant_h(const Dims &m, const Work &w, cudaStream_t s);
+void launch_down(const Dims &m, const StoreLayout &lay, const LayerDev &L, const Work &w,
+                 int num_sms, int *err, cudaStream_t s);
+void launch_combine(const Dims &m, const Work &w, float *x, cudaStream_t s);
+int gemv_setup_attributes(const Dims &m, const StoreLayout &lay);
+// store.cu
+void launch_repack(const Dims &m, const StoreLayout &lay, const uint8_t *aos, size_t aos_stride,
+                   int n, uint8_t *dst, cudaStream_t s);
+void launch_transpose_router(const float *router, float *router_t, int E, int d,
+                             cudaStream_t s);
+
+}  // namespace miag

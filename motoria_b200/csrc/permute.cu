@@ -1,0 +1,143 @@
+// permute.cu -- canonical dispatch order of (token, slot) pairs.
+//
+// The reference runs one token at a time and has no permutation
+// (src/model/forward.c:183-195 loops over the token's own top-k).  Batching
+// tokens needs one: pairs p = t*K + j are stably sorted by expert, so within
+// an expert they stay in (t, j) order.  Deterministic: no order-dependent
+// atomics; ranks come from warp match masks and per-warp prefix counts.
+//
+//   k_perm_count   per chunk of 1024 pairs: stable rank of each pair among
+//                  the chunk's pairs of the same expert, and chunk histograms
+//   k_perm_scan    per expert: chunk bases, counts, offsets, active list
+//   k_perm_scatter perm[pos] = p, inv[p] = pos
+#include "kernels.cuh"
+
+namespace miag {
+
+constexpr int kPermThreads = 256;
+constexpr int kPermWarps = kPermThreads / 32;
+
+__global__ void __launch_bounds__(kPermThreads)
+k_perm_count(const int32_t *idx, int P, int E, int32_t *rank, int32_t *chunk_cnt, int *err) {
+    extern __shared__ int32_t sh[];  // cnt[E], wcnt[kPermWarps][E]
+    int32_t *cnt = sh;
+    int32_t *wcnt = sh + E;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int base = blockIdx.x * kPermChunk;
+    for (int e = tid; e < E; e += kPermThreads) cnt[e] = 0;
+    for (int sub = 0; sub < kPermChunk; sub += kPermThreads) {
+        for (int i = tid; i < kPermWarps * E; i += kPermThreads) wcnt[i] = 0;
+        __syncthreads();
+        const int p = base + sub + tid;
+        int e = -1;
+        if (p < P) {
+            e = idx[p];
+            if (e < 0 || e >= E) {
+                set_error(err, kErrBadExpert);
+                e = -1;
+            }
+        }
+        const unsigned peers = __match_any_sync(0xffffffffu, e);
+        const int lr = __popc(peers & ((1u << lane) - 1u));
+        if (e >= 0 && lr == 0) wcnt[warp * E + e] = __popc(peers);
+        __syncthreads();
+        for (int x = tid; x < E; x += kPermThreads) {
+            int run = cnt[x];
+            for (int w = 0; w < kPermWarps; w++) {
+                int c = wcnt[w * E + x];
+                wcnt[w * E + x] = run;
+                run += c;
+            }
+            cnt[x] = run;
+        }
+        __syncthreads();
+        if (e >= 0) rank[p] = wcnt[warp * E + e] + lr;
+        __syncthreads();
+    }
+    for (int e = tid; e < E; e += kPermThreads) chunk_cnt[(size_t)blockIdx.x * E + e] = cnt[e];
+}
+
+// Exclusive block scan of one value per thread (blockDim.x <= 1024).
+__device__ int block_excl_scan(int v, int *total, int *sh /* >= 33 ints */) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int incl = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        int n = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += n;
+    }
+    if (lane == 31) sh[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+        const int nw = (blockDim.x + 31) >> 5;
+        int s = lane < nw ? sh[lane] : 0;
+        int si = s;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            int n = __shfl_up_sync(0xffffffffu, si, o);
+            if (lane >= o) si += n;
+        }
+        sh[lane] = si - s;
+        if (lane == 31) sh[32] = si;
+    }
+    __syncthreads();
+    int r = sh[warp] + incl - v;
+    *total = sh[32];
+    __syncthreads();
+    return r;
+}
+
+__global__ void __launch_bounds__(1024)
+k_perm_scan(int nchunks, int E, const int32_t *chunk_cnt, int32_t *chunk_base, int32_t *counts,
+            int32_t *offsets, int32_t *active, int32_t *n_active) {
+    __shared__ int sh[33];
+    const int e = threadIdx.x;
+    int run = 0;
+    if (e < E) {
+        for (int c = 0; c < nchunks; c++) {
+            int v = chunk_cnt[(size_t)c * E + e];
+            chunk_base[(size_t)c * E + e] = run;
+            run += v;
+        }
+        counts[e] = run;
+    }
+    int total;
+    const int off = block_excl_scan(e < E ? run : 0, &total, sh);
+    int nact;
+    const int apos = block_excl_scan((e < E && run > 0) ? 1 : 0, &nact, sh);
+    if (e < E) {
+        offsets[e] = off;
+        if (run > 0) active[apos] = e;
+        for (int c = 0; c < nchunks; c++) chunk_base[(size_t)c * E + e] += off;
+    }
+    if (e == 0) {
+        offsets[E] = total;
+        *n_active = nact;
+    }
+}
+
+__global__ void k_perm_scatter(const int32_t *idx, int P, int E, const int32_t *rank,
+                               const int32_t *chunk_base, int32_t *perm, int32_t *inv) {
+    const int p = blockIdx.x * blockDim.x + threadIdx.x;
+    if (p >= P) return;
+    const int e = idx[p];
+    if (e < 0 || e >= E) return;
+    const int pos = chunk_base[(size_t)(p / kPermChunk) * E + e] + rank[p];
+    perm[pos] = p;
+    inv[p] = pos;
+}
+
+void launch_permute(const Dims &m, const Work &w, int *err, cudaStream_t s) {
+    const int P = w.P, E = m.E;
+    const size_t smem = sizeof(int32_t) * (size_t)E * (1 + kPermWarps);
+    if (smem > 48 * 1024)
+        cudaFuncSetAttribute(k_perm_count, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    k_perm_count<<<w.nchunks, kPermThreads, smem, s>>>(w.idx, P, E, w.rank, w.chunk_cnt, err);
+    const int st = ((E + 31) / 32) * 32;
+    k_perm_scan<<<1, st < 64 ? 64 : st, 0, s>>>(w.nchunks, E, w.chunk_cnt, w.chunk_base, w.counts,
+                                                w.offsets, w.active, w.n_active);
+    k_perm_scatter<<<(P + 255) / 256, 256, 0, s>>>(w.idx, P, E, w.rank, w.chunk_base, w.perm,
+                                                   w.inv);
+}
+
+}  // namespace miag

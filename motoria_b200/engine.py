@@ -1,0 +1,166 @@
+"""Host-side mirror of the reference MoE interface over libmiag.
+
+Names follow the reference engine (nextocodeoficial/motorIa):
+
+  MoEEngine.moe(x, layer)   <- static int moe(mia_model*, dims, int layer)
+                               (src/model/forward.c:167-197), batched over tokens
+  MoEEngine.load_experts    <- the mia_expert_loader port
+                               (include/mia/expert_cache.h:8) filling HBM once
+  quantize_row_q8           <- mia_quantize_row_q8 (include/mia/quant.h:18)
+  matvec                    <- mia_matvec (include/mia/matmul.h:11-12)
+
+Errors surface as MiagError carrying the library's message, the way the
+reference returns -1 with text in an err buffer.  There is no CPU path.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+from . import _native as N
+from .synth import Shape
+
+MIA_F32, MIA_Q8_0 = 0, 1
+
+
+def _shape(shape: Shape, n_layers: int) -> N.Shape:
+    return N.Shape(shape.dim, n_layers, shape.n_experts, shape.n_active, shape.expert_hidden,
+                   shape.norm_topk, shape.norm_eps)
+
+
+def blob_bytes(shape: Shape) -> int:
+    s = _shape(shape, 1)
+    return int(N.lib().miag_blob_bytes(C.byref(s)))
+
+
+class MoEEngine:
+    """One libmiag context: HBM-resident experts for n_layers MoE layers."""
+
+    def __init__(self, shape: Shape, n_layers: int = 1, device: int = 0):
+        self.shape = shape
+        self.n_layers = n_layers
+        self._lib = N.lib()
+        self._ctx = C.c_void_p()
+        s = _shape(shape, n_layers)
+        err = N.errbuf()
+        N.check(self._lib.miag_open(C.byref(self._ctx), C.byref(s), device, err, len(err)), err,
+                "miag_open")
+
+    @property
+    def handle(self) -> int:
+        return self._ctx.value
+
+    def close(self) -> None:
+        if self._ctx:
+            self._lib.miag_close(self._ctx)
+            self._ctx = C.c_void_p()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_layer(self, layer: int, ffn_norm: np.ndarray, router: np.ndarray,
+                  bias: np.ndarray | None = None) -> None:
+        fn = np.ascontiguousarray(ffn_norm, dtype=np.float32)
+        rt = np.ascontiguousarray(router, dtype=np.float32)
+        bs = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+        err = N.errbuf()
+        rc = self._lib.miag_set_layer(self._ctx, layer, fn.ctypes.data, rt.ctypes.data,
+                                      None if bs is None else bs.ctypes.data, err, len(err))
+        N.check(rc, err, "miag_set_layer")
+
+    def upload_experts(self, layer: int, blobs: np.ndarray, first: int = 0) -> None:
+        b = np.ascontiguousarray(blobs, dtype=np.uint8)
+        if b.ndim != 2:
+            raise ValueError("blobs must be [n_experts][blob_stride] uint8")
+        err = N.errbuf()
+        rc = self._lib.miag_upload_experts(self._ctx, layer, first, b.shape[0], b.ctypes.data,
+                                           b.shape[1], err, len(err))
+        N.check(rc, err, "miag_upload_experts")
+
+    def load_experts(self, loader) -> None:
+        """loader(layer, expert, dst: memoryview) -> int (0 = ok), the reference port."""
+        nbytes = blob_bytes(self.shape)
+
+        def tramp(_ctx, layer, expert, dst):
+            view = (C.c_uint8 * nbytes).from_address(dst)
+            try:
+                return int(loader(layer, expert, memoryview(view).cast("B")))
+            except Exception:
+                return -1
+
+        cb = N.LOADER(tramp)
+        err = N.errbuf()
+        rc = self._lib.miag_load_experts(self._ctx, cb, None, err, len(err))
+        N.check(rc, err, "miag_load_experts")
+
+    def load_layer(self, layer: int, lay) -> None:
+        """Uploads a synth.Layer (dense tensors + expert blobs)."""
+        self.set_layer(layer, lay.ffn_norm, lay.router, lay.bias)
+        self.upload_experts(layer, lay.blobs)
+
+    def moe(self, x: np.ndarray, layer: int = 0) -> np.ndarray:
+        """Returns x + MoE(x) for x [T][dim] f32 (host in, host out)."""
+        out = np.array(x, dtype=np.float32, order="C", copy=True)
+        if out.ndim == 1:
+            out = out[None, :]
+        err = N.errbuf()
+        rc = self._lib.miag_moe(self._ctx, layer, out.ctypes.data, out.shape[0], err, len(err))
+        N.check(rc, err, "miag_moe")
+        return out.reshape(np.shape(x))
+
+    def moe_device(self, x_ptr: int, n_tokens: int, layer: int = 0, stream: int | None = None):
+        """Enqueues the block on a device buffer x_ptr [n_tokens][dim] (in place)."""
+        err = N.errbuf()
+        rc = self._lib.miag_moe_async(self._ctx, layer, C.c_void_p(x_ptr), n_tokens,
+                                      C.c_void_p(stream or 0), err, len(err))
+        N.check(rc, err, "miag_moe_async")
+
+    def sync(self, stream: int | None = None) -> None:
+        err = N.errbuf()
+        N.check(self._lib.miag_sync(self._ctx, C.c_void_p(stream or 0), err, len(err)), err,
+                "miag_sync")
+
+    def routing(self, n_tokens: int) -> dict:
+        """Routing of the last call: idx, w [T][K]; counts [E]; offsets [E+1]; perm [T*K]."""
+        K, E = self.shape.n_active, self.shape.n_experts
+        idx = np.zeros((n_tokens, K), np.int32)
+        w = np.zeros((n_tokens, K), np.float32)
+        counts = np.zeros(E, np.int32)
+        offsets = np.zeros(E + 1, np.int32)
+        perm = np.zeros(n_tokens * K, np.int32)
+        err = N.errbuf()
+        rc = self._lib.miag_routing(self._ctx, idx.ctypes.data, w.ctypes.data, counts.ctypes.data,
+                                    offsets.ctypes.data, perm.ctypes.data, err, len(err))
+        N.check(rc, err, "miag_routing")
+        return dict(idx=idx, w=w, counts=counts, offsets=offsets, perm=perm)
+
+    def last_launch_count(self) -> int:
+        return int(self._lib.miag_last_launch_count(self._ctx))
+
+
+def quantize_row_q8(x_ptr: int, y_ptr: int, n: int, stream: int | None = None) -> None:
+    """Device mia_quantize_row_q8: x f32 [n] -> y n/32 36-byte blocks."""
+    rc = N.lib().miag_quantize_row_q8(C.c_void_p(x_ptr), C.c_void_p(y_ptr), n,
+                                      C.c_void_p(stream or 0))
+    if rc:
+        raise N.MiagError("miag_quantize_row_q8 failed")
+
+
+def matvec(out_ptr: int, w_ptr: int, wtype: int, x_ptr: int, xq_ptr: int, rows: int, cols: int,
+           stream: int | None = None) -> None:
+    """Device mia_matvec (f32 or Q8_0 rows)."""
+    rc = N.lib().miag_matvec(C.c_void_p(out_ptr), C.c_void_p(w_ptr), wtype, C.c_void_p(x_ptr),
+                             C.c_void_p(xq_ptr), rows, cols, C.c_void_p(stream or 0))
+    if rc:
+        raise N.MiagError("miag_matvec failed")

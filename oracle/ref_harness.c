@@ -1,0 +1,251 @@
+/*
+ * ref_harness.c -- drives the reference engine's own MoE code, compiled from
+ * the reference's sources, so the oracle restatement (moe_oracle.c) and the
+ * golden vectors are pinned to the real thing.
+ *
+ * TEST INFRASTRUCTURE ONLY.  Built by oracle/Makefile into
+ * oracle/_ref/libmia_ref.so from the reference tree (REF=<path>); nothing is
+ * copied into this repository.  The reference's src/model/forward.c is
+ * #included so its file-static moe(), rmsnorm(), softmax() and top_k() are
+ * callable; src/tensor/{matmul,quant}.c, src/storage/expert_cache.c and
+ * src/storage/mia_file.c are compiled unchanged beside it.
+ *
+ * Expert residency: every thread gets its own mia_model and its own
+ * mia_expert_cache whose slab is the caller's read-only blob array with every
+ * (layer, expert) key already resident, so mia_cache_get (expert_cache.c:59-85)
+ * always takes its hit path and nothing is copied.  The LRU links the hit
+ * path rewrites are per thread.
+ */
+#include "src/model/forward.c"
+
+#include <pthread.h>
+#include <stdio.h>
+
+typedef struct {
+    int32_t dim, n_experts, n_active, expert_hidden, norm_topk;
+    float norm_eps;
+} ref_shape;
+
+static void fill_file(mia_file *f, mia_layer *layer, const ref_shape *s,
+                      const float *ffn_norm, const float *router) {
+    memset(f, 0, sizeof(*f));
+    memset(layer, 0, sizeof(*layer));
+    memcpy(f->h.magic, "MIA1", 4);
+    f->h.version = 1;
+    f->h.wtype = MIA_Q8_0;
+    f->h.dim = (uint32_t)s->dim;
+    f->h.n_layers = 1;
+    /* Attention sizes are unused by moe(); keep them small and non-zero so
+     * mia_model_init allocates nothing of size 0. */
+    f->h.n_heads = 1, f->h.n_kv_heads = 1, f->h.head_dim = 32, f->h.vocab = 1;
+    f->h.n_experts = (uint32_t)s->n_experts;
+    f->h.n_active = (uint32_t)s->n_active;
+    f->h.expert_hidden = (uint32_t)s->expert_hidden;
+    f->h.norm_topk = (uint32_t)s->norm_topk;
+    f->h.norm_eps = s->norm_eps;
+    f->h.rope_theta = 1e6f;
+    f->wt = MIA_Q8_0;
+    f->fd = -1;
+    layer->ffn_norm = ffn_norm;
+    layer->router = router;
+    f->layers = layer;
+    /* mia_file.c:275-278 */
+    size_t mat = (size_t)s->expert_hidden * mia_row_bytes(MIA_Q8_0, s->dim);
+    f->off_up = (mat + 63) / 64 * 64;
+    f->off_down = 2 * f->off_up;
+}
+
+static int never_load(void *ctx, int layer, int expert, void *dst) {
+    (void)ctx, (void)layer, (void)expert, (void)dst;
+    return -1;
+}
+
+/* A cache whose every key is resident in the caller's blob array. */
+static int resident_cache(mia_expert_cache *c, int n_experts, size_t stride,
+                          const unsigned char *blobs) {
+    memset(c, 0, sizeof(*c));
+    c->n_layers = 1, c->n_experts = n_experts, c->n_slots = n_experts;
+    c->blob_size = stride;
+    c->slab = (unsigned char *)blobs; /* read only: the hit path never writes */
+    c->slot_of = malloc(sizeof(int) * (size_t)n_experts);
+    c->key_of = malloc(sizeof(int) * (size_t)n_experts);
+    c->prev = malloc(sizeof(int) * (size_t)n_experts);
+    c->next = malloc(sizeof(int) * (size_t)n_experts);
+    if (!c->slot_of || !c->key_of || !c->prev || !c->next) return -1;
+    for (int k = 0; k < n_experts; k++) {
+        c->slot_of[k] = k, c->key_of[k] = k;
+        c->prev[k] = k - 1;
+        c->next[k] = k + 1 < n_experts ? k + 1 : -1;
+    }
+    c->head = 0, c->tail = n_experts - 1;
+    c->load = never_load;
+    return 0;
+}
+
+static void free_cache(mia_expert_cache *c) {
+    free(c->slot_of), free(c->key_of), free(c->prev), free(c->next);
+    memset(c, 0, sizeof(*c));
+}
+
+/* Routing exactly as moe() does it (forward.c:174-181), with the optional
+ * logit bias added between the router matvec and softmax. */
+static void route_ref(mia_model *m, dims s, const float *bias, int32_t *idx,
+                      float *w) {
+    const mia_file *f = m->f;
+    const mia_layer *L = &f->layers[0];
+    int k_idx[64];
+    rmsnorm(m->xn, m->x, L->ffn_norm, s.d, f->h.norm_eps);
+    mia_matvec(m->router, L->router, MIA_F32, m->xn, NULL, s.E, s.d);
+    if (bias)
+        for (int e = 0; e < s.E; e++) m->router[e] += bias[e];
+    softmax(m->router, s.E);
+    top_k(m->router, s.E, s.K, k_idx);
+    float sum = 0;
+    for (int j = 0; j < s.K; j++) sum += w[j] = m->router[k_idx[j]];
+    if (f->h.norm_topk)
+        for (int j = 0; j < s.K; j++) w[j] /= sum;
+    for (int j = 0; j < s.K; j++) idx[j] = k_idx[j];
+}
+
+/* The expert loop of moe() (forward.c:183-195) on routing already made. */
+static int experts_ref(mia_model *m, dims s, const int32_t *idx, const float *w) {
+    const mia_file *f = m->f;
+    for (int j = 0; j < s.K; j++) {
+        const unsigned char *blob = mia_cache_get(m->cache, 0, idx[j]);
+        if (!blob) return -1;
+        mia_matvec(m->gate, blob, f->wt, m->xn, m->xq, s.eh, s.d);
+        mia_matvec(m->up, blob + f->off_up, f->wt, m->xn, m->xq, s.eh, s.d);
+        for (int i = 0; i < s.eh; i++) {
+            float g = m->gate[i];
+            m->gate[i] = g / (1.0f + expf(-g)) * m->up[i];
+        }
+        mia_matvec(m->tmp, blob + f->off_down, f->wt, m->gate, m->xq, s.d, s.eh);
+        for (int i = 0; i < s.d; i++) m->x[i] += w[j] * m->tmp[i];
+    }
+    return 0;
+}
+
+typedef struct {
+    const ref_shape *s;
+    const float *ffn_norm, *router, *bias;
+    const unsigned char *blobs;
+    size_t stride;
+    float *x;
+    int32_t *idx;
+    float *w;
+    int t0, t1, route_only, rc;
+} ref_job;
+
+static void *ref_run(void *arg) {
+    ref_job *J = (ref_job *)arg;
+    mia_file f;
+    mia_layer layer;
+    mia_expert_cache cache;
+    mia_model m;
+    fill_file(&f, &layer, J->s, J->ffn_norm, J->router);
+    J->rc = -1;
+    if (resident_cache(&cache, J->s->n_experts, J->stride, J->blobs) != 0) {
+        free_cache(&cache);
+        return NULL;
+    }
+    if (mia_model_init(&m, &f, &cache, 1) != 0) {
+        free_cache(&cache);
+        return NULL;
+    }
+    dims s = dims_of(&f.h);
+    int32_t lidx[64];
+    float lw[64];
+    J->rc = 0;
+    for (int t = J->t0; t < J->t1 && J->rc == 0; t++) {
+        float *xt = J->x + (size_t)t * s.d;
+        memcpy(m.x, xt, sizeof(float) * (size_t)s.d);
+        if (J->idx || J->w || J->bias || J->route_only) {
+            route_ref(&m, s, J->bias, lidx, lw);
+            if (J->idx) memcpy(J->idx + (size_t)t * s.K, lidx, sizeof(int32_t) * (size_t)s.K);
+            if (J->w) memcpy(J->w + (size_t)t * s.K, lw, sizeof(float) * (size_t)s.K);
+        }
+        if (J->route_only) continue;
+        if (J->bias) {
+            /* xn is already in m->xn from route_ref. */
+            J->rc = experts_ref(&m, s, lidx, lw);
+        } else {
+            /* The unmodified static moe(): it recomputes the routing itself. */
+            J->rc = moe(&m, s, 0);
+        }
+        memcpy(xt, m.x, sizeof(float) * (size_t)s.d);
+    }
+    mia_model_free(&m);
+    free_cache(&cache);
+    return NULL;
+}
+
+static int ref_dispatch(ref_job *proto, int T, int n_threads) {
+    if (proto->s->n_active > 64) return -1;
+    if (n_threads < 1) n_threads = 1;
+    if (n_threads > T) n_threads = T > 0 ? T : 1;
+    pthread_t *th = malloc(sizeof(pthread_t) * (size_t)n_threads);
+    ref_job *jobs = malloc(sizeof(ref_job) * (size_t)n_threads);
+    for (int i = 0; i < n_threads; i++) {
+        jobs[i] = *proto;
+        jobs[i].t0 = (int)((long)T * i / n_threads);
+        jobs[i].t1 = (int)((long)T * (i + 1) / n_threads);
+    }
+    for (int i = 1; i < n_threads; i++) pthread_create(&th[i], NULL, ref_run, &jobs[i]);
+    ref_run(&jobs[0]);
+    int rc = jobs[0].rc;
+    for (int i = 1; i < n_threads; i++) {
+        pthread_join(th[i], NULL);
+        if (jobs[i].rc) rc = jobs[i].rc;
+    }
+    free(th), free(jobs);
+    return rc;
+}
+
+/* MoE block over T tokens (x [T][dim] in/out).  idx/w (nullable) receive
+ * the routing.  bias == NULL runs the reference's unmodified moe(). */
+int ref_moe(const ref_shape *s, const float *ffn_norm, const float *router,
+            const float *bias, const unsigned char *blobs, size_t stride,
+            float *x, int T, int32_t *idx, float *w, int n_threads) {
+    ref_job J;
+    memset(&J, 0, sizeof J);
+    J.s = s, J.ffn_norm = ffn_norm, J.router = router, J.bias = bias;
+    J.blobs = blobs, J.stride = stride, J.x = x, J.idx = idx, J.w = w;
+    return ref_dispatch(&J, T, n_threads);
+}
+
+/* Routing only (x is copied, not modified). */
+int ref_route(const ref_shape *s, const float *ffn_norm, const float *router,
+              const float *bias, const float *x, int T, int32_t *idx, float *w,
+              int n_threads) {
+    float *xc = malloc(sizeof(float) * (size_t)T * (size_t)s->dim);
+    if (!xc) return -1;
+    memcpy(xc, x, sizeof(float) * (size_t)T * (size_t)s->dim);
+    ref_job J;
+    memset(&J, 0, sizeof J);
+    J.s = s, J.ffn_norm = ffn_norm, J.router = router, J.bias = bias;
+    J.x = xc, J.idx = idx, J.w = w, J.route_only = 1;
+    J.stride = 0, J.blobs = NULL;
+    /* resident_cache needs a non-empty table even when nothing is fetched */
+    int rc = ref_dispatch(&J, T, n_threads);
+    free(xc);
+    return rc;
+}
+
+/* Public reference entry points, re-exported under ref_ names. */
+void ref_quantize_row_q8(const float *x, void *y, int n) {
+    mia_quantize_row_q8(x, (mia_block_q8 *)y, n);
+}
+void ref_matvec(float *out, const void *w, int wtype, const float *x, void *xq,
+                int rows, int cols) {
+    mia_matvec(out, w, (mia_wtype)wtype, x, (mia_block_q8 *)xq, rows, cols);
+}
+void ref_matvec_scalar(float *out, const void *w, int wtype, const float *x,
+                       void *xq, int rows, int cols) {
+    mia_matvec_scalar(out, w, (mia_wtype)wtype, x, (mia_block_q8 *)xq, rows, cols);
+}
+void ref_rmsnorm(float *out, const float *x, const float *w, int n, float eps) {
+    rmsnorm(out, x, w, n, eps);
+}
+void ref_softmax(float *x, int n) { softmax(x, n); }
+void ref_top_k(const float *p, int n, int k, int *idx) { top_k(p, n, k, idx); }
+int ref_block_bytes(void) { return (int)sizeof(mia_block_q8); }
