@@ -98,6 +98,10 @@ int miag_sync(miag_ctx *c, void *stream, char *err, size_t errlen);
 int miag_routing(miag_ctx *c, int32_t *idx, float *w, int32_t *counts,
                  int32_t *offsets, int32_t *perm, char *err, size_t errlen);
 
+/* Router logits (+ bias) [n_tokens][n_experts] of the most recent call: the
+ * values forward.c:175 leaves in m->router before softmax. */
+int miag_router_logits(miag_ctx *c, float *logits, char *err, size_t errlen);
+
 /* Device kernels behind the reference's public math ABI, on device pointers
  * and a stream (NULL = legacy default stream):
  *   miag_quantize_row_q8  <- mia_quantize_row_q8 (include/mia/quant.h:18,
@@ -112,6 +116,17 @@ int miag_matvec(float *out, const void *w, int wtype, const float *x,
 
 /* Number of kernels the most recent miag_moe / miag_moe_async launched. */
 int miag_last_launch_count(const miag_ctx *c);
+
+/* Per-kernel timing (no reference counterpart; the reference only has
+ * wall-clock stats, src/app/main.c:146-158).  While enabled, every kernel of
+ * the block is bracketed by CUDA events on the stream it is launched on.
+ * miag_profile_read waits for them and returns, per kernel stage i <
+ * miag_profile_stages(), the summed milliseconds and launch count since the
+ * last read (which resets them).  miag_profile_stage_name(i) names stage i. */
+int miag_profile(miag_ctx *c, int enable);
+int miag_profile_stages(void);
+const char *miag_profile_stage_name(int i);
+int miag_profile_read(miag_ctx *c, double *ms, int32_t *launches, char *err, size_t errlen);
 
 #ifdef __cplusplus
 }

@@ -46,10 +46,15 @@ SIGNATURES = {
     "miag_sync": (C.c_int, [C.c_void_p, C.c_void_p, C.c_char_p, C.c_size_t]),
     "miag_routing": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                C.c_void_p, C.c_char_p, C.c_size_t]),
+    "miag_router_logits": (C.c_int, [C.c_void_p, C.c_void_p, C.c_char_p, C.c_size_t]),
     "miag_quantize_row_q8": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p]),
     "miag_matvec": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_int,
                               C.c_int, C.c_void_p]),
     "miag_last_launch_count": (C.c_int, [C.c_void_p]),
+    "miag_profile": (C.c_int, [C.c_void_p, C.c_int]),
+    "miag_profile_stages": (C.c_int, []),
+    "miag_profile_stage_name": (C.c_char_p, [C.c_int]),
+    "miag_profile_read": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_char_p, C.c_size_t]),
 }
 
 _lib = None

@@ -43,7 +43,45 @@ struct miag_ctx {
     // upload staging
     uint8_t *stage_dev = nullptr, *stage_host = nullptr;
     size_t stage_bytes = 0;
+    // per-kernel profiling: event pairs recorded around each stage
+    bool profiling = false;
+    std::vector<cudaEvent_t> event_pool;
+    std::vector<std::pair<cudaEvent_t, cudaEvent_t>> prof_events[8];
+    int prof_launches[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 };
+
+namespace {
+enum Stage { kRoute = 0, kPermute, kGateUp, kDown, kCombine, kNumStages };
+const char *const kStageNames[kNumStages] = {"route", "topk_permute", "gateup", "down",
+                                             "combine"};
+
+cudaEvent_t take_event(miag_ctx *c) {
+    if (!c->event_pool.empty()) {
+        cudaEvent_t e = c->event_pool.back();
+        c->event_pool.pop_back();
+        return e;
+    }
+    cudaEvent_t e = nullptr;
+    cudaEventCreate(&e);
+    return e;
+}
+
+// Runs one stage's launches, bracketed by events while profiling.
+template <class F>
+void run_stage(miag_ctx *c, int st, int launches, cudaStream_t s, F launch) {
+    c->last_launches += launches;
+    if (!c->profiling) {
+        launch();
+        return;
+    }
+    cudaEvent_t a = take_event(c), b = take_event(c);
+    cudaEventRecord(a, s);
+    launch();
+    cudaEventRecord(b, s);
+    c->prof_events[st].push_back({a, b});
+    c->prof_launches[st] += launches;
+}
+}  // namespace
 
 static void set_err(char *err, size_t errlen, const char *fmt, ...) {
     if (!err || errlen == 0) return;
@@ -153,7 +191,8 @@ extern "C" int miag_open(miag_ctx **out, const miag_shape *shape, int device, ch
         if ((e = cudaMemset(L.experts, 0, E * c->lay.expert_bytes)) != cudaSuccess)
             return fail("cudaMemset(expert store)", e);
         if ((e = cudaMalloc(&L.ffn_norm, d * 4)) != cudaSuccess) return fail("cudaMalloc", e);
-        if ((e = cudaMalloc(&L.router_t, d * E * 4)) != cudaSuccess) return fail("cudaMalloc", e);
+        const size_t Eg = (E + 31) / 32 * 32;  // router stored in 32-expert groups
+        if ((e = cudaMalloc(&L.router_t, d * Eg * 4)) != cudaSuccess) return fail("cudaMalloc", e);
         if ((e = cudaMalloc(&L.bias, E * 4)) != cudaSuccess) return fail("cudaMalloc", e);
     }
     if (gemv_setup_attributes(c->dims, c->lay) != 0) {
@@ -175,6 +214,9 @@ extern "C" void miag_close(miag_ctx *c) {
         cudaFree(L.router_t);
         cudaFree(L.bias);
     }
+    for (auto &v : c->prof_events)
+        for (auto &pr : v) c->event_pool.push_back(pr.first), c->event_pool.push_back(pr.second);
+    for (cudaEvent_t e : c->event_pool) cudaEventDestroy(e);
     cudaFree(c->ws_mem);
     cudaFree(c->d_err);
     cudaFree(c->stage_dev);
@@ -321,14 +363,13 @@ static size_t ws_layout(miag_ctx *c, int T, uint8_t *base, Work *w, float **x_de
     const Dims &m = c->dims;
     const size_t P = (size_t)T * m.K;
     const int nchunks = (int)((P + kPermChunk - 1) / kPermChunk);
-    const int xs = scale_pad(m.d / MIAG_QK), hs = scale_pad(m.eh / MIAG_QK);
+    const int xs = scale_pad(m.d / MIAG_QK);
     uint8_t *p = base;
     Work v{};
     v.T = T, v.P = (int)P, v.nchunks = nchunks;
     v.xq = (int8_t *)bump(p, (size_t)T * m.d);
     v.dx = (float *)bump(p, (size_t)T * xs * 4);
     v.logits = (float *)bump(p, (size_t)T * m.E * 4);
-    v.ticket = (int32_t *)bump(p, (size_t)((T + 1) / 2) * 4);
     v.idx = (int32_t *)bump(p, P * 4);
     v.w = (float *)bump(p, P * 4);
     v.rank = (int32_t *)bump(p, P * 4);
@@ -338,11 +379,10 @@ static size_t ws_layout(miag_ctx *c, int T, uint8_t *base, Work *w, float **x_de
     v.offsets = (int32_t *)bump(p, (size_t)(m.E + 1) * 4);
     v.active = (int32_t *)bump(p, (size_t)m.E * 4);
     v.n_active = (int32_t *)bump(p, 4);
+    v.chunk_pre = (int32_t *)bump(p, (size_t)(m.E + 1) * 4);
     v.perm = (int32_t *)bump(p, P * 4);
     v.inv = (int32_t *)bump(p, P * 4);
     v.h = (float *)bump(p, P * m.eh * 4);
-    v.hq = (int8_t *)bump(p, P * m.eh);
-    v.dh = (float *)bump(p, P * hs * 4);
     v.y = (float *)bump(p, P * m.d * 4);
     float *xd = (float *)bump(p, (size_t)T * m.d * 4);
     if (w) *w = v;
@@ -351,8 +391,8 @@ static size_t ws_layout(miag_ctx *c, int T, uint8_t *base, Work *w, float **x_de
 }
 
 // Sizes the workspace for at least T tokens.  Buffers are laid out for the
-// capacity, so per-call state that must persist (the zeroed route tickets)
-// keeps its address; only the counts change with T.
+// capacity, so buffers keep their addresses while T varies; only the counts
+// change with T.
 static int ensure_ws(miag_ctx *c, int T, char *err, size_t errlen) {
     if (T > c->ws_cap) {
         int cap = c->ws_cap ? c->ws_cap : 64;
@@ -381,13 +421,15 @@ static int enqueue_moe(miag_ctx *c, int layer, float *x_dev, int T, cudaStream_t
     }
     LayerDev L{Ls.ffn_norm, Ls.router_t, Ls.has_bias ? Ls.bias : nullptr, Ls.experts};
     const Work &w = c->ws;
-    launch_route(c->dims, L, x_dev, w, c->d_err, s);
-    launch_permute(c->dims, w, c->d_err, s);
-    launch_gateup(c->dims, c->lay, L, w, c->num_sms, c->d_err, s);
-    launch_quant_h(c->dims, w, s);
-    launch_down(c->dims, c->lay, L, w, c->num_sms, c->d_err, s);
-    launch_combine(c->dims, w, x_dev, s);
-    c->last_launches = 8;
+    c->last_launches = 0;
+    run_stage(c, kRoute, 1, s, [&] { launch_route(c->dims, L, x_dev, w, c->d_err, s); });
+    run_stage(c, kPermute, permute_launches(w.P, c->dims.E), s,
+              [&] { launch_permute(c->dims, w, c->d_err, s); });
+    run_stage(c, kGateUp, 1, s,
+              [&] { launch_gateup(c->dims, c->lay, L, w, c->num_sms, c->d_err, s); });
+    run_stage(c, kDown, 1, s,
+              [&] { launch_down(c->dims, c->lay, L, w, c->num_sms, c->d_err, s); });
+    run_stage(c, kCombine, 1, s, [&] { launch_combine(c->dims, w, x_dev, s); });
     c->last_T = T;
     CU(cudaGetLastError());
     return 0;
@@ -396,8 +438,8 @@ static int enqueue_moe(miag_ctx *c, int layer, float *x_dev, int T, cudaStream_t
 extern "C" int miag_moe_async(miag_ctx *c, int layer, float *x_dev, int n_tokens, void *stream,
                               char *err, size_t errlen) {
     if (check_layer(c, layer, err, errlen)) return -1;
-    if (n_tokens < 0 || (n_tokens > 0 && !x_dev)) {
-        set_err(err, errlen, "bad token buffer");
+    if (n_tokens < 0 || (n_tokens > 0 && !x_dev) || ((uintptr_t)x_dev & 15u)) {
+        set_err(err, errlen, "bad token buffer (device pointer, 16-byte aligned)");
         return -1;
     }
     if (n_tokens == 0) {
@@ -470,4 +512,53 @@ extern "C" int miag_routing(miag_ctx *c, int32_t *idx, float *w, int32_t *counts
     return 0;
 }
 
+extern "C" int miag_router_logits(miag_ctx *c, float *logits, char *err, size_t errlen) {
+    if (!c || !logits) {
+        set_err(err, errlen, "null argument");
+        return -1;
+    }
+    CU(cudaSetDevice(c->device));
+    CU(cudaStreamSynchronize(c->stream));
+    CU(cudaMemcpy(logits, c->ws.logits, (size_t)c->last_T * c->dims.E * 4,
+                  cudaMemcpyDeviceToHost));
+    return 0;
+}
+
 extern "C" int miag_last_launch_count(const miag_ctx *c) { return c ? c->last_launches : 0; }
+
+extern "C" int miag_profile(miag_ctx *c, int enable) {
+    if (!c) return -1;
+    c->profiling = enable != 0;
+    return 0;
+}
+
+extern "C" int miag_profile_stages(void) { return kNumStages; }
+
+extern "C" const char *miag_profile_stage_name(int i) {
+    return i >= 0 && i < kNumStages ? kStageNames[i] : nullptr;
+}
+
+extern "C" int miag_profile_read(miag_ctx *c, double *ms, int32_t *launches, char *err,
+                                 size_t errlen) {
+    if (!c) {
+        set_err(err, errlen, "null context");
+        return -1;
+    }
+    CU(cudaSetDevice(c->device));
+    for (int st = 0; st < kNumStages; st++) {
+        double total = 0.0;
+        for (auto &pr : c->prof_events[st]) {
+            CU(cudaEventSynchronize(pr.second));
+            float t = 0.0f;
+            CU(cudaEventElapsedTime(&t, pr.first, pr.second));
+            total += t;
+            c->event_pool.push_back(pr.first);
+            c->event_pool.push_back(pr.second);
+        }
+        c->prof_events[st].clear();
+        if (ms) ms[st] = total;
+        if (launches) launches[st] = c->prof_launches[st];
+        c->prof_launches[st] = 0;
+    }
+    return 0;
+}

@@ -27,17 +27,27 @@ enum : int {
 constexpr long long kWaitCycles = 2000000000LL;
 
 // ---------------------------------------------------------------------------
-// HBM layout of one layer's expert store ("SoA", repacked from the .mia
-// array-of-36-byte-blocks layout at upload).  Per expert, contiguous:
-//   gu_q  int8  [2*eh][d]        row 2i = gate row i, row 2i+1 = up row i
-//   gu_s  f32   [2*eh][gu_srow]  that row's per-32-block scales (16-B rows)
-//   dn_q  int8  [d][eh]          down rows
-//   dn_s  f32   [d][dn_srow]
-// Every row starts 16-byte aligned, so a row is one bulk-copy unit.
+// HBM layout of one layer's expert store, repacked at upload from the .mia
+// array of 36-byte {f32 d; int8 q[32]} blocks.  Per expert, two matrices:
+//   GU: 2*eh rows x d columns, row 2i = gate row i, row 2i+1 = up row i
+//   DN: d rows x eh columns (down)
+// Each matrix is cut into tiles of 128 rows x 128 bytes of K (4 Q8_0
+// blocks), stored [row tile][k tile], 16 KiB each.  Inside a tile, 8-row
+// atoms of 8 x 128 B hold row r's 16-byte chunk c at chunk c ^ (r % 8): the
+// 128-byte swizzle of the tensor-core K-major layout, which also makes eight
+// rows' same-column chunks land in distinct shared-memory banks.  The scales
+// of a tile, [128 rows][4 blocks] f32 (2 KiB), are stored in the same tile
+// order in a separate plane.  Rows and columns beyond the matrix are zero.
+constexpr int kTileRows = 128;
+constexpr int kTileK = 128;                       // bytes of K per tile = 4 blocks
+constexpr int kTileBytes = kTileRows * kTileK;    // 16 KiB
+constexpr int kTileScaleBytes = kTileRows * 4 * 4;  // 2 KiB
+
 struct StoreLayout {
     int d, eh;
+    int gu_rt, gu_kt;  // GU row tiles, k tiles
+    int dn_rt, dn_kt;
     uint32_t gu_q_off, gu_s_off, dn_q_off, dn_s_off;
-    uint32_t gu_s_row, dn_s_row;  // bytes per scale row (multiple of 16)
     size_t expert_bytes;
 };
 
@@ -46,19 +56,26 @@ inline size_t round_up_sz(size_t n, size_t a) { return (n + a - 1) / a * a; }
 inline StoreLayout make_layout(int d, int eh) {
     StoreLayout L;
     L.d = d, L.eh = eh;
-    L.gu_s_row = (uint32_t)round_up_sz((size_t)(d / MIAG_QK) * 4, 16);
-    L.dn_s_row = (uint32_t)round_up_sz((size_t)(eh / MIAG_QK) * 4, 16);
+    L.gu_rt = (2 * eh + kTileRows - 1) / kTileRows;
+    L.gu_kt = (d + kTileK - 1) / kTileK;
+    L.dn_rt = (d + kTileRows - 1) / kTileRows;
+    L.dn_kt = (eh + kTileK - 1) / kTileK;
     size_t off = 0;
     L.gu_q_off = (uint32_t)off;
-    off = round_up_sz(off + (size_t)2 * eh * d, 256);
+    off += (size_t)L.gu_rt * L.gu_kt * kTileBytes;
     L.gu_s_off = (uint32_t)off;
-    off = round_up_sz(off + (size_t)2 * eh * L.gu_s_row, 256);
+    off += (size_t)L.gu_rt * L.gu_kt * kTileScaleBytes;
     L.dn_q_off = (uint32_t)off;
-    off = round_up_sz(off + (size_t)d * eh, 256);
+    off += (size_t)L.dn_rt * L.dn_kt * kTileBytes;
     L.dn_s_off = (uint32_t)off;
-    off = round_up_sz(off + (size_t)d * L.dn_s_row, 256);
-    L.expert_bytes = off;
+    off += (size_t)L.dn_rt * L.dn_kt * kTileScaleBytes;
+    L.expert_bytes = round_up_sz(off, 1024);
     return L;
+}
+
+// Byte offset of (row r, 16-byte chunk c) inside a 128 x 128 B swizzled tile.
+__host__ __device__ inline uint32_t tile_chunk_offset(int r, int c) {
+    return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
 }
 
 // Shared-memory row stride for a staged row of `bytes`: a multiple of 16
@@ -146,24 +163,6 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
 
 __device__ __forceinline__ void set_error(int *err, int code) {
     if (err) atomicCAS(err, 0, code);
-}
-
-__device__ __forceinline__ int4 ldg_nc_v4(const void *p) {
-    return __ldg(reinterpret_cast<const int4 *>(p));
-}
-
-// Exact int8 dot of one 32-value block held as two 16-byte vectors each.
-__device__ __forceinline__ int dot_block_i8(int4 a0, int4 a1, int4 b0, int4 b1) {
-    int acc = 0;
-    acc = __dp4a(a0.x, b0.x, acc);
-    acc = __dp4a(a0.y, b0.y, acc);
-    acc = __dp4a(a0.z, b0.z, acc);
-    acc = __dp4a(a0.w, b0.w, acc);
-    acc = __dp4a(a1.x, b1.x, acc);
-    acc = __dp4a(a1.y, b1.y, acc);
-    acc = __dp4a(a1.z, b1.z, acc);
-    acc = __dp4a(a1.w, b1.w, acc);
-    return acc;
 }
 
 // One reference Q8_0 step: s += ((float)acc * dw) * dx (matmul.c:25).

@@ -3,113 +3,191 @@
 // Reference: the three mia_matvec calls per active expert in moe()
 // (src/model/forward.c:186-193) -> rows_kernel (src/tensor/matmul.c:75-80)
 // -> dot_q8_scalar (:19-28); SwiGLU :188-191; re-quantization of h inside
-// mia_matvec (:93, quant.c:11-27); weighted combine :194.
+// mia_matvec (:93, quant.c:11-27, done while staging h); weighted combine :194.
 //
-// Work is grouped by expert: every staged weight tile is read from HBM once
-// and applied to all of that expert's (token, slot) pairs.  Persistent CTAs
-// (one per SM) walk a list of items = (active expert, row chunk).  A producer
-// warp streams each item's rows into a ring of shared-memory stages with
-// 1-D TMA bulk copies (one copy per row, into bank-skewed row slots); eight
-// consumer warps compute from shared memory.
+// Work is grouped by expert: every weight tile is read from HBM once per
+// group of up to 32 of that expert's (token, slot) pairs.  An item is
+// (active expert, 128-row tile, chunk of 32 pairs); persistent CTAs (one per
+// SM) own contiguous item ranges, so consecutive items share their
+// activations, which are staged in shared memory once.  A producer thread
+// streams each item's K range, two 16 KiB swizzled tiles (+ their scale
+// tiles) per stage, with 1-D TMA bulk copies into a ring of stages.
 //
-// Lane <-> row: each lane owns one weight row and walks its Q8_0 blocks in
-// order, so the fp32 sum is the reference's serial sum
-//   s += ((float)int_dot * w.d) * x.d
-// and the result equals mia_matvec_scalar bit for bit.
+// Eight consumer warps each own 16 rows of the tile.  Per Q8_0 block (K =
+// 32) a warp issues one int8 tensor-core MMA, m16n8k32 (16 rows x 8 pairs),
+// whose int32 results are the block's exact integer dots.  Every lane holds
+// the same four (row, pair) positions for all blocks, so it carries their
+// fp32 accumulators in registers and applies the reference's step
+//     s = s + ((float)dot * w.d) * x.d        (matmul.c:25, blocks in order)
+// with round-to-nearest intrinsics: the result equals mia_matvec_scalar bit
+// for bit.  Operands come from shared memory through ldmatrix; the 128-byte
+// XOR swizzle of the tiles (and the odd 16-byte stride of activation rows)
+// keeps those reads free of bank conflicts.
+#include <type_traits>
+
 #include "kernels.cuh"
 
 namespace miag {
 
 constexpr int kConsumerWarps = 8;
-constexpr int kGemvThreads = (kConsumerWarps + 1) * 32;
-constexpr int kGuRowPairs = 8;             // gate/up rows per item: 8 gate + 8 up
-constexpr int kGuRows = 2 * kGuRowPairs;
-constexpr int kDnRows = 32;                // down rows per item
+constexpr int kConsumers = kConsumerWarps * 32;
+constexpr int kGemvThreads = kConsumers + 32;
+constexpr int kStageKT = 2;  // k tiles per stage
+constexpr int kStageBytes = kStageKT * (kTileBytes + kTileScaleBytes);
 constexpr int kMaxStages = 8;
-constexpr int kBarBytes = 256;
+constexpr int kBarBytes = 1024;  // keeps every stage 1024-B aligned
 constexpr int kSmemBudget = 227 * 1024;
+constexpr int kMaxNT = kTokChunk / 8;  // n-tiles of 8 pairs per item
+constexpr uint32_t kFull = 0xffffffffu;
 
 struct GemvParams {
     Dims m;
     StoreLayout lay;
     const uint8_t *experts;
-    const int32_t *offsets, *perm, *active, *n_active;
+    const int32_t *offsets, *perm, *active, *n_active, *chunk_pre;
     const int8_t *xq;  // [T][d]
     const float *dx;   // [T][xs]
     float *h;          // [P][eh]
-    const int8_t *hq;  // [P][eh]
-    const float *dh;   // [P][hs]
     float *y;          // [P][d]
     int stages;
-    uint32_t q_stride, s_stride, stage_bytes;
+    uint32_t x_off, x_stride;  // activation region offset in smem, its row stride
     int *err;
 };
 
-struct GuTile {
-    static constexpr int kRows = kGuRows;
-    __device__ static int items_per_expert(const GemvParams &p) { return p.m.eh / kGuRowPairs; }
-    __device__ static uint32_t q_bytes(const GemvParams &p) { return (uint32_t)p.m.d; }
-    __device__ static uint32_t s_bytes(const GemvParams &p) { return p.lay.gu_s_row; }
-    __device__ static size_t q_off(const GemvParams &p, int c) {
-        return p.lay.gu_q_off + (size_t)c * kRows * p.m.d;
-    }
-    __device__ static size_t s_off(const GemvParams &p, int c) {
-        return p.lay.gu_s_off + (size_t)c * kRows * p.lay.gu_s_row;
-    }
-};
-
-struct DnTile {
-    static constexpr int kRows = kDnRows;
-    __device__ static int items_per_expert(const GemvParams &p) { return p.m.d / kDnRows; }
-    __device__ static uint32_t q_bytes(const GemvParams &p) { return (uint32_t)p.m.eh; }
-    __device__ static uint32_t s_bytes(const GemvParams &p) { return p.lay.dn_s_row; }
-    __device__ static size_t q_off(const GemvParams &p, int c) {
-        return p.lay.dn_q_off + (size_t)c * kRows * p.m.eh;
-    }
-    __device__ static size_t s_off(const GemvParams &p, int c) {
-        return p.lay.dn_s_off + (size_t)c * kRows * p.lay.dn_s_row;
-    }
-};
-
-// Serial reference dot of one staged weight row with one activation row.
-__device__ __forceinline__ float row_dot(const uint8_t *qr, const float *sr, const int8_t *xr,
-                                         const float *xs, int nb) {
-    float acc = 0.0f;
-    for (int b0 = 0; b0 < nb; b0 += 4) {
-        const float4 ws = *reinterpret_cast<const float4 *>(sr + b0);
-        const float4 xv = __ldg(reinterpret_cast<const float4 *>(xs + b0));
-        const float wa[4] = {ws.x, ws.y, ws.z, ws.w};
-        const float xa[4] = {xv.x, xv.y, xv.z, xv.w};
-        int dots[4];
-#pragma unroll
-        for (int u = 0; u < 4; u++) {
-            if (b0 + u < nb) {
-                const int b = b0 + u;
-                const int4 w0 = *reinterpret_cast<const int4 *>(qr + 32 * b);
-                const int4 w1 = *reinterpret_cast<const int4 *>(qr + 32 * b + 16);
-                const int4 x0 = ldg_nc_v4(xr + 32 * b);
-                const int4 x1 = ldg_nc_v4(xr + 32 * b + 16);
-                dots[u] = dot_block_i8(w0, w1, x0, x1);
-            }
-        }
-#pragma unroll
-        for (int u = 0; u < 4; u++)
-            if (b0 + u < nb) acc = q8_step(acc, dots[u], wa[u], xa[u]);
-    }
-    return acc;
+__device__ __forceinline__ void consumer_sync() {
+    asm volatile("bar.sync 1, %0;" ::"n"(kConsumers) : "memory");
 }
 
-// Pipeline skeleton shared by the gate/up and down kernels.
-template <class Tile, class Consume>
-__device__ __forceinline__ void run_pipeline(const GemvParams &p, uint8_t *smem, Consume consume) {
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2,
+                                        uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t &r0, uint32_t &r1) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0, %1}, [%2];"
+                 : "=r"(r0), "=r"(r1)
+                 : "r"(addr));
+}
+
+// D = A(16x32 s8, row) * B(32x8 s8, col), int32, exact.
+__device__ __forceinline__ void mma_s8(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                       uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+        "{%8, %9}, {%10, %10, %10, %10};"
+        : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+
+// Item i -> index a of its active expert: largest a with chunk_pre[a]*RT <= i.
+__device__ __forceinline__ int find_active(const int32_t *chunk_pre, int nact, int RT, int item) {
+    int lo = 0, hi = nact;
+    while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (__ldg(chunk_pre + mid) * RT <= item) lo = mid;
+        else hi = mid;
+    }
+    return lo;
+}
+
+struct ItemInfo {
+    int e, rt, tc;
+};
+
+__device__ __forceinline__ ItemInfo decode_item(const GemvParams &p, int nact, int RT, int item) {
+    const int a = find_active(p.chunk_pre, nact, RT, item);
+    const int local = item - __ldg(p.chunk_pre + a) * RT;
+    ItemInfo it;
+    it.e = __ldg(p.active + a);
+    it.tc = local / RT;
+    it.rt = local % RT;
+    return it;
+}
+
+// Consumers: stage the activations of pairs [t0, t0+n) of the expert segment
+// starting at seg0 in the shared region (rows at x_stride, then scale rows at
+// their own odd-16-byte stride).
+//   gate/up: copies xq[token(pair)] and dx[token] (quantized by the router);
+//   down:    quantizes h[pos] here, one thread per 32-block, exactly as
+//            mia_matvec quantizes its input (matmul.c:93, quant.c:11-27).
+template <bool kGU>
+__device__ void fill_region(const GemvParams &p, uint8_t *region, int seg0, int t0, int n,
+                            int row_bytes, int nscale) {
+    const int srow = (int)smem_stride((uint32_t)nscale * 4);  // padded scale row bytes
+    uint8_t *rs = region + (size_t)kTokChunk * p.x_stride;
+    if (kGU) {
+        const int qv = row_bytes / 16, sv = nscale / 4;  // 16-byte vectors per row / scale row
+        const int per = qv + sv;
+        for (int v = threadIdx.x; v < n * per; v += kConsumers) {
+            const int j = v / per, k = v % per;
+            const int t = __ldg(p.perm + seg0 + t0 + j) / p.m.K;
+            if (k < qv)
+                *reinterpret_cast<int4 *>(region + (size_t)j * p.x_stride + 16 * k) =
+                    __ldcg(reinterpret_cast<const int4 *>(p.xq + (size_t)t * row_bytes) + k);
+            else
+                *reinterpret_cast<int4 *>(rs + (size_t)j * srow + 16 * (k - qv)) =
+                    __ldcg(reinterpret_cast<const int4 *>(p.dx + (size_t)t * nscale) + (k - qv));
+        }
+    } else {
+        // one thread per (pair, 32-block), its eight 16-byte loads issued together
+        const int nb = row_bytes / MIAG_QK;
+        for (int task = threadIdx.x; task < n * nb; task += kConsumers) {
+            const int j = task / nb, b = task % nb;
+            const float4 *src = reinterpret_cast<const float4 *>(
+                p.h + (size_t)(seg0 + t0 + j) * row_bytes + b * MIAG_QK);
+            float4 v[8];
+#pragma unroll
+            for (int k = 0; k < 8; k++) v[k] = __ldcg(src + k);
+            float a = 0.0f;
+#pragma unroll
+            for (int k = 0; k < 8; k++)
+                a = fmaxf(a, fmaxf(fmaxf(fabsf(v[k].x), fabsf(v[k].y)),
+                                   fmaxf(fabsf(v[k].z), fabsf(v[k].w))));
+            const float dq = __fdiv_rn(a, 127.0f);
+            const float id = dq != 0.0f ? __fdiv_rn(1.0f, dq) : 0.0f;
+            uint32_t q[8];
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                const uint32_t q0 = (uint8_t)(int8_t)roundf(__fmul_rn(v[k].x, id));
+                const uint32_t q1 = (uint8_t)(int8_t)roundf(__fmul_rn(v[k].y, id));
+                const uint32_t q2 = (uint8_t)(int8_t)roundf(__fmul_rn(v[k].z, id));
+                const uint32_t q3 = (uint8_t)(int8_t)roundf(__fmul_rn(v[k].w, id));
+                q[k] = q0 | (q1 << 8) | (q2 << 16) | (q3 << 24);
+            }
+            uint4 *dst = reinterpret_cast<uint4 *>(region + (size_t)j * p.x_stride + b * MIAG_QK);
+            dst[0] = make_uint4(q[0], q[1], q[2], q[3]);
+            dst[1] = make_uint4(q[4], q[5], q[6], q[7]);
+            reinterpret_cast<float *>(rs + (size_t)j * srow)[b] = dq;
+        }
+    }
+}
+
+// gate+up (kGU) or down: one launch over all items of all active experts.
+template <bool kGU>
+__global__ void __launch_bounds__(kGemvThreads, 1) k_expert_mma(GemvParams p) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    const int d = p.m.d, eh = p.m.eh;
+    const int RT = kGU ? p.lay.gu_rt : p.lay.dn_rt;
+    const int KT = kGU ? p.lay.gu_kt : p.lay.dn_kt;
+    const int Kb = kGU ? d : eh;             // bytes of K (= values)
+    const int rows = kGU ? 2 * eh : d;       // matrix rows
+    const int nb = Kb / MIAG_QK, xs = scale_pad(nb);
+    const int xsp = (int)smem_stride((uint32_t)xs * 4) / 4;  // padded scale row in smem
+    const uint32_t q_off = kGU ? p.lay.gu_q_off : p.lay.dn_q_off;
+    const uint32_t s_off = kGU ? p.lay.gu_s_off : p.lay.dn_s_off;
+    const int NS = (KT + kStageKT - 1) / kStageKT;  // stages per item
+    const int nact = __ldg(p.n_active);
+    const int n_items = __ldg(p.chunk_pre + nact) * RT;
+    const int first = (int)((long)n_items * blockIdx.x / gridDim.x);
+    const int last = (int)((long)n_items * (blockIdx.x + 1) / gridDim.x);
+
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
     uint64_t *empty = full + kMaxStages;
     uint8_t *stages = smem + kBarBytes;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int S = p.stages;
-    const int ipe = Tile::items_per_expert(p);
-    const int n_items = __ldg(p.n_active) * ipe;
-
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; s++) {
             mbar_init(&full[s], 1);
@@ -119,123 +197,186 @@ __device__ __forceinline__ void run_pipeline(const GemvParams &p, uint8_t *smem,
     }
     __syncthreads();
 
-    const uint32_t qb = Tile::q_bytes(p), sb = Tile::s_bytes(p);
     if (warp == kConsumerWarps) {
-        // Producer warp.
+        // ---- producer: stream each item's k tiles, kStageKT per stage.
+        if (lane != 0) return;
         int it = 0;
         bool ok = true;
-        for (int item = blockIdx.x; item < n_items; item += gridDim.x, it++) {
-            const int s = it % S, round = it / S;
-            if (round > 0) {
-                bool got = true;
-                if (lane == 0) got = mbar_wait(&empty[s], (round - 1) & 1);
-                got = __shfl_sync(0xffffffffu, got, 0);
-                if (!got) {
+        for (int item = first; item < last && ok; item++) {
+            const ItemInfo ii = decode_item(p, nact, RT, item);
+            const uint8_t *base = p.experts + (size_t)ii.e * p.lay.expert_bytes;
+            for (int ks = 0; ks < NS; ks++, it++) {
+                const int s = it % S, round = it / S;
+                if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1)) {
                     set_error(p.err, kErrWaitEmpty);
                     ok = false;
                     break;
                 }
-            }
-            const int e = __ldg(p.active + item / ipe), c = item % ipe;
-            const uint8_t *base = p.experts + (size_t)e * p.lay.expert_bytes;
-            const uint8_t *src_q = base + Tile::q_off(p, c);
-            const uint8_t *src_s = base + Tile::s_off(p, c);
-            uint8_t *dst = stages + (size_t)s * p.stage_bytes;
-            if (lane == 0) mbar_arrive_expect_tx(&full[s], (uint32_t)Tile::kRows * (qb + sb));
-            __syncwarp();
-            for (int r = lane; r < Tile::kRows; r += 32) {
-                bulk_g2s(dst + (size_t)r * p.q_stride, src_q + (size_t)r * qb, qb, &full[s]);
-                bulk_g2s(dst + (size_t)Tile::kRows * p.q_stride + (size_t)r * p.s_stride,
-                         src_s + (size_t)r * sb, sb, &full[s]);
+                const int kt0 = ks * kStageKT, nkt = min(kStageKT, KT - kt0);
+                const size_t tile = (size_t)ii.rt * KT + kt0;
+                uint8_t *dst = stages + (size_t)s * kStageBytes;
+                mbar_arrive_expect_tx(&full[s], (uint32_t)nkt * (kTileBytes + kTileScaleBytes));
+                bulk_g2s(dst, base + q_off + tile * kTileBytes, (uint32_t)nkt * kTileBytes, &full[s]);
+                bulk_g2s(dst + kStageKT * kTileBytes, base + s_off + tile * kTileScaleBytes,
+                         (uint32_t)nkt * kTileScaleBytes, &full[s]);
             }
         }
-        if (!ok && lane == 0) {
-            // Let copies already issued land before the CTA's shared memory goes away.
-            const int issued = it;
-            for (int j = issued - 1; j >= 0 && j >= issued - S; j--)
-                mbar_wait(&full[j % S], (j / S) & 1);
+        if (!ok) {
+            // Let issued copies land before the CTA's shared memory goes away.
+            for (int j = it - 1; j >= 0 && j >= it - S; j--) mbar_wait(&full[j % S], (j / S) & 1);
         }
         return;
     }
 
-    // Consumer warps.
+    // ---- consumers
+    uint8_t *region = smem + p.x_off;
+    const float *rsc = reinterpret_cast<const float *>(region + (size_t)kTokChunk * p.x_stride);
+    const int g = lane >> 2, tq = lane & 3;           // mma groupID, thread-in-group
+    const int r0 = 16 * warp + g, r1 = r0 + 8;        // this lane's two rows in the tile
+    // ldmatrix roles: A (x4): lanes 0-7 rows 0-7, 8-15 rows 8-15, 16-31 the same
+    // rows' second 16-byte half.  B (x2): lanes 0-7 pairs 0-7, 8-15 second half.
+    const int a_row = 16 * warp + (lane & 7) + ((lane >> 3) & 1) * 8, a_half = lane >> 4;
+    const int b_pair = lane & 7, b_half = (lane >> 3) & 1;
+    const uint32_t region_addr = smem_addr(region);
+
+    int cur_e = -1, cur_tc = -1;
     int it = 0;
-    for (int item = blockIdx.x; item < n_items; item += gridDim.x, it++) {
-        const int s = it % S, round = it / S;
-        bool got = true;
-        if (lane == 0) got = mbar_wait(&full[s], round & 1);
-        got = __shfl_sync(0xffffffffu, got, 0);
-        if (!got) {
-            set_error(p.err, kErrWaitFull);
-            return;
+    bool failed = false;
+    for (int item = first; item < last; item++) {
+        const ItemInfo ii = decode_item(p, nact, RT, item);
+        const int seg0 = __ldg(p.offsets + ii.e);
+        const int n_e = __ldg(p.offsets + ii.e + 1) - seg0;
+        const int t0 = ii.tc * kTokChunk, nq = min(kTokChunk, n_e - t0);
+        const int NT = (nq + 7) >> 3;
+        if (ii.e != cur_e || ii.tc != cur_tc) {
+            consumer_sync();  // nobody still reads the region
+            fill_region<kGU>(p, region, seg0, t0, nq, Kb, xs);
+            cur_e = ii.e, cur_tc = ii.tc;
+            consumer_sync();
         }
-        const int e = __ldg(p.active + item / ipe), c = item % ipe;
-        const uint8_t *stg = stages + (size_t)s * p.stage_bytes;
-        consume(e, c, stg, stg + (size_t)Tile::kRows * p.q_stride, warp, lane);
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
-    }
-}
-
-__global__ void __launch_bounds__(kGemvThreads, 1) k_gateup(GemvParams p) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    const int d = p.m.d, eh = p.m.eh, K = p.m.K;
-    const int nb = d / MIAG_QK, xs = scale_pad(nb);
-    run_pipeline<GuTile>(p, smem, [&](int e, int c, const uint8_t *sq, const uint8_t *ss, int warp,
-                                      int lane) {
-        const int row = lane & 15, half = lane >> 4;
-        const uint8_t *qr = sq + (size_t)row * p.q_stride;
-        const float *sr = reinterpret_cast<const float *>(ss + (size_t)row * p.s_stride);
-        const int seg0 = __ldg(p.offsets + e), n_e = __ldg(p.offsets + e + 1) - seg0;
-        for (int k0 = 2 * warp; k0 < n_e; k0 += 2 * kConsumerWarps) {
-            const int k = k0 + half;
-            float acc = 0.0f;
-            int pos = 0;
-            if (k < n_e) {
-                pos = seg0 + k;
-                const int t = __ldg(p.perm + pos) / K;
-                acc = row_dot(qr, sr, p.xq + (size_t)t * d, p.dx + (size_t)t * xs, nb);
-            }
-            const float up = __shfl_xor_sync(0xffffffffu, acc, 1);
-            if (k < n_e && (row & 1) == 0)
-                p.h[(size_t)pos * eh + c * kGuRowPairs + (row >> 1)] = swiglu_ref(acc, up);
-        }
-    });
-}
-
-__global__ void __launch_bounds__(kGemvThreads, 1) k_down(GemvParams p) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    const int d = p.m.d, eh = p.m.eh;
-    const int nb = eh / MIAG_QK, hs = scale_pad(nb);
-    run_pipeline<DnTile>(p, smem, [&](int e, int c, const uint8_t *sq, const uint8_t *ss, int warp,
-                                      int lane) {
-        const uint8_t *qr = sq + (size_t)lane * p.q_stride;
-        const float *sr = reinterpret_cast<const float *>(ss + (size_t)lane * p.s_stride);
-        const int seg0 = __ldg(p.offsets + e), n_e = __ldg(p.offsets + e + 1) - seg0;
-        for (int k = warp; k < n_e; k += kConsumerWarps) {
-            const int pos = seg0 + k;
-            const float acc =
-                row_dot(qr, sr, p.hq + (size_t)pos * eh, p.dh + (size_t)pos * hs, nb);
-            p.y[(size_t)pos * d + c * kDnRows + lane] = acc;
-        }
-    });
-}
-
-// Q8_0 of each pair's h (quant.c:11-27), one warp per 32-block.
-__global__ void k_quant_h(const float *h, int P, int eh, int8_t *hq, float *dh) {
-    const int lane = threadIdx.x & 31;
-    const int nb = eh / MIAG_QK, hs = scale_pad(nb);
-    const long gw = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    if (gw >= (long)P * nb) return;
-    const int pos = (int)(gw / nb), b = (int)(gw % nb);
-    const float v = h[(size_t)pos * eh + b * MIAG_QK + lane];
-    float a = fabsf(v);
+        float acc[kMaxNT][4];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
-    const float dq = __fdiv_rn(a, 127.0f);
-    const float id = dq != 0.0f ? __fdiv_rn(1.0f, dq) : 0.0f;
-    hq[(size_t)pos * eh + b * MIAG_QK + lane] = (int8_t)roundf(__fmul_rn(v, id));
-    if (lane == 0) dh[(size_t)pos * hs + b] = dq;
+        for (int n = 0; n < kMaxNT; n++)
+#pragma unroll
+            for (int i = 0; i < 4; i++) acc[n][i] = 0.0f;
+        // B row address of this lane's ldmatrix role, per n-tile (pairs past
+        // nq repeat the last pair; their columns are never written out)
+        uint32_t b_addr[kMaxNT];
+#pragma unroll
+        for (int n = 0; n < kMaxNT; n++)
+            b_addr[n] = region_addr + (uint32_t)min(8 * n + b_pair, nq - 1) * p.x_stride + 16 * b_half;
+
+        for (int ks = 0; ks < NS; ks++, it++) {
+            const int s = it % S, round = it / S;
+            if (!failed) {
+                bool got = true;
+                if (lane == 0) got = mbar_wait(&full[s], round & 1);
+                if (!__shfl_sync(kFull, got, 0)) {
+                    // Keep walking (on stale data) so every consumer reaches the
+                    // same named barriers: no warp may leave early.
+                    set_error(p.err, kErrWaitFull);
+                    failed = true;
+                }
+            }
+            const uint8_t *stg = stages + (size_t)s * kStageBytes;
+            const uint32_t stg_addr = smem_addr(stg);
+            const int kt0 = ks * kStageKT, nkt = min(kStageKT, KT - kt0);
+            for (int kk = 0; kk < nkt; kk++) {
+                const int kt = kt0 + kk;
+                const float *sc = reinterpret_cast<const float *>(stg + kStageKT * kTileBytes +
+                                                                  kk * kTileScaleBytes);
+                const float4 w0 = *reinterpret_cast<const float4 *>(sc + 4 * r0);
+                const float4 w1 = *reinterpret_cast<const float4 *>(sc + 4 * r1);
+                const float wa[4] = {w0.x, w0.y, w0.z, w0.w}, wb[4] = {w1.x, w1.y, w1.z, w1.w};
+                float xa[kMaxNT][4], xb[kMaxNT][4];  // scales of pairs 2tq, 2tq+1 of each n-tile
+#pragma unroll
+                for (int n = 0; n < kMaxNT; n++) {
+                    if (n < NT) {
+                        const int qa = min(8 * n + 2 * tq, nq - 1), qb = min(8 * n + 2 * tq + 1, nq - 1);
+                        const float4 u = *reinterpret_cast<const float4 *>(rsc + (size_t)qa * xsp + 4 * kt);
+                        const float4 v = *reinterpret_cast<const float4 *>(rsc + (size_t)qb * xsp + 4 * kt);
+                        xa[n][0] = u.x, xa[n][1] = u.y, xa[n][2] = u.z, xa[n][3] = u.w;
+                        xb[n][0] = v.x, xb[n][1] = v.y, xb[n][2] = v.z, xb[n][3] = v.w;
+                    }
+                }
+                const uint32_t tile_addr = stg_addr + kk * kTileBytes;
+                const int nbk = min(4, nb - 4 * kt);  // blocks of this k tile inside K
+                // Issue all operand loads and MMAs of the k tile first, so their
+                // latencies overlap; then apply the float steps in block order.
+                uint32_t A[4][4];
+#pragma unroll
+                for (int j = 0; j < 4; j++)
+                    if (j < nbk)
+                        ldsm_x4(tile_addr + tile_chunk_offset(a_row, 2 * j + a_half), A[j][0], A[j][1],
+                                A[j][2], A[j][3]);
+#pragma unroll
+                for (int n = 0; n < kMaxNT; n++) {
+                    if (n < NT) {
+                        uint32_t B[4][2];
+                        int C[4][4];
+#pragma unroll
+                        for (int j = 0; j < 4; j++)
+                            if (j < nbk)
+                                ldsm_x2(b_addr[n] + (uint32_t)(kt * kTileK + 32 * j), B[j][0], B[j][1]);
+#pragma unroll
+                        for (int j = 0; j < 4; j++)
+                            if (j < nbk)
+                                mma_s8(C[j], A[j][0], A[j][1], A[j][2], A[j][3], B[j][0], B[j][1]);
+#pragma unroll
+                        for (int j = 0; j < 4; j++) {
+                            if (j < nbk) {
+                                acc[n][0] = q8_step(acc[n][0], C[j][0], wa[j], xa[n][j]);
+                                acc[n][1] = q8_step(acc[n][1], C[j][1], wa[j], xb[n][j]);
+                                acc[n][2] = q8_step(acc[n][2], C[j][2], wb[j], xa[n][j]);
+                                acc[n][3] = q8_step(acc[n][3], C[j][3], wb[j], xb[n][j]);
+                            }
+                        }
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+        }
+
+        // outputs: this lane holds rows r0, r1 x pairs 8n + 2tq, 8n + 2tq + 1
+        const int R0 = ii.rt * kTileRows + r0, R1 = R0 + 8;
+#pragma unroll
+        for (int n = 0; n < kMaxNT; n++) {
+            if (n >= NT) break;
+            const int qa = 8 * n + 2 * tq, qb = qa + 1;
+            if (kGU) {
+                // rows are interleaved gate (even) / up (odd): the up partner of
+                // row r sits in the lane with groupID g ^ 1, i.e. lane ^ 4.
+                float up[4];
+#pragma unroll
+                for (int i = 0; i < 4; i++) up[i] = __shfl_xor_sync(kFull, acc[n][i], 4);
+                if ((g & 1) == 0) {
+                    const int i0 = R0 >> 1, i1 = R1 >> 1;
+                    if (qa < nq) {
+                        float *hp = p.h + (size_t)(seg0 + t0 + qa) * eh;
+                        if (R0 < rows) hp[i0] = swiglu_ref(acc[n][0], up[0]);
+                        if (R1 < rows) hp[i1] = swiglu_ref(acc[n][2], up[2]);
+                    }
+                    if (qb < nq) {
+                        float *hp = p.h + (size_t)(seg0 + t0 + qb) * eh;
+                        if (R0 < rows) hp[i0] = swiglu_ref(acc[n][1], up[1]);
+                        if (R1 < rows) hp[i1] = swiglu_ref(acc[n][3], up[3]);
+                    }
+                }
+            } else {
+                if (qa < nq) {
+                    float *yp = p.y + (size_t)(seg0 + t0 + qa) * d;
+                    if (R0 < rows) yp[R0] = acc[n][0];
+                    if (R1 < rows) yp[R1] = acc[n][2];
+                }
+                if (qb < nq) {
+                    float *yp = p.y + (size_t)(seg0 + t0 + qb) * d;
+                    if (R0 < rows) yp[R0] = acc[n][1];
+                    if (R1 < rows) yp[R1] = acc[n][3];
+                }
+            }
+        }
+    }
 }
 
 // x[t] += w_j * y_j for j = 0..K-1 in order (forward.c:194).
@@ -252,73 +393,67 @@ __global__ void k_combine(float *x, int d, int K, const float *w, const int32_t 
     x[(size_t)t * d + i] = v;
 }
 
+// ---------------------------------------------------------------------------
+// Host side.
+
 static void fill_params(GemvParams &p, const Dims &m, const StoreLayout &lay, const LayerDev &L,
                         const Work &w, int *err) {
     p.m = m, p.lay = lay, p.experts = L.experts;
     p.offsets = w.offsets, p.perm = w.perm, p.active = w.active, p.n_active = w.n_active;
-    p.xq = w.xq, p.dx = w.dx, p.h = w.h, p.hq = w.hq, p.dh = w.dh, p.y = w.y, p.err = err;
+    p.chunk_pre = w.chunk_pre;
+    p.xq = w.xq, p.dx = w.dx, p.h = w.h, p.y = w.y, p.err = err;
 }
 
-static void gu_geometry(GemvParams &p) {
-    p.q_stride = smem_stride((uint32_t)p.m.d);
-    p.s_stride = smem_stride(p.lay.gu_s_row);
-    p.stage_bytes = (uint32_t)kGuRows * (p.q_stride + p.s_stride);
-    int st = (kSmemBudget - kBarBytes) / (int)p.stage_bytes;
+// Shared memory: barriers | S stages | activation region (rows, then scales).
+static size_t geometry(GemvParams &p, bool gu) {
+    const int Kb = gu ? p.m.d : p.m.eh;
+    const int xs = scale_pad(Kb / MIAG_QK);
+    p.x_stride = smem_stride((uint32_t)Kb);
+    const size_t region =
+        round_up_sz((size_t)kTokChunk * (p.x_stride + smem_stride((uint32_t)xs * 4)), 128);
+    const long room = (long)kSmemBudget - kBarBytes - (long)region;
+    const int st = room > 0 ? (int)(room / kStageBytes) : 0;
     p.stages = st > kMaxStages ? kMaxStages : st;
+    p.x_off = (uint32_t)(kBarBytes + (size_t)p.stages * kStageBytes);
+    return p.x_off + region;
 }
 
-static void dn_geometry(GemvParams &p) {
-    p.q_stride = smem_stride((uint32_t)p.m.eh);
-    p.s_stride = smem_stride(p.lay.dn_s_row);
-    p.stage_bytes = (uint32_t)kDnRows * (p.q_stride + p.s_stride);
-    int st = (kSmemBudget - kBarBytes) / (int)p.stage_bytes;
-    p.stages = st > kMaxStages ? kMaxStages : st;
-}
-
+// The dynamic shared-memory limit is an attribute of the kernel, shared by
+// every context in the process, so it is raised to the whole budget rather
+// than to one shape's need.
 int gemv_setup_attributes(const Dims &m, const StoreLayout &lay) {
     GemvParams p{};
     p.m = m, p.lay = lay;
-    gu_geometry(p);
-    if (p.stages < 2) return -1;
-    size_t smem = kBarBytes + (size_t)p.stages * p.stage_bytes;
-    if (cudaFuncSetAttribute(k_gateup, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-        cudaSuccess)
-        return -1;
-    dn_geometry(p);
-    if (p.stages < 2) return -1;
-    smem = kBarBytes + (size_t)p.stages * p.stage_bytes;
-    if (cudaFuncSetAttribute(k_down, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-        cudaSuccess)
+    if (geometry(p, true) > (size_t)kSmemBudget || p.stages < 2) return -1;
+    if (geometry(p, false) > (size_t)kSmemBudget || p.stages < 2) return -1;
+    if (cudaFuncSetAttribute(k_expert_mma<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kSmemBudget) != cudaSuccess ||
+        cudaFuncSetAttribute(k_expert_mma<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kSmemBudget) != cudaSuccess)
         return -1;
     return 0;
+}
+
+static int grid_for(const Dims &m, int RT, int num_sms, int P) {
+    // items <= RT * (chunks), chunks <= P / kTokChunk + (active experts)
+    const long max_items = (long)RT * ((long)P / kTokChunk + m.E);
+    return (int)(max_items < num_sms ? max_items : num_sms);
 }
 
 void launch_gateup(const Dims &m, const StoreLayout &lay, const LayerDev &L, const Work &w,
                    int num_sms, int *err, cudaStream_t s) {
     GemvParams p{};
     fill_params(p, m, lay, L, w, err);
-    gu_geometry(p);
-    const size_t smem = kBarBytes + (size_t)p.stages * p.stage_bytes;
-    const int max_items = m.E * (m.eh / kGuRowPairs);
-    const int grid = num_sms < max_items ? num_sms : max_items;
-    k_gateup<<<grid, kGemvThreads, smem, s>>>(p);
+    const size_t smem = geometry(p, true);
+    k_expert_mma<true><<<grid_for(m, lay.gu_rt, num_sms, w.P), kGemvThreads, smem, s>>>(p);
 }
 
 void launch_down(const Dims &m, const StoreLayout &lay, const LayerDev &L, const Work &w,
                  int num_sms, int *err, cudaStream_t s) {
     GemvParams p{};
     fill_params(p, m, lay, L, w, err);
-    dn_geometry(p);
-    const size_t smem = kBarBytes + (size_t)p.stages * p.stage_bytes;
-    const int max_items = m.E * (m.d / kDnRows);
-    const int grid = num_sms < max_items ? num_sms : max_items;
-    k_down<<<grid, kGemvThreads, smem, s>>>(p);
-}
-
-void launch_quant_h(const Dims &m, const Work &w, cudaStream_t s) {
-    const long warps = (long)w.P * (m.eh / MIAG_QK);
-    const long blocks = (warps * 32 + 255) / 256;
-    k_quant_h<<<(unsigned)blocks, 256, 0, s>>>(w.h, w.P, m.eh, w.hq, w.dh);
+    const size_t smem = geometry(p, false);
+    k_expert_mma<false><<<grid_for(m, lay.dn_rt, num_sms, w.P), kGemvThreads, smem, s>>>(p);
 }
 
 void launch_combine(const Dims &m, const Work &w, float *x, cudaStream_t s) {

@@ -11,7 +11,6 @@ struct Work {
     int8_t *xq;            // [T][d]        quantized normalised input (Q8_0 values)
     float *dx;             // [T][xs_pad]   its block scales
     float *logits;         // [T][E]        router logits (+ bias)
-    int32_t *ticket;       // [ceil(T/2)]   route token-group completion tickets (self-resetting)
     int32_t *idx;          // [T][K]
     float *w;              // [T][K]
     int32_t *rank;         // [P]           stable rank of a pair inside its chunk
@@ -21,17 +20,16 @@ struct Work {
     int32_t *offsets;      // [E+1]
     int32_t *active;       // [E]           experts with >= 1 pair, ascending
     int32_t *n_active;     // [1]
+    int32_t *chunk_pre;    // [E+1]         exclusive prefix over active experts of ceil(n_e / kTokChunk)
     int32_t *perm;         // [P]           pair id at each sorted position
     int32_t *inv;          // [P]           sorted position of each pair
     float *h;              // [P][eh]       silu(gate) * up, sorted order
-    int8_t *hq;            // [P][eh]       Q8_0 values of h
-    float *dh;             // [P][hs_pad]
     float *y;              // [P][d]        down projections, sorted order
 };
 
 struct LayerDev {
     const float *ffn_norm;  // [d]
-    const float *router_t;  // [d][E]  router transposed (column e contiguous over d)
+    const float *router_t;  // [ceil(E/32)][d][32]  router, 32-expert groups contiguous
     const float *bias;      // [E] or nullptr
     const uint8_t *experts; // E * layout.expert_bytes
 };
@@ -42,16 +40,17 @@ struct Dims {
 };
 
 constexpr int kPermChunk = 1024;
+constexpr int kTokChunk = 32;  // pairs of one expert handled per expert-GEMV item
 
 // route.cu
 void launch_route(const Dims &m, const LayerDev &L, const float *x, const Work &w,
                   int *err, cudaStream_t s);
-// permute.cu
+// permute.cu (includes softmax / top-k)
 void launch_permute(const Dims &m, const Work &w, int *err, cudaStream_t s);
+int permute_launches(int P, int E);
 // gemv.cu
 void launch_gateup(const Dims &m, const StoreLayout &lay, const LayerDev &L, const Work &w,
                    int num_sms, int *err, cudaStream_t s);
-void launch_quant_h(const Dims &m, const Work &w, cudaStream_t s);
 void launch_down(const Dims &m, const StoreLayout &lay, const LayerDev &L, const Work &w,
                  int num_sms, int *err, cudaStream_t s);
 void launch_combine(const Dims &m, const Work &w, float *x, cudaStream_t s);

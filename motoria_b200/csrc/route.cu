@@ -1,20 +1,22 @@
-// route.cu -- rmsnorm + activation quantization + router + softmax/top-k.
+// route.cu -- rmsnorm + activation quantization + router logits.
 //
 // Reference: src/model/forward.c:174-181 (rmsnorm :75-81, router matvec
 // src/tensor/matmul.c:13-17, softmax :95-101, top_k :104-114) and the
 // activation quantizer src/tensor/quant.c:11-27 that mia_matvec applies to
 // xn before the expert gate/up products (matmul.c:93).
 //
-// Grid: (token groups of R, expert groups of 32).  Each CTA is one warp:
-//   1. rmsnorm of its R tokens into shared memory, certified to equal the
-//      reference's serial double sum (see rms_scale);
+// Grid: (token groups, expert groups of 32).  A CTA has W consumer warps,
+// each owning R tokens, and one producer warp:
+//   1. each warp rmsnorms its tokens into shared memory, certified to equal
+//      the reference's serial double sum (see rms_scale);
 //   2. expert-group 0 quantizes xn to Q8_0 for the expert GEMVs;
-//   3. lane e computes the router logit of expert 32*eg + e for the R tokens
-//      as the reference's serial fp32 sum (rounded multiply, then rounded
-//      add, i = 0..d-1 in order; f32x2 instructions round each half exactly
-//      like the scalar ones);
-//   4. the last CTA of a token group to finish (atomic ticket, no waiting)
-//      runs softmax, top-k and renormalisation for the group.
+//   3. lane e computes the router logit of expert 32*eg + e for the warp's
+//      tokens as the reference's serial fp32 sum (rounded multiply, then
+//      rounded add, i = 0..d-1 in order).  The group's router slice, stored
+//      [group][i][32] so it is contiguous, streams through a ring of
+//      shared-memory chunks that the producer fills with 1-D TMA bulk copies
+//      and all consumer warps read;
+// Softmax, top-k and renormalisation run afterwards in topk.cu.
 #include "kernels.cuh"
 
 namespace miag {
@@ -31,30 +33,23 @@ __device__ __forceinline__ float rms_scale_of(double ss, int n, float eps) {
 // The warp-parallel sum therefore brackets the reference's value; the scale
 // is monotone in the sum, so when both ends of the bracket give the same
 // float the reference's float is that one.  Otherwise (probability ~1e-5)
-// lane 0 repeats the serial sum.
-__device__ float rms_scale(const float *x, int n, float eps, int lane) {
-    double ss = 0.0;
-    for (int i = lane; i < n; i += 32) {
-        double v = (double)x[i];
-        ss = __dadd_rn(ss, __dmul_rn(v, v));
-    }
+// lane 0 repeats the serial sum over x (shared memory).
+__device__ float rms_scale_certified(double ss, const float *x, int n, float eps, int lane) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) ss = __dadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+    const double rel = (2.02 * (double)n + 8.0) * 1.1102230246251565e-16;  // 2^-53
+    // lanes 0 and 1 evaluate the two ends of the bracket at the same time
+    const float end = rms_scale_of(ss * (lane == 0 ? 1.0 - rel : 1.0 + rel), n, eps);
+    const float a = __shfl_sync(0xffffffffu, end, 0), b = __shfl_sync(0xffffffffu, end, 1);
+    if (a == b) return a;
     float r = 0.0f;
     if (lane == 0) {
-        const double rel = (2.02 * (double)n + 8.0) * 1.1102230246251565e-16;  // 2^-53
-        float a = rms_scale_of(ss * (1.0 - rel), n, eps);
-        float b = rms_scale_of(ss * (1.0 + rel), n, eps);
-        if (a == b) {
-            r = a;
-        } else {
-            double s2 = 0.0;
-            for (int i = 0; i < n; i++) {
-                double v = (double)x[i];
-                s2 = __dadd_rn(s2, __dmul_rn(v, v));
-            }
-            r = rms_scale_of(s2, n, eps);
+        double s2 = 0.0;
+        for (int i = 0; i < n; i++) {
+            const double v = (double)x[i];
+            s2 = __dadd_rn(s2, __dmul_rn(v, v));
         }
+        r = rms_scale_of(s2, n, eps);
     }
     return __shfl_sync(0xffffffffu, r, 0);
 }
@@ -67,174 +62,239 @@ struct RouteParams {
     int8_t *xq;          // [T][d]
     float *dx;           // [T][xs_pad]
     float *logits;       // [T][E]
-    int32_t *ticket;     // [ceil(T/R)]
-    int32_t *idx;        // [T][K]
-    float *w;            // [T][K]
     int *err;
 };
 
-// Softmax, top-k and renormalisation of one token's logits (one warp).
-__device__ void topk_token(const RouteParams &p, int t, float *buf, int lane) {
-    const int E = p.m.E, K = p.m.K;
-    const float *lg = p.logits + (size_t)t * E;
-    float mx = -INFINITY;
-    for (int e = lane; e < E; e += 32) mx = fmaxf(mx, __ldcg(lg + e));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    for (int e = lane; e < E; e += 32) buf[e] = expf_cr(__fsub_rn(__ldcg(lg + e), mx));
-    __syncwarp();
-    float sum = 0.0f;
-    if (lane == 0)
-        for (int e = 0; e < E; e++) sum = __fadd_rn(sum, buf[e]);  // forward.c:99 order
-    sum = __shfl_sync(0xffffffffu, sum, 0);
-    for (int e = lane; e < E; e += 32) buf[e] = __fdiv_rn(buf[e], sum);
-    __syncwarp();
-    // K rounds of first-maximum selection (forward.c:104-114): ties go to the
-    // lower index; `taken` bit k of a lane marks expert lane + 32k.
-    uint32_t taken = 0;
-    int sel[64];
-    for (int j = 0; j < K; j++) {
-        float bv = -INFINITY;
-        int bi = 0x7fffffff;
-        for (int e = lane, k = 0; e < E; e += 32, k++) {
-            float v = buf[e];
-            if (!((taken >> k) & 1u) && (bi == 0x7fffffff || v > bv)) bv = v, bi = e;
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            bool take = (oi != 0x7fffffff) &&
-                        (bi == 0x7fffffff || ov > bv || (ov == bv && oi < bi));
-            if (take) bv = ov, bi = oi;
-        }
-        sel[j] = bi;
-        if (bi != 0x7fffffff && (bi & 31) == lane) taken |= 1u << (bi >> 5);
-    }
-    if (lane == 0) {
-        float s = 0.0f, wv[64];
-        for (int j = 0; j < K; j++) {
-            wv[j] = buf[sel[j]];
-            s = __fadd_rn(s, wv[j]);  // forward.c:179
-        }
-        for (int j = 0; j < K; j++) {
-            p.idx[(size_t)t * K + j] = sel[j];
-            p.w[(size_t)t * K + j] = p.m.norm_topk ? __fdiv_rn(wv[j], s) : wv[j];
-        }
-    }
-    __syncwarp();
+constexpr int kRouteChunk = 64;   // router rows i per bulk-copied chunk (64 x 128 B)
+constexpr int kRouteStages = 8;
+
+// Shared memory: barriers | ring [kRouteStages][kRouteChunk][32] f32 |
+// x, then xn in place [W*R][d] f32 | ffn_norm [d] f32.
+constexpr int kRouteBarBytes = 256;
+__host__ __device__ inline size_t route_smem(int d, int E, int R, int W) {
+    (void)E;
+    return kRouteBarBytes + (size_t)kRouteStages * kRouteChunk * 128 + (size_t)W * R * d * 4 +
+           (size_t)d * 4;
 }
 
+// Grid: (token groups of W*R, expert groups of 32); W consumer warps own R
+// tokens each, one producer warp streams the group's rows and router slice.
 template <int R>
-__global__ void __launch_bounds__(32) k_route(RouteParams p) {
-    extern __shared__ __align__(16) float sm[];  // xn [d][R], then E floats of top-k scratch
-    const int d = p.m.d, E = p.m.E, lane = threadIdx.x;
-    const int t0 = blockIdx.x * R;
-    const int nt = min(R, p.T - t0);
-    float *xn = sm;
+__global__ void __launch_bounds__(9 * 32) k_route(RouteParams p, int W) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int d = p.m.d, E = p.m.E;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem);
+    uint64_t *empty = full + kRouteStages;
+    uint64_t *xbar = empty + kRouteStages;
+    float *ring = reinterpret_cast<float *>(smem + kRouteBarBytes);
+    float *xs_all = ring + (size_t)kRouteStages * kRouteChunk * 32;  // [W*R][d]
+    float *norm = xs_all + (size_t)W * R * d;
+    const int nchunks = (d + kRouteChunk - 1) / kRouteChunk;
+    const float *slice = p.L.router_t + (size_t)blockIdx.y * d * 32;
+    const int tg0 = blockIdx.x * W * R;                 // first token of the CTA
+    const int ntok = min(W * R, p.T - tg0);             // tokens present
 
-    // 1. rmsnorm of the group's tokens (forward.c:75-81 with w = ffn_norm).
-    for (int r = 0; r < R; r++) {
-        if (r < nt) {
-            const float *x = p.x + (size_t)(t0 + r) * d;
-            float inv = rms_scale(x, d, p.m.eps, lane);
-            for (int i = lane; i < d; i += 32)
-                xn[i * R + r] = __fmul_rn(__fmul_rn(x[i], inv), p.L.ffn_norm[i]);
-        } else {
-            for (int i = lane; i < d; i += 32) xn[i * R + r] = 0.0f;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kRouteStages; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], W);
+        }
+        mbar_init(xbar, 1);
+        fence_barrier_init();
+    }
+    __syncthreads();
+
+    if (warp == W) {
+        // Producer: the CTA's token rows and ffn_norm, then router chunks.
+        if (lane == 0) {
+            const uint32_t xbytes = (uint32_t)ntok * d * 4;
+            mbar_arrive_expect_tx(xbar, xbytes + (uint32_t)d * 4);
+            bulk_g2s(xs_all, p.x + (size_t)tg0 * d, xbytes, xbar);
+            bulk_g2s(norm, p.L.ffn_norm, (uint32_t)d * 4, xbar);
+            for (int ch = 0; ch < nchunks; ch++) {
+                const int s = ch % kRouteStages, round = ch / kRouteStages;
+                if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1)) {
+                    set_error(p.err, kErrWaitEmpty);
+                    for (int j = ch - 1; j >= 0 && j >= ch - kRouteStages; j--)
+                        mbar_wait(&full[j % kRouteStages], (j / kRouteStages) & 1);
+                    mbar_wait(xbar, 0);
+                    break;
+                }
+                const int rows = min(kRouteChunk, d - ch * kRouteChunk);
+                const uint32_t bytes = (uint32_t)rows * 128u;
+                mbar_arrive_expect_tx(&full[s], bytes);
+                bulk_g2s(ring + (size_t)s * kRouteChunk * 32,
+                         slice + (size_t)ch * kRouteChunk * 32, bytes, &full[s]);
+            }
+        }
+        return;
+    }
+
+    const int tw0 = tg0 + warp * R;  // this warp's first token
+    const int nt = max(0, min(R, p.T - tw0));
+    float *xw = xs_all + (size_t)warp * R * d;  // this warp's rows: x, then xn in place
+    bool failed = false;
+    {
+        bool got = true;
+        if (lane == 0) got = mbar_wait(xbar, 0);
+        if (!__shfl_sync(0xffffffffu, got, 0)) {
+            set_error(p.err, kErrWaitFull);
+            failed = true;
         }
     }
-    __syncwarp();
 
-    // 2. Q8_0 of xn (quant.c:11-27), once per token.
-    if (blockIdx.y == 0) {
-        const int nb = d / MIAG_QK, xs = scale_pad(nb);
-        for (int r = 0; r < nt; r++) {
-            for (int b = 0; b < nb; b++) {
-                float v = xn[(b * MIAG_QK + lane) * R + r];
+    // 1.+2. rmsnorm (forward.c:75-81) and Q8_0 of xn (quant.c:11-27).  Lane l
+    // holds elements 4l + 128k (k < d/128) of a token: eight lanes cover one
+    // 32-block, so block maxima take three shuffles.
+    const int nq4 = d / 128;  // float4 per lane (d is a multiple of 32; see tail)
+    for (int r = 0; r < nt; r++) {
+        float *xr = xw + (size_t)r * d;
+        double ss = 0.0;
+        for (int k = 0; k < nq4; k++) {
+            const float4 v = *reinterpret_cast<const float4 *>(xr + 4 * lane + 128 * k);
+            ss = __dadd_rn(ss, __dmul_rn((double)v.x, (double)v.x));
+            ss = __dadd_rn(ss, __dmul_rn((double)v.y, (double)v.y));
+            ss = __dadd_rn(ss, __dmul_rn((double)v.z, (double)v.z));
+            ss = __dadd_rn(ss, __dmul_rn((double)v.w, (double)v.w));
+        }
+        for (int i = 128 * nq4 + lane; i < d; i += 32) {  // d % 128 tail
+            const double v = (double)xr[i];
+            ss = __dadd_rn(ss, __dmul_rn(v, v));
+        }
+        const float inv = rms_scale_certified(ss, xr, d, p.m.eps, lane);
+        const int t = tw0 + r;
+        for (int k = 0; k < nq4; k++) {
+            const int i = 4 * lane + 128 * k;
+            float4 v = *reinterpret_cast<const float4 *>(xr + i);
+            const float4 w = *reinterpret_cast<const float4 *>(norm + i);
+            v.x = __fmul_rn(__fmul_rn(v.x, inv), w.x);
+            v.y = __fmul_rn(__fmul_rn(v.y, inv), w.y);
+            v.z = __fmul_rn(__fmul_rn(v.z, inv), w.z);
+            v.w = __fmul_rn(__fmul_rn(v.w, inv), w.w);
+            *reinterpret_cast<float4 *>(xr + i) = v;
+            if (blockIdx.y == 0) {
+                float a = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+                a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 1));
+                a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 2));
+                a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 4));
+                const float dq = __fdiv_rn(a, 127.0f);
+                const float id = dq != 0.0f ? __fdiv_rn(1.0f, dq) : 0.0f;
+                const uint32_t q0 = (uint8_t)(int8_t)roundf(__fmul_rn(v.x, id));
+                const uint32_t q1 = (uint8_t)(int8_t)roundf(__fmul_rn(v.y, id));
+                const uint32_t q2 = (uint8_t)(int8_t)roundf(__fmul_rn(v.z, id));
+                const uint32_t q3 = (uint8_t)(int8_t)roundf(__fmul_rn(v.w, id));
+                *reinterpret_cast<uint32_t *>(p.xq + (size_t)t * d + i) =
+                    q0 | (q1 << 8) | (q2 << 16) | (q3 << 24);
+                if ((lane & 7) == 0) p.dx[(size_t)t * scale_pad(d / MIAG_QK) + i / MIAG_QK] = dq;
+            }
+        }
+        for (int i = 128 * nq4 + lane; i < d; i += 32) {  // tail (d % 128 == 32, 64, 96)
+            xr[i] = __fmul_rn(__fmul_rn(xr[i], inv), norm[i]);
+        }
+        if (blockIdx.y == 0 && 128 * nq4 < d) {
+            // tail blocks: one warp-wide pass per 32-block
+            for (int b = 4 * nq4; b < d / MIAG_QK; b++) {
+                const float v = xr[b * MIAG_QK + lane];
                 float a = fabsf(v);
 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
-                float dq = __fdiv_rn(a, 127.0f);
-                float id = dq != 0.0f ? __fdiv_rn(1.0f, dq) : 0.0f;
-                p.xq[(size_t)(t0 + r) * d + b * MIAG_QK + lane] = (int8_t)roundf(__fmul_rn(v, id));
-                if (lane == 0) p.dx[(size_t)(t0 + r) * xs + b] = dq;
+                const float dq = __fdiv_rn(a, 127.0f);
+                const float id = dq != 0.0f ? __fdiv_rn(1.0f, dq) : 0.0f;
+                p.xq[(size_t)t * d + b * MIAG_QK + lane] = (int8_t)roundf(__fmul_rn(v, id));
+                if (lane == 0) p.dx[(size_t)t * scale_pad(d / MIAG_QK) + b] = dq;
             }
         }
     }
+    __syncwarp();
 
     // 3. Router logits, serial over i like dot_f32_scalar (matmul.c:13-17).
-    const int e = blockIdx.y * 32 + lane;
-    if (e < E) {
-        float acc[R];
+    float acc[R];
 #pragma unroll
-        for (int r = 0; r < R; r++) acc[r] = 0.0f;
-        const float *wt = p.L.router_t + e;
-        int i = 0;
-        for (; i + 8 <= d; i += 8) {
-            float wv[8];
-#pragma unroll
-            for (int u = 0; u < 8; u++) wv[u] = __ldg(wt + (size_t)(i + u) * E);
-#pragma unroll
-            for (int u = 0; u < 8; u++) {
-                const float *xv = xn + (i + u) * R;
-#pragma unroll
-                for (int r = 0; r + 1 < R; r += 2) {
-                    float2 pr = __fmul2_rn(make_float2(wv[u], wv[u]), make_float2(xv[r], xv[r + 1]));
-                    float2 a2 = __fadd2_rn(make_float2(acc[r], acc[r + 1]), pr);
-                    acc[r] = a2.x, acc[r + 1] = a2.y;
-                }
-                if (R & 1) acc[R - 1] = __fadd_rn(acc[R - 1], __fmul_rn(wv[u], xv[R - 1]));
+    for (int r = 0; r < R; r++) acc[r] = 0.0f;
+    for (int ch = 0; ch < nchunks; ch++) {
+        const int s = ch % kRouteStages;
+        if (!failed) {
+            bool got = true;
+            if (lane == 0) got = mbar_wait(&full[s], (ch / kRouteStages) & 1);
+            if (!__shfl_sync(0xffffffffu, got, 0)) {
+                set_error(p.err, kErrWaitFull);
+                failed = true;
             }
         }
-        for (; i < d; i++) {
-            float wv = __ldg(wt + (size_t)i * E);
+        const float *wc = ring + (size_t)s * kRouteChunk * 32 + lane;
+        const int i0 = ch * kRouteChunk, rows = min(kRouteChunk, d - i0);
+        for (int u = 0; u < rows; u += 16) {  // rows is a multiple of 32
+            float4 xv[R][4];
+            float wv[16];
 #pragma unroll
-            for (int r = 0; r < R; r++) acc[r] = __fadd_rn(acc[r], __fmul_rn(wv, xn[i * R + r]));
+            for (int r = 0; r < R; r++)
+#pragma unroll
+                for (int q = 0; q < 4; q++)
+                    xv[r][q] = *reinterpret_cast<const float4 *>(xw + (size_t)r * d + i0 + u + 4 * q);
+#pragma unroll
+            for (int k = 0; k < 16; k++) wv[k] = wc[(u + k) * 32];
+            // Scalar round-to-nearest intrinsics: the compiler never fuses
+            // them (paired f32x2 forms do get contracted into an FMA).
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+#pragma unroll
+                for (int r = 0; r < R; r++) {
+                    acc[r] = __fadd_rn(acc[r], __fmul_rn(wv[4 * q + 0], xv[r][q].x));
+                    acc[r] = __fadd_rn(acc[r], __fmul_rn(wv[4 * q + 1], xv[r][q].y));
+                    acc[r] = __fadd_rn(acc[r], __fmul_rn(wv[4 * q + 2], xv[r][q].z));
+                    acc[r] = __fadd_rn(acc[r], __fmul_rn(wv[4 * q + 3], xv[r][q].w));
+                }
+            }
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    const int e = blockIdx.y * 32 + lane;
+    if (e < E) {
         for (int r = 0; r < nt; r++) {
             float l = acc[r];
             if (p.L.bias) l = __fadd_rn(l, p.L.bias[e]);
-            p.logits[(size_t)(t0 + r) * E + e] = l;
+            p.logits[(size_t)(tw0 + r) * E + e] = l;
         }
     }
 
-    // 4. Last CTA of the token group runs softmax/top-k.
-    __threadfence();
-    __syncwarp();
-    int last = 0;
-    if (lane == 0) last = atomicAdd(p.ticket + blockIdx.x, 1) == (int)gridDim.y - 1;
-    last = __shfl_sync(0xffffffffu, last, 0);
-    if (!last) return;
-    __threadfence();
-    float *buf = sm + (size_t)d * R;
-    for (int r = 0; r < nt; r++) topk_token(p, t0 + r, buf, lane);
-    if (lane == 0) p.ticket[blockIdx.x] = 0;
 }
 
-int route_group(int T) { return T <= 256 ? 2 : (T <= 1024 ? 4 : 8); }
+// Tokens per warp R and consumer warps W by batch size.
+static void route_shape(int T, int &R, int &W) {
+    if (T <= 1) R = 1, W = 1;
+    else if (T <= 256) R = 2, W = 4;
+    else if (T <= 1024) R = 4, W = 4;
+    else R = 8, W = 2;
+}
 
 void launch_route(const Dims &m, const LayerDev &L, const float *x, const Work &w, int *err,
                   cudaStream_t s) {
     RouteParams p;
     p.m = m, p.L = L, p.x = x, p.T = w.T;
-    p.xq = w.xq, p.dx = w.dx, p.logits = w.logits, p.ticket = w.ticket;
-    p.idx = w.idx, p.w = w.w, p.err = err;
-    const int R = route_group(w.T);
-    dim3 grid((w.T + R - 1) / R, (m.E + 31) / 32);
-    size_t smem = ((size_t)m.d * R + (size_t)m.E) * sizeof(float);
+    p.xq = w.xq, p.dx = w.dx, p.logits = w.logits, p.err = err;
+    int R, W;
+    route_shape(w.T, R, W);
+    dim3 grid((w.T + R * W - 1) / (R * W), (m.E + 31) / 32);
+    const size_t smem = route_smem(m.d, m.E, R, W);
+    const int threads = (W + 1) * 32;
     switch (R) {
+        case 1:
+            cudaFuncSetAttribute(k_route<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            k_route<1><<<grid, threads, smem, s>>>(p, W);
+            break;
         case 2:
             cudaFuncSetAttribute(k_route<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            k_route<2><<<grid, 32, smem, s>>>(p);
+            k_route<2><<<grid, threads, smem, s>>>(p, W);
             break;
         case 4:
             cudaFuncSetAttribute(k_route<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            k_route<4><<<grid, 32, smem, s>>>(p);
+            k_route<4><<<grid, threads, smem, s>>>(p, W);
             break;
         default:
             cudaFuncSetAttribute(k_route<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            k_route<8><<<grid, 32, smem, s>>>(p);
+            k_route<8><<<grid, threads, smem, s>>>(p, W);
             break;
     }
 }

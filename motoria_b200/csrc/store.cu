@@ -4,13 +4,15 @@
 // (src/storage/expert_cache.c:59-85): blobs arrive in .mia layout (gate | up
 // | down, each a row-major matrix of 36-byte {f32 d; int8 q[32]} blocks,
 // src/storage/mia_file.c:275-278) and are repacked on the device into the
-// row-aligned planes of StoreLayout (common.cuh).  Values are copied, never
-// re-quantized, so the stored weights are the reference's bit for bit.
+// swizzled 128 x 128 B tiles of StoreLayout (common.cuh).  Values are
+// copied, never re-quantized, so the stored weights are the reference's bit
+// for bit.
 #include "kernels.cuh"
 
 namespace miag {
 
-// One thread per Q8_0 block of one output row.
+// One thread per Q8_0 block of one matrix row: the 32 int8 values become two
+// 16-byte chunks of a swizzled tile, the scale one f32 of the scale tile.
 __global__ void k_repack(const uint8_t *aos, size_t aos_stride, size_t off_up, size_t off_down,
                          int d, int eh, StoreLayout lay, uint8_t *dst) {
     const int row = blockIdx.x;  // 0 .. 2*eh + d - 1
@@ -18,47 +20,52 @@ __global__ void k_repack(const uint8_t *aos, size_t aos_stride, size_t off_up, s
     const uint8_t *blob = aos + (size_t)ex * aos_stride;
     uint8_t *out = dst + (size_t)ex * lay.expert_bytes;
     const uint8_t *src;
-    uint8_t *q_out;
-    float *s_out;
-    int nb;
-    uint32_t s_row;
+    uint8_t *q_plane;
+    float *s_plane;
+    int nb, r, kt_count;
     if (row < 2 * eh) {
         const int i = row >> 1;
         nb = d / MIAG_QK;
         src = blob + ((row & 1) ? off_up : 0) + (size_t)i * nb * 36;
-        q_out = out + lay.gu_q_off + (size_t)row * d;
-        s_out = reinterpret_cast<float *>(out + lay.gu_s_off + (size_t)row * lay.gu_s_row);
-        s_row = lay.gu_s_row;
+        q_plane = out + lay.gu_q_off;
+        s_plane = reinterpret_cast<float *>(out + lay.gu_s_off);
+        r = row, kt_count = lay.gu_kt;
     } else {
-        const int r = row - 2 * eh;
+        r = row - 2 * eh;
         nb = eh / MIAG_QK;
         src = blob + off_down + (size_t)r * nb * 36;
-        q_out = out + lay.dn_q_off + (size_t)r * eh;
-        s_out = reinterpret_cast<float *>(out + lay.dn_s_off + (size_t)r * lay.dn_s_row);
-        s_row = lay.dn_s_row;
+        q_plane = out + lay.dn_q_off;
+        s_plane = reinterpret_cast<float *>(out + lay.dn_s_off);
+        kt_count = lay.dn_kt;
     }
+    const int rt = r / kTileRows, rr = r % kTileRows;
     for (int b = threadIdx.x; b < nb; b += blockDim.x) {
         const uint32_t *blk = reinterpret_cast<const uint32_t *>(src + (size_t)b * 36);
-        s_out[b] = __uint_as_float(blk[0]);
-        uint32_t *qo = reinterpret_cast<uint32_t *>(q_out + (size_t)b * MIAG_QK);
+        const int kt = b / 4, jb = b % 4;
+        const size_t tile = (size_t)rt * kt_count + kt;
+        s_plane[tile * (kTileScaleBytes / 4) + rr * 4 + jb] = __uint_as_float(blk[0]);
+        uint8_t *tq = q_plane + tile * kTileBytes;
 #pragma unroll
-        for (int k = 0; k < 8; k++) qo[k] = blk[1 + k];
+        for (int h = 0; h < 2; h++) {
+            uint4 v = make_uint4(blk[1 + 4 * h], blk[2 + 4 * h], blk[3 + 4 * h], blk[4 + 4 * h]);
+            *reinterpret_cast<uint4 *>(tq + tile_chunk_offset(rr, 2 * jb + h)) = v;
+        }
     }
-    // zero the 16-byte padding of the scale row
-    for (int b = nb + threadIdx.x; b < (int)(s_row / 4); b += blockDim.x) s_out[b] = 0.0f;
 }
 
-__global__ void k_transpose(const float *in, float *out, int rows, int cols) {
+// router [E][d] -> grouped [ceil(E/32)][d][32]: a group of 32 experts is one
+// contiguous slice, row i holding those experts' weights for input i.
+__global__ void k_group_router(const float *in, float *out, int E, int d) {
     __shared__ float tile[32][33];
-    const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+    const int i0 = blockIdx.x * 32, g = blockIdx.y;
     for (int k = threadIdx.y; k < 32; k += blockDim.y) {
-        const int r = r0 + k, c = c0 + threadIdx.x;
-        if (r < rows && c < cols) tile[k][threadIdx.x] = in[(size_t)r * cols + c];
+        const int e = g * 32 + k, i = i0 + threadIdx.x;
+        tile[k][threadIdx.x] = (e < E && i < d) ? in[(size_t)e * d + i] : 0.0f;
     }
     __syncthreads();
     for (int k = threadIdx.y; k < 32; k += blockDim.y) {
-        const int c = c0 + k, r = r0 + threadIdx.x;
-        if (r < rows && c < cols) out[(size_t)c * rows + r] = tile[threadIdx.x][k];
+        const int i = i0 + k;
+        if (i < d) out[((size_t)g * d + i) * 32 + threadIdx.x] = tile[threadIdx.x][k];
     }
 }
 
@@ -71,10 +78,10 @@ void launch_repack(const Dims &m, const StoreLayout &lay, const uint8_t *aos, si
     k_repack<<<grid, 64, 0, s>>>(aos, aos_stride, off_up, off_down, m.d, m.eh, lay, dst);
 }
 
-void launch_transpose_router(const float *router, float *router_t, int E, int d,
+void launch_transpose_router(const float *router, float *router_g, int E, int d,
                              cudaStream_t s) {
     dim3 grid((d + 31) / 32, (E + 31) / 32);
-    k_transpose<<<grid, dim3(32, 8), 0, s>>>(router, router_t, E, d);
+    k_group_router<<<grid, dim3(32, 8), 0, s>>>(router, router_g, E, d);
 }
 
 }  // namespace miag

@@ -119,6 +119,14 @@ class MoEEngine:
         N.check(rc, err, "miag_moe")
         return out.reshape(np.shape(x))
 
+    def moe_inplace(self, x: np.ndarray, layer: int = 0) -> None:
+        """x += MoE(x) on a C-contiguous f32 host array (pinned or not), in place."""
+        if x.dtype != np.float32 or not x.flags["C_CONTIGUOUS"] or x.ndim != 2:
+            raise ValueError("x must be a C-contiguous float32 [T][dim] array")
+        err = N.errbuf()
+        rc = self._lib.miag_moe(self._ctx, layer, x.ctypes.data, x.shape[0], err, len(err))
+        N.check(rc, err, "miag_moe")
+
     def moe_device(self, x_ptr: int, n_tokens: int, layer: int = 0, stream: int | None = None):
         """Enqueues the block on a device buffer x_ptr [n_tokens][dim] (in place)."""
         err = N.errbuf()
@@ -145,8 +153,31 @@ class MoEEngine:
         N.check(rc, err, "miag_routing")
         return dict(idx=idx, w=w, counts=counts, offsets=offsets, perm=perm)
 
+    def router_logits(self, n_tokens: int) -> np.ndarray:
+        """Router logits (+ bias) [T][E] of the last call."""
+        out = np.zeros((n_tokens, self.shape.n_experts), np.float32)
+        err = N.errbuf()
+        N.check(self._lib.miag_router_logits(self._ctx, out.ctypes.data, err, len(err)), err,
+                "miag_router_logits")
+        return out
+
     def last_launch_count(self) -> int:
         return int(self._lib.miag_last_launch_count(self._ctx))
+
+    def profile(self, enable: bool = True) -> None:
+        """Brackets every kernel stage of later calls with CUDA events."""
+        self._lib.miag_profile(self._ctx, int(enable))
+
+    def profile_read(self) -> dict:
+        """{stage: (milliseconds, launches)} since the last read."""
+        n = self._lib.miag_profile_stages()
+        ms = np.zeros(n, np.float64)
+        launches = np.zeros(n, np.int32)
+        err = N.errbuf()
+        N.check(self._lib.miag_profile_read(self._ctx, ms.ctypes.data, launches.ctypes.data, err,
+                                            len(err)), err, "miag_profile_read")
+        return {self._lib.miag_profile_stage_name(i).decode(): (float(ms[i]), int(launches[i]))
+                for i in range(n)}
 
 
 def quantize_row_q8(x_ptr: int, y_ptr: int, n: int, stream: int | None = None) -> None:
