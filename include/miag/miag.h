@@ -87,6 +87,23 @@ int miag_moe(miag_ctx *c, int layer, float *x, int n_tokens, char *err,
 int miag_moe_async(miag_ctx *c, int layer, float *x_dev, int n_tokens,
                    void *stream, char *err, size_t errlen);
 
+/* The MoE block with nothing allocated during the call.  No counterpart in
+ * the reference (motorIa sizes all scratch once, from its RAM budget).  For
+ * callers that cannot let a call allocate device memory: an engine that
+ * reserves every byte of HBM up front under a fixed budget, or a serving
+ * loop that cannot take cudaMalloc's implicit device-wide synchronisation in
+ * the middle of a step (miag_moe_async grows its workspace with cudaMalloc
+ * when a batch is larger than any before it).  Same kernels and results as
+ * miag_moe_async; x_dev and stream as there.  The scratch is one fixed
+ * 8 MiB array inside the loaded library, held by every GPU that loads
+ * libmiag until the process exits, which bounds a batch to about 90 tokens
+ * at Qwen3-30B-A3B shapes; larger batches return -1 with a message.  The
+ * first call on a device looks the array's address up (make it before any
+ * stream capture).  All calls share the array, so calls whose work overlaps
+ * on the GPU race on it and must be serialised by the caller. */
+int miag_moe_noalloc(miag_ctx *c, int layer, float *x_dev, int n_tokens,
+                     void *stream, char *err, size_t errlen);
+
 /* Waits for the context's work on `stream` (NULL = own stream) and reports
  * any device-side error (a bounded wait that gave up, a bad index). */
 int miag_sync(miag_ctx *c, void *stream, char *err, size_t errlen);

@@ -43,6 +43,8 @@ SIGNATURES = {
     "miag_moe": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_char_p, C.c_size_t]),
     "miag_moe_async": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p,
                                  C.c_char_p, C.c_size_t]),
+    "miag_moe_noalloc": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p,
+                                   C.c_char_p, C.c_size_t]),
     "miag_sync": (C.c_int, [C.c_void_p, C.c_void_p, C.c_char_p, C.c_size_t]),
     "miag_routing": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                C.c_void_p, C.c_char_p, C.c_size_t]),

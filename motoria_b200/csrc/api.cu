@@ -562,3 +562,20 @@ extern "C" int miag_profile_read(miag_ctx *c, double *ms, int32_t *launches, cha
     }
     return 0;
 }
+
+// Read-only view of a context's layer for other launch sequences (noalloc.cu).
+namespace miag {
+int ctx_view(const miag_ctx *c, int layer, CtxView *v) {
+    if (!c || layer < 0 || layer >= c->shape.n_layers) return -1;
+    const LayerState &Ls = c->layers[(size_t)layer];
+    if (!Ls.dense_set) return -1;
+    v->device = c->device;
+    v->num_sms = c->num_sms;
+    v->stream = c->stream;
+    v->dims = c->dims;
+    v->lay = c->lay;
+    v->layer = LayerDev{Ls.ffn_norm, Ls.router_t, Ls.has_bias ? Ls.bias : nullptr, Ls.experts};
+    v->d_err = c->d_err;
+    return 0;
+}
+}  // namespace miag

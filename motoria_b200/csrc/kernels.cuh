@@ -42,6 +42,17 @@ struct Dims {
 constexpr int kPermChunk = 1024;
 constexpr int kTokChunk = 32;  // pairs of one expert handled per expert-GEMV item
 
+// Device-side view of one layer of a context (api.cu), for launch sequences
+// that bring their own workspace.
+struct CtxView {
+    int device, num_sms;
+    cudaStream_t stream;  // the context's own stream
+    Dims dims;
+    StoreLayout lay;
+    LayerDev layer;
+    int *d_err;
+};
+
 // route.cu
 void launch_route(const Dims &m, const LayerDev &L, const float *x, const Work &w,
                   int *err, cudaStream_t s);
