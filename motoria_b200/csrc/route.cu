@@ -78,7 +78,8 @@ __host__ __device__ inline size_t route_smem(int d, int E, int R, int W) {
 }
 
 // Grid: (token groups of W*R, expert groups of 32); W consumer warps own R
-// tokens each, one producer warp streams the group's rows and router slice.
+// tokens each and loads them itself; one producer warp streams the group's
+// router slice.
 template <int R>
 __global__ void __launch_bounds__(9 * 32) k_route(RouteParams p, int W) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -86,39 +87,31 @@ __global__ void __launch_bounds__(9 * 32) k_route(RouteParams p, int W) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
     uint64_t *empty = full + kRouteStages;
-    uint64_t *xbar = empty + kRouteStages;
     float *ring = reinterpret_cast<float *>(smem + kRouteBarBytes);
     float *xs_all = ring + (size_t)kRouteStages * kRouteChunk * 32;  // [W*R][d]
     float *norm = xs_all + (size_t)W * R * d;
     const int nchunks = (d + kRouteChunk - 1) / kRouteChunk;
     const float *slice = p.L.router_t + (size_t)blockIdx.y * d * 32;
     const int tg0 = blockIdx.x * W * R;                 // first token of the CTA
-    const int ntok = min(W * R, p.T - tg0);             // tokens present
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kRouteStages; s++) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], W);
         }
-        mbar_init(xbar, 1);
         fence_barrier_init();
     }
     __syncthreads();
 
     if (warp == W) {
-        // Producer: the CTA's token rows and ffn_norm, then router chunks.
+        // Producer: the router chunks.
         if (lane == 0) {
-            const uint32_t xbytes = (uint32_t)ntok * d * 4;
-            mbar_arrive_expect_tx(xbar, xbytes + (uint32_t)d * 4);
-            bulk_g2s(xs_all, p.x + (size_t)tg0 * d, xbytes, xbar);
-            bulk_g2s(norm, p.L.ffn_norm, (uint32_t)d * 4, xbar);
             for (int ch = 0; ch < nchunks; ch++) {
                 const int s = ch % kRouteStages, round = ch / kRouteStages;
                 if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1)) {
                     set_error(p.err, kErrWaitEmpty);
                     for (int j = ch - 1; j >= 0 && j >= ch - kRouteStages; j--)
                         mbar_wait(&full[j % kRouteStages], (j / kRouteStages) & 1);
-                    mbar_wait(xbar, 0);
                     break;
                 }
                 const int rows = min(kRouteChunk, d - ch * kRouteChunk);
@@ -135,14 +128,16 @@ __global__ void __launch_bounds__(9 * 32) k_route(RouteParams p, int W) {
     const int nt = max(0, min(R, p.T - tw0));
     float *xw = xs_all + (size_t)warp * R * d;  // this warp's rows: x, then xn in place
     bool failed = false;
-    {
-        bool got = true;
-        if (lane == 0) got = mbar_wait(xbar, 0);
-        if (!__shfl_sync(0xffffffffu, got, 0)) {
-            set_error(p.err, kErrWaitFull);
-            failed = true;
-        }
-    }
+    // The warp's token rows and the shared ffn_norm come in through plain
+    // coalesced loads: with these rows bulk-copied instead, the norm and the
+    // router loop that follow measured 2-2.5x slower on B200.
+    for (int r = 0; r < nt; r++)
+        for (int i = 4 * lane; i < d; i += 128)
+            *reinterpret_cast<float4 *>(xw + (size_t)r * d + i) =
+                __ldg(reinterpret_cast<const float4 *>(p.x + (size_t)(tw0 + r) * d + i));
+    for (int i = 4 * (warp * 32 + lane); i < d; i += 128 * W)
+        *reinterpret_cast<float4 *>(norm + i) = __ldg(reinterpret_cast<const float4 *>(p.L.ffn_norm + i));
+    named_barrier_sync(1, W * 32);  // consumer warps only
 
     // 1.+2. rmsnorm (forward.c:75-81) and Q8_0 of xn (quant.c:11-27).  Lane l
     // holds elements 4l + 128k (k < d/128) of a token: eight lanes cover one
@@ -150,20 +145,24 @@ __global__ void __launch_bounds__(9 * 32) k_route(RouteParams p, int W) {
     const int nq4 = d / 128;  // float4 per lane (d is a multiple of 32; see tail)
     for (int r = 0; r < nt; r++) {
         float *xr = xw + (size_t)r * d;
-        double ss = 0.0;
+        // four independent partial sums: the certified bracket covers any order
+        double s4[4] = {0.0, 0.0, 0.0, 0.0};
         for (int k = 0; k < nq4; k++) {
             const float4 v = *reinterpret_cast<const float4 *>(xr + 4 * lane + 128 * k);
-            ss = __dadd_rn(ss, __dmul_rn((double)v.x, (double)v.x));
-            ss = __dadd_rn(ss, __dmul_rn((double)v.y, (double)v.y));
-            ss = __dadd_rn(ss, __dmul_rn((double)v.z, (double)v.z));
-            ss = __dadd_rn(ss, __dmul_rn((double)v.w, (double)v.w));
+            s4[0] = __dadd_rn(s4[0], __dmul_rn((double)v.x, (double)v.x));
+            s4[1] = __dadd_rn(s4[1], __dmul_rn((double)v.y, (double)v.y));
+            s4[2] = __dadd_rn(s4[2], __dmul_rn((double)v.z, (double)v.z));
+            s4[3] = __dadd_rn(s4[3], __dmul_rn((double)v.w, (double)v.w));
         }
         for (int i = 128 * nq4 + lane; i < d; i += 32) {  // d % 128 tail
             const double v = (double)xr[i];
-            ss = __dadd_rn(ss, __dmul_rn(v, v));
+            s4[0] = __dadd_rn(s4[0], __dmul_rn(v, v));
         }
+        const double ss = __dadd_rn(__dadd_rn(s4[0], s4[1]), __dadd_rn(s4[2], s4[3]));
         const float inv = rms_scale_certified(ss, xr, d, p.m.eps, lane);
         const int t = tw0 + r;
+        // xn in place; then Q8_0 in groups of four float4 (sixteen values
+        // per lane) so the block maxima, divisions and roundings overlap.
         for (int k = 0; k < nq4; k++) {
             const int i = 4 * lane + 128 * k;
             float4 v = *reinterpret_cast<const float4 *>(xr + i);
@@ -173,20 +172,39 @@ __global__ void __launch_bounds__(9 * 32) k_route(RouteParams p, int W) {
             v.z = __fmul_rn(__fmul_rn(v.z, inv), w.z);
             v.w = __fmul_rn(__fmul_rn(v.w, inv), w.w);
             *reinterpret_cast<float4 *>(xr + i) = v;
-            if (blockIdx.y == 0) {
-                float a = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-                a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 1));
-                a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 2));
-                a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 4));
-                const float dq = __fdiv_rn(a, 127.0f);
-                const float id = dq != 0.0f ? __fdiv_rn(1.0f, dq) : 0.0f;
-                const uint32_t q0 = (uint8_t)(int8_t)roundf(__fmul_rn(v.x, id));
-                const uint32_t q1 = (uint8_t)(int8_t)roundf(__fmul_rn(v.y, id));
-                const uint32_t q2 = (uint8_t)(int8_t)roundf(__fmul_rn(v.z, id));
-                const uint32_t q3 = (uint8_t)(int8_t)roundf(__fmul_rn(v.w, id));
-                *reinterpret_cast<uint32_t *>(p.xq + (size_t)t * d + i) =
-                    q0 | (q1 << 8) | (q2 << 16) | (q3 << 24);
-                if ((lane & 7) == 0) p.dx[(size_t)t * scale_pad(d / MIAG_QK) + i / MIAG_QK] = dq;
+        }
+        if (blockIdx.y == 0) {
+            const int xs = scale_pad(d / MIAG_QK);
+            for (int k0 = 0; k0 < nq4; k0 += 4) {
+                float4 v[4];
+                float a[4], dq[4], id[4];
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    v[u] = k0 + u < nq4 ? *reinterpret_cast<const float4 *>(xr + 4 * lane + 128 * (k0 + u))
+                                        : make_float4(0.f, 0.f, 0.f, 0.f);
+                    a[u] = fmaxf(fmaxf(fabsf(v[u].x), fabsf(v[u].y)), fmaxf(fabsf(v[u].z), fabsf(v[u].w)));
+                }
+#pragma unroll
+                for (int o = 1; o < 8; o <<= 1)
+#pragma unroll
+                    for (int u = 0; u < 4; u++) a[u] = fmaxf(a[u], __shfl_xor_sync(0xffffffffu, a[u], o));
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    dq[u] = __fdiv_rn(a[u], 127.0f);
+                    id[u] = dq[u] != 0.0f ? __fdiv_rn(1.0f, dq[u]) : 0.0f;
+                }
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    if (k0 + u >= nq4) break;
+                    const int i = 4 * lane + 128 * (k0 + u);
+                    const uint32_t q0 = (uint8_t)(int8_t)roundf(__fmul_rn(v[u].x, id[u]));
+                    const uint32_t q1 = (uint8_t)(int8_t)roundf(__fmul_rn(v[u].y, id[u]));
+                    const uint32_t q2 = (uint8_t)(int8_t)roundf(__fmul_rn(v[u].z, id[u]));
+                    const uint32_t q3 = (uint8_t)(int8_t)roundf(__fmul_rn(v[u].w, id[u]));
+                    *reinterpret_cast<uint32_t *>(p.xq + (size_t)t * d + i) =
+                        q0 | (q1 << 8) | (q2 << 16) | (q3 << 24);
+                    if ((lane & 7) == 0) p.dx[(size_t)t * xs + i / MIAG_QK] = dq[u];
+                }
             }
         }
         for (int i = 128 * nq4 + lane; i < d; i += 32) {  // tail (d % 128 == 32, 64, 96)
