@@ -279,12 +279,12 @@ __global__ void __launch_bounds__(9 * 32) k_route(RouteParams p, int W) {
 
 }
 
-// Tokens per warp R and consumer warps W by batch size.
+// Tokens per warp R and consumer warps W by batch size (a sweep on B200 over
+// T = 1..2048: one token per warp while there are few tokens, so more CTAs
+// share the serial sums; two tokens and eight warps beyond).
 static void route_shape(int T, int &R, int &W) {
-    if (T <= 1) R = 1, W = 1;
-    else if (T <= 256) R = 2, W = 4;
-    else if (T <= 1024) R = 4, W = 4;
-    else R = 8, W = 2;
+    if (T <= 128) R = 1, W = 4;
+    else R = 2, W = 8;
 }
 
 void launch_route(const Dims &m, const LayerDev &L, const float *x, const Work &w, int *err,
@@ -302,17 +302,9 @@ void launch_route(const Dims &m, const LayerDev &L, const float *x, const Work &
             cudaFuncSetAttribute(k_route<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
             k_route<1><<<grid, threads, smem, s>>>(p, W);
             break;
-        case 2:
+        default:
             cudaFuncSetAttribute(k_route<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
             k_route<2><<<grid, threads, smem, s>>>(p, W);
-            break;
-        case 4:
-            cudaFuncSetAttribute(k_route<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            k_route<4><<<grid, threads, smem, s>>>(p, W);
-            break;
-        default:
-            cudaFuncSetAttribute(k_route<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            k_route<8><<<grid, threads, smem, s>>>(p, W);
             break;
     }
 }
