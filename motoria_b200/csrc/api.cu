@@ -183,12 +183,15 @@ extern "C" int miag_open(miag_ctx **out, const miag_shape *shape, int device, ch
     if ((e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking)) != cudaSuccess)
         return fail("cudaStreamCreate", e);
     if ((e = cudaMalloc(&c->d_err, sizeof(int))) != cudaSuccess) return fail("cudaMalloc(err)", e);
-    if ((e = cudaMemset(c->d_err, 0, sizeof(int))) != cudaSuccess) return fail("cudaMemset", e);
+    // Zero-fills go on the context stream: it is non-blocking, so a plain
+    // cudaMemset (legacy default stream) would not be ordered with its kernels.
+    if ((e = cudaMemsetAsync(c->d_err, 0, sizeof(int), c->stream)) != cudaSuccess)
+        return fail("cudaMemset", e);
     const size_t E = (size_t)shape->n_experts, d = (size_t)shape->dim;
     for (auto &L : c->layers) {
         if ((e = cudaMalloc(&L.experts, E * c->lay.expert_bytes)) != cudaSuccess)
             return fail("cudaMalloc(expert store)", e);
-        if ((e = cudaMemset(L.experts, 0, E * c->lay.expert_bytes)) != cudaSuccess)
+        if ((e = cudaMemsetAsync(L.experts, 0, E * c->lay.expert_bytes, c->stream)) != cudaSuccess)
             return fail("cudaMemset(expert store)", e);
         if ((e = cudaMalloc(&L.ffn_norm, d * 4)) != cudaSuccess) return fail("cudaMalloc", e);
         const size_t Eg = (E + 31) / 32 * 32;  // router stored in 32-expert groups
@@ -200,6 +203,7 @@ extern "C" int miag_open(miag_ctx **out, const miag_shape *shape, int device, ch
         miag_close(c);
         return -1;
     }
+    if ((e = cudaStreamSynchronize(c->stream)) != cudaSuccess) return fail("zero-fill", e);
     *out = c;
     return 0;
 }
@@ -402,7 +406,10 @@ static int ensure_ws(miag_ctx *c, int T, char *err, size_t errlen) {
         cudaFree(c->ws_mem);
         c->ws_mem = nullptr, c->ws_cap = 0;
         CU(cudaMalloc(&c->ws_mem, bytes));
-        CU(cudaMemset(c->ws_mem, 0, bytes));
+        // on the context stream, finished before any stream (the caller's
+        // included) can use the buffers
+        CU(cudaMemsetAsync(c->ws_mem, 0, bytes, c->stream));
+        CU(cudaStreamSynchronize(c->stream));
         c->ws_bytes = bytes;
         c->ws_cap = cap;
     }
@@ -456,7 +463,8 @@ static int read_device_error(miag_ctx *c, char *err, size_t errlen) {
     int code = 0;
     CU(cudaMemcpy(&code, c->d_err, sizeof(int), cudaMemcpyDeviceToHost));
     if (code == 0) return 0;
-    CU(cudaMemset(c->d_err, 0, sizeof(int)));
+    CU(cudaMemsetAsync(c->d_err, 0, sizeof(int), c->stream));
+    CU(cudaStreamSynchronize(c->stream));
     const char *what = code == kErrWaitFull    ? "a consumer timed out waiting for a staged tile"
                        : code == kErrWaitEmpty ? "the producer timed out waiting for a free stage"
                        : code == kErrBadExpert ? "a routing index was out of range"

@@ -9,9 +9,10 @@
 // group of up to 32 of that expert's (token, slot) pairs.  An item is
 // (active expert, 128-row tile, chunk of 32 pairs); persistent CTAs (one per
 // SM) own contiguous item ranges, so consecutive items share their
-// activations, which are staged in shared memory once.  A producer thread
-// streams each item's K range, two 16 KiB swizzled tiles (+ their scale
-// tiles) per stage, with 1-D TMA bulk copies into a ring of stages.
+// activations, which are staged in shared memory once.  Each item's K range
+// streams through a ring of stages in shared memory, one 1-D TMA bulk copy
+// of two tile units (16 KiB swizzled int8 tile + its 2 KiB of scales, each)
+// per stage; the warp that releases a stage last issues its refill.
 //
 // Eight consumer warps each own 16 rows of the tile.  Per Q8_0 block (K =
 // 32) a warp issues one int8 tensor-core MMA, m16n8k32 (16 rows x 8 pairs),
@@ -31,13 +32,13 @@ namespace miag {
 
 constexpr int kConsumerWarps = 8;
 constexpr int kConsumers = kConsumerWarps * 32;
-constexpr int kGemvThreads = kConsumers + 32;
+constexpr int kGemvThreads = kConsumers;  // no producer warp: see run_item
+constexpr int kItemTable = 512;           // decoded items cached per CTA
 constexpr int kStageKT = 2;  // k tiles per stage
-constexpr int kStageBytes = kStageKT * (kTileBytes + kTileScaleBytes);
+constexpr int kStageBytes = kStageKT * kUnitBytes;  // one bulk copy
 constexpr int kMaxStages = 8;
 constexpr int kBarBytes = 1024;  // keeps every stage 1024-B aligned
 constexpr int kSmemBudget = 227 * 1024;
-constexpr int kMaxNT = kTokChunk / 8;  // n-tiles of 8 pairs per item
 constexpr uint32_t kFull = 0xffffffffu;
 
 struct GemvParams {
@@ -51,12 +52,11 @@ struct GemvParams {
     float *y;          // [P][d]
     int stages;
     uint32_t x_off, x_stride;  // activation region offset in smem, its row stride
+    uint32_t table_off;        // decoded-item table offset in smem
     int *err;
 };
 
-__device__ __forceinline__ void consumer_sync() {
-    asm volatile("bar.sync 1, %0;" ::"n"(kConsumers) : "memory");
-}
+__device__ __forceinline__ void consumer_sync() { __syncthreads(); }
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2,
                                         uint32_t &r3) {
@@ -71,14 +71,29 @@ __device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t &r0, uint32_t &r
                  : "r"(addr));
 }
 
-// D = A(16x32 s8, row) * B(32x8 s8, col), int32, exact.
+// The int8 MMA accumulates onto kMagicBits, the bit pattern of 1.5 * 2^23.
+// A Q8_0 block dot satisfies |dot| <= 32 * 127 * 127 < 2^22, so the int32
+// result, read as a float, is exactly 12582912 + dot (same binade, unit ulp)
+// and one exact subtraction gives (float)dot.  The conversion so runs on the
+// FMA pipe; as an int-to-float conversion it saturated the conversion unit.
+constexpr int kMagicBits = 0x4B400000;
+constexpr float kMagic = 12582912.0f;
+
+// D = A(16x32 s8, row) * B(32x8 s8, col) + kMagicBits, int32, exact.
 __device__ __forceinline__ void mma_s8(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                        uint32_t a3, uint32_t b0, uint32_t b1) {
     asm volatile(
         "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
         "{%8, %9}, {%10, %10, %10, %10};"
         : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(kMagicBits));
+}
+
+// The reference step s += ((float)dot * dw) * dx (matmul.c:25) on a magic
+// accumulator m = kMagicBits + dot.
+__device__ __forceinline__ float q8_step_magic(float s, int m, float dw, float dx) {
+    const float dot = __fsub_rn(__int_as_float(m), kMagic);
+    return __fadd_rn(s, __fmul_rn(__fmul_rn(dot, dw), dx));
 }
 
 // Item i -> index a of its active expert: largest a with chunk_pre[a]*RT <= i.
@@ -104,6 +119,49 @@ __device__ __forceinline__ ItemInfo decode_item(const GemvParams &p, int nact, i
     it.tc = local / RT;
     it.rt = local % RT;
     return it;
+}
+
+// The head of the CTA's shared memory: the ring's barriers and counters, and
+// what a refill needs to know about the CTA's item range.
+struct RingHead {
+    uint64_t full[kMaxStages];      // stage holds its k tiles (TMA complete_tx)
+    uint32_t released[kMaxStages];  // warps done with the stage, summed over rounds
+    int first, total, nact;         // first item, stages to stream, active experts
+};
+static_assert(sizeof(RingHead) <= kBarBytes, "ring head");
+
+// Item `item` of this CTA, from the shared table when it holds it.
+__device__ __forceinline__ ItemInfo item_at(const GemvParams &p, const int2 *table, int first,
+                                            int nact, int RT, int item) {
+    const int k = item - first;
+    if (k < kItemTable) {
+        const int2 v = table[k];
+        ItemInfo ii;
+        ii.e = v.x, ii.rt = v.y & 255, ii.tc = v.y >> 8;
+        return ii;
+    }
+    return decode_item(p, nact, RT, item);
+}
+
+// Issues the bulk copies of ring iteration j (item first + j / NS, k stage
+// j % NS) into its stage s = j % S, completing on full[s].
+template <bool kGU>
+__device__ void issue_iteration(const GemvParams &p, uint8_t *smem, int j) {
+    RingHead *h = reinterpret_cast<RingHead *>(smem);
+    const int RT = kGU ? p.lay.gu_rt : p.lay.dn_rt;
+    const int KT = kGU ? p.lay.gu_kt : p.lay.dn_kt;
+    const int NS = (KT + kStageKT - 1) / kStageKT;
+    const int s = j % p.stages, ks = j % NS;
+    const ItemInfo ii = item_at(p, reinterpret_cast<const int2 *>(smem + p.table_off), h->first,
+                                h->nact, RT, h->first + j / NS);
+    const uint8_t *base = p.experts + (size_t)ii.e * p.lay.expert_bytes;
+    const int kt0 = ks * kStageKT, nkt = min(kStageKT, KT - kt0);
+    const size_t unit = (size_t)ii.rt * KT + kt0;
+    uint8_t *dst = smem + kBarBytes + (size_t)s * kStageBytes;
+    uint64_t *bar = &h->full[s];
+    mbar_arrive_expect_tx(bar, (uint32_t)nkt * kUnitBytes);
+    bulk_g2s(dst, base + (kGU ? p.lay.gu_off : p.lay.dn_off) + unit * kUnitBytes,
+             (uint32_t)nkt * kUnitBytes, bar);
 }
 
 // Consumers: stage the activations of pairs [t0, t0+n) of the expert segment
@@ -164,6 +222,197 @@ __device__ void fill_region(const GemvParams &p, uint8_t *region, int seg0, int 
     }
 }
 
+__device__ __forceinline__ float4 lds128(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(addr));
+    return v;
+}
+
+// Per-lane roles in the warp's 16-row slice of a tile, as shared-memory
+// byte offsets fixed for the whole kernel.
+struct Lanes {
+    int g, tq;              // mma groupID, thread-in-group
+    int r0;                 // first of this lane's two rows (r0, r0 + 8) in the tile
+    uint32_t w0, w1;        // offsets of rows r0, r0 + 8 in a scale tile
+    uint32_t b_off;         // ldmatrix B role: pair row lane & 7, 16-byte half
+    int b_pair;
+    uint32_t a_off[4];      // ldmatrix A role: swizzled offset of block j in a tile
+};
+
+__device__ __forceinline__ Lanes lane_roles(int warp, int lane) {
+    Lanes l;
+    l.g = lane >> 2, l.tq = lane & 3;
+    l.r0 = 16 * warp + l.g;
+    l.w0 = 16u * (uint32_t)l.r0, l.w1 = 16u * (uint32_t)(l.r0 + 8);
+    // A (x4): lanes 0-7 rows 0-7, 8-15 rows 8-15, 16-31 the same rows' second
+    // 16-byte half.  B (x2): lanes 0-7 pairs 0-7, 8-15 their second half.
+    const int a_row = 16 * warp + (lane & 7) + ((lane >> 3) & 1) * 8, a_half = lane >> 4;
+#pragma unroll
+    for (int j = 0; j < 4; j++) l.a_off[j] = tile_chunk_offset(a_row, 2 * j + a_half);
+    l.b_pair = lane & 7;
+    l.b_off = 16u * (uint32_t)((lane >> 3) & 1);
+    return l;
+}
+
+// One k tile (4 Q8_0 blocks; kFull = all four inside K) for NT n-tiles of
+// 8 pairs.  tile/sc: the k tile's int8 and scale tiles in the stage.
+template <int NT, bool kFull>
+__device__ __forceinline__ void k_tile(float (&acc)[NT][4], uint32_t tile, uint32_t sc, int kt,
+                                       int nbk, const Lanes &ln, const uint32_t (&b_row)[NT],
+                                       const uint32_t (&xa)[NT], const uint32_t (&xb)[NT]) {
+    uint32_t A[4][4];
+#pragma unroll
+    for (int j = 0; j < 4; j++)
+        if (kFull || j < nbk) ldsm_x4(tile + ln.a_off[j], A[j][0], A[j][1], A[j][2], A[j][3]);
+    const float4 w0 = lds128(sc + ln.w0), w1 = lds128(sc + ln.w1);
+    const float wa[4] = {w0.x, w0.y, w0.z, w0.w}, wb[4] = {w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+    for (int n = 0; n < NT; n++) {
+        const uint32_t brow = b_row[n] + (uint32_t)(kt * kTileK);
+        uint32_t B[4][2];
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+            if (kFull || j < nbk) ldsm_x2(brow + 32 * j, B[j][0], B[j][1]);
+        const float4 u = lds128(xa[n] + 16u * (uint32_t)kt), v = lds128(xb[n] + 16u * (uint32_t)kt);
+        const float sa[4] = {u.x, u.y, u.z, u.w}, sb[4] = {v.x, v.y, v.z, v.w};
+        int C[4][4];
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+            if (kFull || j < nbk) mma_s8(C[j], A[j][0], A[j][1], A[j][2], A[j][3], B[j][0], B[j][1]);
+        // block order, as the reference's loop over blocks
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            if (kFull || j < nbk) {
+                acc[n][0] = q8_step_magic(acc[n][0], C[j][0], wa[j], sa[j]);
+                acc[n][1] = q8_step_magic(acc[n][1], C[j][1], wa[j], sb[j]);
+                acc[n][2] = q8_step_magic(acc[n][2], C[j][2], wb[j], sa[j]);
+                acc[n][3] = q8_step_magic(acc[n][3], C[j][3], wb[j], sb[j]);
+            }
+        }
+    }
+}
+
+// What one item needs besides the kernel parameters.
+struct ItemCtx {
+    uint32_t stages;         // shared address of stage 0
+    uint32_t x_rows, x_scl;  // shared addresses of the activation rows / scale rows
+    uint32_t xsp_bytes;      // scale row stride (bytes)
+    int S, KT, NS, nb, rows;
+    int rt, seg0, t0, nq;    // the item: row tile, expert segment, first pair, pairs
+};
+
+// One item: its k tiles through the ring, then its outputs.
+//
+// There is no producer warp.  Thread 0 issues the first S stages; after
+// that, the warp that is the last of the eight to finish with a stage
+// refills it with the iteration S ahead.  With eight warps per CTA the
+// register file allows 255 registers a thread (a ninth warp capped it at
+// 168, which the tile shapes exceed).
+template <bool kGU, int NT>
+__device__ __forceinline__ void run_item(const GemvParams &p, const ItemCtx &ic, const Lanes &ln,
+                                         uint8_t *smem, int &it, bool &failed) {
+    RingHead *head = reinterpret_cast<RingHead *>(smem);
+    const int lane = threadIdx.x & 31;
+    const int nq = ic.nq;
+    // per n-tile: this lane's B row (pairs past nq repeat the last pair; their
+    // columns are never written out) and the scale rows of its two columns
+    uint32_t b_row[NT], xa[NT], xb[NT];
+#pragma unroll
+    for (int n = 0; n < NT; n++) {
+        b_row[n] = ic.x_rows + (uint32_t)min(8 * n + ln.b_pair, nq - 1) * p.x_stride + ln.b_off;
+        xa[n] = ic.x_scl + (uint32_t)min(8 * n + 2 * ln.tq, nq - 1) * ic.xsp_bytes;
+        xb[n] = ic.x_scl + (uint32_t)min(8 * n + 2 * ln.tq + 1, nq - 1) * ic.xsp_bytes;
+    }
+    float acc[NT][4];
+#pragma unroll
+    for (int n = 0; n < NT; n++)
+#pragma unroll
+        for (int i = 0; i < 4; i++) acc[n][i] = 0.0f;
+
+    const bool full_tiles = (ic.KT % kStageKT) == 0 && 4 * ic.KT == ic.nb;
+    for (int ks = 0; ks < ic.NS; ks++, it++) {
+        const int s = it % ic.S, round = it / ic.S;
+        if (!failed) {
+            bool got = true;
+            if (lane == 0) got = mbar_wait(&head->full[s], round & 1);
+            if (!__shfl_sync(kFull, got, 0)) {
+                // Keep walking (on stale data) so every consumer reaches the
+                // same named barriers: no warp may leave early.
+                set_error(p.err, kErrWaitFull);
+                failed = true;
+            }
+        }
+        const uint32_t stg = ic.stages + (uint32_t)(s * kStageBytes);
+        const uint32_t scl = stg + kTileBytes;  // unit kk: tile at kk units, its scales after it
+        const int kt0 = ks * kStageKT;
+        if (full_tiles) {
+            // both k tiles in straight-line code while the registers allow
+#pragma unroll (NT == 1 ? kStageKT : 1)
+            for (int kk = 0; kk < kStageKT; kk++)
+                k_tile<NT, true>(acc, stg + kk * kUnitBytes, scl + kk * kUnitBytes, kt0 + kk, 4,
+                                 ln, b_row, xa, xb);
+        } else {
+            const int nkt = min(kStageKT, ic.KT - kt0);
+            for (int kk = 0; kk < nkt; kk++)
+                k_tile<NT, false>(acc, stg + kk * kUnitBytes, scl + kk * kUnitBytes, kt0 + kk,
+                                  min(4, ic.nb - 4 * (kt0 + kk)), ln, b_row, xa, xb);
+        }
+        __syncwarp();
+        if (lane == 0) {
+            // release the stage; the eighth release of a round refills it
+            __threadfence_block();
+            const uint32_t done = atomicAdd(&head->released[s], 1u);
+            if ((done % kConsumerWarps) == kConsumerWarps - 1 && it + ic.S < head->total) {
+                __threadfence_block();
+                fence_proxy_async_smem();
+                issue_iteration<kGU>(p, smem, it + ic.S);
+            }
+        }
+    }
+
+    // outputs: this lane holds rows r0, r0 + 8 x pairs 8n + 2tq, 8n + 2tq + 1
+    const int R0 = ic.rt * kTileRows + ln.r0, R1 = R0 + 8;
+    const int rows = ic.rows;
+#pragma unroll
+    for (int n = 0; n < NT; n++) {
+        const int qa = 8 * n + 2 * ln.tq, qb = qa + 1;
+        if (kGU) {
+            // rows are interleaved gate (even) / up (odd): the up partner of
+            // row r sits in the lane with groupID g ^ 1, i.e. lane ^ 4.
+            float up[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) up[i] = __shfl_xor_sync(kFull, acc[n][i], 4);
+            if ((ln.g & 1) == 0) {
+                const int eh = p.m.eh, i0 = R0 >> 1, i1 = R1 >> 1;
+                if (qa < nq) {
+                    float *hp = p.h + (size_t)(ic.seg0 + ic.t0 + qa) * eh;
+                    if (R0 < rows) hp[i0] = swiglu_ref(acc[n][0], up[0]);
+                    if (R1 < rows) hp[i1] = swiglu_ref(acc[n][2], up[2]);
+                }
+                if (qb < nq) {
+                    float *hp = p.h + (size_t)(ic.seg0 + ic.t0 + qb) * eh;
+                    if (R0 < rows) hp[i0] = swiglu_ref(acc[n][1], up[1]);
+                    if (R1 < rows) hp[i1] = swiglu_ref(acc[n][3], up[3]);
+                }
+            }
+        } else {
+            const int d = p.m.d;
+            if (qa < nq) {
+                float *yp = p.y + (size_t)(ic.seg0 + ic.t0 + qa) * d;
+                if (R0 < rows) yp[R0] = acc[n][0];
+                if (R1 < rows) yp[R1] = acc[n][2];
+            }
+            if (qb < nq) {
+                float *yp = p.y + (size_t)(ic.seg0 + ic.t0 + qb) * d;
+                if (R0 < rows) yp[R0] = acc[n][1];
+                if (R1 < rows) yp[R1] = acc[n][3];
+            }
+        }
+    }
+}
+
 // gate+up (kGU) or down: one launch over all items of all active experts.
 template <bool kGU>
 __global__ void __launch_bounds__(kGemvThreads, 1) k_expert_mma(GemvParams p) {
@@ -175,207 +424,72 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_expert_mma(GemvParams p) {
     const int rows = kGU ? 2 * eh : d;       // matrix rows
     const int nb = Kb / MIAG_QK, xs = scale_pad(nb);
     const int xsp = (int)smem_stride((uint32_t)xs * 4) / 4;  // padded scale row in smem
-    const uint32_t q_off = kGU ? p.lay.gu_q_off : p.lay.dn_q_off;
-    const uint32_t s_off = kGU ? p.lay.gu_s_off : p.lay.dn_s_off;
     const int NS = (KT + kStageKT - 1) / kStageKT;  // stages per item
     const int nact = __ldg(p.n_active);
     const int n_items = __ldg(p.chunk_pre + nact) * RT;
     const int first = (int)((long)n_items * blockIdx.x / gridDim.x);
     const int last = (int)((long)n_items * (blockIdx.x + 1) / gridDim.x);
 
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem);
-    uint64_t *empty = full + kMaxStages;
+    RingHead *head = reinterpret_cast<RingHead *>(smem);
     uint8_t *stages = smem + kBarBytes;
+    int2 *table = reinterpret_cast<int2 *>(smem + p.table_off);
     const int S = p.stages;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n_mine = last - first;
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; s++) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kConsumerWarps);
+            mbar_init(&head->full[s], 1);
+            head->released[s] = 0;
         }
+        head->first = first, head->total = n_mine * NS, head->nact = nact;
         fence_barrier_init();
     }
-    __syncthreads();
-
-    if (warp == kConsumerWarps) {
-        // ---- producer: stream each item's k tiles, kStageKT per stage.
-        if (lane != 0) return;
-        int it = 0;
-        bool ok = true;
-        for (int item = first; item < last && ok; item++) {
-            const ItemInfo ii = decode_item(p, nact, RT, item);
-            const uint8_t *base = p.experts + (size_t)ii.e * p.lay.expert_bytes;
-            for (int ks = 0; ks < NS; ks++, it++) {
-                const int s = it % S, round = it / S;
-                if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1)) {
-                    set_error(p.err, kErrWaitEmpty);
-                    ok = false;
-                    break;
-                }
-                const int kt0 = ks * kStageKT, nkt = min(kStageKT, KT - kt0);
-                const size_t tile = (size_t)ii.rt * KT + kt0;
-                uint8_t *dst = stages + (size_t)s * kStageBytes;
-                mbar_arrive_expect_tx(&full[s], (uint32_t)nkt * (kTileBytes + kTileScaleBytes));
-                bulk_g2s(dst, base + q_off + tile * kTileBytes, (uint32_t)nkt * kTileBytes, &full[s]);
-                bulk_g2s(dst + kStageKT * kTileBytes, base + s_off + tile * kTileScaleBytes,
-                         (uint32_t)nkt * kTileScaleBytes, &full[s]);
-            }
-        }
-        if (!ok) {
-            // Let issued copies land before the CTA's shared memory goes away.
-            for (int j = it - 1; j >= 0 && j >= it - S; j--) mbar_wait(&full[j % S], (j / S) & 1);
-        }
-        return;
+    for (int k = threadIdx.x; k < min(n_mine, kItemTable); k += kGemvThreads) {
+        const ItemInfo ii = decode_item(p, nact, RT, first + k);
+        table[k] = make_int2(ii.e, ii.rt | (ii.tc << 8));
     }
+    __syncthreads();
+    if (threadIdx.x == 0)
+        for (int j = 0; j < min(S, n_mine * NS); j++) issue_iteration<kGU>(p, smem, j);
 
     // ---- consumers
     uint8_t *region = smem + p.x_off;
-    const float *rsc = reinterpret_cast<const float *>(region + (size_t)kTokChunk * p.x_stride);
-    const int g = lane >> 2, tq = lane & 3;           // mma groupID, thread-in-group
-    const int r0 = 16 * warp + g, r1 = r0 + 8;        // this lane's two rows in the tile
-    // ldmatrix roles: A (x4): lanes 0-7 rows 0-7, 8-15 rows 8-15, 16-31 the same
-    // rows' second 16-byte half.  B (x2): lanes 0-7 pairs 0-7, 8-15 second half.
-    const int a_row = 16 * warp + (lane & 7) + ((lane >> 3) & 1) * 8, a_half = lane >> 4;
-    const int b_pair = lane & 7, b_half = (lane >> 3) & 1;
-    const uint32_t region_addr = smem_addr(region);
+    const Lanes ln = lane_roles(warp, lane);
+    ItemCtx ic;
+    ic.stages = smem_addr(stages);
+    ic.x_rows = smem_addr(region);
+    ic.x_scl = ic.x_rows + (uint32_t)kTokChunk * p.x_stride;
+    ic.xsp_bytes = 4u * (uint32_t)xsp;
+    ic.S = S, ic.KT = KT, ic.NS = NS, ic.nb = nb, ic.rows = rows;
 
     int cur_e = -1, cur_tc = -1;
     int it = 0;
     bool failed = false;
     for (int item = first; item < last; item++) {
-        const ItemInfo ii = decode_item(p, nact, RT, item);
+        const ItemInfo ii = item_at(p, table, first, nact, RT, item);
         const int seg0 = __ldg(p.offsets + ii.e);
         const int n_e = __ldg(p.offsets + ii.e + 1) - seg0;
         const int t0 = ii.tc * kTokChunk, nq = min(kTokChunk, n_e - t0);
-        const int NT = (nq + 7) >> 3;
         if (ii.e != cur_e || ii.tc != cur_tc) {
             consumer_sync();  // nobody still reads the region
             fill_region<kGU>(p, region, seg0, t0, nq, Kb, xs);
             cur_e = ii.e, cur_tc = ii.tc;
             consumer_sync();
         }
-        float acc[kMaxNT][4];
-#pragma unroll
-        for (int n = 0; n < kMaxNT; n++)
-#pragma unroll
-            for (int i = 0; i < 4; i++) acc[n][i] = 0.0f;
-        // B row address of this lane's ldmatrix role, per n-tile (pairs past
-        // nq repeat the last pair; their columns are never written out)
-        uint32_t b_addr[kMaxNT];
-#pragma unroll
-        for (int n = 0; n < kMaxNT; n++)
-            b_addr[n] = region_addr + (uint32_t)min(8 * n + b_pair, nq - 1) * p.x_stride + 16 * b_half;
-
-        for (int ks = 0; ks < NS; ks++, it++) {
-            const int s = it % S, round = it / S;
-            if (!failed) {
-                bool got = true;
-                if (lane == 0) got = mbar_wait(&full[s], round & 1);
-                if (!__shfl_sync(kFull, got, 0)) {
-                    // Keep walking (on stale data) so every consumer reaches the
-                    // same named barriers: no warp may leave early.
-                    set_error(p.err, kErrWaitFull);
-                    failed = true;
-                }
-            }
-            const uint8_t *stg = stages + (size_t)s * kStageBytes;
-            const uint32_t stg_addr = smem_addr(stg);
-            const int kt0 = ks * kStageKT, nkt = min(kStageKT, KT - kt0);
-            for (int kk = 0; kk < nkt; kk++) {
-                const int kt = kt0 + kk;
-                const float *sc = reinterpret_cast<const float *>(stg + kStageKT * kTileBytes +
-                                                                  kk * kTileScaleBytes);
-                const float4 w0 = *reinterpret_cast<const float4 *>(sc + 4 * r0);
-                const float4 w1 = *reinterpret_cast<const float4 *>(sc + 4 * r1);
-                const float wa[4] = {w0.x, w0.y, w0.z, w0.w}, wb[4] = {w1.x, w1.y, w1.z, w1.w};
-                float xa[kMaxNT][4], xb[kMaxNT][4];  // scales of pairs 2tq, 2tq+1 of each n-tile
-#pragma unroll
-                for (int n = 0; n < kMaxNT; n++) {
-                    if (n < NT) {
-                        const int qa = min(8 * n + 2 * tq, nq - 1), qb = min(8 * n + 2 * tq + 1, nq - 1);
-                        const float4 u = *reinterpret_cast<const float4 *>(rsc + (size_t)qa * xsp + 4 * kt);
-                        const float4 v = *reinterpret_cast<const float4 *>(rsc + (size_t)qb * xsp + 4 * kt);
-                        xa[n][0] = u.x, xa[n][1] = u.y, xa[n][2] = u.z, xa[n][3] = u.w;
-                        xb[n][0] = v.x, xb[n][1] = v.y, xb[n][2] = v.z, xb[n][3] = v.w;
-                    }
-                }
-                const uint32_t tile_addr = stg_addr + kk * kTileBytes;
-                const int nbk = min(4, nb - 4 * kt);  // blocks of this k tile inside K
-                // Issue all operand loads and MMAs of the k tile first, so their
-                // latencies overlap; then apply the float steps in block order.
-                uint32_t A[4][4];
-#pragma unroll
-                for (int j = 0; j < 4; j++)
-                    if (j < nbk)
-                        ldsm_x4(tile_addr + tile_chunk_offset(a_row, 2 * j + a_half), A[j][0], A[j][1],
-                                A[j][2], A[j][3]);
-#pragma unroll
-                for (int n = 0; n < kMaxNT; n++) {
-                    if (n < NT) {
-                        uint32_t B[4][2];
-                        int C[4][4];
-#pragma unroll
-                        for (int j = 0; j < 4; j++)
-                            if (j < nbk)
-                                ldsm_x2(b_addr[n] + (uint32_t)(kt * kTileK + 32 * j), B[j][0], B[j][1]);
-#pragma unroll
-                        for (int j = 0; j < 4; j++)
-                            if (j < nbk)
-                                mma_s8(C[j], A[j][0], A[j][1], A[j][2], A[j][3], B[j][0], B[j][1]);
-#pragma unroll
-                        for (int j = 0; j < 4; j++) {
-                            if (j < nbk) {
-                                acc[n][0] = q8_step(acc[n][0], C[j][0], wa[j], xa[n][j]);
-                                acc[n][1] = q8_step(acc[n][1], C[j][1], wa[j], xb[n][j]);
-                                acc[n][2] = q8_step(acc[n][2], C[j][2], wb[j], xa[n][j]);
-                                acc[n][3] = q8_step(acc[n][3], C[j][3], wb[j], xb[n][j]);
-                            }
-                        }
-                    }
-                }
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[s]);
+        ic.rt = ii.rt, ic.seg0 = seg0, ic.t0 = t0, ic.nq = nq;
+        switch ((nq + 7) >> 3) {
+            case 1: run_item<kGU, 1>(p, ic, ln, smem, it, failed); break;
+            case 2: run_item<kGU, 2>(p, ic, ln, smem, it, failed); break;
+            case 3: run_item<kGU, 3>(p, ic, ln, smem, it, failed); break;
+            default: run_item<kGU, 4>(p, ic, ln, smem, it, failed); break;
         }
-
-        // outputs: this lane holds rows r0, r1 x pairs 8n + 2tq, 8n + 2tq + 1
-        const int R0 = ii.rt * kTileRows + r0, R1 = R0 + 8;
-#pragma unroll
-        for (int n = 0; n < kMaxNT; n++) {
-            if (n >= NT) break;
-            const int qa = 8 * n + 2 * tq, qb = qa + 1;
-            if (kGU) {
-                // rows are interleaved gate (even) / up (odd): the up partner of
-                // row r sits in the lane with groupID g ^ 1, i.e. lane ^ 4.
-                float up[4];
-#pragma unroll
-                for (int i = 0; i < 4; i++) up[i] = __shfl_xor_sync(kFull, acc[n][i], 4);
-                if ((g & 1) == 0) {
-                    const int i0 = R0 >> 1, i1 = R1 >> 1;
-                    if (qa < nq) {
-                        float *hp = p.h + (size_t)(seg0 + t0 + qa) * eh;
-                        if (R0 < rows) hp[i0] = swiglu_ref(acc[n][0], up[0]);
-                        if (R1 < rows) hp[i1] = swiglu_ref(acc[n][2], up[2]);
-                    }
-                    if (qb < nq) {
-                        float *hp = p.h + (size_t)(seg0 + t0 + qb) * eh;
-                        if (R0 < rows) hp[i0] = swiglu_ref(acc[n][1], up[1]);
-                        if (R1 < rows) hp[i1] = swiglu_ref(acc[n][3], up[3]);
-                    }
-                }
-            } else {
-                if (qa < nq) {
-                    float *yp = p.y + (size_t)(seg0 + t0 + qa) * d;
-                    if (R0 < rows) yp[R0] = acc[n][0];
-                    if (R1 < rows) yp[R1] = acc[n][2];
-                }
-                if (qb < nq) {
-                    float *yp = p.y + (size_t)(seg0 + t0 + qb) * d;
-                    if (R0 < rows) yp[R0] = acc[n][1];
-                    if (R1 < rows) yp[R1] = acc[n][3];
-                }
-            }
-        }
+    }
+    // After a timed-out wait, let every issued copy land (bounded) before the
+    // CTA's shared memory goes away.  All refills are issued by now.
+    if (__syncthreads_or(failed) && threadIdx.x == 0) {
+        const int total = n_mine * NS;
+        for (int j = total - 1; j >= 0 && j >= total - S; j--)
+            mbar_wait(&head->full[j % S], (j / S) & 1);
     }
 }
 
@@ -411,11 +525,13 @@ static size_t geometry(GemvParams &p, bool gu) {
     p.x_stride = smem_stride((uint32_t)Kb);
     const size_t region =
         round_up_sz((size_t)kTokChunk * (p.x_stride + smem_stride((uint32_t)xs * 4)), 128);
-    const long room = (long)kSmemBudget - kBarBytes - (long)region;
+    const size_t table = (size_t)kItemTable * sizeof(int2);
+    const long room = (long)kSmemBudget - kBarBytes - (long)region - (long)table;
     const int st = room > 0 ? (int)(room / kStageBytes) : 0;
     p.stages = st > kMaxStages ? kMaxStages : st;
     p.x_off = (uint32_t)(kBarBytes + (size_t)p.stages * kStageBytes);
-    return p.x_off + region;
+    p.table_off = (uint32_t)(p.x_off + region);
+    return p.table_off + table;
 }
 
 // The dynamic shared-memory limit is an attribute of the kernel, shared by
@@ -424,6 +540,7 @@ static size_t geometry(GemvParams &p, bool gu) {
 int gemv_setup_attributes(const Dims &m, const StoreLayout &lay) {
     GemvParams p{};
     p.m = m, p.lay = lay;
+    if (lay.gu_rt > 255 || lay.dn_rt > 255) return -1;  // the item table packs rt in 8 bits
     if (geometry(p, true) > (size_t)kSmemBudget || p.stages < 2) return -1;
     if (geometry(p, false) > (size_t)kSmemBudget || p.stages < 2) return -1;
     if (cudaFuncSetAttribute(k_expert_mma<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,

@@ -4,7 +4,7 @@
 // (src/storage/expert_cache.c:59-85): blobs arrive in .mia layout (gate | up
 // | down, each a row-major matrix of 36-byte {f32 d; int8 q[32]} blocks,
 // src/storage/mia_file.c:275-278) and are repacked on the device into the
-// swizzled 128 x 128 B tiles of StoreLayout (common.cuh).  Values are
+// swizzled 128 x 128 B tile units of StoreLayout (common.cuh).  Values are
 // copied, never re-quantized, so the stored weights are the reference's bit
 // for bit.
 #include "kernels.cuh"
@@ -20,31 +20,27 @@ __global__ void k_repack(const uint8_t *aos, size_t aos_stride, size_t off_up, s
     const uint8_t *blob = aos + (size_t)ex * aos_stride;
     uint8_t *out = dst + (size_t)ex * lay.expert_bytes;
     const uint8_t *src;
-    uint8_t *q_plane;
-    float *s_plane;
+    uint8_t *units;
     int nb, r, kt_count;
     if (row < 2 * eh) {
         const int i = row >> 1;
         nb = d / MIAG_QK;
         src = blob + ((row & 1) ? off_up : 0) + (size_t)i * nb * 36;
-        q_plane = out + lay.gu_q_off;
-        s_plane = reinterpret_cast<float *>(out + lay.gu_s_off);
+        units = out + lay.gu_off;
         r = row, kt_count = lay.gu_kt;
     } else {
         r = row - 2 * eh;
         nb = eh / MIAG_QK;
         src = blob + off_down + (size_t)r * nb * 36;
-        q_plane = out + lay.dn_q_off;
-        s_plane = reinterpret_cast<float *>(out + lay.dn_s_off);
+        units = out + lay.dn_off;
         kt_count = lay.dn_kt;
     }
     const int rt = r / kTileRows, rr = r % kTileRows;
     for (int b = threadIdx.x; b < nb; b += blockDim.x) {
         const uint32_t *blk = reinterpret_cast<const uint32_t *>(src + (size_t)b * 36);
         const int kt = b / 4, jb = b % 4;
-        const size_t tile = (size_t)rt * kt_count + kt;
-        s_plane[tile * (kTileScaleBytes / 4) + rr * 4 + jb] = __uint_as_float(blk[0]);
-        uint8_t *tq = q_plane + tile * kTileBytes;
+        uint8_t *tq = units + ((size_t)rt * kt_count + kt) * kUnitBytes;
+        reinterpret_cast<float *>(tq + kTileBytes)[rr * 4 + jb] = __uint_as_float(blk[0]);
 #pragma unroll
         for (int h = 0; h < 2; h++) {
             uint4 v = make_uint4(blk[1 + 4 * h], blk[2 + 4 * h], blk[3 + 4 * h], blk[4 + 4 * h]);
