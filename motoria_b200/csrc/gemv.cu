@@ -53,6 +53,7 @@ struct GemvParams {
     int stages;
     uint32_t x_off, x_stride;  // activation region offset in smem, its row stride
     uint32_t table_off;        // decoded-item table offset in smem
+    float one;                 // 1.0f, opaque to the compiler (see q8_step_x2)
     int *err;
 };
 
@@ -89,11 +90,39 @@ __device__ __forceinline__ void mma_s8(int (&c)[4], uint32_t a0, uint32_t a1, ui
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(kMagicBits));
 }
 
-// The reference step s += ((float)dot * dw) * dx (matmul.c:25) on a magic
-// accumulator m = kMagicBits + dot.
-__device__ __forceinline__ float q8_step_magic(float s, int m, float dw, float dx) {
-    const float dot = __fsub_rn(__int_as_float(m), kMagic);
-    return __fadd_rn(s, __fmul_rn(__fmul_rn(dot, dw), dx));
+// Two f32 lanes in one 64-bit register: the packed FP32 instructions of
+// sm_100 (FADD2, FMUL2, FFMA2) do one operation on both.
+__device__ __forceinline__ uint64_t pack2(float lo, float hi) {
+    uint64_t v;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(v) : "f"(lo), "f"(hi));
+    return v;
+}
+__device__ __forceinline__ uint64_t pack2i(int lo, int hi) {
+    uint64_t v;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(v) : "r"(lo), "r"(hi));
+    return v;
+}
+__device__ __forceinline__ float2 unpack2(uint64_t v) {
+    float2 r;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+    return r;
+}
+
+// The reference step s += ((float)dot * dw) * dx (matmul.c:25) for two
+// accumulators at once, on magic MMA results m = kMagicBits + dot.  Each
+// operation is rounded on its own, as in the reference: the dot is exact,
+// then two rounded products.  The product is added as fma(v, one, s) with
+// one = 1.0 from a kernel argument: v * 1 is exact, so this rounds once like
+// the add -- and the compiler, which contracts a packed multiply feeding a
+// packed add into one FFMA2 even when both are written with .rn (measured on
+// sm_100a), finds no multiply-add pair here to contract.
+__device__ __forceinline__ void q8_step_x2(uint64_t &s, uint64_t m, uint64_t w2, uint64_t x2,
+                                           uint64_t neg_magic2, uint64_t one2) {
+    uint64_t t;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(t) : "l"(m), "l"(neg_magic2));
+    asm("mul.rn.f32x2 %0, %0, %1;" : "+l"(t) : "l"(w2));
+    asm("mul.rn.f32x2 %0, %0, %1;" : "+l"(t) : "l"(x2));
+    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(s) : "l"(t), "l"(one2));
 }
 
 // Item i -> index a of its active expert: largest a with chunk_pre[a]*RT <= i.
@@ -165,15 +194,17 @@ __device__ void issue_iteration(const GemvParams &p, uint8_t *smem, int j) {
 }
 
 // Consumers: stage the activations of pairs [t0, t0+n) of the expert segment
-// starting at seg0 in the shared region (rows at x_stride, then scale rows at
-// their own odd-16-byte stride).
+// starting at seg0 in the shared region: int8 rows at x_stride, then the
+// scales of pairs 2q and 2q+1 interleaved in one row per q, [block][2] f32 at
+// their own odd-16-byte stride, so a lane loads its two pair columns' scales
+// of a block as one f32 pair.
 //   gate/up: copies xq[token(pair)] and dx[token] (quantized by the router);
 //   down:    quantizes h[pos] here, one thread per 32-block, exactly as
 //            mia_matvec quantizes its input (matmul.c:93, quant.c:11-27).
 template <bool kGU>
 __device__ void fill_region(const GemvParams &p, uint8_t *region, int seg0, int t0, int n,
                             int row_bytes, int nscale) {
-    const int srow = (int)smem_stride((uint32_t)nscale * 4);  // padded scale row bytes
+    const int srow = (int)smem_stride((uint32_t)nscale * 8);  // scale row of a pair of pairs
     uint8_t *rs = region + (size_t)kTokChunk * p.x_stride;
     if (kGU) {
         const int qv = row_bytes / 16, sv = nscale / 4;  // 16-byte vectors per row / scale row
@@ -184,9 +215,11 @@ __device__ void fill_region(const GemvParams &p, uint8_t *region, int seg0, int 
             if (k < qv)
                 *reinterpret_cast<int4 *>(region + (size_t)j * p.x_stride + 16 * k) =
                     __ldcg(reinterpret_cast<const int4 *>(p.xq + (size_t)t * row_bytes) + k);
-            else
-                *reinterpret_cast<int4 *>(rs + (size_t)j * srow + 16 * (k - qv)) =
-                    __ldcg(reinterpret_cast<const int4 *>(p.dx + (size_t)t * nscale) + (k - qv));
+            else {
+                const float4 v4 = __ldcg(reinterpret_cast<const float4 *>(p.dx + (size_t)t * nscale) + (k - qv));
+                float *dst = reinterpret_cast<float *>(rs + (size_t)(j >> 1) * srow) + 8 * (k - qv) + (j & 1);
+                dst[0] = v4.x, dst[2] = v4.y, dst[4] = v4.z, dst[6] = v4.w;
+            }
         }
     } else {
         // one thread per (pair, 32-block), its eight 16-byte loads issued together
@@ -217,7 +250,7 @@ __device__ void fill_region(const GemvParams &p, uint8_t *region, int seg0, int 
             uint4 *dst = reinterpret_cast<uint4 *>(region + (size_t)j * p.x_stride + b * MIAG_QK);
             dst[0] = make_uint4(q[0], q[1], q[2], q[3]);
             dst[1] = make_uint4(q[4], q[5], q[6], q[7]);
-            reinterpret_cast<float *>(rs + (size_t)j * srow)[b] = dq;
+            reinterpret_cast<float *>(rs + (size_t)(j >> 1) * srow)[2 * b + (j & 1)] = dq;
         }
     }
 }
@@ -256,18 +289,25 @@ __device__ __forceinline__ Lanes lane_roles(int warp, int lane) {
     return l;
 }
 
+__device__ __forceinline__ void lds_2x64(uint32_t addr, uint64_t &a, uint64_t &b) {
+    asm volatile("ld.shared.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "r"(addr));
+}
+
 // One k tile (4 Q8_0 blocks; kFull = all four inside K) for NT n-tiles of
 // 8 pairs.  tile/sc: the k tile's int8 and scale tiles in the stage.
+// acc[n][0]: row r0 x pairs (2tq, 2tq+1) of n-tile n; acc[n][1]: row r0 + 8.
 template <int NT, bool kFull>
-__device__ __forceinline__ void k_tile(float (&acc)[NT][4], uint32_t tile, uint32_t sc, int kt,
+__device__ __forceinline__ void k_tile(uint64_t (&acc)[NT][2], uint32_t tile, uint32_t sc, int kt,
                                        int nbk, const Lanes &ln, const uint32_t (&b_row)[NT],
-                                       const uint32_t (&xa)[NT], const uint32_t (&xb)[NT]) {
+                                       const uint32_t (&xp)[NT], uint64_t neg_magic2,
+                                       uint64_t one2) {
     uint32_t A[4][4];
 #pragma unroll
     for (int j = 0; j < 4; j++)
         if (kFull || j < nbk) ldsm_x4(tile + ln.a_off[j], A[j][0], A[j][1], A[j][2], A[j][3]);
     const float4 w0 = lds128(sc + ln.w0), w1 = lds128(sc + ln.w1);
-    const float wa[4] = {w0.x, w0.y, w0.z, w0.w}, wb[4] = {w1.x, w1.y, w1.z, w1.w};
+    const uint64_t wa[4] = {pack2(w0.x, w0.x), pack2(w0.y, w0.y), pack2(w0.z, w0.z), pack2(w0.w, w0.w)};
+    const uint64_t wb[4] = {pack2(w1.x, w1.x), pack2(w1.y, w1.y), pack2(w1.z, w1.z), pack2(w1.w, w1.w)};
 #pragma unroll
     for (int n = 0; n < NT; n++) {
         const uint32_t brow = b_row[n] + (uint32_t)(kt * kTileK);
@@ -275,8 +315,9 @@ __device__ __forceinline__ void k_tile(float (&acc)[NT][4], uint32_t tile, uint3
 #pragma unroll
         for (int j = 0; j < 4; j++)
             if (kFull || j < nbk) ldsm_x2(brow + 32 * j, B[j][0], B[j][1]);
-        const float4 u = lds128(xa[n] + 16u * (uint32_t)kt), v = lds128(xb[n] + 16u * (uint32_t)kt);
-        const float sa[4] = {u.x, u.y, u.z, u.w}, sb[4] = {v.x, v.y, v.z, v.w};
+        uint64_t x2[4];  // per block: the scales of this lane's two pair columns
+        lds_2x64(xp[n] + 32u * (uint32_t)kt, x2[0], x2[1]);
+        lds_2x64(xp[n] + 32u * (uint32_t)kt + 16u, x2[2], x2[3]);
         int C[4][4];
 #pragma unroll
         for (int j = 0; j < 4; j++)
@@ -285,10 +326,8 @@ __device__ __forceinline__ void k_tile(float (&acc)[NT][4], uint32_t tile, uint3
 #pragma unroll
         for (int j = 0; j < 4; j++) {
             if (kFull || j < nbk) {
-                acc[n][0] = q8_step_magic(acc[n][0], C[j][0], wa[j], sa[j]);
-                acc[n][1] = q8_step_magic(acc[n][1], C[j][1], wa[j], sb[j]);
-                acc[n][2] = q8_step_magic(acc[n][2], C[j][2], wb[j], sa[j]);
-                acc[n][3] = q8_step_magic(acc[n][3], C[j][3], wb[j], sb[j]);
+                q8_step_x2(acc[n][0], pack2i(C[j][0], C[j][1]), wa[j], x2[j], neg_magic2, one2);
+                q8_step_x2(acc[n][1], pack2i(C[j][2], C[j][3]), wb[j], x2[j], neg_magic2, one2);
             }
         }
     }
@@ -298,9 +337,20 @@ __device__ __forceinline__ void k_tile(float (&acc)[NT][4], uint32_t tile, uint3
 struct ItemCtx {
     uint32_t stages;         // shared address of stage 0
     uint32_t x_rows, x_scl;  // shared addresses of the activation rows / scale rows
-    uint32_t xsp_bytes;      // scale row stride (bytes)
+    uint32_t xpp_bytes;      // stride of the scale rows (one per pair of pairs)
     int S, KT, NS, nb, rows;
     int rt, seg0, t0, nq;    // the item: row tile, expert segment, first pair, pairs
+};
+
+// Position in the ring: iteration it uses stage s = it % S in phase
+// (it / S) & 1; advanced without divisions.
+struct RingPos {
+    int it, s;
+    uint32_t phase;
+    __device__ __forceinline__ void next(int S) {
+        it++;
+        if (++s == S) s = 0, phase ^= 1u;
+    }
 };
 
 // One item: its k tiles through the ring, then its outputs.
@@ -312,34 +362,32 @@ struct ItemCtx {
 // 168, which the tile shapes exceed).
 template <bool kGU, int NT>
 __device__ __forceinline__ void run_item(const GemvParams &p, const ItemCtx &ic, const Lanes &ln,
-                                         uint8_t *smem, int &it, bool &failed) {
+                                         uint8_t *smem, RingPos &rp, bool &failed) {
     RingHead *head = reinterpret_cast<RingHead *>(smem);
     const int lane = threadIdx.x & 31;
     const int nq = ic.nq;
     // per n-tile: this lane's B row (pairs past nq repeat the last pair; their
-    // columns are never written out) and the scale rows of its two columns
-    uint32_t b_row[NT], xa[NT], xb[NT];
+    // columns are never written out) and the scale row of its two columns
+    uint32_t b_row[NT], xp[NT];
 #pragma unroll
     for (int n = 0; n < NT; n++) {
         b_row[n] = ic.x_rows + (uint32_t)min(8 * n + ln.b_pair, nq - 1) * p.x_stride + ln.b_off;
-        xa[n] = ic.x_scl + (uint32_t)min(8 * n + 2 * ln.tq, nq - 1) * ic.xsp_bytes;
-        xb[n] = ic.x_scl + (uint32_t)min(8 * n + 2 * ln.tq + 1, nq - 1) * ic.xsp_bytes;
+        xp[n] = ic.x_scl + (uint32_t)(4 * n + ln.tq) * ic.xpp_bytes;
     }
-    float acc[NT][4];
+    const uint64_t neg_magic2 = pack2(-kMagic, -kMagic), one2 = pack2(p.one, p.one);
+    uint64_t acc[NT][2];
 #pragma unroll
-    for (int n = 0; n < NT; n++)
-#pragma unroll
-        for (int i = 0; i < 4; i++) acc[n][i] = 0.0f;
+    for (int n = 0; n < NT; n++) acc[n][0] = acc[n][1] = 0ull;  // +0.0f in both lanes
 
     const bool full_tiles = (ic.KT % kStageKT) == 0 && 4 * ic.KT == ic.nb;
-    for (int ks = 0; ks < ic.NS; ks++, it++) {
-        const int s = it % ic.S, round = it / ic.S;
+    for (int ks = 0; ks < ic.NS; ks++, rp.next(ic.S)) {
+        const int s = rp.s;
         if (!failed) {
             bool got = true;
-            if (lane == 0) got = mbar_wait(&head->full[s], round & 1);
+            if (lane == 0) got = mbar_wait(&head->full[s], rp.phase);
             if (!__shfl_sync(kFull, got, 0)) {
                 // Keep walking (on stale data) so every consumer reaches the
-                // same named barriers: no warp may leave early.
+                // same barriers: no warp may leave early.
                 set_error(p.err, kErrWaitFull);
                 failed = true;
             }
@@ -352,22 +400,22 @@ __device__ __forceinline__ void run_item(const GemvParams &p, const ItemCtx &ic,
 #pragma unroll (NT == 1 ? kStageKT : 1)
             for (int kk = 0; kk < kStageKT; kk++)
                 k_tile<NT, true>(acc, stg + kk * kUnitBytes, scl + kk * kUnitBytes, kt0 + kk, 4,
-                                 ln, b_row, xa, xb);
+                                 ln, b_row, xp, neg_magic2, one2);
         } else {
             const int nkt = min(kStageKT, ic.KT - kt0);
             for (int kk = 0; kk < nkt; kk++)
                 k_tile<NT, false>(acc, stg + kk * kUnitBytes, scl + kk * kUnitBytes, kt0 + kk,
-                                  min(4, ic.nb - 4 * (kt0 + kk)), ln, b_row, xa, xb);
+                                  min(4, ic.nb - 4 * (kt0 + kk)), ln, b_row, xp, neg_magic2, one2);
         }
         __syncwarp();
         if (lane == 0) {
             // release the stage; the eighth release of a round refills it
             __threadfence_block();
             const uint32_t done = atomicAdd(&head->released[s], 1u);
-            if ((done % kConsumerWarps) == kConsumerWarps - 1 && it + ic.S < head->total) {
+            if ((done % kConsumerWarps) == kConsumerWarps - 1 && rp.it + ic.S < head->total) {
                 __threadfence_block();
                 fence_proxy_async_smem();
-                issue_iteration<kGU>(p, smem, it + ic.S);
+                issue_iteration<kGU>(p, smem, rp.it + ic.S);
             }
         }
     }
@@ -378,36 +426,38 @@ __device__ __forceinline__ void run_item(const GemvParams &p, const ItemCtx &ic,
 #pragma unroll
     for (int n = 0; n < NT; n++) {
         const int qa = 8 * n + 2 * ln.tq, qb = qa + 1;
+        const float2 u0 = unpack2(acc[n][0]), u1 = unpack2(acc[n][1]);
+        const float o[4] = {u0.x, u0.y, u1.x, u1.y};  // (r0,qa) (r0,qb) (r1,qa) (r1,qb)
         if (kGU) {
             // rows are interleaved gate (even) / up (odd): the up partner of
             // row r sits in the lane with groupID g ^ 1, i.e. lane ^ 4.
             float up[4];
 #pragma unroll
-            for (int i = 0; i < 4; i++) up[i] = __shfl_xor_sync(kFull, acc[n][i], 4);
+            for (int i = 0; i < 4; i++) up[i] = __shfl_xor_sync(kFull, o[i], 4);
             if ((ln.g & 1) == 0) {
                 const int eh = p.m.eh, i0 = R0 >> 1, i1 = R1 >> 1;
                 if (qa < nq) {
                     float *hp = p.h + (size_t)(ic.seg0 + ic.t0 + qa) * eh;
-                    if (R0 < rows) hp[i0] = swiglu_ref(acc[n][0], up[0]);
-                    if (R1 < rows) hp[i1] = swiglu_ref(acc[n][2], up[2]);
+                    if (R0 < rows) hp[i0] = swiglu_ref(o[0], up[0]);
+                    if (R1 < rows) hp[i1] = swiglu_ref(o[2], up[2]);
                 }
                 if (qb < nq) {
                     float *hp = p.h + (size_t)(ic.seg0 + ic.t0 + qb) * eh;
-                    if (R0 < rows) hp[i0] = swiglu_ref(acc[n][1], up[1]);
-                    if (R1 < rows) hp[i1] = swiglu_ref(acc[n][3], up[3]);
+                    if (R0 < rows) hp[i0] = swiglu_ref(o[1], up[1]);
+                    if (R1 < rows) hp[i1] = swiglu_ref(o[3], up[3]);
                 }
             }
         } else {
             const int d = p.m.d;
             if (qa < nq) {
                 float *yp = p.y + (size_t)(ic.seg0 + ic.t0 + qa) * d;
-                if (R0 < rows) yp[R0] = acc[n][0];
-                if (R1 < rows) yp[R1] = acc[n][2];
+                if (R0 < rows) yp[R0] = o[0];
+                if (R1 < rows) yp[R1] = o[2];
             }
             if (qb < nq) {
                 float *yp = p.y + (size_t)(ic.seg0 + ic.t0 + qb) * d;
-                if (R0 < rows) yp[R0] = acc[n][1];
-                if (R1 < rows) yp[R1] = acc[n][3];
+                if (R0 < rows) yp[R0] = o[1];
+                if (R1 < rows) yp[R1] = o[3];
             }
         }
     }
@@ -423,7 +473,6 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_expert_mma(GemvParams p) {
     const int Kb = kGU ? d : eh;             // bytes of K (= values)
     const int rows = kGU ? 2 * eh : d;       // matrix rows
     const int nb = Kb / MIAG_QK, xs = scale_pad(nb);
-    const int xsp = (int)smem_stride((uint32_t)xs * 4) / 4;  // padded scale row in smem
     const int NS = (KT + kStageKT - 1) / kStageKT;  // stages per item
     const int nact = __ldg(p.n_active);
     const int n_items = __ldg(p.chunk_pre + nact) * RT;
@@ -459,11 +508,11 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_expert_mma(GemvParams p) {
     ic.stages = smem_addr(stages);
     ic.x_rows = smem_addr(region);
     ic.x_scl = ic.x_rows + (uint32_t)kTokChunk * p.x_stride;
-    ic.xsp_bytes = 4u * (uint32_t)xsp;
+    ic.xpp_bytes = smem_stride((uint32_t)xs * 8);
     ic.S = S, ic.KT = KT, ic.NS = NS, ic.nb = nb, ic.rows = rows;
 
     int cur_e = -1, cur_tc = -1;
-    int it = 0;
+    RingPos rp{0, 0, 0u};
     bool failed = false;
     for (int item = first; item < last; item++) {
         const ItemInfo ii = item_at(p, table, first, nact, RT, item);
@@ -478,10 +527,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_expert_mma(GemvParams p) {
         }
         ic.rt = ii.rt, ic.seg0 = seg0, ic.t0 = t0, ic.nq = nq;
         switch ((nq + 7) >> 3) {
-            case 1: run_item<kGU, 1>(p, ic, ln, smem, it, failed); break;
-            case 2: run_item<kGU, 2>(p, ic, ln, smem, it, failed); break;
-            case 3: run_item<kGU, 3>(p, ic, ln, smem, it, failed); break;
-            default: run_item<kGU, 4>(p, ic, ln, smem, it, failed); break;
+            case 1: run_item<kGU, 1>(p, ic, ln, smem, rp, failed); break;
+            case 2: run_item<kGU, 2>(p, ic, ln, smem, rp, failed); break;
+            case 3: run_item<kGU, 3>(p, ic, ln, smem, rp, failed); break;
+            default: run_item<kGU, 4>(p, ic, ln, smem, rp, failed); break;
         }
     }
     // After a timed-out wait, let every issued copy land (bounded) before the
@@ -516,6 +565,7 @@ static void fill_params(GemvParams &p, const Dims &m, const StoreLayout &lay, co
     p.offsets = w.offsets, p.perm = w.perm, p.active = w.active, p.n_active = w.n_active;
     p.chunk_pre = w.chunk_pre;
     p.xq = w.xq, p.dx = w.dx, p.h = w.h, p.y = w.y, p.err = err;
+    p.one = 1.0f;
 }
 
 // Shared memory: barriers | S stages | activation region (rows, then scales).
@@ -523,8 +573,8 @@ static size_t geometry(GemvParams &p, bool gu) {
     const int Kb = gu ? p.m.d : p.m.eh;
     const int xs = scale_pad(Kb / MIAG_QK);
     p.x_stride = smem_stride((uint32_t)Kb);
-    const size_t region =
-        round_up_sz((size_t)kTokChunk * (p.x_stride + smem_stride((uint32_t)xs * 4)), 128);
+    const size_t region = round_up_sz(
+        (size_t)kTokChunk * p.x_stride + (size_t)(kTokChunk / 2) * smem_stride((uint32_t)xs * 8), 128);
     const size_t table = (size_t)kItemTable * sizeof(int2);
     const long room = (long)kSmemBudget - kBarBytes - (long)region - (long)table;
     const int st = room > 0 ? (int)(room / kStageBytes) : 0;
