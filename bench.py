@@ -11,10 +11,13 @@ batched decode of 64 tokens per GPU.  Prints ONE JSON line on rank 0.
 
   value      tokens/s of the whole job, inputs resident in HBM, device-timed
              (CUDA events around each step on the launching stream, L2
-             flushed between steps outside the events, max over ranks)
+             flushed between steps outside the events -- a 256 MiB buffer
+             written, then read back -- max over ranks)
   e2e        the same metric through the public host API (miag_moe with
              pinned host buffers: H2D of x and D2H of the result every step)
-  roofline   the dominant kernel's algorithmic bytes / its mean event time
+  roofline   the dominant kernel's algorithmic bytes / its mean duration,
+             from CUDA events around each kernel on its stream in a second
+             pass of the same steps (the timed pass carries no such events)
   cpu_baseline  the reference engine built from its sources (oracle/_ref)
              or the oracle port, on this host's cores, rank 0 at N=1
   --impl reference  times the reference CPU implementation (all host threads)
@@ -147,7 +150,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.Q}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
+                 "--format=csv,noheader,nounits", "-lms", "25"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
@@ -240,9 +243,14 @@ def run_ours(args, T_desc, T, rms, zipf):
             dist.barrier()
             torch.cuda.synchronize(dev)
 
+    flush_sink = torch.zeros((), dtype=torch.int64, device=dev)
+
     def one_step(ev=None):
         x.copy_(x0)
+        # write a buffer larger than L2, then read it: the L2 holds none of the
+        # step's data and no dirty lines whose write-back the step would pay
         flush.zero_()
+        flush_sink.add_(flush.sum())
         if ev:
             ev[0].record(stream)
         eng.moe_device(x.data_ptr(), T, stream=sp)
@@ -258,17 +266,23 @@ def run_ours(args, T_desc, T, rms, zipf):
 
     events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
               for _ in range(args.steps)]
-    eng.profile(True)
-    eng.profile_read()
     barrier()
     with ClockSampler(local) as clk:
         for i in range(args.steps):
             one_step(events[i])
         barrier()
     eng.sync(sp)
+    total_ms = sum(a.elapsed_time(b) for a, b in events)
+    # Per-kernel durations: the same steps again, each kernel bracketed by
+    # CUDA events on the stream it is launched on (kept out of the timed pass
+    # above so the brackets do not stretch the step).
+    eng.profile(True)
+    eng.profile_read()
+    for i in range(args.steps):
+        one_step()
+    eng.sync(sp)
     prof = eng.profile_read()
     eng.profile(False)
-    total_ms = sum(a.elapsed_time(b) for a, b in events)
     t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
     if dist:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -317,7 +331,7 @@ def run_ours(args, T_desc, T, rms, zipf):
                        "experts": shape.n_experts, "top_k": shape.n_active, "dim": shape.dim,
                        "expert_hidden": shape.expert_hidden, "active_experts": n_act,
                        "weights": "Q8_0 HBM-resident",
-                       "l2": "flushed (256 MiB write) between steps, outside the timed events",
+                       "l2": "flushed between steps outside the timed events (256 MiB written, then read back)",
                        "parallelism": "replicas" if world > 1 else "single"},
             "e2e": {"value": e2e_value, "unit": UNIT,
                     "h2d_bytes_per_step": T * shape.dim * 4,
@@ -342,7 +356,7 @@ def run_ours(args, T_desc, T, rms, zipf):
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="config2")

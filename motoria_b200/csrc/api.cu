@@ -52,7 +52,7 @@ struct miag_ctx {
 
 namespace {
 enum Stage { kRoute = 0, kPermute, kGateUp, kDown, kCombine, kNumStages };
-const char *const kStageNames[kNumStages] = {"route", "topk_permute", "gateup", "down",
+const char *const kStageNames[kNumStages] = {"route", "permute", "gateup", "down",
                                              "combine"};
 
 cudaEvent_t take_event(miag_ctx *c) {
@@ -371,6 +371,7 @@ static size_t ws_layout(miag_ctx *c, int T, uint8_t *base, Work *w, float **x_de
     uint8_t *p = base;
     Work v{};
     v.T = T, v.P = (int)P, v.nchunks = nchunks;
+    v.tg_count = (int32_t *)bump(p, (size_t)T * 4);  // zeroed with the workspace, kept zero by the router
     v.xq = (int8_t *)bump(p, (size_t)T * m.d);
     v.dx = (float *)bump(p, (size_t)T * xs * 4);
     v.logits = (float *)bump(p, (size_t)T * m.E * 4);

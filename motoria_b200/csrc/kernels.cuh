@@ -25,6 +25,7 @@ struct Work {
     int32_t *inv;          // [P]           sorted position of each pair
     float *h;              // [P][eh]       silu(gate) * up, sorted order
     float *y;              // [P][d]        down projections, sorted order
+    int32_t *tg_count;     // [T]           route: CTAs done per token group; zero between calls
 };
 
 struct LayerDev {

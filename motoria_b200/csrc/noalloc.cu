@@ -16,10 +16,12 @@
 // before any stream capture that contains later calls.
 //
 // All calls share the one array and it keeps whatever the last call left
-// there.  Every buffer of the block is written before it is read, so nothing
-// has to start at zero; but two calls whose work overlaps on the GPU (other
-// streams, other contexts on the same device) race on it and must be
-// serialised by the caller.
+// there.  One thing in it must start at zero: the router's per-token-group
+// counters, which sit first, at a fixed place for every batch size; the array
+// starts zeroed when the library loads and every call leaves them at zero
+// again.  Every other buffer of the block is written before it is read.  Two
+// calls whose work overlaps on the GPU (other streams, other contexts on the
+// same device) race on the array and must be serialised by the caller.
 #include <cstdio>
 #include <mutex>
 
@@ -74,6 +76,8 @@ size_t bump(uint8_t *&p, size_t bytes) {
     return off;
 }
 
+constexpr int kNoAllocGroups = 1024;  // token-group counters, at offset 0
+
 // Lays the block's buffers for T tokens out from `base`; returns the bytes used.
 size_t layout(const Dims &m, int T, uint8_t *base, Work *w) {
     const size_t P = (size_t)T * m.K;
@@ -82,6 +86,7 @@ size_t layout(const Dims &m, int T, uint8_t *base, Work *w) {
     uint8_t *p = base;
     Work v{};
     v.T = T, v.P = (int)P, v.nchunks = nchunks;
+    v.tg_count = reinterpret_cast<int32_t *>(bump(p, (size_t)kNoAllocGroups * 4));
     v.xq = reinterpret_cast<int8_t *>(bump(p, (size_t)T * m.d));
     v.dx = reinterpret_cast<float *>(bump(p, (size_t)T * xs * 4));
     v.logits = reinterpret_cast<float *>(bump(p, (size_t)T * m.E * 4));
@@ -118,7 +123,7 @@ extern "C" int miag_moe_noalloc(miag_ctx *c, int layer, float *x_dev, int n_toke
     }
     if (n_tokens == 0) return 0;
     const size_t need = layout(v.dims, n_tokens, nullptr, nullptr);
-    if (need > kNoAllocScratchBytes) {
+    if (need > kNoAllocScratchBytes || n_tokens > kNoAllocGroups) {
         if (err && errlen)
             snprintf(err, errlen,
                      "miag_moe_noalloc: %d tokens need %zu bytes of scratch, more than its fixed "

@@ -6,17 +6,15 @@
 // an expert they stay in (t, j) order.  Deterministic: no order-dependent
 // atomics; ranks come from warp match masks and per-warp prefix counts.
 //
+// The top-k indices come from the router kernel (route.cu).
 // Small batches (T*K <= 1024 pairs), one CTA of 1024 threads:
-//   k_topk_permute_small  top-k of every token (one warp per token), then
-//                         ranks, counts, offsets, active list and scatter
+//   k_permute_small  ranks, counts, offsets, active list and scatter
 // Larger batches:
-//   k_topk         top-k, one warp per token
 //   k_perm_count   per chunk of 1024 pairs: stable rank of each pair among
 //                  the chunk's pairs of the same expert, and chunk histograms
 //   k_perm_scan    per expert: chunk bases, counts, offsets, active list
 //   k_perm_scatter perm[pos] = p, inv[p] = pos
 #include "kernels.cuh"
-#include "topk.cuh"
 
 namespace miag {
 
@@ -138,36 +136,19 @@ __global__ void k_perm_scatter(const int32_t *idx, int P, int E, const int32_t *
     inv[p] = pos;
 }
 
-// Top-k of T tokens, one warp per token (logits [T][E] -> idx, w [T][K]).
-__global__ void __launch_bounds__(256) k_topk(const float *logits, int T, int E, int K,
-                                              int norm_topk, int32_t *idx, float *w) {
-    extern __shared__ float tk_buf[];  // [8 warps][E]
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int t = blockIdx.x * 8 + warp;
-    if (t >= T) return;
-    topk_warp(logits + (size_t)t * E, E, K, norm_topk, idx + (size_t)t * K, w + (size_t)t * K,
-              tk_buf + (size_t)warp * E, lane);
-}
-
-// Everything between the router logits and the expert products, for at most
-// 1024 pairs, in one CTA of 1024 threads.
+// Everything between the top-k and the expert products, for at most 1024
+// pairs, in one CTA of 1024 threads (one pair each).
 __global__ void __launch_bounds__(1024)
-k_topk_permute_small(const float *logits, int T, int E, int K, int norm_topk, int32_t *idx,
-                     float *w, int32_t *counts, int32_t *offsets, int32_t *active,
-                     int32_t *n_active, int32_t *chunk_pre, int32_t *perm, int32_t *inv,
-                     int *err) {
-    extern __shared__ int32_t sm_i[];  // top-k scratch [32][E] f32, then wcnt [32][E], base [E]
+k_permute_small(const int32_t *idx, int P, int E, int32_t *counts, int32_t *offsets,
+                int32_t *active, int32_t *n_active, int32_t *chunk_pre, int32_t *perm,
+                int32_t *inv, int *err) {
+    extern __shared__ int32_t sm_i[];  // wcnt [32][E], base [E]
     __shared__ int sh[33];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    float *tk = reinterpret_cast<float *>(sm_i);
-    int32_t *wcnt = sm_i + 32 * E;
+    int32_t *wcnt = sm_i;
     int32_t *base = wcnt + 32 * E;
-    for (int t = warp; t < T; t += 32)
-        topk_warp(logits + (size_t)t * E, E, K, norm_topk, idx + (size_t)t * K,
-                  w + (size_t)t * K, tk + (size_t)warp * E, lane);
     for (int i = tid; i < 32 * E; i += 1024) wcnt[i] = 0;
-    __syncthreads();  // idx of every token written (same CTA: visible after the barrier)
-    const int P = T * K;
+    __syncthreads();
     const int p = tid;
     int e = -1;
     if (p < P) {
@@ -217,20 +198,14 @@ k_topk_permute_small(const float *logits, int T, int E, int K, int norm_topk, in
 
 void launch_permute(const Dims &m, const Work &w, int *err, cudaStream_t s) {
     const int P = w.P, E = m.E;
-    const size_t small_smem = (size_t)(32 * E) * 4 * 2 + (size_t)E * 4;
+    const size_t small_smem = (size_t)(32 * E) * 4 + (size_t)E * 4;
     if (P <= kPermChunk && small_smem <= 200 * 1024) {
-        const size_t smem = small_smem;
-        cudaFuncSetAttribute(k_topk_permute_small, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)smem);
-        k_topk_permute_small<<<1, 1024, smem, s>>>(w.logits, w.T, E, m.K, m.norm_topk, w.idx, w.w,
-                                                   w.counts, w.offsets, w.active, w.n_active,
-                                                   w.chunk_pre, w.perm, w.inv, err);
+        cudaFuncSetAttribute(k_permute_small, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)small_smem);
+        k_permute_small<<<1, 1024, small_smem, s>>>(w.idx, P, E, w.counts, w.offsets, w.active,
+                                                     w.n_active, w.chunk_pre, w.perm, w.inv, err);
         return;
     }
-    const size_t tk_smem = (size_t)8 * E * 4;
-    if (tk_smem > 48 * 1024)
-        cudaFuncSetAttribute(k_topk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tk_smem);
-    k_topk<<<(w.T + 7) / 8, 256, tk_smem, s>>>(w.logits, w.T, E, m.K, m.norm_topk, w.idx, w.w);
     const size_t smem = sizeof(int32_t) * (size_t)E * (1 + kPermWarps);
     if (smem > 48 * 1024)
         cudaFuncSetAttribute(k_perm_count, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -243,7 +218,7 @@ void launch_permute(const Dims &m, const Work &w, int *err, cudaStream_t s) {
 }
 
 int permute_launches(int P, int E) {
-    return (P <= kPermChunk && (size_t)(32 * E) * 8 + (size_t)E * 4 <= 200 * 1024) ? 1 : 4;
+    return (P <= kPermChunk && (size_t)(32 * E) * 4 + (size_t)E * 4 <= 200 * 1024) ? 1 : 3;
 }
 
 }  // namespace miag

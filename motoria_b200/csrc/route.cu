@@ -1,4 +1,4 @@
-// route.cu -- rmsnorm + activation quantization + router logits.
+// route.cu -- rmsnorm + activation quantization + router logits + top-k.
 //
 // Reference: src/model/forward.c:174-181 (rmsnorm :75-81, router matvec
 // src/tensor/matmul.c:13-17, softmax :95-101, top_k :104-114) and the
@@ -16,8 +16,11 @@
 //      [group][i][32] so it is contiguous, streams through a ring of
 //      shared-memory chunks that the producer fills with 1-D TMA bulk copies
 //      and all consumer warps read;
-// Softmax, top-k and renormalisation run afterwards in topk.cu.
+//   4. the last CTA of a token group to finish (a counter per group) runs
+//      softmax, top-k and renormalisation for the group's tokens (topk.cuh),
+//      one warp per token.
 #include "kernels.cuh"
+#include "topk.cuh"
 
 namespace miag {
 
@@ -62,14 +65,18 @@ struct RouteParams {
     int8_t *xq;          // [T][d]
     float *dx;           // [T][xs_pad]
     float *logits;       // [T][E]
+    int32_t *idx;        // [T][K]  top-k experts
+    float *w;            // [T][K]  their weights
+    int32_t *tg_count;   // [token groups]: zero between calls
     int *err;
 };
 
-constexpr int kRouteChunk = 64;   // router rows i per bulk-copied chunk (64 x 128 B)
-constexpr int kRouteStages = 8;
+constexpr int kRouteChunk = 256;  // router rows per bulk copy: 256 x 128 B = 32 KiB
+constexpr int kRouteStages = 4;
 
 // Shared memory: barriers | ring [kRouteStages][kRouteChunk][32] f32 |
-// x, then xn in place [W*R][d] f32 | ffn_norm [d] f32.
+// x, then xn in place [W*R][d] f32 | ffn_norm [d] f32.  After the router loop
+// the ring is free and holds the top-k scratch, E floats per warp.
 constexpr int kRouteBarBytes = 256;
 __host__ __device__ inline size_t route_smem(int d, int E, int R, int W) {
     (void)E;
@@ -77,9 +84,28 @@ __host__ __device__ inline size_t route_smem(int d, int E, int R, int W) {
            (size_t)d * 4;
 }
 
+// Sixteen router rows for R tokens: acc[r] += w_i * xn[r][i], i = i0..i0+15
+// in order, each product and sum rounded (matmul.c:13-17).  Scalar
+// round-to-nearest intrinsics: the compiler never fuses them.
+template <int R>
+__device__ __forceinline__ void router_rows16(float (&acc)[R], const float (&wv)[16],
+                                              const float4 (&xv)[R][4]) {
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+#pragma unroll
+        for (int r = 0; r < R; r++) {
+            acc[r] = __fadd_rn(acc[r], __fmul_rn(wv[4 * q + 0], xv[r][q].x));
+            acc[r] = __fadd_rn(acc[r], __fmul_rn(wv[4 * q + 1], xv[r][q].y));
+            acc[r] = __fadd_rn(acc[r], __fmul_rn(wv[4 * q + 2], xv[r][q].z));
+            acc[r] = __fadd_rn(acc[r], __fmul_rn(wv[4 * q + 3], xv[r][q].w));
+        }
+    }
+}
+
 // Grid: (token groups of W*R, expert groups of 32); W consumer warps own R
-// tokens each and loads them itself; one producer warp streams the group's
-// router slice.
+// tokens each and load them themselves; one producer warp streams the
+// group's router slice.  The last of a token group's CTAs to finish its
+// logits also runs softmax / top-k / renormalisation for the group's tokens.
 template <int R>
 __global__ void __launch_bounds__(9 * 32) k_route(RouteParams p, int W) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -87,6 +113,7 @@ __global__ void __launch_bounds__(9 * 32) k_route(RouteParams p, int W) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
     uint64_t *empty = full + kRouteStages;
+    int *last_flag = reinterpret_cast<int *>(empty + kRouteStages);
     float *ring = reinterpret_cast<float *>(smem + kRouteBarBytes);
     float *xs_all = ring + (size_t)kRouteStages * kRouteChunk * 32;  // [W*R][d]
     float *norm = xs_all + (size_t)W * R * d;
@@ -104,7 +131,9 @@ __global__ void __launch_bounds__(9 * 32) k_route(RouteParams p, int W) {
     __syncthreads();
 
     if (warp == W) {
-        // Producer: the router chunks.
+        // Producer: the router chunks, 32 KiB bulk copies (on B200 a bulk copy
+        // occupies the copy engine ~0.26 us whatever its size up to ~8 KiB,
+        // so small chunks cap the SM's ingest).
         if (lane == 0) {
             for (int ch = 0; ch < nchunks; ch++) {
                 const int s = ch % kRouteStages, round = ch / kRouteStages;
@@ -138,7 +167,6 @@ __global__ void __launch_bounds__(9 * 32) k_route(RouteParams p, int W) {
     for (int i = 4 * (warp * 32 + lane); i < d; i += 128 * W)
         *reinterpret_cast<float4 *>(norm + i) = __ldg(reinterpret_cast<const float4 *>(p.L.ffn_norm + i));
     named_barrier_sync(1, W * 32);  // consumer warps only
-
     // 1.+2. rmsnorm (forward.c:75-81) and Q8_0 of xn (quant.c:11-27).  Lane l
     // holds elements 4l + 128k (k < d/128) of a token: eight lanes cover one
     // 32-block, so block maxima take three shuffles.
@@ -227,6 +255,8 @@ __global__ void __launch_bounds__(9 * 32) k_route(RouteParams p, int W) {
     __syncwarp();
 
     // 3. Router logits, serial over i like dot_f32_scalar (matmul.c:13-17).
+    // Each step's sixteen router rows are loaded before the previous
+    // sixteen's arithmetic, so the loads' latency hides behind it.
     float acc[R];
 #pragma unroll
     for (int r = 0; r < R; r++) acc[r] = 0.0f;
@@ -241,29 +271,36 @@ __global__ void __launch_bounds__(9 * 32) k_route(RouteParams p, int W) {
             }
         }
         const float *wc = ring + (size_t)s * kRouteChunk * 32 + lane;
-        const int i0 = ch * kRouteChunk, rows = min(kRouteChunk, d - i0);
-        for (int u = 0; u < rows; u += 16) {  // rows is a multiple of 32
-            float4 xv[R][4];
-            float wv[16];
+        const float *xc = xw + (size_t)ch * kRouteChunk;
+        const int rows = min(kRouteChunk, d - ch * kRouteChunk);  // a multiple of 32
+        float wv[16], wn[16];
+        float4 xv[R][4], xn[R][4];
+#pragma unroll
+        for (int k = 0; k < 16; k++) wv[k] = wc[k * 32];
+#pragma unroll
+        for (int r = 0; r < R; r++)
+#pragma unroll
+            for (int q = 0; q < 4; q++) xv[r][q] = *reinterpret_cast<const float4 *>(xc + (size_t)r * d + 4 * q);
+        for (int u = 0; u < rows; u += 32) {
+            // rows u+16 .. u+31 (always inside the chunk: rows % 32 == 0)
+#pragma unroll
+            for (int k = 0; k < 16; k++) wn[k] = wc[(u + 16 + k) * 32];
 #pragma unroll
             for (int r = 0; r < R; r++)
 #pragma unroll
                 for (int q = 0; q < 4; q++)
-                    xv[r][q] = *reinterpret_cast<const float4 *>(xw + (size_t)r * d + i0 + u + 4 * q);
+                    xn[r][q] = *reinterpret_cast<const float4 *>(xc + (size_t)r * d + u + 16 + 4 * q);
+            router_rows16<R>(acc, wv, xv);
+            // rows u+32 .. u+47 of this chunk (clamped on the last step: loaded, unused)
+            const int v = min(u + 32, rows - 16);
 #pragma unroll
-            for (int k = 0; k < 16; k++) wv[k] = wc[(u + k) * 32];
-            // Scalar round-to-nearest intrinsics: the compiler never fuses
-            // them (paired f32x2 forms do get contracted into an FMA).
+            for (int k = 0; k < 16; k++) wv[k] = wc[(v + k) * 32];
 #pragma unroll
-            for (int q = 0; q < 4; q++) {
+            for (int r = 0; r < R; r++)
 #pragma unroll
-                for (int r = 0; r < R; r++) {
-                    acc[r] = __fadd_rn(acc[r], __fmul_rn(wv[4 * q + 0], xv[r][q].x));
-                    acc[r] = __fadd_rn(acc[r], __fmul_rn(wv[4 * q + 1], xv[r][q].y));
-                    acc[r] = __fadd_rn(acc[r], __fmul_rn(wv[4 * q + 2], xv[r][q].z));
-                    acc[r] = __fadd_rn(acc[r], __fmul_rn(wv[4 * q + 3], xv[r][q].w));
-                }
-            }
+                for (int q = 0; q < 4; q++)
+                    xv[r][q] = *reinterpret_cast<const float4 *>(xc + (size_t)r * d + v + 4 * q);
+            router_rows16<R>(acc, wn, xn);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
@@ -277,21 +314,42 @@ __global__ void __launch_bounds__(9 * 32) k_route(RouteParams p, int W) {
         }
     }
 
+    // 4. Softmax, top-k, renormalisation (forward.c:176-181), by the token
+    // group's last CTA once all expert groups' logits are out.  Writers fence
+    // before counting; the last one fences after, then reads through L2.
+    __threadfence();
+    named_barrier_sync(1, W * 32);
+    if (threadIdx.x == 0) {
+        const int before = atomicAdd(&p.tg_count[blockIdx.x], 1);
+        const int last = before == (int)gridDim.y - 1;
+        if (last) p.tg_count[blockIdx.x] = 0;  // back to zero for the next call
+        *last_flag = last;
+    }
+    named_barrier_sync(1, W * 32);
+    if (!*last_flag) return;
+    __threadfence();
+    float *buf = ring + (size_t)warp * E;  // the ring is idle now: every chunk was consumed
+    for (int r = 0; r < nt; r++) {
+        const int t = tw0 + r;
+        topk_warp(p.logits + (size_t)t * E, E, p.m.K, p.m.norm_topk, p.idx + (size_t)t * p.m.K,
+                  p.w + (size_t)t * p.m.K, buf, lane);
+    }
 }
 
-// Tokens per warp R and consumer warps W by batch size (a sweep on B200 over
-// T = 1..2048: one token per warp while there are few tokens, so more CTAs
-// share the serial sums; two tokens and eight warps beyond).
+// Tokens per warp R and consumer warps W by batch size: one token per warp
+// while there are few tokens, so more CTAs share the serial sums; two tokens
+// per warp beyond (eight token rows fit beside the 128 KiB ring).
 static void route_shape(int T, int &R, int &W) {
     if (T <= 128) R = 1, W = 4;
-    else R = 2, W = 8;
+    else R = 2, W = 4;
 }
 
 void launch_route(const Dims &m, const LayerDev &L, const float *x, const Work &w, int *err,
                   cudaStream_t s) {
     RouteParams p;
     p.m = m, p.L = L, p.x = x, p.T = w.T;
-    p.xq = w.xq, p.dx = w.dx, p.logits = w.logits, p.err = err;
+    p.xq = w.xq, p.dx = w.dx, p.logits = w.logits, p.idx = w.idx, p.w = w.w;
+    p.tg_count = w.tg_count, p.err = err;
     int R, W;
     route_shape(w.T, R, W);
     dim3 grid((w.T + R * W - 1) / (R * W), (m.E + 31) / 32);
