@@ -9,7 +9,8 @@
 // each owning R tokens, and one producer warp:
 //   1. each warp rmsnorms its tokens into shared memory, certified to equal
 //      the reference's serial double sum (see rms_scale);
-//   2. expert-group 0 quantizes xn to Q8_0 for the expert GEMVs;
+//   2. the expert groups' CTAs quantize xn to Q8_0 for the expert GEMVs,
+//      each a share of the blocks;
 //   3. lane e computes the router logit of expert 32*eg + e for the warp's
 //      tokens as the reference's serial fp32 sum (rounded multiply, then
 //      rounded add, i = 0..d-1 in order).  The group's router slice, stored
@@ -84,20 +85,28 @@ __host__ __device__ inline size_t route_smem(int d, int E, int R, int W) {
            (size_t)d * 4;
 }
 
-// Sixteen router rows for R tokens: acc[r] += w_i * xn[r][i], i = i0..i0+15
-// in order, each product and sum rounded (matmul.c:13-17).  Scalar
-// round-to-nearest intrinsics: the compiler never fuses them.
+// Router rows [u, u + 64) of a chunk for R tokens: acc[r] += w_i * xn[r][i]
+// in order, each product and sum rounded (matmul.c:13-17), with scalar
+// round-to-nearest intrinsics, which the compiler never fuses.  Written as
+// one straight run (loads at compile-time offsets): on B200 this measured
+// ~6.4 cycles a row for one token and ~4.5 a token-row for two, against
+// ~7.5 and ~4.9 for a software-pipelined form.
 template <int R>
-__device__ __forceinline__ void router_rows16(float (&acc)[R], const float (&wv)[16],
-                                              const float4 (&xv)[R][4]) {
+__device__ __forceinline__ void router_rows64(float (&acc)[R], const float *wc, const float *xc,
+                                              int d) {
 #pragma unroll
-    for (int q = 0; q < 4; q++) {
+    for (int k4 = 0; k4 < 64; k4 += 4) {
+        float4 xv[R];
+#pragma unroll
+        for (int r = 0; r < R; r++) xv[r] = *reinterpret_cast<const float4 *>(xc + (size_t)r * d + k4);
+        const float w0 = wc[(k4 + 0) * 32], w1 = wc[(k4 + 1) * 32];
+        const float w2 = wc[(k4 + 2) * 32], w3 = wc[(k4 + 3) * 32];
 #pragma unroll
         for (int r = 0; r < R; r++) {
-            acc[r] = __fadd_rn(acc[r], __fmul_rn(wv[4 * q + 0], xv[r][q].x));
-            acc[r] = __fadd_rn(acc[r], __fmul_rn(wv[4 * q + 1], xv[r][q].y));
-            acc[r] = __fadd_rn(acc[r], __fmul_rn(wv[4 * q + 2], xv[r][q].z));
-            acc[r] = __fadd_rn(acc[r], __fmul_rn(wv[4 * q + 3], xv[r][q].w));
+            acc[r] = __fadd_rn(acc[r], __fmul_rn(w0, xv[r].x));
+            acc[r] = __fadd_rn(acc[r], __fmul_rn(w1, xv[r].y));
+            acc[r] = __fadd_rn(acc[r], __fmul_rn(w2, xv[r].z));
+            acc[r] = __fadd_rn(acc[r], __fmul_rn(w3, xv[r].w));
         }
     }
 }
@@ -107,7 +116,7 @@ __device__ __forceinline__ void router_rows16(float (&acc)[R], const float (&wv)
 // group's router slice.  The last of a token group's CTAs to finish its
 // logits also runs softmax / top-k / renormalisation for the group's tokens.
 template <int R>
-__global__ void __launch_bounds__(9 * 32) k_route(RouteParams p, int W) {
+__global__ void __launch_bounds__(9 * 32, 1) k_route(RouteParams p, int W) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int d = p.m.d, E = p.m.E;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -160,12 +169,35 @@ __global__ void __launch_bounds__(9 * 32) k_route(RouteParams p, int W) {
     // The warp's token rows and the shared ffn_norm come in through plain
     // coalesced loads: with these rows bulk-copied instead, the norm and the
     // router loop that follow measured 2-2.5x slower on B200.
-    for (int r = 0; r < nt; r++)
-        for (int i = 4 * lane; i < d; i += 128)
-            *reinterpret_cast<float4 *>(xw + (size_t)r * d + i) =
-                __ldg(reinterpret_cast<const float4 *>(p.x + (size_t)(tw0 + r) * d + i));
-    for (int i = 4 * (warp * 32 + lane); i < d; i += 128 * W)
-        *reinterpret_cast<float4 *>(norm + i) = __ldg(reinterpret_cast<const float4 *>(p.L.ffn_norm + i));
+    // Loads go out eight at a time before their stores, so a row costs about
+    // one memory latency rather than one per float4.
+    for (int r = 0; r < nt; r++) {
+        const float4 *src = reinterpret_cast<const float4 *>(p.x + (size_t)(tw0 + r) * d);
+        float4 *dst = reinterpret_cast<float4 *>(xw + (size_t)r * d);
+        for (int i0 = lane; i0 < d / 4; i0 += 8 * 32) {
+            float4 v[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++)
+                if (i0 + 32 * u < d / 4) v[u] = __ldg(src + i0 + 32 * u);
+#pragma unroll
+            for (int u = 0; u < 8; u++)
+                if (i0 + 32 * u < d / 4) dst[i0 + 32 * u] = v[u];
+        }
+    }
+    {
+        const float4 *src = reinterpret_cast<const float4 *>(p.L.ffn_norm);
+        float4 *dst = reinterpret_cast<float4 *>(norm);
+        const int stride = 32 * W;
+        for (int i0 = warp * 32 + lane; i0 < d / 4; i0 += 4 * stride) {
+            float4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++)
+                if (i0 + stride * u < d / 4) v[u] = __ldg(src + i0 + stride * u);
+#pragma unroll
+            for (int u = 0; u < 4; u++)
+                if (i0 + stride * u < d / 4) dst[i0 + stride * u] = v[u];
+        }
+    }
     named_barrier_sync(1, W * 32);  // consumer warps only
     // 1.+2. rmsnorm (forward.c:75-81) and Q8_0 of xn (quant.c:11-27).  Lane l
     // holds elements 4l + 128k (k < d/128) of a token: eight lanes cover one
@@ -201,9 +233,11 @@ __global__ void __launch_bounds__(9 * 32) k_route(RouteParams p, int W) {
             v.w = __fmul_rn(__fmul_rn(v.w, inv), w.w);
             *reinterpret_cast<float4 *>(xr + i) = v;
         }
-        if (blockIdx.y == 0) {
+        {
+            // the expert-group CTAs of a token share the quantization: group
+            // g takes every G-th run of four float4 per lane (16 blocks)
             const int xs = scale_pad(d / MIAG_QK);
-            for (int k0 = 0; k0 < nq4; k0 += 4) {
+            for (int k0 = 4 * (int)blockIdx.y; k0 < nq4; k0 += 4 * (int)gridDim.y) {
                 float4 v[4];
                 float a[4], dq[4], id[4];
 #pragma unroll
@@ -255,8 +289,6 @@ __global__ void __launch_bounds__(9 * 32) k_route(RouteParams p, int W) {
     __syncwarp();
 
     // 3. Router logits, serial over i like dot_f32_scalar (matmul.c:13-17).
-    // Each step's sixteen router rows are loaded before the previous
-    // sixteen's arithmetic, so the loads' latency hides behind it.
     float acc[R];
 #pragma unroll
     for (int r = 0; r < R; r++) acc[r] = 0.0f;
@@ -272,35 +304,21 @@ __global__ void __launch_bounds__(9 * 32) k_route(RouteParams p, int W) {
         }
         const float *wc = ring + (size_t)s * kRouteChunk * 32 + lane;
         const float *xc = xw + (size_t)ch * kRouteChunk;
-        const int rows = min(kRouteChunk, d - ch * kRouteChunk);  // a multiple of 32
-        float wv[16], wn[16];
-        float4 xv[R][4], xn[R][4];
+        // a warp past the last token only keeps the ring turning
+        const int rows = nt > 0 ? min(kRouteChunk, d - ch * kRouteChunk) : 0;
+        int u = 0;
+        for (; u + 64 <= rows; u += 64) router_rows64<R>(acc, wc + u * 32, xc + u, d);
+        for (; u < rows; u += 4) {  // d % 64 tail, rows of four (d is a multiple of 32)
+            float4 xv[R];
 #pragma unroll
-        for (int k = 0; k < 16; k++) wv[k] = wc[k * 32];
+            for (int r = 0; r < R; r++) xv[r] = *reinterpret_cast<const float4 *>(xc + (size_t)r * d + u);
 #pragma unroll
-        for (int r = 0; r < R; r++)
-#pragma unroll
-            for (int q = 0; q < 4; q++) xv[r][q] = *reinterpret_cast<const float4 *>(xc + (size_t)r * d + 4 * q);
-        for (int u = 0; u < rows; u += 32) {
-            // rows u+16 .. u+31 (always inside the chunk: rows % 32 == 0)
-#pragma unroll
-            for (int k = 0; k < 16; k++) wn[k] = wc[(u + 16 + k) * 32];
-#pragma unroll
-            for (int r = 0; r < R; r++)
-#pragma unroll
-                for (int q = 0; q < 4; q++)
-                    xn[r][q] = *reinterpret_cast<const float4 *>(xc + (size_t)r * d + u + 16 + 4 * q);
-            router_rows16<R>(acc, wv, xv);
-            // rows u+32 .. u+47 of this chunk (clamped on the last step: loaded, unused)
-            const int v = min(u + 32, rows - 16);
-#pragma unroll
-            for (int k = 0; k < 16; k++) wv[k] = wc[(v + k) * 32];
-#pragma unroll
-            for (int r = 0; r < R; r++)
-#pragma unroll
-                for (int q = 0; q < 4; q++)
-                    xv[r][q] = *reinterpret_cast<const float4 *>(xc + (size_t)r * d + v + 4 * q);
-            router_rows16<R>(acc, wn, xn);
+            for (int r = 0; r < R; r++) {
+                acc[r] = __fadd_rn(acc[r], __fmul_rn(wc[(u + 0) * 32], xv[r].x));
+                acc[r] = __fadd_rn(acc[r], __fmul_rn(wc[(u + 1) * 32], xv[r].y));
+                acc[r] = __fadd_rn(acc[r], __fmul_rn(wc[(u + 2) * 32], xv[r].z));
+                acc[r] = __fadd_rn(acc[r], __fmul_rn(wc[(u + 3) * 32], xv[r].w));
+            }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
@@ -331,16 +349,18 @@ __global__ void __launch_bounds__(9 * 32) k_route(RouteParams p, int W) {
     float *buf = ring + (size_t)warp * E;  // the ring is idle now: every chunk was consumed
     for (int r = 0; r < nt; r++) {
         const int t = tw0 + r;
-        topk_warp(p.logits + (size_t)t * E, E, p.m.K, p.m.norm_topk, p.idx + (size_t)t * p.m.K,
-                  p.w + (size_t)t * p.m.K, buf, lane);
+        topk_warp_any(p.logits + (size_t)t * E, E, p.m.K, p.m.norm_topk,
+                      p.idx + (size_t)t * p.m.K, p.w + (size_t)t * p.m.K, buf, lane);
     }
 }
 
-// Tokens per warp R and consumer warps W by batch size: one token per warp
-// while there are few tokens, so more CTAs share the serial sums; two tokens
-// per warp beyond (eight token rows fit beside the 128 KiB ring).
+// Tokens per warp R and consumer warps W by batch size.  The warps of a CTA
+// all read each router row from shared memory, and four of them (with the
+// ring's own fill) saturate it, so few-token batches use two warps of one
+// token each and more CTAs; larger ones two tokens per warp, which reads a
+// row once for both (eight token rows fit beside the 128 KiB ring).
 static void route_shape(int T, int &R, int &W) {
-    if (T <= 128) R = 1, W = 4;
+    if (T <= 128) R = 1, W = 2;
     else R = 2, W = 4;
 }
 
