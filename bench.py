@@ -200,6 +200,19 @@ def stage_bytes(shape, T, counts):
     }, n_act
 
 
+def ncu_traffic(workload: str, kernel: str):
+    """DRAM bytes (read + write) per launch of `kernel` from the committed ncu
+    summary of this workload (profiles/*.md, a `traffic:` marker), or None."""
+    import re
+
+    pat = re.compile(r"<!-- traffic: workload=(\S+) kernel=(\S+) bytes=(\d+) -->")
+    for f in sorted((ROOT / "profiles").glob("*.md")):
+        for w, k, n in pat.findall(f.read_text()):
+            if w == workload and k == kernel:
+                return int(n)
+    return None
+
+
 def run_ours(args, T_desc, T, rms, zipf):
     import torch
 
@@ -337,7 +350,8 @@ def run_ours(args, T_desc, T, rms, zipf):
                     "h2d_bytes_per_step": T * shape.dim * 4,
                     "d2h_bytes_per_step": T * shape.dim * 4},
             "roofline": {"bound": "hbm", "kernel": top, "achieved": achieved, "peak": hbm_gbs,
-                         "unit": "GB/s", "frac": achieved / hbm_gbs, "traffic": None,
+                         "unit": "GB/s", "frac": achieved / hbm_gbs,
+                         "traffic": ncu_traffic(args.workload, top),
                          "peak_source": f"{peak_kind} hbm_gbs",
                          "block_achieved_gbs": block_bytes / (total_ms / args.steps / 1e3) / 1e9},
             "stages_ms": {k: round(v, 5) for k, v in stage_ms.items()},
