@@ -34,10 +34,12 @@ constexpr int kConsumerWarps = 8;
 constexpr int kConsumers = kConsumerWarps * 32;
 constexpr int kGemvThreads = kConsumers;  // no producer warp: see run_item
 constexpr int kItemTable = 512;           // decoded items cached per CTA
+constexpr int kTableBytes = kItemTable * 8;
 constexpr int kStageKT = 2;  // k tiles per stage
 constexpr int kStageBytes = kStageKT * kUnitBytes;  // one bulk copy
-constexpr int kMaxStages = 8;
-constexpr int kBarBytes = 1024;  // keeps every stage 1024-B aligned
+constexpr int kMaxStages = 12;
+constexpr int kBarBytes = 1024;
+constexpr int kRingOff = kBarBytes + kTableBytes;  // head | item table | ring | activations
 constexpr int kSmemBudget = 227 * 1024;
 constexpr uint32_t kFull = 0xffffffffu;
 
@@ -51,8 +53,7 @@ struct GemvParams {
     float *h;          // [P][eh]
     float *y;          // [P][d]
     int stages;
-    uint32_t x_off, x_stride;  // activation region offset in smem, its row stride
-    uint32_t table_off;        // decoded-item table offset in smem
+    uint32_t x_stride;         // row stride of the staged activations
     float one;                 // 1.0f, opaque to the compiler (see q8_step_x2)
     int *err;
 };
@@ -156,6 +157,8 @@ struct RingHead {
     uint64_t full[kMaxStages];      // stage holds its k tiles (TMA complete_tx)
     uint32_t released[kMaxStages];  // warps done with the stage, summed over rounds
     int first, total, nact;         // first item, stages to stream, active experts
+    int S;                          // this CTA's ring depth
+    int nq_max;                     // largest pair chunk among this CTA's items
 };
 static_assert(sizeof(RingHead) <= kBarBytes, "ring head");
 
@@ -180,17 +183,26 @@ __device__ void issue_iteration(const GemvParams &p, uint8_t *smem, int j) {
     const int RT = kGU ? p.lay.gu_rt : p.lay.dn_rt;
     const int KT = kGU ? p.lay.gu_kt : p.lay.dn_kt;
     const int NS = (KT + kStageKT - 1) / kStageKT;
-    const int s = j % p.stages, ks = j % NS;
-    const ItemInfo ii = item_at(p, reinterpret_cast<const int2 *>(smem + p.table_off), h->first,
+    const int s = j % h->S, ks = j % NS;
+    const ItemInfo ii = item_at(p, reinterpret_cast<const int2 *>(smem + kBarBytes), h->first,
                                 h->nact, RT, h->first + j / NS);
     const uint8_t *base = p.experts + (size_t)ii.e * p.lay.expert_bytes;
     const int kt0 = ks * kStageKT, nkt = min(kStageKT, KT - kt0);
     const size_t unit = (size_t)ii.rt * KT + kt0;
-    uint8_t *dst = smem + kBarBytes + (size_t)s * kStageBytes;
+    uint8_t *dst = smem + kRingOff + (size_t)s * kStageBytes;
     uint64_t *bar = &h->full[s];
     mbar_arrive_expect_tx(bar, (uint32_t)nkt * kUnitBytes);
     bulk_g2s(dst, base + (kGU ? p.lay.gu_off : p.lay.dn_off) + unit * kUnitBytes,
              (uint32_t)nkt * kUnitBytes, bar);
+}
+
+// Bytes of the activation region for chunks of up to nq pairs: nq int8 rows
+// at x_stride, then the pair-interleaved scale rows that the lanes of
+// ceil(nq/8) n-tiles address (four per n-tile).
+__host__ __device__ inline uint32_t region_size(int nq, int Kb, uint32_t x_stride, int xs) {
+    (void)Kb;
+    const uint32_t b = (uint32_t)nq * x_stride + 4u * (uint32_t)((nq + 7) / 8) * smem_stride((uint32_t)xs * 8);
+    return (b + 127u) & ~127u;
 }
 
 // Consumers: stage the activations of pairs [t0, t0+n) of the expert segment
@@ -202,10 +214,10 @@ __device__ void issue_iteration(const GemvParams &p, uint8_t *smem, int j) {
 //   down:    quantizes h[pos] here, one thread per 32-block, exactly as
 //            mia_matvec quantizes its input (matmul.c:93, quant.c:11-27).
 template <bool kGU>
-__device__ void fill_region(const GemvParams &p, uint8_t *region, int seg0, int t0, int n,
-                            int row_bytes, int nscale) {
+__device__ void fill_region(const GemvParams &p, uint8_t *region, int rows_cap, int seg0, int t0,
+                            int n, int row_bytes, int nscale) {
     const int srow = (int)smem_stride((uint32_t)nscale * 8);  // scale row of a pair of pairs
-    uint8_t *rs = region + (size_t)kTokChunk * p.x_stride;
+    uint8_t *rs = region + (size_t)rows_cap * p.x_stride;
     if (kGU) {
         const int qv = row_bytes / 16, sv = nscale / 4;  // 16-byte vectors per row / scale row
         const int per = qv + sv;
@@ -480,34 +492,44 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_expert_mma(GemvParams p) {
     const int last = (int)((long)n_items * (blockIdx.x + 1) / gridDim.x);
 
     RingHead *head = reinterpret_cast<RingHead *>(smem);
-    uint8_t *stages = smem + kBarBytes;
-    int2 *table = reinterpret_cast<int2 *>(smem + p.table_off);
-    const int S = p.stages;
+    uint8_t *stages = smem + kRingOff;
+    int2 *table = reinterpret_cast<int2 *>(smem + kBarBytes);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_mine = last - first;
+    if (threadIdx.x == 0) head->nq_max = 1;
+    __syncthreads();
+    // Decode this CTA's items and find its largest pair chunk: the activation
+    // region is sized for that, and the rest of shared memory deepens the ring.
+    int my_nq = 1;
+    for (int k = threadIdx.x; k < n_mine; k += kGemvThreads) {
+        const ItemInfo ii = decode_item(p, nact, RT, first + k);
+        if (k < kItemTable) table[k] = make_int2(ii.e, ii.rt | (ii.tc << 8));
+        const int n_e = __ldg(p.offsets + ii.e + 1) - __ldg(p.offsets + ii.e);
+        my_nq = max(my_nq, min(kTokChunk, n_e - ii.tc * kTokChunk));
+    }
+    atomicMax(&head->nq_max, my_nq);
+    __syncthreads();
+    const uint32_t region_bytes = region_size(head->nq_max, Kb, p.x_stride, xs);
+    const int S = min(kMaxStages, (int)((kSmemBudget - kRingOff - (int)region_bytes) / kStageBytes));
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; s++) {
             mbar_init(&head->full[s], 1);
             head->released[s] = 0;
         }
-        head->first = first, head->total = n_mine * NS, head->nact = nact;
+        head->first = first, head->total = n_mine * NS, head->nact = nact, head->S = S;
         fence_barrier_init();
-    }
-    for (int k = threadIdx.x; k < min(n_mine, kItemTable); k += kGemvThreads) {
-        const ItemInfo ii = decode_item(p, nact, RT, first + k);
-        table[k] = make_int2(ii.e, ii.rt | (ii.tc << 8));
     }
     __syncthreads();
     if (threadIdx.x == 0)
         for (int j = 0; j < min(S, n_mine * NS); j++) issue_iteration<kGU>(p, smem, j);
 
     // ---- consumers
-    uint8_t *region = smem + p.x_off;
+    uint8_t *region = smem + kRingOff + (size_t)S * kStageBytes;
     const Lanes ln = lane_roles(warp, lane);
     ItemCtx ic;
     ic.stages = smem_addr(stages);
     ic.x_rows = smem_addr(region);
-    ic.x_scl = ic.x_rows + (uint32_t)kTokChunk * p.x_stride;
+    ic.x_scl = ic.x_rows + (uint32_t)head->nq_max * p.x_stride;
     ic.xpp_bytes = smem_stride((uint32_t)xs * 8);
     ic.S = S, ic.KT = KT, ic.NS = NS, ic.nb = nb, ic.rows = rows;
 
@@ -521,7 +543,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_expert_mma(GemvParams p) {
         const int t0 = ii.tc * kTokChunk, nq = min(kTokChunk, n_e - t0);
         if (ii.e != cur_e || ii.tc != cur_tc) {
             consumer_sync();  // nobody still reads the region
-            fill_region<kGU>(p, region, seg0, t0, nq, Kb, xs);
+            fill_region<kGU>(p, region, head->nq_max, seg0, t0, nq, Kb, xs);
             cur_e = ii.e, cur_tc = ii.tc;
             consumer_sync();
         }
@@ -568,20 +590,16 @@ static void fill_params(GemvParams &p, const Dims &m, const StoreLayout &lay, co
     p.one = 1.0f;
 }
 
-// Shared memory: barriers | S stages | activation region (rows, then scales).
-static size_t geometry(GemvParams &p, bool gu) {
+// Shared memory: head | item table | ring | activation region.  Every CTA
+// gets the whole budget and splits it itself: the region for its largest
+// chunk, the rest as ring stages.  Returns the stages a full 32-pair chunk
+// leaves (the fewest any CTA gets).
+static int geometry(GemvParams &p, bool gu) {
     const int Kb = gu ? p.m.d : p.m.eh;
     const int xs = scale_pad(Kb / MIAG_QK);
     p.x_stride = smem_stride((uint32_t)Kb);
-    const size_t region = round_up_sz(
-        (size_t)kTokChunk * p.x_stride + (size_t)(kTokChunk / 2) * smem_stride((uint32_t)xs * 8), 128);
-    const size_t table = (size_t)kItemTable * sizeof(int2);
-    const long room = (long)kSmemBudget - kBarBytes - (long)region - (long)table;
-    const int st = room > 0 ? (int)(room / kStageBytes) : 0;
-    p.stages = st > kMaxStages ? kMaxStages : st;
-    p.x_off = (uint32_t)(kBarBytes + (size_t)p.stages * kStageBytes);
-    p.table_off = (uint32_t)(p.x_off + region);
-    return p.table_off + table;
+    const long room = (long)kSmemBudget - kRingOff - (long)region_size(kTokChunk, Kb, p.x_stride, xs);
+    return room > 0 ? (int)(room / kStageBytes) : 0;
 }
 
 // The dynamic shared-memory limit is an attribute of the kernel, shared by
@@ -591,8 +609,7 @@ int gemv_setup_attributes(const Dims &m, const StoreLayout &lay) {
     GemvParams p{};
     p.m = m, p.lay = lay;
     if (lay.gu_rt > 255 || lay.dn_rt > 255) return -1;  // the item table packs rt in 8 bits
-    if (geometry(p, true) > (size_t)kSmemBudget || p.stages < 2) return -1;
-    if (geometry(p, false) > (size_t)kSmemBudget || p.stages < 2) return -1;
+    if (geometry(p, true) < 2 || geometry(p, false) < 2) return -1;
     if (cudaFuncSetAttribute(k_expert_mma<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kSmemBudget) != cudaSuccess ||
         cudaFuncSetAttribute(k_expert_mma<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -611,16 +628,16 @@ void launch_gateup(const Dims &m, const StoreLayout &lay, const LayerDev &L, con
                    int num_sms, int *err, cudaStream_t s) {
     GemvParams p{};
     fill_params(p, m, lay, L, w, err);
-    const size_t smem = geometry(p, true);
-    k_expert_mma<true><<<grid_for(m, lay.gu_rt, num_sms, w.P), kGemvThreads, smem, s>>>(p);
+    geometry(p, true);
+    k_expert_mma<true><<<grid_for(m, lay.gu_rt, num_sms, w.P), kGemvThreads, kSmemBudget, s>>>(p);
 }
 
 void launch_down(const Dims &m, const StoreLayout &lay, const LayerDev &L, const Work &w,
                  int num_sms, int *err, cudaStream_t s) {
     GemvParams p{};
     fill_params(p, m, lay, L, w, err);
-    const size_t smem = geometry(p, false);
-    k_expert_mma<false><<<grid_for(m, lay.dn_rt, num_sms, w.P), kGemvThreads, smem, s>>>(p);
+    geometry(p, false);
+    k_expert_mma<false><<<grid_for(m, lay.dn_rt, num_sms, w.P), kGemvThreads, kSmemBudget, s>>>(p);
 }
 
 void launch_combine(const Dims &m, const Work &w, float *x, cudaStream_t s) {
