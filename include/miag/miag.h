@@ -104,6 +104,35 @@ int miag_moe_async(miag_ctx *c, int layer, float *x_dev, int n_tokens,
 int miag_moe_noalloc(miag_ctx *c, int layer, float *x_dev, int n_tokens,
                      void *stream, char *err, size_t errlen);
 
+/* The same block in three device steps, for expert parallelism: each GPU
+ * routes its own tokens, the caller moves (row, expert) pairs to the GPUs
+ * that hold the experts, those run the expert products, and the results come
+ * back to be combined where the tokens live.  moe() (forward.c:174-194) is
+ * exactly route -> experts -> combine; the split changes no arithmetic, so
+ * the results are those of miag_moe_async bit for bit.  All pointers are
+ * device pointers; all calls only enqueue on `stream` (NULL = own stream).
+ *
+ * miag_route_async: forward.c:174-181 for n_tokens rows of x [n][dim]:
+ *   idx, w [n][n_active] (the top-k and its weights), and the Q8_0 form of
+ *   the normalised rows that the expert products read (quant.c:11-27):
+ *   xq [n][dim] int8 values, dx [n][miag_dx_stride()] f32 block scales.
+ * miag_experts_async: the expert products of n_pairs pairs; pair p is row
+ *   pair_row[p] (< n_rows) of xq/dx against expert pair_expert[p]
+ *   (forward.c:186-193, SwiGLU included): y [n_pairs][dim] f32, in pair order.
+ * miag_combine_async: x[t] += sum_j w[t][j] * y[t*n_active + j], j in order
+ *   (forward.c:194), for t < n_tokens. */
+int miag_route_async(miag_ctx *c, int layer, const float *x_dev, int n_tokens,
+                     int32_t *idx, float *w, int8_t *xq, float *dx, void *stream,
+                     char *err, size_t errlen);
+int miag_experts_async(miag_ctx *c, int layer, const int8_t *xq, const float *dx,
+                       int n_rows, const int32_t *pair_row,
+                       const int32_t *pair_expert, int n_pairs, float *y,
+                       void *stream, char *err, size_t errlen);
+int miag_combine_async(miag_ctx *c, float *x_dev, int n_tokens, const float *w,
+                       const float *y, void *stream, char *err, size_t errlen);
+/* f32 scales per row of dx: dim/32 rounded up to a multiple of four. */
+int miag_dx_stride(const miag_shape *s);
+
 /* Waits for the context's work on `stream` (NULL = own stream) and reports
  * any device-side error (a bounded wait that gave up, a bad index). */
 int miag_sync(miag_ctx *c, void *stream, char *err, size_t errlen);

@@ -504,6 +504,95 @@ extern "C" int miag_moe(miag_ctx *c, int layer, float *x, int n_tokens, char *er
     return read_device_error(c, err, errlen);
 }
 
+// ---- The block in three device steps, for callers that move pairs between
+// GPUs in between (expert parallelism): route here, experts where they live,
+// combine back here.
+
+extern "C" int miag_route_async(miag_ctx *c, int layer, const float *x_dev, int n_tokens,
+                                int32_t *idx, float *wts, int8_t *xq, float *dx, void *stream,
+                                char *err, size_t errlen) {
+    if (check_layer(c, layer, err, errlen)) return -1;
+    if (n_tokens < 0 || (n_tokens > 0 && (!x_dev || !idx || !wts || !xq || !dx)) ||
+        ((uintptr_t)x_dev & 15u) || ((uintptr_t)xq & 15u) || ((uintptr_t)dx & 15u)) {
+        set_err(err, errlen, "bad buffers (device pointers; x, xq, dx 16-byte aligned)");
+        return -1;
+    }
+    const LayerState &Ls = c->layers[(size_t)layer];
+    if (!Ls.dense_set) {
+        set_err(err, errlen, "layer %d has no router / ffn_norm (miag_set_layer)", layer);
+        return -1;
+    }
+    c->last_launches = 0;
+    if (n_tokens == 0) return 0;
+    CU(cudaSetDevice(c->device));
+    if (ensure_ws(c, n_tokens, err, errlen)) return -1;
+    const cudaStream_t s = stream ? (cudaStream_t)stream : c->stream;
+    const LayerDev L{Ls.ffn_norm, Ls.router_t, Ls.has_bias ? Ls.bias : nullptr, Ls.experts};
+    Work w = c->ws;  // logits and the token-group counters stay in the workspace
+    w.idx = idx, w.w = wts, w.xq = xq, w.dx = dx;
+    run_stage(c, kRoute, 1, s, [&] { launch_route(c->dims, L, x_dev, w, c->d_err, s); });
+    CU(cudaGetLastError());
+    return 0;
+}
+
+extern "C" int miag_experts_async(miag_ctx *c, int layer, const int8_t *xq, const float *dx,
+                                  int n_rows, const int32_t *pair_row, const int32_t *pair_expert,
+                                  int n_pairs, float *y, void *stream, char *err, size_t errlen) {
+    if (check_layer(c, layer, err, errlen)) return -1;
+    if (n_pairs < 0 || n_rows < 0 ||
+        (n_pairs > 0 && (!xq || !dx || !pair_row || !pair_expert || !y || n_rows == 0)) ||
+        ((uintptr_t)xq & 15u) || ((uintptr_t)dx & 15u)) {
+        set_err(err, errlen, "bad buffers (device pointers; xq, dx 16-byte aligned)");
+        return -1;
+    }
+    c->last_launches = 0;
+    if (n_pairs == 0) return 0;
+    CU(cudaSetDevice(c->device));
+    // the workspace is laid out by tokens; size it for n_pairs pairs
+    if (ensure_ws(c, (n_pairs + c->dims.K - 1) / c->dims.K, err, errlen)) return -1;
+    const cudaStream_t s = stream ? (cudaStream_t)stream : c->stream;
+    const LayerState &Ls = c->layers[(size_t)layer];
+    const LayerDev L{Ls.ffn_norm, Ls.router_t, Ls.has_bias ? Ls.bias : nullptr, Ls.experts};
+    Work w = c->ws;
+    w.P = n_pairs, w.nchunks = (n_pairs + kPermChunk - 1) / kPermChunk;
+    w.idx = const_cast<int32_t *>(pair_expert);  // read only by the permutation
+    w.xq = const_cast<int8_t *>(xq), w.dx = const_cast<float *>(dx);
+    w.pair_row = pair_row, w.n_rows = n_rows, w.y = y;
+    run_stage(c, kPermute, permute_launches(w.P, c->dims.E), s,
+              [&] { launch_permute(c->dims, w, c->d_err, s); });
+    run_stage(c, kGateUp, 1, s,
+              [&] { launch_gateup(c->dims, c->lay, L, w, c->num_sms, c->d_err, s); });
+    run_stage(c, kDown, 1, s,
+              [&] { launch_down(c->dims, c->lay, L, w, c->num_sms, c->d_err, s); });
+    CU(cudaGetLastError());
+    return 0;
+}
+
+extern "C" int miag_dx_stride(const miag_shape *s) {
+    return s ? scale_pad(s->dim / MIAG_QK) : 0;
+}
+
+extern "C" int miag_combine_async(miag_ctx *c, float *x_dev, int n_tokens, const float *wts,
+                                  const float *y, void *stream, char *err, size_t errlen) {
+    if (!c) {
+        set_err(err, errlen, "null context");
+        return -1;
+    }
+    if (n_tokens < 0 || (n_tokens > 0 && (!x_dev || !wts || !y))) {
+        set_err(err, errlen, "bad buffers (device pointers)");
+        return -1;
+    }
+    c->last_launches = 0;
+    if (n_tokens == 0) return 0;
+    CU(cudaSetDevice(c->device));
+    const cudaStream_t s = stream ? (cudaStream_t)stream : c->stream;
+    Work w{};
+    w.T = n_tokens, w.w = const_cast<float *>(wts), w.y = const_cast<float *>(y);
+    run_stage(c, kCombine, 1, s, [&] { launch_combine(c->dims, w, x_dev, s); });
+    CU(cudaGetLastError());
+    return 0;
+}
+
 extern "C" int miag_routing(miag_ctx *c, int32_t *idx, float *w, int32_t *counts, int32_t *offsets,
                             int32_t *perm, char *err, size_t errlen) {
     if (!c) {

@@ -105,7 +105,8 @@ __device__ __forceinline__ float swiglu_ref(float g, float u) {
 }
 
 // ---------------------------------------------------------------------------
-// mbarrier / bulk-copy (TMA 1-D) wrappers.  No cluster multicast anywhere.
+// mbarrier / bulk-copy (TMA 1-D) wrappers; every copy lands in this CTA's own
+// shared memory.
 __device__ __forceinline__ uint32_t smem_addr(const void *p) {
     return (uint32_t)__cvta_generic_to_shared(p);
 }

@@ -48,10 +48,12 @@ struct GemvParams {
     StoreLayout lay;
     const uint8_t *experts;
     const int32_t *offsets, *perm, *active, *n_active, *chunk_pre;
-    const int8_t *xq;  // [T][d]
-    const float *dx;   // [T][xs]
-    float *h;          // [P][eh]
-    float *y;          // [P][d]
+    const int8_t *xq;  // [rows][d]
+    const float *dx;   // [rows][xs]
+    const int32_t *pair_row;  // [P] activation row of each pair, or null: pair / K
+    int n_rows;        // rows of xq / dx
+    float *h;          // [P][eh], sorted order
+    float *y;          // [P][d], pair order
     int stages;
     uint32_t x_stride;         // row stride of the staged activations
     float one;                 // 1.0f, opaque to the compiler (see q8_step_x2)
@@ -223,7 +225,12 @@ __device__ void fill_region(const GemvParams &p, uint8_t *region, int rows_cap, 
         const int per = qv + sv;
         for (int v = threadIdx.x; v < n * per; v += kConsumers) {
             const int j = v / per, k = v % per;
-            const int t = __ldg(p.perm + seg0 + t0 + j) / p.m.K;
+            const int pr = __ldg(p.perm + seg0 + t0 + j);
+            int t = p.pair_row ? __ldg(p.pair_row + pr) : pr / p.m.K;
+            if (t < 0 || t >= p.n_rows) {  // a caller's row index out of range
+                set_error(p.err, kErrBadExpert);
+                t = 0;
+            }
             if (k < qv)
                 *reinterpret_cast<int4 *>(region + (size_t)j * p.x_stride + 16 * k) =
                     __ldcg(reinterpret_cast<const int4 *>(p.xq + (size_t)t * row_bytes) + k);
@@ -460,14 +467,16 @@ __device__ __forceinline__ void run_item(const GemvParams &p, const ItemCtx &ic,
                 }
             }
         } else {
+            // y goes out in pair order, so the combine (and a remote caller)
+            // finds pair t*K + j's row without the permutation
             const int d = p.m.d;
             if (qa < nq) {
-                float *yp = p.y + (size_t)(ic.seg0 + ic.t0 + qa) * d;
+                float *yp = p.y + (size_t)__ldg(p.perm + ic.seg0 + ic.t0 + qa) * d;
                 if (R0 < rows) yp[R0] = o[0];
                 if (R1 < rows) yp[R1] = o[2];
             }
             if (qb < nq) {
-                float *yp = p.y + (size_t)(ic.seg0 + ic.t0 + qb) * d;
+                float *yp = p.y + (size_t)__ldg(p.perm + ic.seg0 + ic.t0 + qb) * d;
                 if (R0 < rows) yp[R0] = o[1];
                 if (R1 < rows) yp[R1] = o[3];
             }
@@ -565,16 +574,14 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_expert_mma(GemvParams p) {
 }
 
 // x[t] += w_j * y_j for j = 0..K-1 in order (forward.c:194).
-__global__ void k_combine(float *x, int d, int K, const float *w, const int32_t *inv,
-                          const float *y) {
+// y is in pair order: pair t*K + j is token t's j-th expert.
+__global__ void k_combine(float *x, int d, int K, const float *w, const float *y) {
     const int t = blockIdx.x;
     const int i = blockIdx.y * blockDim.x + threadIdx.x;
     if (i >= d) return;
     float v = x[(size_t)t * d + i];
-    for (int j = 0; j < K; j++) {
-        const int pos = __ldg(inv + (size_t)t * K + j);
-        v = __fadd_rn(v, __fmul_rn(__ldg(w + (size_t)t * K + j), y[(size_t)pos * d + i]));
-    }
+    for (int j = 0; j < K; j++)
+        v = __fadd_rn(v, __fmul_rn(__ldg(w + (size_t)t * K + j), y[((size_t)t * K + j) * d + i]));
     x[(size_t)t * d + i] = v;
 }
 
@@ -587,6 +594,7 @@ static void fill_params(GemvParams &p, const Dims &m, const StoreLayout &lay, co
     p.offsets = w.offsets, p.perm = w.perm, p.active = w.active, p.n_active = w.n_active;
     p.chunk_pre = w.chunk_pre;
     p.xq = w.xq, p.dx = w.dx, p.h = w.h, p.y = w.y, p.err = err;
+    p.pair_row = w.pair_row, p.n_rows = w.pair_row ? w.n_rows : w.T;
     p.one = 1.0f;
 }
 
@@ -642,7 +650,7 @@ void launch_down(const Dims &m, const StoreLayout &lay, const LayerDev &L, const
 
 void launch_combine(const Dims &m, const Work &w, float *x, cudaStream_t s) {
     dim3 grid(w.T, (m.d + 255) / 256);
-    k_combine<<<grid, 256, 0, s>>>(x, m.d, m.K, w.w, w.inv, w.y);
+    k_combine<<<grid, 256, 0, s>>>(x, m.d, m.K, w.w, w.y);
 }
 
 }  // namespace miag

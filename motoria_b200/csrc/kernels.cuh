@@ -26,6 +26,8 @@ struct Work {
     float *h;              // [P][eh]       silu(gate) * up, sorted order
     float *y;              // [P][d]        down projections, sorted order
     int32_t *tg_count;     // [T]           route: CTAs done per token group; zero between calls
+    const int32_t *pair_row;  // [P]        expert products over given pairs: each pair's row of
+    int n_rows;               //              xq/dx (null: pair p is row p / K, the moe() case)
 };
 
 struct LayerDev {

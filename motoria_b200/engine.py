@@ -134,6 +134,44 @@ class MoEEngine:
                                       C.c_void_p(stream or 0), err, len(err))
         N.check(rc, err, "miag_moe_async")
 
+    # -- the block in three device steps (expert parallelism; see ep.py)
+    def dx_stride(self) -> int:
+        """f32 block scales per row of the dx buffers of route/experts."""
+        return int(self._lib.miag_dx_stride(C.byref(_shape(self.shape, 1))))
+
+    def route_device(self, x_ptr: int, n_tokens: int, idx_ptr: int, w_ptr: int, xq_ptr: int,
+                     dx_ptr: int, layer: int = 0, stream: int | None = None) -> None:
+        """Enqueues the router on x [n][dim]: idx, w [n][K]; xq [n][dim] int8 and
+        dx [n][dx_stride] f32, the Q8_0 form of the normalised rows."""
+        err = N.errbuf()
+        rc = self._lib.miag_route_async(self._ctx, layer, C.c_void_p(x_ptr), n_tokens,
+                                        C.c_void_p(idx_ptr), C.c_void_p(w_ptr),
+                                        C.c_void_p(xq_ptr), C.c_void_p(dx_ptr),
+                                        C.c_void_p(stream or 0), err, len(err))
+        N.check(rc, err, "miag_route_async")
+
+    def experts_device(self, xq_ptr: int, dx_ptr: int, n_rows: int, pair_row_ptr: int,
+                       pair_expert_ptr: int, n_pairs: int, y_ptr: int, layer: int = 0,
+                       stream: int | None = None) -> None:
+        """Enqueues the expert products of n_pairs (row, expert) pairs: y [n_pairs][dim]
+        in pair order."""
+        err = N.errbuf()
+        rc = self._lib.miag_experts_async(self._ctx, layer, C.c_void_p(xq_ptr),
+                                          C.c_void_p(dx_ptr), n_rows, C.c_void_p(pair_row_ptr),
+                                          C.c_void_p(pair_expert_ptr), n_pairs,
+                                          C.c_void_p(y_ptr), C.c_void_p(stream or 0), err,
+                                          len(err))
+        N.check(rc, err, "miag_experts_async")
+
+    def combine_device(self, x_ptr: int, n_tokens: int, w_ptr: int, y_ptr: int,
+                       stream: int | None = None) -> None:
+        """Enqueues x[t] += sum_j w[t][j] * y[t*K + j], j in order."""
+        err = N.errbuf()
+        rc = self._lib.miag_combine_async(self._ctx, C.c_void_p(x_ptr), n_tokens,
+                                          C.c_void_p(w_ptr), C.c_void_p(y_ptr),
+                                          C.c_void_p(stream or 0), err, len(err))
+        N.check(rc, err, "miag_combine_async")
+
     def sync(self, stream: int | None = None) -> None:
         err = N.errbuf()
         N.check(self._lib.miag_sync(self._ctx, C.c_void_p(stream or 0), err, len(err)), err,

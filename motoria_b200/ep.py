@@ -1,0 +1,217 @@
+"""Expert parallelism for the MoE block: experts sharded over the GPUs of one
+node, tokens exchanged with NCCL all-to-all.
+
+The reference runs the block on one device (src/model/forward.c:167-197); the
+sharded form here computes exactly the same numbers.  moe() is route ->
+expert products -> combine, and only the middle step needs an expert's
+weights, so:
+
+1. every rank routes its own tokens (miag_route_async: top-k, weights, and
+   the Q8_0 form of the normalised rows that the expert products read);
+2. each token row goes once to every rank that holds one of its experts
+   (contiguous placement: rank g holds experts [g*E/G, (g+1)*E/G)), with one
+   (row, expert) record per pair, over all_to_all_single;
+3. each rank runs the expert products of the pairs it received
+   (miag_experts_async) -- the same kernels on the same bytes;
+4. the results (one f32 row per pair) go back the reverse way, and
+5. the origin combines them in top-k order (miag_combine_async).
+
+Because the combine keeps the reference's order of adds (x + w_0 y_0 + w_1 y_1
++ ...), results come back per pair rather than as per-rank partial sums;
+a partial sum would reassociate the adds.  The outputs therefore equal the
+single-GPU block bit for bit.
+
+The plan (who sends what where) is built with device tensor operations; the
+collectives are torch.distributed's (NCCL on GPUs, gloo in the CPU tests).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+
+@dataclass
+class DispatchPlan:
+    """What one rank sends, for G ranks and its T tokens of K pairs each."""
+
+    send_rows: torch.Tensor      # [R] token of each row sent, grouped by destination, ascending
+    rows_per_dest: torch.Tensor  # [G] rows to each destination
+    pair_order: torch.Tensor     # [P] pair ids (t*K + j) grouped by destination, ascending
+    pairs_per_dest: torch.Tensor  # [G]
+    pair_meta: torch.Tensor      # [P, 2] int32: (row within the destination's block, expert)
+
+
+def plan_dispatch(idx: torch.Tensor, experts_per_rank: int, world: int) -> DispatchPlan:
+    """idx [T][K] int32 top-k experts -> the rows and pair records to send.
+
+    A row goes to a destination once however many of the token's experts
+    live there; within a destination rows keep token order and pairs keep
+    pair order, so every rank sees the same canonical ordering."""
+    T, K = idx.shape
+    dev = idx.device
+    dest = (idx.long() // experts_per_rank)                         # [T, K]
+    hit = torch.zeros((T, world), dtype=torch.bool, device=dev)
+    hit.scatter_(1, dest, True)
+    rows_per_dest = hit.sum(0)                                       # [G]
+    gt = hit.t().nonzero()                                           # [(g, t)] g-major, t ascending
+    send_rows = gt[:, 1]
+    row_in_block = hit.long().cumsum(0) - 1                          # [T, G] index of t in g's block
+    pair_ids = torch.arange(T * K, device=dev)
+    key = dest.reshape(-1) * (T * K) + pair_ids                     # g-major, then pair order
+    pair_order = torch.argsort(key)
+    d_sorted = dest.reshape(-1)[pair_order]
+    pairs_per_dest = torch.bincount(d_sorted, minlength=world)
+    t_sorted = pair_order // K
+    meta = torch.stack([row_in_block[t_sorted, d_sorted], idx.reshape(-1)[pair_order].long()], 1)
+    return DispatchPlan(send_rows, rows_per_dest, pair_order, pairs_per_dest,
+                        meta.to(torch.int32))
+
+
+class EngineOps:
+    """The three device steps of a MoEEngine on torch tensors, enqueued on the
+    tensors' device's current stream."""
+
+    def __init__(self, engine, layer: int = 0):
+        self.eng, self.layer = engine, layer
+        sh = engine.shape
+        self.dim, self.K, self.E = sh.dim, sh.n_active, sh.n_experts
+        self.xs = engine.dx_stride()
+
+    def _stream(self, t: torch.Tensor) -> int:
+        # torch's default stream has handle 0, which the library reads as
+        # "the context's own stream" (a non-blocking one, not ordered with
+        # torch's work): name the legacy default stream explicitly instead
+        # (cudaStreamLegacy == 1).
+        return torch.cuda.current_stream(t.device).cuda_stream or 1
+
+    def route(self, x: torch.Tensor):
+        T, dev = x.shape[0], x.device
+        idx = torch.empty((T, self.K), dtype=torch.int32, device=dev)
+        w = torch.empty((T, self.K), dtype=torch.float32, device=dev)
+        xq = torch.empty((T, self.dim), dtype=torch.int8, device=dev)
+        dx = torch.empty((T, self.xs), dtype=torch.float32, device=dev)
+        self.eng.route_device(x.data_ptr(), T, idx.data_ptr(), w.data_ptr(), xq.data_ptr(),
+                              dx.data_ptr(), layer=self.layer, stream=self._stream(x))
+        return idx, w, xq, dx
+
+    def experts(self, xq: torch.Tensor, dx: torch.Tensor, pair_row: torch.Tensor,
+                pair_expert: torch.Tensor) -> torch.Tensor:
+        P = pair_row.numel()
+        y = torch.empty((P, self.dim), dtype=torch.float32, device=xq.device)
+        self.eng.experts_device(xq.data_ptr(), dx.data_ptr(), xq.shape[0], pair_row.data_ptr(),
+                                pair_expert.data_ptr(), P, y.data_ptr(), layer=self.layer,
+                                stream=self._stream(xq))
+        return y
+
+    def combine(self, x: torch.Tensor, w: torch.Tensor, y: torch.Tensor) -> None:
+        self.eng.combine_device(x.data_ptr(), x.shape[0], w.data_ptr(), y.data_ptr(),
+                                stream=self._stream(x))
+
+
+def _a2a(dist, out: torch.Tensor, inp: torch.Tensor, out_splits, in_splits, group=None):
+    dist.all_to_all_single(out, inp, out_splits, in_splits, group=group)
+    return out
+
+
+class ExpertParallelMoE:
+    """The MoE block over the ranks of a process group, one GPU each.
+
+    `ops` runs the three device steps (EngineOps over this rank's MoEEngine,
+    whose store must hold at least this rank's experts).  forward() updates
+    the residual x [T][dim] (f32) in place, like miag_moe.
+    """
+
+    def __init__(self, ops, group=None):
+        import torch.distributed as dist
+
+        self.dist = dist
+        self.ops = ops
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        if ops.E % self.world:
+            raise ValueError(f"{ops.E} experts do not split evenly over {self.world} ranks")
+        self.per_rank = ops.E // self.world
+
+    def experts_of(self, rank: int) -> range:
+        return range(rank * self.per_rank, (rank + 1) * self.per_rank)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        dist, ops, G = self.dist, self.ops, self.world
+        T, K, dev = x.shape[0], ops.K, x.device
+        idx, w, xq, dx = ops.route(x)
+        plan = plan_dispatch(idx, self.per_rank, G)
+
+        # counts: rows and pairs per (source, destination)
+        cnt = torch.stack([plan.rows_per_dest, plan.pairs_per_dest], 1).to(torch.int64)  # [G, 2]
+        cnt_in = torch.empty_like(cnt)
+        _a2a(dist, cnt_in, cnt, [1] * G, [1] * G, self.group)
+        c_out, c_in = cnt.cpu(), cnt_in.cpu()
+        rows_out, pairs_out = c_out[:, 0].tolist(), c_out[:, 1].tolist()
+        rows_in, pairs_in = c_in[:, 0].tolist(), c_in[:, 1].tolist()
+        R_in, P_in = sum(rows_in), sum(pairs_in)
+
+        # dispatch: the Q8_0 rows and the pair records
+        xq_in = torch.empty((R_in, xq.shape[1]), dtype=xq.dtype, device=dev)
+        dx_in = torch.empty((R_in, dx.shape[1]), dtype=dx.dtype, device=dev)
+        meta_in = torch.empty((P_in, 2), dtype=torch.int32, device=dev)
+        _a2a(dist, xq_in, xq[plan.send_rows].contiguous(), rows_in, rows_out, self.group)
+        _a2a(dist, dx_in, dx[plan.send_rows].contiguous(), rows_in, rows_out, self.group)
+        _a2a(dist, meta_in, plan.pair_meta.contiguous(), pairs_in, pairs_out, self.group)
+
+        # a pair's row index is local to its source's block: add the block start
+        starts = torch.tensor([0] + rows_in[:-1], dtype=torch.int64, device=dev).cumsum(0)
+        src_of_pair = torch.repeat_interleave(torch.arange(G, device=dev),
+                                              torch.tensor(pairs_in, device=dev))
+        pair_row = (meta_in[:, 0].long() + starts[src_of_pair]).to(torch.int32).contiguous()
+        y_in = ops.experts(xq_in, dx_in, pair_row, meta_in[:, 1].contiguous())
+
+        # results back, then into pair order (t*K + j) for the combine
+        y_back = torch.empty((T * K, y_in.shape[1]), dtype=y_in.dtype, device=dev)
+        _a2a(dist, y_back, y_in, pairs_out, pairs_in, self.group)
+        y = torch.empty_like(y_back)
+        y[plan.pair_order] = y_back
+        ops.combine(x, w, y)
+        return x
+
+
+def simulate(ops, x: torch.Tensor, world: int) -> torch.Tensor:
+    """One process plays `world` ranks: the same plan, the exchange as local
+    copies, each virtual rank's received pairs in an expert call of their
+    own.  For tests without several GPUs.  x [G][T][dim]: each virtual
+    rank's tokens; updated in place."""
+    G, T, K = x.shape[0], x.shape[1], ops.K
+    per = ops.E // world
+    routed = []
+    for r in range(G):
+        idx, w, xq, dx = ops.route(x[r])
+        routed.append((w, xq, dx, plan_dispatch(idx, per, G)))
+    y_back = [None] * G
+    parts = [[] for _ in range(G)]
+    for g in range(G):  # destination g receives from every source, in source order
+        xq_in, dx_in, rows, exps, srcs, base = [], [], [], [], [], 0
+        for s in range(G):
+            w, xq, dx, plan = routed[s]
+            r0 = int(plan.rows_per_dest[:g].sum()); r1 = r0 + int(plan.rows_per_dest[g])
+            p0 = int(plan.pairs_per_dest[:g].sum()); p1 = p0 + int(plan.pairs_per_dest[g])
+            sel = plan.send_rows[r0:r1]
+            xq_in.append(xq[sel]); dx_in.append(dx[sel])
+            rows.append(plan.pair_meta[p0:p1, 0].long() + base)
+            exps.append(plan.pair_meta[p0:p1, 1])
+            srcs.append((s, p1 - p0))
+            base += r1 - r0
+        y_g = ops.experts(torch.cat(xq_in).contiguous(), torch.cat(dx_in).contiguous(),
+                          torch.cat(rows).to(torch.int32).contiguous(), torch.cat(exps).contiguous())
+        off = 0
+        for s, n in srcs:
+            parts[s].append(y_g[off:off + n])
+            off += n
+    for r in range(G):
+        w, xq, dx, plan = routed[r]
+        y_back[r] = torch.cat(parts[r])  # destination-major: the plan's pair order
+        y = torch.empty_like(y_back[r])
+        y[plan.pair_order] = y_back[r]
+        ops.combine(x[r], w, y)
+    return x
