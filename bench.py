@@ -23,9 +23,15 @@ batched decode of 64 tokens per GPU.  Prints ONE JSON line on rank 0.
   --impl reference  times the reference CPU implementation (all host threads)
              on the same workload and prints its own line.
 
-Multi-GPU (torchrun, N>1): every rank holds all experts and runs its own
-tokens (replicas: the block is per-token independent, so tokens shard with
-no data-path collective); scaling is weak (tokens per GPU fixed).
+Multi-GPU (torchrun, N>1), scaling weak (tokens per GPU fixed):
+  config5, the expert-parallel configuration: motoria_b200.ep.  Each rank
+    holds E/N experts (--ep-placement contiguous, as specified, or strided)
+    and routes its own tokens; (row, expert) pairs go to the experts' ranks
+    and the results come back over NCCL all-to-all; outputs equal the one-GPU
+    block bit for bit.
+  config1-3: replicas.  Every rank holds all experts and serves its own
+    batch; the block is independent per token, so there is no data-path
+    collective.
 """
 
 from __future__ import annotations
@@ -57,6 +63,7 @@ WORKLOADS = {
     "config3": ("MoE block, prefill of 2048 tokens, Zipf-biased router", 2048, False, True),
     "config5": ("MoE block, 4096 tokens per GPU, Zipf-biased router", 4096, False, True),
 }
+EP_WORKLOADS = ("config5",)  # the expert-parallel configuration; the others run replicas
 
 
 def load_peaks():
@@ -183,20 +190,24 @@ class ClockSampler:
                 "samples": len(rows)}
 
 
-def stage_bytes(shape, T, counts):
+def stage_bytes(shape, T, counts, rows=None, pairs=None):
     """Algorithmic HBM bytes per launch of each stage (weights streamed once
-    per active expert; activations read/written once)."""
+    per active expert; activations read/written once).  T tokens are routed
+    and combined here; the expert kernels see `pairs` pairs over `rows`
+    activation rows (T*K and T on one GPU; what arrived, under expert
+    parallelism)."""
     d, eh, E, K = shape.dim, shape.expert_hidden, shape.n_experts, shape.n_active
-    P = T * K
+    P = T * K if pairs is None else pairs
+    R = T if rows is None else rows
     n_act = int((counts > 0).sum())
     gu_w = 2 * eh * (d + d // 32 * 4)    # gate + up: int8 rows + f32 block scales
     dn_w = d * (eh + eh // 32 * 4)
     return {
         "route": E * d * 4 + T * d * 4 + T * (d + d // 8) + T * K * 8,
         "permute": P * 4 * 6 + E * 16,
-        "gateup": n_act * gu_w + T * (d + d // 8) + P * eh * 4,
+        "gateup": n_act * gu_w + R * (d + d // 8) + P * eh * 4,
         "down": n_act * dn_w + P * eh * 4 + P * d * 4,
-        "combine": P * d * 4 + 2 * T * d * 4 + P * 8,
+        "combine": T * K * d * 4 + 2 * T * d * 4 + T * K * 8,
     }, n_act
 
 
@@ -238,7 +249,17 @@ def run_ours(args, T_desc, T, rms, zipf):
     lay = synth.layer(shape, SEED, zipf=zipf)
     x_host = synth.tokens(shape, XSEED + 1000 * rank, T, rms_normalise=rms)
     eng = MoEEngine(shape, n_layers=1, device=local)
-    eng.load_layer(0, lay)
+    ep = None
+    if world > 1 and args.workload in EP_WORKLOADS:
+        # expert parallelism: this rank holds E/N experts (placement below)
+        from motoria_b200.ep import EngineOps, ExpertParallelMoE
+
+        ep = ExpertParallelMoE(EngineOps(eng), placement=args.ep_placement)
+        eng.set_layer(0, lay.ffn_norm, lay.router, lay.bias)
+        for e in ep.experts_of(rank):
+            eng.upload_experts(0, lay.blobs[e:e + 1], first=e)
+    else:  # one GPU, or replicas: every rank holds all experts and serves its own batch
+        eng.load_layer(0, lay)
 
     dev = torch.device("cuda", local)
     x0 = torch.from_numpy(x_host).to(dev)
@@ -266,16 +287,23 @@ def run_ours(args, T_desc, T, rms, zipf):
         flush_sink.add_(flush.sum())
         if ev:
             ev[0].record(stream)
-        eng.moe_device(x.data_ptr(), T, stream=sp)
+        if ep:
+            ep.forward(x)
+        else:
+            eng.moe_device(x.data_ptr(), T, stream=sp)
         if ev:
             ev[1].record(stream)
 
     for _ in range(args.warmup):
         one_step()
     eng.sync(sp)
-    routing = eng.routing(T)
-    per_stage_bytes, n_act = stage_bytes(shape, T, routing["counts"])
-    launches_per_step = eng.last_launch_count()
+    if ep:
+        R_in, P_in, pe = ep.last_received
+        counts = torch.bincount(pe.long(), minlength=shape.n_experts).cpu().numpy()
+        per_stage_bytes, n_act = stage_bytes(shape, T, counts, rows=R_in, pairs=P_in)
+    else:
+        routing = eng.routing(T)
+        per_stage_bytes, n_act = stage_bytes(shape, T, routing["counts"])
 
     events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
               for _ in range(args.steps)]
@@ -296,6 +324,7 @@ def run_ours(args, T_desc, T, rms, zipf):
     eng.sync(sp)
     prof = eng.profile_read()
     eng.profile(False)
+    launches_per_step = sum(v[1] for v in prof.values()) // args.steps
     t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
     if dist:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -305,14 +334,23 @@ def run_ours(args, T_desc, T, rms, zipf):
     # e2e: the public host API, pinned host buffers, H2D + D2H every step.
     xp = torch.empty((T, shape.dim), dtype=torch.float32, pin_memory=True)
     xp_np = xp.numpy()
-    for _ in range(args.warmup):
+
+    def e2e_step():
         xp_np[:] = x_host
-        eng.moe_inplace(xp_np)
+        if ep:  # H2D, the sharded block, D2H, on this rank's stream
+            x.copy_(xp, non_blocking=True)
+            ep.forward(x)
+            xp.copy_(x, non_blocking=True)
+            stream.synchronize()
+        else:
+            eng.moe_inplace(xp_np)
+
+    for _ in range(args.warmup):
+        e2e_step()
     barrier()
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        xp_np[:] = x_host
-        eng.moe_inplace(xp_np)
+        e2e_step()
     e2e_s = time.perf_counter() - t0
     te = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
     if dist:
@@ -345,7 +383,9 @@ def run_ours(args, T_desc, T, rms, zipf):
                        "expert_hidden": shape.expert_hidden, "active_experts": n_act,
                        "weights": "Q8_0 HBM-resident",
                        "l2": "flushed between steps outside the timed events (256 MiB written, then read back)",
-                       "parallelism": "replicas" if world > 1 else "single"},
+                       "parallelism": (f"ep{world} ({args.ep_placement})" if ep else
+                                       "replicas" if world > 1 else "single"),
+                       "experts_per_gpu": shape.n_experts // world if ep else shape.n_experts},
             "e2e": {"value": e2e_value, "unit": UNIT,
                     "h2d_bytes_per_step": T * shape.dim * 4,
                     "d2h_bytes_per_step": T * shape.dim * 4},
@@ -375,6 +415,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="config2")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--ep-placement", choices=["contiguous", "strided"], default="contiguous",
+                    help="expert placement of the expert-parallel run (config5, N>1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -119,8 +119,9 @@ int miag_moe_noalloc(miag_ctx *c, int layer, float *x_dev, int n_tokens,
  * miag_experts_async: the expert products of n_pairs pairs; pair p is row
  *   pair_row[p] (< n_rows) of xq/dx against expert pair_expert[p]
  *   (forward.c:186-193, SwiGLU included): y [n_pairs][dim] f32, in pair order.
- * miag_combine_async: x[t] += sum_j w[t][j] * y[t*n_active + j], j in order
- *   (forward.c:194), for t < n_tokens. */
+ * miag_combine_async: x[t] += sum_j w[t][j] * y[row(t*n_active + j)], j in
+ *   order (forward.c:194), for t < n_tokens; row(p) = y_pos[p], or p when
+ *   y_pos is NULL (y in pair order). */
 int miag_route_async(miag_ctx *c, int layer, const float *x_dev, int n_tokens,
                      int32_t *idx, float *w, int8_t *xq, float *dx, void *stream,
                      char *err, size_t errlen);
@@ -129,7 +130,8 @@ int miag_experts_async(miag_ctx *c, int layer, const int8_t *xq, const float *dx
                        const int32_t *pair_expert, int n_pairs, float *y,
                        void *stream, char *err, size_t errlen);
 int miag_combine_async(miag_ctx *c, float *x_dev, int n_tokens, const float *w,
-                       const float *y, void *stream, char *err, size_t errlen);
+                       const float *y, const int32_t *y_pos, void *stream,
+                       char *err, size_t errlen);
 /* f32 scales per row of dx: dim/32 rounded up to a multiple of four. */
 int miag_dx_stride(const miag_shape *s);
 

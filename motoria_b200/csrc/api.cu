@@ -573,7 +573,8 @@ extern "C" int miag_dx_stride(const miag_shape *s) {
 }
 
 extern "C" int miag_combine_async(miag_ctx *c, float *x_dev, int n_tokens, const float *wts,
-                                  const float *y, void *stream, char *err, size_t errlen) {
+                                  const float *y, const int32_t *y_pos, void *stream, char *err,
+                                  size_t errlen) {
     if (!c) {
         set_err(err, errlen, "null context");
         return -1;
@@ -587,7 +588,7 @@ extern "C" int miag_combine_async(miag_ctx *c, float *x_dev, int n_tokens, const
     CU(cudaSetDevice(c->device));
     const cudaStream_t s = stream ? (cudaStream_t)stream : c->stream;
     Work w{};
-    w.T = n_tokens, w.w = const_cast<float *>(wts), w.y = const_cast<float *>(y);
+    w.T = n_tokens, w.w = const_cast<float *>(wts), w.y = const_cast<float *>(y), w.y_pos = y_pos;
     run_stage(c, kCombine, 1, s, [&] { launch_combine(c->dims, w, x_dev, s); });
     CU(cudaGetLastError());
     return 0;

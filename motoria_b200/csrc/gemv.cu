@@ -574,14 +574,19 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_expert_mma(GemvParams p) {
 }
 
 // x[t] += w_j * y_j for j = 0..K-1 in order (forward.c:194).
-// y is in pair order: pair t*K + j is token t's j-th expert.
-__global__ void k_combine(float *x, int d, int K, const float *w, const float *y) {
+// Pair t*K + j is token t's j-th expert; its row of y is pos[t*K + j]
+// (pos null: y is in pair order).
+__global__ void k_combine(float *x, int d, int K, const float *w, const float *y,
+                          const int32_t *pos) {
     const int t = blockIdx.x;
     const int i = blockIdx.y * blockDim.x + threadIdx.x;
     if (i >= d) return;
     float v = x[(size_t)t * d + i];
-    for (int j = 0; j < K; j++)
-        v = __fadd_rn(v, __fmul_rn(__ldg(w + (size_t)t * K + j), y[((size_t)t * K + j) * d + i]));
+    for (int j = 0; j < K; j++) {
+        const size_t p = (size_t)t * K + j;
+        const size_t row = pos ? (size_t)__ldg(pos + p) : p;
+        v = __fadd_rn(v, __fmul_rn(__ldg(w + p), y[row * d + i]));
+    }
     x[(size_t)t * d + i] = v;
 }
 
@@ -650,7 +655,7 @@ void launch_down(const Dims &m, const StoreLayout &lay, const LayerDev &L, const
 
 void launch_combine(const Dims &m, const Work &w, float *x, cudaStream_t s) {
     dim3 grid(w.T, (m.d + 255) / 256);
-    k_combine<<<grid, 256, 0, s>>>(x, m.d, m.K, w.w, w.y);
+    k_combine<<<grid, 256, 0, s>>>(x, m.d, m.K, w.w, w.y, w.y_pos);
 }
 
 }  // namespace miag

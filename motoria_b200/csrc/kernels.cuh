@@ -28,6 +28,7 @@ struct Work {
     int32_t *tg_count;     // [T]           route: CTAs done per token group; zero between calls
     const int32_t *pair_row;  // [P]        expert products over given pairs: each pair's row of
     int n_rows;               //              xq/dx (null: pair p is row p / K, the moe() case)
+    const int32_t *y_pos;     // [P]        combine: row of y holding pair p (null: row p)
 };
 
 struct LayerDev {

@@ -164,12 +164,14 @@ class MoEEngine:
         N.check(rc, err, "miag_experts_async")
 
     def combine_device(self, x_ptr: int, n_tokens: int, w_ptr: int, y_ptr: int,
-                       stream: int | None = None) -> None:
-        """Enqueues x[t] += sum_j w[t][j] * y[t*K + j], j in order."""
+                       y_pos_ptr: int = 0, stream: int | None = None) -> None:
+        """Enqueues x[t] += sum_j w[t][j] * y[row(t*K + j)], j in order; row(p) =
+        y_pos[p], or p without y_pos."""
         err = N.errbuf()
         rc = self._lib.miag_combine_async(self._ctx, C.c_void_p(x_ptr), n_tokens,
                                           C.c_void_p(w_ptr), C.c_void_p(y_ptr),
-                                          C.c_void_p(stream or 0), err, len(err))
+                                          C.c_void_p(y_pos_ptr or 0), C.c_void_p(stream or 0),
+                                          err, len(err))
         N.check(rc, err, "miag_combine_async")
 
     def sync(self, stream: int | None = None) -> None:

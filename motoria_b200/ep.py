@@ -34,16 +34,34 @@ import torch
 
 @dataclass
 class DispatchPlan:
-    """What one rank sends, for G ranks and its T tokens of K pairs each."""
+    """What one rank sends, for G ranks and its T tokens of K pairs each.
+    Built with device operations only (no host synchronisation)."""
 
-    send_rows: torch.Tensor      # [R] token of each row sent, grouped by destination, ascending
+    row_keys: torch.Tensor       # [T*G] g*T + t of every (token, destination) row to send,
+                                 #   ascending; the first rows_per_dest.sum() are real
     rows_per_dest: torch.Tensor  # [G] rows to each destination
     pair_order: torch.Tensor     # [P] pair ids (t*K + j) grouped by destination, ascending
     pairs_per_dest: torch.Tensor  # [G]
-    pair_meta: torch.Tensor      # [P, 2] int32: (row within the destination's block, expert)
+    pair_dest: torch.Tensor      # [P] destination of each pair in pair_order
+    pair_meta: torch.Tensor      # [P, 2] int32: (row within the destination's block from
+                                 #   this rank, expert)
+
+    def send_rows(self, n: int, T: int) -> torch.Tensor:
+        """The first n row keys as token indices (n = rows_per_dest.sum())."""
+        return self.row_keys[:n] % max(T, 1)
 
 
-def plan_dispatch(idx: torch.Tensor, experts_per_rank: int, world: int) -> DispatchPlan:
+def owner(expert: torch.Tensor, experts_per_rank: int, world: int, placement: str) -> torch.Tensor:
+    """Rank holding each expert: contiguous blocks of E/G experts (the
+    specified placement), or strided, expert e on rank e mod G (spreads a
+    skewed load such as config 3's Zipf bias over the ranks)."""
+    if placement == "strided":
+        return expert % world
+    return expert // experts_per_rank
+
+
+def plan_dispatch(idx: torch.Tensor, experts_per_rank: int, world: int,
+                  placement: str = "contiguous") -> DispatchPlan:
     """idx [T][K] int32 top-k experts -> the rows and pair records to send.
 
     A row goes to a destination once however many of the token's experts
@@ -51,21 +69,23 @@ def plan_dispatch(idx: torch.Tensor, experts_per_rank: int, world: int) -> Dispa
     pair order, so every rank sees the same canonical ordering."""
     T, K = idx.shape
     dev = idx.device
-    dest = (idx.long() // experts_per_rank)                         # [T, K]
+    dest = owner(idx.long(), experts_per_rank, world, placement)      # [T, K]
     hit = torch.zeros((T, world), dtype=torch.bool, device=dev)
     hit.scatter_(1, dest, True)
     rows_per_dest = hit.sum(0)                                       # [G]
-    gt = hit.t().nonzero()                                           # [(g, t)] g-major, t ascending
-    send_rows = gt[:, 1]
+    # (g, t) keys of the hits first, ascending; misses after them
+    key = torch.arange(world, device=dev)[:, None] * T + torch.arange(T, device=dev)[None, :]
+    key = torch.where(hit.t(), key, torch.full_like(key, world * T))
+    row_keys = torch.sort(key.reshape(-1)).values
     row_in_block = hit.long().cumsum(0) - 1                          # [T, G] index of t in g's block
     pair_ids = torch.arange(T * K, device=dev)
-    key = dest.reshape(-1) * (T * K) + pair_ids                     # g-major, then pair order
-    pair_order = torch.argsort(key)
+    pkey = dest.reshape(-1) * (T * K) + pair_ids                    # g-major, then pair order
+    pair_order = torch.argsort(pkey)
     d_sorted = dest.reshape(-1)[pair_order]
     pairs_per_dest = torch.bincount(d_sorted, minlength=world)
     t_sorted = pair_order // K
     meta = torch.stack([row_in_block[t_sorted, d_sorted], idx.reshape(-1)[pair_order].long()], 1)
-    return DispatchPlan(send_rows, rows_per_dest, pair_order, pairs_per_dest,
+    return DispatchPlan(row_keys, rows_per_dest, pair_order, pairs_per_dest, d_sorted,
                         meta.to(torch.int32))
 
 
@@ -105,9 +125,11 @@ class EngineOps:
                                 stream=self._stream(xq))
         return y
 
-    def combine(self, x: torch.Tensor, w: torch.Tensor, y: torch.Tensor) -> None:
+    def combine(self, x: torch.Tensor, w: torch.Tensor, y: torch.Tensor,
+                y_pos: torch.Tensor | None = None) -> None:
+        """x[t] += sum_j w[t][j] * y[row(t*K + j)]; row(p) = y_pos[p], or p."""
         self.eng.combine_device(x.data_ptr(), x.shape[0], w.data_ptr(), y.data_ptr(),
-                                stream=self._stream(x))
+                                0 if y_pos is None else y_pos.data_ptr(), stream=self._stream(x))
 
 
 def _a2a(dist, out: torch.Tensor, inp: torch.Tensor, out_splits, in_splits, group=None):
@@ -123,61 +145,77 @@ class ExpertParallelMoE:
     the residual x [T][dim] (f32) in place, like miag_moe.
     """
 
-    def __init__(self, ops, group=None):
+    def __init__(self, ops, group=None, placement: str = "contiguous"):
         import torch.distributed as dist
 
+        if placement not in ("contiguous", "strided"):
+            raise ValueError(f"unknown placement {placement!r}")
         self.dist = dist
         self.ops = ops
         self.group = group
+        self.placement = placement
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
         if ops.E % self.world:
             raise ValueError(f"{ops.E} experts do not split evenly over {self.world} ranks")
         self.per_rank = ops.E // self.world
 
-    def experts_of(self, rank: int) -> range:
-        return range(rank * self.per_rank, (rank + 1) * self.per_rank)
+    def experts_of(self, rank: int) -> list[int]:
+        """The experts this placement puts on `rank` (its store must hold them)."""
+        if self.placement == "strided":
+            return list(range(rank, self.ops.E, self.world))
+        return list(range(rank * self.per_rank, (rank + 1) * self.per_rank))
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        dist, ops, G = self.dist, self.ops, self.world
+        dist, ops, G, me = self.dist, self.ops, self.world, self.rank
         T, K, dev = x.shape[0], ops.K, x.device
         idx, w, xq, dx = ops.route(x)
-        plan = plan_dispatch(idx, self.per_rank, G)
+        plan = plan_dispatch(idx, self.per_rank, G, self.placement)
 
-        # counts: rows and pairs per (source, destination)
+        # Every rank's (rows, pairs) per destination: one all_gather, one
+        # host synchronisation for the collectives' split sizes.
         cnt = torch.stack([plan.rows_per_dest, plan.pairs_per_dest], 1).to(torch.int64)  # [G, 2]
-        cnt_in = torch.empty_like(cnt)
-        _a2a(dist, cnt_in, cnt, [1] * G, [1] * G, self.group)
-        c_out, c_in = cnt.cpu(), cnt_in.cpu()
-        rows_out, pairs_out = c_out[:, 0].tolist(), c_out[:, 1].tolist()
-        rows_in, pairs_in = c_in[:, 0].tolist(), c_in[:, 1].tolist()
-        R_in, P_in = sum(rows_in), sum(pairs_in)
+        M = torch.empty((G * G, 2), dtype=torch.int64, device=dev)
+        dist.all_gather_into_tensor(M, cnt, group=self.group)
+        M = M.view(G, G, 2)                                              # [src, dst, (rows, pairs)]
+        # where this rank's rows start in each destination's receive buffer
+        row_start = (M[:, :, 0].cumsum(0) - M[:, :, 0])[me]              # [G]
+        Mh = M.cpu()
+        rows_out, pairs_out = Mh[me, :, 0].tolist(), Mh[me, :, 1].tolist()
+        rows_in, pairs_in = Mh[:, me, 0].tolist(), Mh[:, me, 1].tolist()
+        R_out, R_in, P_in = sum(rows_out), sum(rows_in), sum(pairs_in)
 
-        # dispatch: the Q8_0 rows and the pair records
-        xq_in = torch.empty((R_in, xq.shape[1]), dtype=xq.dtype, device=dev)
-        dx_in = torch.empty((R_in, dx.shape[1]), dtype=dx.dtype, device=dev)
+        # dispatch: each row as one record (int8 values, then the f32 block
+        # scales), and the pair records with rows numbered in the receiver
+        rows = plan.send_rows(R_out, T)
+        rec_w = xq.shape[1] + dx.shape[1] * 4
+        rec = torch.empty((R_out, rec_w), dtype=torch.uint8, device=dev)
+        rec[:, :xq.shape[1]] = xq[rows].view(torch.uint8)
+        rec[:, xq.shape[1]:] = dx[rows].view(torch.uint8)
+        meta = plan.pair_meta.clone()
+        meta[:, 0] += row_start[plan.pair_dest].to(torch.int32)
+        rec_in = torch.empty((R_in, rec_w), dtype=torch.uint8, device=dev)
         meta_in = torch.empty((P_in, 2), dtype=torch.int32, device=dev)
-        _a2a(dist, xq_in, xq[plan.send_rows].contiguous(), rows_in, rows_out, self.group)
-        _a2a(dist, dx_in, dx[plan.send_rows].contiguous(), rows_in, rows_out, self.group)
-        _a2a(dist, meta_in, plan.pair_meta.contiguous(), pairs_in, pairs_out, self.group)
+        _a2a(dist, rec_in, rec, rows_in, rows_out, self.group)
+        _a2a(dist, meta_in, meta, pairs_in, pairs_out, self.group)
+        xq_in = rec_in[:, :xq.shape[1]].contiguous().view(torch.int8)
+        dx_in = rec_in[:, xq.shape[1]:].contiguous().view(torch.float32)
+        pair_row = meta_in[:, 0].contiguous()
+        pair_expert = meta_in[:, 1].contiguous()
+        self.last_received = (R_in, P_in, pair_expert)
+        y_in = ops.experts(xq_in, dx_in, pair_row, pair_expert)
 
-        # a pair's row index is local to its source's block: add the block start
-        starts = torch.tensor([0] + rows_in[:-1], dtype=torch.int64, device=dev).cumsum(0)
-        src_of_pair = torch.repeat_interleave(torch.arange(G, device=dev),
-                                              torch.tensor(pairs_in, device=dev))
-        pair_row = (meta_in[:, 0].long() + starts[src_of_pair]).to(torch.int32).contiguous()
-        y_in = ops.experts(xq_in, dx_in, pair_row, meta_in[:, 1].contiguous())
-
-        # results back, then into pair order (t*K + j) for the combine
+        # results back in this rank's send order; the combine finds pair p at
+        # row y_pos[p] of it
         y_back = torch.empty((T * K, y_in.shape[1]), dtype=y_in.dtype, device=dev)
         _a2a(dist, y_back, y_in, pairs_out, pairs_in, self.group)
-        y = torch.empty_like(y_back)
-        y[plan.pair_order] = y_back
-        ops.combine(x, w, y)
+        y_pos = torch.empty(T * K, dtype=torch.int32, device=dev)
+        y_pos[plan.pair_order] = torch.arange(T * K, dtype=torch.int32, device=dev)
+        ops.combine(x, w, y_back, y_pos)
         return x
 
 
-def simulate(ops, x: torch.Tensor, world: int) -> torch.Tensor:
+def simulate(ops, x: torch.Tensor, world: int, placement: str = "contiguous") -> torch.Tensor:
     """One process plays `world` ranks: the same plan, the exchange as local
     copies, each virtual rank's received pairs in an expert call of their
     own.  For tests without several GPUs.  x [G][T][dim]: each virtual
@@ -187,7 +225,7 @@ def simulate(ops, x: torch.Tensor, world: int) -> torch.Tensor:
     routed = []
     for r in range(G):
         idx, w, xq, dx = ops.route(x[r])
-        routed.append((w, xq, dx, plan_dispatch(idx, per, G)))
+        routed.append((w, xq, dx, plan_dispatch(idx, per, G, placement)))
     y_back = [None] * G
     parts = [[] for _ in range(G)]
     for g in range(G):  # destination g receives from every source, in source order
@@ -196,7 +234,7 @@ def simulate(ops, x: torch.Tensor, world: int) -> torch.Tensor:
             w, xq, dx, plan = routed[s]
             r0 = int(plan.rows_per_dest[:g].sum()); r1 = r0 + int(plan.rows_per_dest[g])
             p0 = int(plan.pairs_per_dest[:g].sum()); p1 = p0 + int(plan.pairs_per_dest[g])
-            sel = plan.send_rows[r0:r1]
+            sel = plan.send_rows(int(plan.rows_per_dest.sum()), T)[r0:r1]
             xq_in.append(xq[sel]); dx_in.append(dx[sel])
             rows.append(plan.pair_meta[p0:p1, 0].long() + base)
             exps.append(plan.pair_meta[p0:p1, 1])

@@ -25,17 +25,17 @@ def main():
     shape = synth.QWEN3_30B_A3B
     T = int(os.environ.get("EP_TOKENS", "300"))
     lay = synth.layer(shape, 1234, zipf=True)
-    per = shape.n_experts // world
-    mine = range(rank * per, (rank + 1) * per)
     ep_eng = MoEEngine(shape, n_layers=1, device=local)
+    ep = ExpertParallelMoE(EngineOps(ep_eng), placement=os.environ.get("EP_PLACEMENT", "contiguous"))
     ep_eng.set_layer(0, lay.ffn_norm, lay.router, lay.bias)
-    ep_eng.upload_experts(0, lay.blobs[mine.start:mine.stop], first=mine.start)
+    for e in ep.experts_of(rank):  # only this rank's experts
+        ep_eng.upload_experts(0, lay.blobs[e:e + 1], first=e)
     full = MoEEngine(shape, n_layers=1, device=local)
     full.load_layer(0, lay)
     x_host = synth.tokens(shape, 500 + rank, T)
     want = full.moe(x_host.copy())
     x = torch.from_numpy(x_host).cuda()
-    ExpertParallelMoE(EngineOps(ep_eng)).forward(x)
+    ep.forward(x)
     torch.cuda.synchronize()
     ep_eng.sync()  # reports any device-side error of the sharded steps
     got = x.cpu().numpy()

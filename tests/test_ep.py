@@ -45,8 +45,10 @@ class FakeOps:
         r = pair_row.long()
         return xq[r].float() * (pair_expert.float() + 1)[:, None] + dx[r, :1]
 
-    def combine(self, x, w, y):
+    def combine(self, x, w, y, y_pos=None):
         T = x.shape[0]
+        if y_pos is not None:
+            y = y[y_pos.long()]
         yy = y.view(T, K, D)
         for j in range(K):
             x += w[:, j:j + 1] * yy[:, j]
@@ -71,15 +73,16 @@ def test_plan_sends_each_row_once_per_destination():
     ops = FakeOps()
     x = tokens(0, 50)
     idx = ops.route(x)[0]
-    for world in (1, 2, 4, 8):
+    for world, placement in ((1, "contiguous"), (2, "contiguous"), (4, "contiguous"),
+                             (8, "contiguous"), (4, "strided")):
         per = E // world
-        plan = plan_dispatch(idx, per, world)
-        dest = idx.long() // per
+        plan = plan_dispatch(idx, per, world, placement)
+        dest = idx.long() // per if placement == "contiguous" else idx.long() % world
         assert int(plan.pairs_per_dest.sum()) == idx.numel()
-        assert plan.send_rows.numel() == int(plan.rows_per_dest.sum())
+        assert int((plan.row_keys < world * x.shape[0]).sum()) == int(plan.rows_per_dest.sum())
         r0 = p0 = 0
         for g in range(world):
-            rows = plan.send_rows[r0:r0 + int(plan.rows_per_dest[g])]
+            rows = plan.send_rows(int(plan.rows_per_dest.sum()), x.shape[0])[r0:r0 + int(plan.rows_per_dest[g])]
             want = torch.nonzero((dest == g).any(1)).flatten()
             assert torch.equal(rows, want)              # each token once, ascending
             pairs = plan.pair_order[p0:p0 + int(plan.pairs_per_dest[g])]
@@ -87,7 +90,7 @@ def test_plan_sends_each_row_once_per_destination():
             meta = plan.pair_meta[p0:p0 + int(plan.pairs_per_dest[g])]
             assert torch.equal(rows[meta[:, 0].long()], pairs // K)   # record -> its row
             assert torch.equal(meta[:, 1], idx.reshape(-1)[pairs])
-            assert bool(((meta[:, 1] // per) == g).all())
+            assert bool((dest.reshape(-1)[pairs] == g).all())
             r0 += int(plan.rows_per_dest[g])
             p0 += int(plan.pairs_per_dest[g])
 
@@ -98,7 +101,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, T, out):
+def _worker(rank, world, port, T, placement, out):
     import torch.distributed as dist
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -106,7 +109,7 @@ def _worker(rank, world, port, T, out):
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         ops = FakeOps()
-        ep = ExpertParallelMoE(ops)
+        ep = ExpertParallelMoE(ops, placement=placement)
         x = tokens(rank, T[rank])
         want = reference(ops, x.clone())
         got = ep.forward(x.clone())
@@ -115,12 +118,15 @@ def _worker(rank, world, port, T, out):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,T", [(2, (37, 21)), (4, (9, 0, 30, 5))])
-def test_gloo_ranks_match_the_unsharded_block(world, T):
+@pytest.mark.parametrize("world,T,placement", [(2, (37, 21), "contiguous"),
+                                               (4, (9, 0, 30, 5), "contiguous"),
+                                               (4, (20, 11, 0, 7), "strided")])
+def test_gloo_ranks_match_the_unsharded_block(world, T, placement):
     ctx = torch.multiprocessing.get_context("spawn")
     out = ctx.Manager().dict()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, T, out)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, T, placement, out))
+             for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:

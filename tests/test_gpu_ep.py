@@ -50,8 +50,9 @@ def test_split_steps_equal_the_block(torch_cuda, T):
         assert np.array_equal(_bits(x.cpu().numpy()), _bits(want))
 
 
-@pytest.mark.parametrize("G", [2, 4, 8])
-def test_simulated_ranks_equal_the_block(torch_cuda, G):
+@pytest.mark.parametrize("G,placement", [(2, "contiguous"), (4, "contiguous"), (8, "contiguous"),
+                                         (4, "strided")])
+def test_simulated_ranks_equal_the_block(torch_cuda, G, placement):
     torch = torch_cuda
     lay = get_layer(QWEN, True)  # Zipf-biased: rank 0 holds the hot experts
     T = 96
@@ -60,7 +61,7 @@ def test_simulated_ranks_equal_the_block(torch_cuda, G):
         xs = np.stack([synth.tokens(QWEN, 900 + r, T) for r in range(G)])
         want = np.stack([eng.moe(xs[r].copy()) for r in range(G)])
         x = torch.from_numpy(xs).cuda()
-        simulate(EngineOps(eng), x, G)
+        simulate(EngineOps(eng), x, G, placement)
         torch.cuda.synchronize()
         eng.sync()
         assert np.array_equal(_bits(x.cpu().numpy()), _bits(want))
