@@ -198,12 +198,22 @@ __device__ void issue_iteration(const GemvParams &p, uint8_t *smem, int j) {
              (uint32_t)nkt * kUnitBytes, bar);
 }
 
+// N-tiles (of 8 pairs) the consumers run for a chunk of nq pairs.  Two
+// regimes, chosen per launch from the batch: few pairs per expert (decode)
+// runs one, two or four n-tiles; many (prefill) one or four, the set whose
+// four-tile path keeps every value in registers (three shapes in one kernel
+// spill a little, which the wide path feels and the narrow one does not).
+__host__ __device__ inline int n_tiles(int nq, bool wide) {
+    return nq <= 8 ? 1 : (!wide && nq <= 16) ? 2 : 4;
+}
+
 // Bytes of the activation region for chunks of up to nq pairs: nq int8 rows
 // at x_stride, then the pair-interleaved scale rows that the lanes of
-// ceil(nq/8) n-tiles address (four per n-tile).
-__host__ __device__ inline uint32_t region_size(int nq, int Kb, uint32_t x_stride, int xs) {
-    (void)Kb;
-    const uint32_t b = (uint32_t)nq * x_stride + 4u * (uint32_t)((nq + 7) / 8) * smem_stride((uint32_t)xs * 8);
+// n_tiles(nq) n-tiles address (four per n-tile, whether or not those pairs
+// exist).
+__host__ __device__ inline uint32_t region_size(int nq, bool wide, uint32_t x_stride, int xs) {
+    const uint32_t b = (uint32_t)nq * x_stride +
+                       4u * (uint32_t)n_tiles(nq, wide) * smem_stride((uint32_t)xs * 8);
     return (b + 127u) & ~127u;
 }
 
@@ -290,6 +300,7 @@ struct Lanes {
     uint32_t w0, w1;        // offsets of rows r0, r0 + 8 in a scale tile
     uint32_t b_off;         // ldmatrix B role: pair row lane & 7, 16-byte half
     int b_pair;
+    uint32_t b_blk;         // ldmatrix.x4 B role: lanes 16-31 load the next block
     uint32_t a_off[4];      // ldmatrix A role: swizzled offset of block j in a tile
 };
 
@@ -305,6 +316,7 @@ __device__ __forceinline__ Lanes lane_roles(int warp, int lane) {
     for (int j = 0; j < 4; j++) l.a_off[j] = tile_chunk_offset(a_row, 2 * j + a_half);
     l.b_pair = lane & 7;
     l.b_off = 16u * (uint32_t)((lane >> 3) & 1);
+    l.b_blk = (uint32_t)(lane >> 4);
     return l;
 }
 
@@ -327,26 +339,46 @@ __device__ __forceinline__ void k_tile(uint64_t (&acc)[NT][2], uint32_t tile, ui
     const float4 w0 = lds128(sc + ln.w0), w1 = lds128(sc + ln.w1);
     const uint64_t wa[4] = {pack2(w0.x, w0.x), pack2(w0.y, w0.y), pack2(w0.z, w0.z), pack2(w0.w, w0.w)};
     const uint64_t wb[4] = {pack2(w1.x, w1.x), pack2(w1.y, w1.y), pack2(w1.z, w1.z), pack2(w1.w, w1.w)};
+    // Two n-tiles at a time: both tiles' dots first, then the steps block by
+    // block across them (four independent accumulator chains per step).
 #pragma unroll
-    for (int n = 0; n < NT; n++) {
-        const uint32_t brow = b_row[n] + (uint32_t)(kt * kTileK);
-        uint32_t B[4][2];
+    for (int n0 = 0; n0 < NT; n0 += 2) {
+        constexpr int G = 2;
+        int C[G][4][4];
+        uint64_t x2[G][4];  // per n-tile and block: the scales of this lane's two pair columns
 #pragma unroll
-        for (int j = 0; j < 4; j++)
-            if (kFull || j < nbk) ldsm_x2(brow + 32 * j, B[j][0], B[j][1]);
-        uint64_t x2[4];  // per block: the scales of this lane's two pair columns
-        lds_2x64(xp[n] + 32u * (uint32_t)kt, x2[0], x2[1]);
-        lds_2x64(xp[n] + 32u * (uint32_t)kt + 16u, x2[2], x2[3]);
-        int C[4][4];
+        for (int g = 0; g < G; g++) {
+            const int n = n0 + g;
+            if (n >= NT) break;
+            const uint32_t brow = b_row[n] + (uint32_t)(kt * kTileK);
+            uint32_t B[4][2];
+            if (kFull) {
+                // one ldmatrix.x4 per two blocks: lanes 16-31 address the second block
+                const uint32_t b4 = brow + 32u * ln.b_blk;
+                ldsm_x4(b4, B[0][0], B[0][1], B[1][0], B[1][1]);
+                ldsm_x4(b4 + 64u, B[2][0], B[2][1], B[3][0], B[3][1]);
+            } else {
 #pragma unroll
-        for (int j = 0; j < 4; j++)
-            if (kFull || j < nbk) mma_s8(C[j], A[j][0], A[j][1], A[j][2], A[j][3], B[j][0], B[j][1]);
+                for (int j = 0; j < 4; j++)
+                    if (j < nbk) ldsm_x2(brow + 32 * j, B[j][0], B[j][1]);
+            }
+            lds_2x64(xp[n] + 32u * (uint32_t)kt, x2[g][0], x2[g][1]);
+            lds_2x64(xp[n] + 32u * (uint32_t)kt + 16u, x2[g][2], x2[g][3]);
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+                if (kFull || j < nbk) mma_s8(C[g][j], A[j][0], A[j][1], A[j][2], A[j][3], B[j][0], B[j][1]);
+        }
         // block order, as the reference's loop over blocks
 #pragma unroll
         for (int j = 0; j < 4; j++) {
             if (kFull || j < nbk) {
-                q8_step_x2(acc[n][0], pack2i(C[j][0], C[j][1]), wa[j], x2[j], neg_magic2, one2);
-                q8_step_x2(acc[n][1], pack2i(C[j][2], C[j][3]), wb[j], x2[j], neg_magic2, one2);
+#pragma unroll
+                for (int g = 0; g < G; g++) {
+                    const int n = n0 + g;
+                    if (n >= NT) break;
+                    q8_step_x2(acc[n][0], pack2i(C[g][j][0], C[g][j][1]), wa[j], x2[g][j], neg_magic2, one2);
+                    q8_step_x2(acc[n][1], pack2i(C[g][j][2], C[g][j][3]), wb[j], x2[g][j], neg_magic2, one2);
+                }
             }
         }
     }
@@ -485,7 +517,7 @@ __device__ __forceinline__ void run_item(const GemvParams &p, const ItemCtx &ic,
 }
 
 // gate+up (kGU) or down: one launch over all items of all active experts.
-template <bool kGU>
+template <bool kGU, bool kWide>
 __global__ void __launch_bounds__(kGemvThreads, 1) k_expert_mma(GemvParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     const int d = p.m.d, eh = p.m.eh;
@@ -518,7 +550,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_expert_mma(GemvParams p) {
     }
     atomicMax(&head->nq_max, my_nq);
     __syncthreads();
-    const uint32_t region_bytes = region_size(head->nq_max, Kb, p.x_stride, xs);
+    const uint32_t region_bytes = region_size(head->nq_max, kWide, p.x_stride, xs);
     const int S = min(kMaxStages, (int)((kSmemBudget - kRingOff - (int)region_bytes) / kStageBytes));
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; s++) {
@@ -557,12 +589,13 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_expert_mma(GemvParams p) {
             consumer_sync();
         }
         ic.rt = ii.rt, ic.seg0 = seg0, ic.t0 = t0, ic.nq = nq;
-        switch ((nq + 7) >> 3) {
-            case 1: run_item<kGU, 1>(p, ic, ln, smem, rp, failed); break;
-            case 2: run_item<kGU, 2>(p, ic, ln, smem, rp, failed); break;
-            case 3: run_item<kGU, 3>(p, ic, ln, smem, rp, failed); break;
-            default: run_item<kGU, 4>(p, ic, ln, smem, rp, failed); break;
-        }
+        // Two tile shapes (more do not fit the registers without spilling):
+        // one n-tile of 8 pairs, or four (32 pairs; columns past nq are
+        // computed on repeated rows and not written).
+        const int nt = n_tiles(nq, kWide);
+        if (nt == 1) run_item<kGU, 1>(p, ic, ln, smem, rp, failed);
+        else if (!kWide && nt == 2) run_item<kGU, kWide ? 4 : 2>(p, ic, ln, smem, rp, failed);
+        else run_item<kGU, 4>(p, ic, ln, smem, rp, failed);
     }
     // After a timed-out wait, let every issued copy land (bounded) before the
     // CTA's shared memory goes away.  All refills are issued by now.
@@ -611,7 +644,8 @@ static int geometry(GemvParams &p, bool gu) {
     const int Kb = gu ? p.m.d : p.m.eh;
     const int xs = scale_pad(Kb / MIAG_QK);
     p.x_stride = smem_stride((uint32_t)Kb);
-    const long room = (long)kSmemBudget - kRingOff - (long)region_size(kTokChunk, Kb, p.x_stride, xs);
+    const long room =
+        (long)kSmemBudget - kRingOff - (long)region_size(kTokChunk, true, p.x_stride, xs);
     return room > 0 ? (int)(room / kStageBytes) : 0;
 }
 
@@ -623,13 +657,18 @@ int gemv_setup_attributes(const Dims &m, const StoreLayout &lay) {
     p.m = m, p.lay = lay;
     if (lay.gu_rt > 255 || lay.dn_rt > 255) return -1;  // the item table packs rt in 8 bits
     if (geometry(p, true) < 2 || geometry(p, false) < 2) return -1;
-    if (cudaFuncSetAttribute(k_expert_mma<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kSmemBudget) != cudaSuccess ||
-        cudaFuncSetAttribute(k_expert_mma<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kSmemBudget) != cudaSuccess)
+    const auto attr = cudaFuncAttributeMaxDynamicSharedMemorySize;
+    if (cudaFuncSetAttribute(k_expert_mma<true, false>, attr, kSmemBudget) != cudaSuccess ||
+        cudaFuncSetAttribute(k_expert_mma<true, true>, attr, kSmemBudget) != cudaSuccess ||
+        cudaFuncSetAttribute(k_expert_mma<false, false>, attr, kSmemBudget) != cudaSuccess ||
+        cudaFuncSetAttribute(k_expert_mma<false, true>, attr, kSmemBudget) != cudaSuccess)
         return -1;
     return 0;
 }
+
+// The prefill regime once an expert gets more than one n-tile of pairs on
+// average.
+static bool wide_regime(const Dims &m, const Work &w) { return (long)w.P > 8L * m.E; }
 
 static int grid_for(const Dims &m, int RT, int num_sms, int P) {
     // items <= RT * (chunks), chunks <= P / kTokChunk + (active experts)
@@ -642,7 +681,9 @@ void launch_gateup(const Dims &m, const StoreLayout &lay, const LayerDev &L, con
     GemvParams p{};
     fill_params(p, m, lay, L, w, err);
     geometry(p, true);
-    k_expert_mma<true><<<grid_for(m, lay.gu_rt, num_sms, w.P), kGemvThreads, kSmemBudget, s>>>(p);
+    const dim3 grid(grid_for(m, lay.gu_rt, num_sms, w.P));
+    if (wide_regime(m, w)) k_expert_mma<true, true><<<grid, kGemvThreads, kSmemBudget, s>>>(p);
+    else k_expert_mma<true, false><<<grid, kGemvThreads, kSmemBudget, s>>>(p);
 }
 
 void launch_down(const Dims &m, const StoreLayout &lay, const LayerDev &L, const Work &w,
@@ -650,7 +691,9 @@ void launch_down(const Dims &m, const StoreLayout &lay, const LayerDev &L, const
     GemvParams p{};
     fill_params(p, m, lay, L, w, err);
     geometry(p, false);
-    k_expert_mma<false><<<grid_for(m, lay.dn_rt, num_sms, w.P), kGemvThreads, kSmemBudget, s>>>(p);
+    const dim3 grid(grid_for(m, lay.dn_rt, num_sms, w.P));
+    if (wide_regime(m, w)) k_expert_mma<false, true><<<grid, kGemvThreads, kSmemBudget, s>>>(p);
+    else k_expert_mma<false, false><<<grid, kGemvThreads, kSmemBudget, s>>>(p);
 }
 
 void launch_combine(const Dims &m, const Work &w, float *x, cudaStream_t s) {
