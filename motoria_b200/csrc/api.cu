@@ -579,8 +579,9 @@ extern "C" int miag_combine_async(miag_ctx *c, float *x_dev, int n_tokens, const
         set_err(err, errlen, "null context");
         return -1;
     }
-    if (n_tokens < 0 || (n_tokens > 0 && (!x_dev || !wts || !y))) {
-        set_err(err, errlen, "bad buffers (device pointers)");
+    if (n_tokens < 0 || (n_tokens > 0 && (!x_dev || !wts || !y)) || ((uintptr_t)x_dev & 15u) ||
+        ((uintptr_t)y & 15u)) {
+        set_err(err, errlen, "bad buffers (device pointers; x and y 16-byte aligned)");
         return -1;
     }
     c->last_launches = 0;

@@ -608,19 +608,38 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_expert_mma(GemvParams p) {
 
 // x[t] += w_j * y_j for j = 0..K-1 in order (forward.c:194).
 // Pair t*K + j is token t's j-th expert; its row of y is pos[t*K + j]
-// (pos null: y is in pair order).
+// (pos null: y is in pair order).  A thread owns four columns (d % 4 == 0)
+// and loads all K of its y rows before the ordered adds.
+constexpr int kCombineMaxK = 16;
 __global__ void k_combine(float *x, int d, int K, const float *w, const float *y,
                           const int32_t *pos) {
     const int t = blockIdx.x;
-    const int i = blockIdx.y * blockDim.x + threadIdx.x;
+    const int i = 4 * (blockIdx.y * blockDim.x + threadIdx.x);
     if (i >= d) return;
-    float v = x[(size_t)t * d + i];
-    for (int j = 0; j < K; j++) {
-        const size_t p = (size_t)t * K + j;
-        const size_t row = pos ? (size_t)__ldg(pos + p) : p;
-        v = __fadd_rn(v, __fmul_rn(__ldg(w + p), y[row * d + i]));
+    float4 v = *reinterpret_cast<const float4 *>(x + (size_t)t * d + i);
+    for (int j0 = 0; j0 < K; j0 += kCombineMaxK) {  // slots in order, 16 loads in flight
+        float4 yv[kCombineMaxK];
+        float wv[kCombineMaxK];
+#pragma unroll
+        for (int u = 0; u < kCombineMaxK; u++) {
+            if (j0 + u < K) {
+                const size_t p = (size_t)t * K + j0 + u;
+                const size_t row = pos ? (size_t)__ldg(pos + p) : p;
+                wv[u] = __ldg(w + p);
+                yv[u] = __ldcs(reinterpret_cast<const float4 *>(y + row * d + i));
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kCombineMaxK; u++) {
+            if (j0 + u < K) {
+                v.x = __fadd_rn(v.x, __fmul_rn(wv[u], yv[u].x));
+                v.y = __fadd_rn(v.y, __fmul_rn(wv[u], yv[u].y));
+                v.z = __fadd_rn(v.z, __fmul_rn(wv[u], yv[u].z));
+                v.w = __fadd_rn(v.w, __fmul_rn(wv[u], yv[u].w));
+            }
+        }
     }
-    x[(size_t)t * d + i] = v;
+    *reinterpret_cast<float4 *>(x + (size_t)t * d + i) = v;
 }
 
 // ---------------------------------------------------------------------------
@@ -697,8 +716,8 @@ void launch_down(const Dims &m, const StoreLayout &lay, const LayerDev &L, const
 }
 
 void launch_combine(const Dims &m, const Work &w, float *x, cudaStream_t s) {
-    dim3 grid(w.T, (m.d + 255) / 256);
-    k_combine<<<grid, 256, 0, s>>>(x, m.d, m.K, w.w, w.y, w.y_pos);
+    dim3 grid(w.T, (m.d / 4 + 127) / 128);
+    k_combine<<<grid, 128, 0, s>>>(x, m.d, m.K, w.w, w.y, w.y_pos);
 }
 
 }  // namespace miag

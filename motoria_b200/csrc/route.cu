@@ -73,15 +73,14 @@ struct RouteParams {
 };
 
 constexpr int kRouteChunk = 256;  // router rows per bulk copy: 256 x 128 B = 32 KiB
-constexpr int kRouteStages = 4;
+constexpr int kRouteStages = 4;   // ring depth at most (a launch may use fewer)
 
-// Shared memory: barriers | ring [kRouteStages][kRouteChunk][32] f32 |
+// Shared memory: barriers | ring [stages][kRouteChunk][32] f32 |
 // x, then xn in place [W*R][d] f32 | ffn_norm [d] f32.  After the router loop
 // the ring is free and holds the top-k scratch, E floats per warp.
 constexpr int kRouteBarBytes = 256;
-__host__ __device__ inline size_t route_smem(int d, int E, int R, int W) {
-    (void)E;
-    return kRouteBarBytes + (size_t)kRouteStages * kRouteChunk * 128 + (size_t)W * R * d * 4 +
+__host__ __device__ inline size_t route_smem(int d, int R, int W, int stages) {
+    return kRouteBarBytes + (size_t)stages * kRouteChunk * 128 + (size_t)W * R * d * 4 +
            (size_t)d * 4;
 }
 
@@ -116,7 +115,7 @@ __device__ __forceinline__ void router_rows64(float (&acc)[R], const float *wc, 
 // group's router slice.  The last of a token group's CTAs to finish its
 // logits also runs softmax / top-k / renormalisation for the group's tokens.
 template <int R>
-__global__ void __launch_bounds__(9 * 32, 1) k_route(RouteParams p, int W) {
+__global__ void __launch_bounds__(9 * 32, 1) k_route(RouteParams p, int W, int stages) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int d = p.m.d, E = p.m.E;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -124,14 +123,14 @@ __global__ void __launch_bounds__(9 * 32, 1) k_route(RouteParams p, int W) {
     uint64_t *empty = full + kRouteStages;
     int *last_flag = reinterpret_cast<int *>(empty + kRouteStages);
     float *ring = reinterpret_cast<float *>(smem + kRouteBarBytes);
-    float *xs_all = ring + (size_t)kRouteStages * kRouteChunk * 32;  // [W*R][d]
+    float *xs_all = ring + (size_t)stages * kRouteChunk * 32;  // [W*R][d]
     float *norm = xs_all + (size_t)W * R * d;
     const int nchunks = (d + kRouteChunk - 1) / kRouteChunk;
     const float *slice = p.L.router_t + (size_t)blockIdx.y * d * 32;
     const int tg0 = blockIdx.x * W * R;                 // first token of the CTA
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kRouteStages; s++) {
+        for (int s = 0; s < stages; s++) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], W);
         }
@@ -145,11 +144,11 @@ __global__ void __launch_bounds__(9 * 32, 1) k_route(RouteParams p, int W) {
         // so small chunks cap the SM's ingest).
         if (lane == 0) {
             for (int ch = 0; ch < nchunks; ch++) {
-                const int s = ch % kRouteStages, round = ch / kRouteStages;
+                const int s = ch % stages, round = ch / stages;
                 if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1)) {
                     set_error(p.err, kErrWaitEmpty);
-                    for (int j = ch - 1; j >= 0 && j >= ch - kRouteStages; j--)
-                        mbar_wait(&full[j % kRouteStages], (j / kRouteStages) & 1);
+                    for (int j = ch - 1; j >= 0 && j >= ch - stages; j--)
+                        mbar_wait(&full[j % stages], (j / stages) & 1);
                     break;
                 }
                 const int rows = min(kRouteChunk, d - ch * kRouteChunk);
@@ -293,10 +292,10 @@ __global__ void __launch_bounds__(9 * 32, 1) k_route(RouteParams p, int W) {
 #pragma unroll
     for (int r = 0; r < R; r++) acc[r] = 0.0f;
     for (int ch = 0; ch < nchunks; ch++) {
-        const int s = ch % kRouteStages;
+        const int s = ch % stages;
         if (!failed) {
             bool got = true;
-            if (lane == 0) got = mbar_wait(&full[s], (ch / kRouteStages) & 1);
+            if (lane == 0) got = mbar_wait(&full[s], (ch / stages) & 1);
             if (!__shfl_sync(0xffffffffu, got, 0)) {
                 set_error(p.err, kErrWaitFull);
                 failed = true;
@@ -354,14 +353,22 @@ __global__ void __launch_bounds__(9 * 32, 1) k_route(RouteParams p, int W) {
     }
 }
 
-// Tokens per warp R and consumer warps W by batch size.  The warps of a CTA
-// all read each router row from shared memory, and four of them (with the
-// ring's own fill) saturate it, so few-token batches use two warps of one
-// token each and more CTAs; larger ones two tokens per warp, which reads a
-// row once for both (eight token rows fit beside the 128 KiB ring).
-static void route_shape(int T, int &R, int &W) {
-    if (T <= 128) R = 1, W = 2;
-    else R = 2, W = 4;
+// Tokens per warp R, consumer warps W and ring depth by batch size.  The
+// warps of a CTA all read each router row from shared memory, and four of
+// them (with the ring's own fill) saturate it, so few-token batches use two
+// warps of one token each and more CTAs.  Larger batches put more tokens on
+// a warp, which reads a row once for all of them; their rows then take the
+// shared memory a deeper ring would.
+static void route_shape(int T, int &R, int &W, int &stages) {
+    if (T <= 128) R = 1, W = 2, stages = 4;
+    else R = 2, W = 8, stages = 2;  // B200 sweep at T = 300..2048: best of R 2-4, W 1-8
+}
+
+template <int R>
+static void launch_r(const RouteParams &p, dim3 grid, int W, int stages, size_t smem,
+                     cudaStream_t s) {
+    cudaFuncSetAttribute(k_route<R>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    k_route<R><<<grid, (W + 1) * 32, smem, s>>>(p, W, stages);
 }
 
 void launch_route(const Dims &m, const LayerDev &L, const float *x, const Work &w, int *err,
@@ -370,21 +377,13 @@ void launch_route(const Dims &m, const LayerDev &L, const float *x, const Work &
     p.m = m, p.L = L, p.x = x, p.T = w.T;
     p.xq = w.xq, p.dx = w.dx, p.logits = w.logits, p.idx = w.idx, p.w = w.w;
     p.tg_count = w.tg_count, p.err = err;
-    int R, W;
-    route_shape(w.T, R, W);
-    dim3 grid((w.T + R * W - 1) / (R * W), (m.E + 31) / 32);
-    const size_t smem = route_smem(m.d, m.E, R, W);
-    const int threads = (W + 1) * 32;
-    switch (R) {
-        case 1:
-            cudaFuncSetAttribute(k_route<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            k_route<1><<<grid, threads, smem, s>>>(p, W);
-            break;
-        default:
-            cudaFuncSetAttribute(k_route<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            k_route<2><<<grid, threads, smem, s>>>(p, W);
-            break;
-    }
+    int R, W, stages;
+    route_shape(w.T, R, W, stages);
+    const dim3 grid((w.T + R * W - 1) / (R * W), (m.E + 31) / 32);
+    const size_t smem = route_smem(m.d, R, W, stages);
+    if (R == 1) launch_r<1>(p, grid, W, stages, smem, s);
+    else if (R == 2) launch_r<2>(p, grid, W, stages, smem, s);
+    else launch_r<4>(p, grid, W, stages, smem, s);
 }
 
 }  // namespace miag
