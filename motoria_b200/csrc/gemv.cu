@@ -153,13 +153,11 @@ __device__ __forceinline__ ItemInfo decode_item(const GemvParams &p, int nact, i
     return it;
 }
 
-// The head of the CTA's shared memory: the ring's barriers and counters, and
-// what a refill needs to know about the CTA's item range.
+// The head of the CTA's shared memory: the ring's barriers and release
+// counters, and the CTA's largest pair chunk.
 struct RingHead {
     uint64_t full[kMaxStages];      // stage holds its k tiles (TMA complete_tx)
     uint32_t released[kMaxStages];  // warps done with the stage, summed over rounds
-    int first, total, nact;         // first item, stages to stream, active experts
-    int S;                          // this CTA's ring depth
     int nq_max;                     // largest pair chunk among this CTA's items
 };
 static_assert(sizeof(RingHead) <= kBarBytes, "ring head");
@@ -177,25 +175,69 @@ __device__ __forceinline__ ItemInfo item_at(const GemvParams &p, const int2 *tab
     return decode_item(p, nact, RT, item);
 }
 
-// Issues the bulk copies of ring iteration j (item first + j / NS, k stage
-// j % NS) into its stage s = j % S, completing on full[s].
-template <bool kGU>
-__device__ void issue_iteration(const GemvParams &p, uint8_t *smem, int j) {
+// Item k of this CTA as its table entry (e, rt | tc << 8).
+__device__ __forceinline__ int2 item_entry(const GemvParams &p, const int2 *table, int first,
+                                           int nact, int RT, int k) {
+    if (k < kItemTable) return table[k];
+    const ItemInfo ii = decode_item(p, nact, RT, first + k);
+    return make_int2(ii.e, ii.rt | (ii.tc << 8));
+}
+
+// The CTA's copy stream: iteration j brings k stage ks of its item k
+// (counted from the CTA's first item) into ring stage j % S.
+//
+// Every warp walks its own Feed in step with its ring position, S
+// iterations ahead, so the warp that frees a stage last issues the refill
+// straight from registers.  (Working the source out at that moment -- three
+// runtime divisions and a table read queued behind the tile loads of the
+// other warps -- cost about as much as the copy's whole k-stage of compute,
+// and it fell on the one warp that, being slowed by it, stayed the last.)
+struct FeedCtx {
+    const uint8_t *weights;  // this matrix (gate/up or down) of expert 0
+    const int2 *table;
+    size_t expert_bytes;
+    int first, n_mine, nact, RT, KT, NS;
+};
+
+struct Feed {
+    const uint8_t *src;  // bytes of iteration j
+    int j, ks, k;
+    int2 next;           // table entry of item k + 1
+};
+
+__device__ __forceinline__ const uint8_t *item_src(const FeedCtx &fc, int2 v) {
+    return fc.weights + (size_t)v.x * fc.expert_bytes + (size_t)(v.y & 255) * fc.KT * kUnitBytes;
+}
+
+__device__ __forceinline__ Feed feed_at(const GemvParams &p, const FeedCtx &fc, int j0) {
+    Feed f;
+    f.j = j0, f.k = j0 / fc.NS, f.ks = j0 % fc.NS;
+    f.src = f.k < fc.n_mine
+                ? item_src(fc, item_entry(p, fc.table, fc.first, fc.nact, fc.RT, f.k)) +
+                      (size_t)f.ks * kStageBytes
+                : nullptr;
+    f.next = f.k + 1 < fc.n_mine ? item_entry(p, fc.table, fc.first, fc.nact, fc.RT, f.k + 1)
+                                 : make_int2(0, 0);
+    return f;
+}
+
+__device__ __forceinline__ void feed_next(const GemvParams &p, const FeedCtx &fc, Feed &f) {
+    f.j++;
+    if (++f.ks == fc.NS) {
+        f.ks = 0, f.k++;
+        f.src = item_src(fc, f.next);
+        if (f.k + 1 < fc.n_mine) f.next = item_entry(p, fc.table, fc.first, fc.nact, fc.RT, f.k + 1);
+    } else {
+        f.src += kStageBytes;
+    }
+}
+
+// Issues iteration f.j into stage s, completing on its full barrier.
+__device__ __forceinline__ void feed_issue(const FeedCtx &fc, const Feed &f, uint8_t *smem, int s) {
     RingHead *h = reinterpret_cast<RingHead *>(smem);
-    const int RT = kGU ? p.lay.gu_rt : p.lay.dn_rt;
-    const int KT = kGU ? p.lay.gu_kt : p.lay.dn_kt;
-    const int NS = (KT + kStageKT - 1) / kStageKT;
-    const int s = j % h->S, ks = j % NS;
-    const ItemInfo ii = item_at(p, reinterpret_cast<const int2 *>(smem + kBarBytes), h->first,
-                                h->nact, RT, h->first + j / NS);
-    const uint8_t *base = p.experts + (size_t)ii.e * p.lay.expert_bytes;
-    const int kt0 = ks * kStageKT, nkt = min(kStageKT, KT - kt0);
-    const size_t unit = (size_t)ii.rt * KT + kt0;
-    uint8_t *dst = smem + kRingOff + (size_t)s * kStageBytes;
-    uint64_t *bar = &h->full[s];
-    mbar_arrive_expect_tx(bar, (uint32_t)nkt * kUnitBytes);
-    bulk_g2s(dst, base + (kGU ? p.lay.gu_off : p.lay.dn_off) + unit * kUnitBytes,
-             (uint32_t)nkt * kUnitBytes, bar);
+    const uint32_t bytes = (uint32_t)min(kStageKT, fc.KT - f.ks * kStageKT) * kUnitBytes;
+    mbar_arrive_expect_tx(&h->full[s], bytes);
+    bulk_g2s(smem + kRingOff + (size_t)s * kStageBytes, f.src, bytes, &h->full[s]);
 }
 
 // N-tiles (of 8 pairs) the consumers run for a chunk of nq pairs.  Two
@@ -390,6 +432,7 @@ struct ItemCtx {
     uint32_t x_rows, x_scl;  // shared addresses of the activation rows / scale rows
     uint32_t xpp_bytes;      // stride of the scale rows (one per pair of pairs)
     int S, KT, NS, nb, rows;
+    int total;               // iterations this CTA streams
     int rt, seg0, t0, nq;    // the item: row tile, expert segment, first pair, pairs
 };
 
@@ -408,12 +451,13 @@ struct RingPos {
 //
 // There is no producer warp.  Thread 0 issues the first S stages; after
 // that, the warp that is the last of the eight to finish with a stage
-// refills it with the iteration S ahead.  With eight warps per CTA the
+// refills it with the iteration S ahead, which its Feed holds.  With eight warps per CTA the
 // register file allows 255 registers a thread (a ninth warp capped it at
 // 168, which the tile shapes exceed).
 template <bool kGU, int NT>
 __device__ __forceinline__ void run_item(const GemvParams &p, const ItemCtx &ic, const Lanes &ln,
-                                         uint8_t *smem, RingPos &rp, bool &failed) {
+                                         uint8_t *smem, RingPos &rp, const FeedCtx &fc, Feed &fd,
+                                         bool &failed) {
     RingHead *head = reinterpret_cast<RingHead *>(smem);
     const int lane = threadIdx.x & 31;
     const int nq = ic.nq;
@@ -463,12 +507,13 @@ __device__ __forceinline__ void run_item(const GemvParams &p, const ItemCtx &ic,
             // release the stage; the eighth release of a round refills it
             __threadfence_block();
             const uint32_t done = atomicAdd(&head->released[s], 1u);
-            if ((done % kConsumerWarps) == kConsumerWarps - 1 && rp.it + ic.S < head->total) {
+            if ((done % kConsumerWarps) == kConsumerWarps - 1 && fd.j < ic.total) {
                 __threadfence_block();
                 fence_proxy_async_smem();
-                issue_iteration<kGU>(p, smem, rp.it + ic.S);
+                feed_issue(fc, fd, smem, s);
             }
         }
+        feed_next(p, fc, fd);
     }
 
     // outputs: this lane holds rows r0, r0 + 8 x pairs 8n + 2tq, 8n + 2tq + 1
@@ -557,12 +602,19 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_expert_mma(GemvParams p) {
             mbar_init(&head->full[s], 1);
             head->released[s] = 0;
         }
-        head->first = first, head->total = n_mine * NS, head->nact = nact, head->S = S;
         fence_barrier_init();
     }
     __syncthreads();
-    if (threadIdx.x == 0)
-        for (int j = 0; j < min(S, n_mine * NS); j++) issue_iteration<kGU>(p, smem, j);
+    FeedCtx fc;
+    fc.weights = p.experts + (kGU ? p.lay.gu_off : p.lay.dn_off);
+    fc.table = table, fc.expert_bytes = p.lay.expert_bytes;
+    fc.first = first, fc.n_mine = n_mine, fc.nact = nact, fc.RT = RT, fc.KT = KT, fc.NS = NS;
+    const int total = n_mine * NS;
+    if (threadIdx.x == 0) {
+        Feed f = feed_at(p, fc, 0);
+        for (int j = 0; j < min(S, total); j++, feed_next(p, fc, f)) feed_issue(fc, f, smem, j);
+    }
+    Feed fd = feed_at(p, fc, S);  // the refill of iteration 0
 
     // ---- consumers
     uint8_t *region = smem + kRingOff + (size_t)S * kStageBytes;
@@ -572,7 +624,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_expert_mma(GemvParams p) {
     ic.x_rows = smem_addr(region);
     ic.x_scl = ic.x_rows + (uint32_t)head->nq_max * p.x_stride;
     ic.xpp_bytes = smem_stride((uint32_t)xs * 8);
-    ic.S = S, ic.KT = KT, ic.NS = NS, ic.nb = nb, ic.rows = rows;
+    ic.S = S, ic.KT = KT, ic.NS = NS, ic.nb = nb, ic.rows = rows, ic.total = total;
 
     int cur_e = -1, cur_tc = -1;
     RingPos rp{0, 0, 0u};
@@ -593,14 +645,13 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_expert_mma(GemvParams p) {
         // one n-tile of 8 pairs, or four (32 pairs; columns past nq are
         // computed on repeated rows and not written).
         const int nt = n_tiles(nq, kWide);
-        if (nt == 1) run_item<kGU, 1>(p, ic, ln, smem, rp, failed);
-        else if (!kWide && nt == 2) run_item<kGU, kWide ? 4 : 2>(p, ic, ln, smem, rp, failed);
-        else run_item<kGU, 4>(p, ic, ln, smem, rp, failed);
+        if (nt == 1) run_item<kGU, 1>(p, ic, ln, smem, rp, fc, fd, failed);
+        else if (!kWide && nt == 2) run_item<kGU, kWide ? 4 : 2>(p, ic, ln, smem, rp, fc, fd, failed);
+        else run_item<kGU, 4>(p, ic, ln, smem, rp, fc, fd, failed);
     }
     // After a timed-out wait, let every issued copy land (bounded) before the
     // CTA's shared memory goes away.  All refills are issued by now.
     if (__syncthreads_or(failed) && threadIdx.x == 0) {
-        const int total = n_mine * NS;
         for (int j = total - 1; j >= 0 && j >= total - S; j--)
             mbar_wait(&head->full[j % S], (j / S) & 1);
     }
