@@ -95,9 +95,9 @@ int miag_moe_async(miag_ctx *c, int layer, float *x_dev, int n_tokens,
  * the middle of a step (miag_moe_async grows its workspace with cudaMalloc
  * when a batch is larger than any before it).  Same kernels and results as
  * miag_moe_async; x_dev and stream as there.  The scratch is one fixed
- * 8 MiB array inside the loaded library, held by every GPU that loads
- * libmiag until the process exits, which bounds a batch to about 90 tokens
- * at Qwen3-30B-A3B shapes; larger batches return -1 with a message.  The
+ * 11 MiB array inside the loaded library, held by every GPU that loads
+ * libmiag until the process exits, which bounds a batch to 92 tokens at
+ * Qwen3-30B-A3B shapes; larger batches return -1 with a message.  The
  * first call on a device looks the array's address up (make it before any
  * stream capture).  All calls share the array, so calls whose work overlaps
  * on the GPU race on it and must be serialised by the caller. */

@@ -387,7 +387,9 @@ static size_t ws_layout(miag_ctx *c, int T, uint8_t *base, Work *w, float **x_de
     v.chunk_pre = (int32_t *)bump(p, (size_t)(m.E + 1) * 4);
     v.perm = (int32_t *)bump(p, P * 4);
     v.inv = (int32_t *)bump(p, P * 4);
-    v.h = (float *)bump(p, P * m.eh * 4);
+    v.h = (float *)bump(p, P * 2 * m.eh * 4);
+    v.hq = (int8_t *)bump(p, P * m.eh);
+    v.hs = (float *)bump(p, P * scale_pad(m.eh / MIAG_QK) * 4);
     v.y = (float *)bump(p, P * m.d * 4);
     float *xd = (float *)bump(p, (size_t)T * m.d * 4);
     if (w) *w = v;
@@ -435,7 +437,7 @@ static int enqueue_moe(miag_ctx *c, int layer, float *x_dev, int T, cudaStream_t
               [&] { launch_permute(c->dims, w, c->d_err, s); });
     run_stage(c, kGateUp, 1, s,
               [&] { launch_gateup(c->dims, c->lay, L, w, c->num_sms, c->d_err, s); });
-    run_stage(c, kDown, 1, s,
+    run_stage(c, kDown, 2, s,
               [&] { launch_down(c->dims, c->lay, L, w, c->num_sms, c->d_err, s); });
     run_stage(c, kCombine, 1, s, [&] { launch_combine(c->dims, w, x_dev, s); });
     c->last_T = T;
@@ -562,7 +564,7 @@ extern "C" int miag_experts_async(miag_ctx *c, int layer, const int8_t *xq, cons
               [&] { launch_permute(c->dims, w, c->d_err, s); });
     run_stage(c, kGateUp, 1, s,
               [&] { launch_gateup(c->dims, c->lay, L, w, c->num_sms, c->d_err, s); });
-    run_stage(c, kDown, 1, s,
+    run_stage(c, kDown, 2, s,
               [&] { launch_down(c->dims, c->lay, L, w, c->num_sms, c->d_err, s); });
     CU(cudaGetLastError());
     return 0;

@@ -2,8 +2,9 @@
 //
 // Reference: the three mia_matvec calls per active expert in moe()
 // (src/model/forward.c:186-193) -> rows_kernel (src/tensor/matmul.c:75-80)
-// -> dot_q8_scalar (:19-28); SwiGLU :188-191; re-quantization of h inside
-// mia_matvec (:93, quant.c:11-27, done while staging h); weighted combine :194.
+// -> dot_q8_scalar (:19-28); SwiGLU :188-191 and the re-quantization of h
+// inside mia_matvec (:93, quant.c:11-27) in k_swiglu_q8 between the two
+// expert launches; weighted combine :194.
 //
 // Work is grouped by expert: every weight tile is read from HBM once per
 // group of up to 32 of that expert's (token, slot) pairs.  An item is
@@ -33,8 +34,8 @@ namespace miag {
 constexpr int kConsumerWarps = 8;
 constexpr int kConsumers = kConsumerWarps * 32;
 constexpr int kGemvThreads = kConsumers;  // no producer warp: see run_item
-constexpr int kItemTable = 512;           // decoded items cached per CTA
-constexpr int kTableBytes = kItemTable * 8;
+constexpr int kItemTable = 256;           // decoded items cached per CTA
+constexpr int kTableBytes = kItemTable * 16;
 constexpr int kStageKT = 2;  // k tiles per stage
 constexpr int kStageBytes = kStageKT * kUnitBytes;  // one bulk copy
 constexpr int kMaxStages = 12;
@@ -52,7 +53,9 @@ struct GemvParams {
     const float *dx;   // [rows][xs]
     const int32_t *pair_row;  // [P] activation row of each pair, or null: pair / K
     int n_rows;        // rows of xq / dx
-    float *h;          // [P][eh], sorted order
+    float *h;          // [P][2 eh] gate/up products (gate even, up odd), sorted order
+    const int8_t *hq;  // [P][eh]   Q8_0 h = silu(gate) * up, sorted order (down's input)
+    const float *hs;   // [P][xs]   its block scales
     float *y;          // [P][d], pair order
     int stages;
     uint32_t x_stride;         // row stride of the staged activations
@@ -139,8 +142,10 @@ __device__ __forceinline__ int find_active(const int32_t *chunk_pre, int nact, i
     return lo;
 }
 
+// An item: expert e, row tile rt, pair chunk tc, which covers pairs
+// [seg0 + 32 tc, + nq) of the expert-sorted order.
 struct ItemInfo {
-    int e, rt, tc;
+    int e, rt, tc, seg0, nq;
 };
 
 __device__ __forceinline__ ItemInfo decode_item(const GemvParams &p, int nact, int RT, int item) {
@@ -150,7 +155,19 @@ __device__ __forceinline__ ItemInfo decode_item(const GemvParams &p, int nact, i
     it.e = __ldg(p.active + a);
     it.tc = local / RT;
     it.rt = local % RT;
+    it.seg0 = __ldg(p.offsets + it.e);
+    it.nq = min(kTokChunk, __ldg(p.offsets + it.e + 1) - it.seg0 - it.tc * kTokChunk);
     return it;
+}
+
+// Table form of an item: (e, rt | tc << 8, seg0, nq).
+__device__ __forceinline__ int4 pack_item(const ItemInfo &ii) {
+    return make_int4(ii.e, ii.rt | (ii.tc << 8), ii.seg0, ii.nq);
+}
+__device__ __forceinline__ ItemInfo unpack_item(int4 v) {
+    ItemInfo ii;
+    ii.e = v.x, ii.rt = v.y & 255, ii.tc = v.y >> 8, ii.seg0 = v.z, ii.nq = v.w;
+    return ii;
 }
 
 // The head of the CTA's shared memory: the ring's barriers and release
@@ -163,24 +180,18 @@ struct RingHead {
 static_assert(sizeof(RingHead) <= kBarBytes, "ring head");
 
 // Item `item` of this CTA, from the shared table when it holds it.
-__device__ __forceinline__ ItemInfo item_at(const GemvParams &p, const int2 *table, int first,
+__device__ __forceinline__ ItemInfo item_at(const GemvParams &p, const int4 *table, int first,
                                             int nact, int RT, int item) {
     const int k = item - first;
-    if (k < kItemTable) {
-        const int2 v = table[k];
-        ItemInfo ii;
-        ii.e = v.x, ii.rt = v.y & 255, ii.tc = v.y >> 8;
-        return ii;
-    }
+    if (k < kItemTable) return unpack_item(table[k]);
     return decode_item(p, nact, RT, item);
 }
 
-// Item k of this CTA as its table entry (e, rt | tc << 8).
-__device__ __forceinline__ int2 item_entry(const GemvParams &p, const int2 *table, int first,
+// Item k of this CTA as its table entry.
+__device__ __forceinline__ int4 item_entry(const GemvParams &p, const int4 *table, int first,
                                            int nact, int RT, int k) {
     if (k < kItemTable) return table[k];
-    const ItemInfo ii = decode_item(p, nact, RT, first + k);
-    return make_int2(ii.e, ii.rt | (ii.tc << 8));
+    return pack_item(decode_item(p, nact, RT, first + k));
 }
 
 // The CTA's copy stream: iteration j brings k stage ks of its item k
@@ -194,7 +205,7 @@ __device__ __forceinline__ int2 item_entry(const GemvParams &p, const int2 *tabl
 // and it fell on the one warp that, being slowed by it, stayed the last.)
 struct FeedCtx {
     const uint8_t *weights;  // this matrix (gate/up or down) of expert 0
-    const int2 *table;
+    const int4 *table;
     size_t expert_bytes;
     int first, n_mine, nact, RT, KT, NS;
 };
@@ -202,10 +213,10 @@ struct FeedCtx {
 struct Feed {
     const uint8_t *src;  // bytes of iteration j
     int j, ks, k;
-    int2 next;           // table entry of item k + 1
+    int4 next;           // table entry of item k + 1
 };
 
-__device__ __forceinline__ const uint8_t *item_src(const FeedCtx &fc, int2 v) {
+__device__ __forceinline__ const uint8_t *item_src(const FeedCtx &fc, int4 v) {
     return fc.weights + (size_t)v.x * fc.expert_bytes + (size_t)(v.y & 255) * fc.KT * kUnitBytes;
 }
 
@@ -217,7 +228,7 @@ __device__ __forceinline__ Feed feed_at(const GemvParams &p, const FeedCtx &fc, 
                       (size_t)f.ks * kStageBytes
                 : nullptr;
     f.next = f.k + 1 < fc.n_mine ? item_entry(p, fc.table, fc.first, fc.nact, fc.RT, f.k + 1)
-                                 : make_int2(0, 0);
+                                 : make_int4(0, 0, 0, 0);
     return f;
 }
 
@@ -264,66 +275,81 @@ __host__ __device__ inline uint32_t region_size(int nq, bool wide, uint32_t x_st
 // scales of pairs 2q and 2q+1 interleaved in one row per q, [block][2] f32 at
 // their own odd-16-byte stride, so a lane loads its two pair columns' scales
 // of a block as one f32 pair.
-//   gate/up: copies xq[token(pair)] and dx[token] (quantized by the router);
-//   down:    quantizes h[pos] here, one thread per 32-block, exactly as
-//            mia_matvec quantizes its input (matmul.c:93, quant.c:11-27).
+//   gate/up: xq[token(pair)] and dx[token] (quantized by the router);
+//   down:    hq[pair] and hs[pair] (quantized by k_swiglu_q8).
 template <bool kGU>
 __device__ void fill_region(const GemvParams &p, uint8_t *region, int rows_cap, int seg0, int t0,
                             int n, int row_bytes, int nscale) {
     const int srow = (int)smem_stride((uint32_t)nscale * 8);  // scale row of a pair of pairs
     uint8_t *rs = region + (size_t)rows_cap * p.x_stride;
-    if (kGU) {
-        const int qv = row_bytes / 16, sv = nscale / 4;  // 16-byte vectors per row / scale row
-        const int per = qv + sv;
-        for (int v = threadIdx.x; v < n * per; v += kConsumers) {
-            const int j = v / per, k = v % per;
-            const int pr = __ldg(p.perm + seg0 + t0 + j);
-            int t = p.pair_row ? __ldg(p.pair_row + pr) : pr / p.m.K;
+    const int8_t *q_src = kGU ? p.xq : p.hq;
+    const float *s_src = kGU ? p.dx : p.hs;
+    const int qv = row_bytes / 16, sv = nscale / 4;  // 16-byte vectors per row / scale row
+    const int per = qv + sv;
+    for (int v = threadIdx.x; v < n * per; v += kConsumers) {
+        const int j = v / per, k = v % per;
+        int t = seg0 + t0 + j;
+        if (kGU) {
+            const int pr = __ldg(p.perm + t);
+            t = p.pair_row ? __ldg(p.pair_row + pr) : pr / p.m.K;
             if (t < 0 || t >= p.n_rows) {  // a caller's row index out of range
                 set_error(p.err, kErrBadExpert);
                 t = 0;
             }
-            if (k < qv)
-                *reinterpret_cast<int4 *>(region + (size_t)j * p.x_stride + 16 * k) =
-                    __ldcg(reinterpret_cast<const int4 *>(p.xq + (size_t)t * row_bytes) + k);
-            else {
-                const float4 v4 = __ldcg(reinterpret_cast<const float4 *>(p.dx + (size_t)t * nscale) + (k - qv));
-                float *dst = reinterpret_cast<float *>(rs + (size_t)(j >> 1) * srow) + 8 * (k - qv) + (j & 1);
-                dst[0] = v4.x, dst[2] = v4.y, dst[4] = v4.z, dst[6] = v4.w;
-            }
         }
-    } else {
-        // one thread per (pair, 32-block), its eight 16-byte loads issued together
-        const int nb = row_bytes / MIAG_QK;
-        for (int task = threadIdx.x; task < n * nb; task += kConsumers) {
-            const int j = task / nb, b = task % nb;
-            const float4 *src = reinterpret_cast<const float4 *>(
-                p.h + (size_t)(seg0 + t0 + j) * row_bytes + b * MIAG_QK);
-            float4 v[8];
-#pragma unroll
-            for (int k = 0; k < 8; k++) v[k] = __ldcg(src + k);
-            float a = 0.0f;
-#pragma unroll
-            for (int k = 0; k < 8; k++)
-                a = fmaxf(a, fmaxf(fmaxf(fabsf(v[k].x), fabsf(v[k].y)),
-                                   fmaxf(fabsf(v[k].z), fabsf(v[k].w))));
-            const float dq = __fdiv_rn(a, 127.0f);
-            const float id = dq != 0.0f ? __fdiv_rn(1.0f, dq) : 0.0f;
-            uint32_t q[8];
-#pragma unroll
-            for (int k = 0; k < 8; k++) {
-                const uint32_t q0 = (uint8_t)(int8_t)roundf(__fmul_rn(v[k].x, id));
-                const uint32_t q1 = (uint8_t)(int8_t)roundf(__fmul_rn(v[k].y, id));
-                const uint32_t q2 = (uint8_t)(int8_t)roundf(__fmul_rn(v[k].z, id));
-                const uint32_t q3 = (uint8_t)(int8_t)roundf(__fmul_rn(v[k].w, id));
-                q[k] = q0 | (q1 << 8) | (q2 << 16) | (q3 << 24);
-            }
-            uint4 *dst = reinterpret_cast<uint4 *>(region + (size_t)j * p.x_stride + b * MIAG_QK);
-            dst[0] = make_uint4(q[0], q[1], q[2], q[3]);
-            dst[1] = make_uint4(q[4], q[5], q[6], q[7]);
-            reinterpret_cast<float *>(rs + (size_t)(j >> 1) * srow)[2 * b + (j & 1)] = dq;
+        if (k < qv)
+            *reinterpret_cast<int4 *>(region + (size_t)j * p.x_stride + 16 * k) =
+                __ldcg(reinterpret_cast<const int4 *>(q_src + (size_t)t * row_bytes) + k);
+        else {
+            const float4 v4 = __ldcg(reinterpret_cast<const float4 *>(s_src + (size_t)t * nscale) + (k - qv));
+            float *dst = reinterpret_cast<float *>(rs + (size_t)(j >> 1) * srow) + 8 * (k - qv) + (j & 1);
+            dst[0] = v4.x, dst[2] = v4.y, dst[4] = v4.z, dst[6] = v4.w;
         }
     }
+}
+
+// h = silu(gate) * up (forward.c:188-191) for every pair, quantized to Q8_0
+// exactly as mia_matvec quantizes its input (matmul.c:93, quant.c:11-27):
+// one thread per (pair, 32-block), its sixteen 16-byte loads of the block's
+// (gate, up) values issued together.  A launch of its own because the SiLU's
+// exp runs in double precision (expf_cr): at full occupancy its latency
+// hides; in the expert launches' eight warps per SM it did not.
+__global__ void k_swiglu_q8(const float *gu, int P, int eh, int xs, int8_t *hq, float *hs) {
+    const int nb = eh / MIAG_QK;
+    const long task = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (task >= (long)P * nb) return;
+    const int j = (int)(task / nb), b = (int)(task % nb);
+    const float4 *src = reinterpret_cast<const float4 *>(gu + (size_t)j * 2 * eh + (size_t)b * 2 * MIAG_QK);
+    float4 g[16];
+#pragma unroll
+    for (int k = 0; k < 16; k++) g[k] = __ldg(src + k);
+    float4 v[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        v[k].x = swiglu_ref(g[2 * k].x, g[2 * k].y);
+        v[k].y = swiglu_ref(g[2 * k].z, g[2 * k].w);
+        v[k].z = swiglu_ref(g[2 * k + 1].x, g[2 * k + 1].y);
+        v[k].w = swiglu_ref(g[2 * k + 1].z, g[2 * k + 1].w);
+    }
+    float a = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 8; k++)
+        a = fmaxf(a, fmaxf(fmaxf(fabsf(v[k].x), fabsf(v[k].y)), fmaxf(fabsf(v[k].z), fabsf(v[k].w))));
+    const float dq = __fdiv_rn(a, 127.0f);
+    const float id = dq != 0.0f ? __fdiv_rn(1.0f, dq) : 0.0f;
+    uint32_t q[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        const uint32_t q0 = (uint8_t)(int8_t)roundf(__fmul_rn(v[k].x, id));
+        const uint32_t q1 = (uint8_t)(int8_t)roundf(__fmul_rn(v[k].y, id));
+        const uint32_t q2 = (uint8_t)(int8_t)roundf(__fmul_rn(v[k].z, id));
+        const uint32_t q3 = (uint8_t)(int8_t)roundf(__fmul_rn(v[k].w, id));
+        q[k] = q0 | (q1 << 8) | (q2 << 16) | (q3 << 24);
+    }
+    uint4 *dst = reinterpret_cast<uint4 *>(hq + (size_t)j * eh + (size_t)b * MIAG_QK);
+    dst[0] = make_uint4(q[0], q[1], q[2], q[3]);
+    dst[1] = make_uint4(q[4], q[5], q[6], q[7]);
+    hs[(size_t)j * xs + b] = dq;
 }
 
 __device__ __forceinline__ float4 lds128(uint32_t addr) {
@@ -525,23 +551,17 @@ __device__ __forceinline__ void run_item(const GemvParams &p, const ItemCtx &ic,
         const float2 u0 = unpack2(acc[n][0]), u1 = unpack2(acc[n][1]);
         const float o[4] = {u0.x, u0.y, u1.x, u1.y};  // (r0,qa) (r0,qb) (r1,qa) (r1,qb)
         if (kGU) {
-            // rows are interleaved gate (even) / up (odd): the up partner of
-            // row r sits in the lane with groupID g ^ 1, i.e. lane ^ 4.
-            float up[4];
-#pragma unroll
-            for (int i = 0; i < 4; i++) up[i] = __shfl_xor_sync(kFull, o[i], 4);
-            if ((ln.g & 1) == 0) {
-                const int eh = p.m.eh, i0 = R0 >> 1, i1 = R1 >> 1;
-                if (qa < nq) {
-                    float *hp = p.h + (size_t)(ic.seg0 + ic.t0 + qa) * eh;
-                    if (R0 < rows) hp[i0] = swiglu_ref(o[0], up[0]);
-                    if (R1 < rows) hp[i1] = swiglu_ref(o[2], up[2]);
-                }
-                if (qb < nq) {
-                    float *hp = p.h + (size_t)(ic.seg0 + ic.t0 + qb) * eh;
-                    if (R0 < rows) hp[i0] = swiglu_ref(o[1], up[1]);
-                    if (R1 < rows) hp[i1] = swiglu_ref(o[3], up[3]);
-                }
+            // the products as they are, gate (even rows) beside up (odd
+            // rows); the down launch forms silu(gate) * up while staging them
+            if (qa < nq) {
+                float *hp = p.h + (size_t)(ic.seg0 + ic.t0 + qa) * rows;
+                if (R0 < rows) hp[R0] = o[0];
+                if (R1 < rows) hp[R1] = o[2];
+            }
+            if (qb < nq) {
+                float *hp = p.h + (size_t)(ic.seg0 + ic.t0 + qb) * rows;
+                if (R0 < rows) hp[R0] = o[1];
+                if (R1 < rows) hp[R1] = o[3];
             }
         } else {
             // y goes out in pair order, so the combine (and a remote caller)
@@ -579,7 +599,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_expert_mma(GemvParams p) {
 
     RingHead *head = reinterpret_cast<RingHead *>(smem);
     uint8_t *stages = smem + kRingOff;
-    int2 *table = reinterpret_cast<int2 *>(smem + kBarBytes);
+    int4 *table = reinterpret_cast<int4 *>(smem + kBarBytes);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_mine = last - first;
     if (threadIdx.x == 0) head->nq_max = 1;
@@ -589,9 +609,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_expert_mma(GemvParams p) {
     int my_nq = 1;
     for (int k = threadIdx.x; k < n_mine; k += kGemvThreads) {
         const ItemInfo ii = decode_item(p, nact, RT, first + k);
-        if (k < kItemTable) table[k] = make_int2(ii.e, ii.rt | (ii.tc << 8));
-        const int n_e = __ldg(p.offsets + ii.e + 1) - __ldg(p.offsets + ii.e);
-        my_nq = max(my_nq, min(kTokChunk, n_e - ii.tc * kTokChunk));
+        if (k < kItemTable) table[k] = pack_item(ii);
+        my_nq = max(my_nq, ii.nq);
     }
     atomicMax(&head->nq_max, my_nq);
     __syncthreads();
@@ -631,9 +650,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_expert_mma(GemvParams p) {
     bool failed = false;
     for (int item = first; item < last; item++) {
         const ItemInfo ii = item_at(p, table, first, nact, RT, item);
-        const int seg0 = __ldg(p.offsets + ii.e);
-        const int n_e = __ldg(p.offsets + ii.e + 1) - seg0;
-        const int t0 = ii.tc * kTokChunk, nq = min(kTokChunk, n_e - t0);
+        const int seg0 = ii.seg0, t0 = ii.tc * kTokChunk, nq = ii.nq;
         if (ii.e != cur_e || ii.tc != cur_tc) {
             consumer_sync();  // nobody still reads the region
             fill_region<kGU>(p, region, head->nq_max, seg0, t0, nq, Kb, xs);
@@ -701,7 +718,7 @@ static void fill_params(GemvParams &p, const Dims &m, const StoreLayout &lay, co
     p.m = m, p.lay = lay, p.experts = L.experts;
     p.offsets = w.offsets, p.perm = w.perm, p.active = w.active, p.n_active = w.n_active;
     p.chunk_pre = w.chunk_pre;
-    p.xq = w.xq, p.dx = w.dx, p.h = w.h, p.y = w.y, p.err = err;
+    p.xq = w.xq, p.dx = w.dx, p.h = w.h, p.hq = w.hq, p.hs = w.hs, p.y = w.y, p.err = err;
     p.pair_row = w.pair_row, p.n_rows = w.pair_row ? w.n_rows : w.T;
     p.one = 1.0f;
 }
@@ -758,6 +775,11 @@ void launch_gateup(const Dims &m, const StoreLayout &lay, const LayerDev &L, con
 
 void launch_down(const Dims &m, const StoreLayout &lay, const LayerDev &L, const Work &w,
                  int num_sms, int *err, cudaStream_t s) {
+    if (w.P > 0) {
+        const long tasks = (long)w.P * (m.eh / MIAG_QK);
+        k_swiglu_q8<<<(unsigned)((tasks + 127) / 128), 128, 0, s>>>(
+            w.h, w.P, m.eh, scale_pad(m.eh / MIAG_QK), w.hq, w.hs);
+    }
     GemvParams p{};
     fill_params(p, m, lay, L, w, err);
     geometry(p, false);

@@ -23,8 +23,10 @@ struct Work {
     int32_t *chunk_pre;    // [E+1]         exclusive prefix over active experts of ceil(n_e / kTokChunk)
     int32_t *perm;         // [P]           pair id at each sorted position
     int32_t *inv;          // [P]           sorted position of each pair
-    float *h;              // [P][eh]       silu(gate) * up, sorted order
-    float *y;              // [P][d]        down projections, sorted order
+    float *h;              // [P][2 eh]     gate/up products (gate even, up odd), sorted order
+    int8_t *hq;            // [P][eh]       Q8_0 silu(gate) * up, sorted order
+    float *hs;             // [P][xs_h]     its block scales (xs_h = scale_pad(eh / 32))
+    float *y;              // [P][d]        down projections, pair order
     int32_t *tg_count;     // [T]           route: CTAs done per token group; zero between calls
     const int32_t *pair_row;  // [P]        expert products over given pairs: each pair's row of
     int n_rows;               //              xq/dx (null: pair p is row p / K, the moe() case)

@@ -36,7 +36,7 @@ using namespace miag;
 
 namespace {
 
-constexpr size_t kNoAllocScratchBytes = (size_t)8 << 20;  // 8 MiB per device
+constexpr size_t kNoAllocScratchBytes = (size_t)11 << 20;  // 11 MiB per device
 constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
@@ -102,7 +102,9 @@ size_t layout(const Dims &m, int T, uint8_t *base, Work *w) {
     v.chunk_pre = reinterpret_cast<int32_t *>(bump(p, (size_t)(m.E + 1) * 4));
     v.perm = reinterpret_cast<int32_t *>(bump(p, P * 4));
     v.inv = reinterpret_cast<int32_t *>(bump(p, P * 4));
-    v.h = reinterpret_cast<float *>(bump(p, P * m.eh * 4));
+    v.h = reinterpret_cast<float *>(bump(p, P * 2 * m.eh * 4));
+    v.hq = reinterpret_cast<int8_t *>(bump(p, P * m.eh));
+    v.hs = reinterpret_cast<float *>(bump(p, P * scale_pad(m.eh / MIAG_QK) * 4));
     v.y = reinterpret_cast<float *>(bump(p, P * m.d * 4));
     if (w) *w = v;
     return (size_t)(p - base);

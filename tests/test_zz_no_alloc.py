@@ -63,6 +63,8 @@ def test_noalloc_refuses_batches_beyond_its_array(torch_cuda):
         xd = torch.zeros((T, shape.dim), dtype=torch.float32, device="cuda")
         rc, msg = noalloc(eng, xd.data_ptr(), T)
         assert rc == -1 and "scratch" in msg
-        rc, msg = noalloc(eng, xd.data_ptr(), 90)  # the largest batch that fits
+        rc, msg = noalloc(eng, xd.data_ptr(), 93)
+        assert rc == -1 and "scratch" in msg
+        rc, msg = noalloc(eng, xd.data_ptr(), 92)  # the largest batch that fits
         assert rc == 0, msg
         eng.sync()
