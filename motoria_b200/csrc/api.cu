@@ -385,6 +385,8 @@ static size_t ws_layout(miag_ctx *c, int T, uint8_t *base, Work *w, float **x_de
     v.active = (int32_t *)bump(p, (size_t)m.E * 4);
     v.n_active = (int32_t *)bump(p, 4);
     v.chunk_pre = (int32_t *)bump(p, (size_t)(m.E + 1) * 4);
+    v.chunk_info = (int4 *)bump(p, (P / kTokChunkNarrow + m.E + 1) * 16);
+    v.max_chunk = (int32_t *)bump(p, 4);
     v.perm = (int32_t *)bump(p, P * 4);
     v.inv = (int32_t *)bump(p, P * 4);
     v.h = (float *)bump(p, P * 2 * m.eh * 4);
@@ -471,6 +473,7 @@ static int read_device_error(miag_ctx *c, char *err, size_t errlen) {
     const char *what = code == kErrWaitFull    ? "a consumer timed out waiting for a staged tile"
                        : code == kErrWaitEmpty ? "the producer timed out waiting for a free stage"
                        : code == kErrBadExpert ? "a routing index was out of range"
+                       : code == kErrItemList  ? "an expert launch's work list named a tile outside the store"
                                                : "unknown device error";
     set_err(err, errlen, "device error %d: %s", code, what);
     return -1;

@@ -21,6 +21,7 @@ enum : int {
     kErrWaitFull = 1,     // a consumer gave up waiting for a staged tile
     kErrWaitEmpty = 2,    // the producer gave up waiting for a free stage
     kErrBadExpert = 3,    // a routing index outside [0, E)
+    kErrItemList = 4,     // an expert launch's work list named a tile outside the store
 };
 
 // Bounded spin: about one second at B200 clocks.

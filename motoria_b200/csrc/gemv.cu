@@ -49,6 +49,8 @@ struct GemvParams {
     StoreLayout lay;
     const uint8_t *experts;
     const int32_t *offsets, *perm, *active, *n_active, *chunk_pre;
+    const int4 *chunk_info;    // per pair chunk: (expert, chunk of it, segment start, pairs)
+    const int32_t *max_chunk;  // largest chunk
     const int8_t *xq;  // [rows][d]
     const float *dx;   // [rows][xs]
     const int32_t *pair_row;  // [P] activation row of each pair, or null: pair / K
@@ -58,6 +60,7 @@ struct GemvParams {
     const float *hs;   // [P][xs]   its block scales
     float *y;          // [P][d], pair order
     int stages;
+    int chunk;                 // pairs per chunk (tok_chunk)
     uint32_t x_stride;         // row stride of the staged activations
     float one;                 // 1.0f, opaque to the compiler (see q8_step_x2)
     int *err;
@@ -131,32 +134,19 @@ __device__ __forceinline__ void q8_step_x2(uint64_t &s, uint64_t m, uint64_t w2,
     asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(s) : "l"(t), "l"(one2));
 }
 
-// Item i -> index a of its active expert: largest a with chunk_pre[a]*RT <= i.
-__device__ __forceinline__ int find_active(const int32_t *chunk_pre, int nact, int RT, int item) {
-    int lo = 0, hi = nact;
-    while (hi - lo > 1) {
-        const int mid = (lo + hi) >> 1;
-        if (__ldg(chunk_pre + mid) * RT <= item) lo = mid;
-        else hi = mid;
-    }
-    return lo;
-}
-
 // An item: expert e, row tile rt, pair chunk tc, which covers pairs
 // [seg0 + 32 tc, + nq) of the expert-sorted order.
 struct ItemInfo {
     int e, rt, tc, seg0, nq;
 };
 
-__device__ __forceinline__ ItemInfo decode_item(const GemvParams &p, int nact, int RT, int item) {
-    const int a = find_active(p.chunk_pre, nact, RT, item);
-    const int local = item - __ldg(p.chunk_pre + a) * RT;
+// Item `item` of the launch: row tile item % RT of pair chunk item / RT in
+// the permutation's chunk list (experts ascending, chunks in order).
+__device__ __forceinline__ ItemInfo decode_item(const GemvParams &p, int RT, int item) {
+    const int4 c = __ldg(p.chunk_info + item / RT);
     ItemInfo it;
-    it.e = __ldg(p.active + a);
-    it.tc = local / RT;
-    it.rt = local % RT;
-    it.seg0 = __ldg(p.offsets + it.e);
-    it.nq = min(kTokChunk, __ldg(p.offsets + it.e + 1) - it.seg0 - it.tc * kTokChunk);
+    it.e = c.x, it.tc = c.y, it.seg0 = c.z, it.nq = c.w;
+    it.rt = item % RT;
     return it;
 }
 
@@ -171,27 +161,19 @@ __device__ __forceinline__ ItemInfo unpack_item(int4 v) {
 }
 
 // The head of the CTA's shared memory: the ring's barriers and release
-// counters, and the CTA's largest pair chunk.
+// counters, and the activation rows of the chunk being staged.
 struct RingHead {
     uint64_t full[kMaxStages];      // stage holds its k tiles (TMA complete_tx)
     uint32_t released[kMaxStages];  // warps done with the stage, summed over rounds
-    int nq_max;                     // largest pair chunk among this CTA's items
+    int tok[kTokChunk];             // activation rows of the pairs being staged
 };
 static_assert(sizeof(RingHead) <= kBarBytes, "ring head");
 
-// Item `item` of this CTA, from the shared table when it holds it.
-__device__ __forceinline__ ItemInfo item_at(const GemvParams &p, const int4 *table, int first,
-                                            int nact, int RT, int item) {
-    const int k = item - first;
-    if (k < kItemTable) return unpack_item(table[k]);
-    return decode_item(p, nact, RT, item);
-}
-
-// Item k of this CTA as its table entry.
+// Item first + k of the launch (this CTA's k-th) as its table entry.
 __device__ __forceinline__ int4 item_entry(const GemvParams &p, const int4 *table, int first,
-                                           int nact, int RT, int k) {
+                                           int RT, int k) {
     if (k < kItemTable) return table[k];
-    return pack_item(decode_item(p, nact, RT, first + k));
+    return pack_item(decode_item(p, RT, first + k));
 }
 
 // The CTA's copy stream: iteration j brings k stage ks of its item k
@@ -207,7 +189,8 @@ struct FeedCtx {
     const uint8_t *weights;  // this matrix (gate/up or down) of expert 0
     const int4 *table;
     size_t expert_bytes;
-    int first, n_mine, nact, RT, KT, NS;
+    int first, RT, KT, NS, E;
+    int n_items;             // items in the CTA's list as far as this thread knows
 };
 
 struct Feed {
@@ -216,19 +199,21 @@ struct Feed {
     int4 next;           // table entry of item k + 1
 };
 
+// Source of an item's first k stage; null for an entry naming a tile outside
+// the store, which is then never copied.
 __device__ __forceinline__ const uint8_t *item_src(const FeedCtx &fc, int4 v) {
+    if ((unsigned)v.x >= (unsigned)fc.E || (v.y & 255) >= fc.RT) return nullptr;
     return fc.weights + (size_t)v.x * fc.expert_bytes + (size_t)(v.y & 255) * fc.KT * kUnitBytes;
 }
 
 __device__ __forceinline__ Feed feed_at(const GemvParams &p, const FeedCtx &fc, int j0) {
     Feed f;
     f.j = j0, f.k = j0 / fc.NS, f.ks = j0 % fc.NS;
-    f.src = f.k < fc.n_mine
-                ? item_src(fc, item_entry(p, fc.table, fc.first, fc.nact, fc.RT, f.k)) +
-                      (size_t)f.ks * kStageBytes
-                : nullptr;
-    f.next = f.k + 1 < fc.n_mine ? item_entry(p, fc.table, fc.first, fc.nact, fc.RT, f.k + 1)
-                                 : make_int4(0, 0, 0, 0);
+    const uint8_t *src = f.k < fc.n_items ? item_src(fc, item_entry(p, fc.table, fc.first, fc.RT, f.k))
+                                          : nullptr;
+    f.src = src ? src + (size_t)f.ks * kStageBytes : nullptr;
+    f.next = f.k + 1 < fc.n_items ? item_entry(p, fc.table, fc.first, fc.RT, f.k + 1)
+                                  : make_int4(0, 0, 0, 0);
     return f;
 }
 
@@ -237,27 +222,33 @@ __device__ __forceinline__ void feed_next(const GemvParams &p, const FeedCtx &fc
     if (++f.ks == fc.NS) {
         f.ks = 0, f.k++;
         f.src = item_src(fc, f.next);
-        if (f.k + 1 < fc.n_mine) f.next = item_entry(p, fc.table, fc.first, fc.nact, fc.RT, f.k + 1);
+        if (f.k + 1 < fc.n_items) f.next = item_entry(p, fc.table, fc.first, fc.RT, f.k + 1);
     } else {
-        f.src += kStageBytes;
+        f.src = f.src ? f.src + kStageBytes : nullptr;
     }
 }
 
-// Issues iteration f.j into stage s, completing on its full barrier.
-__device__ __forceinline__ void feed_issue(const FeedCtx &fc, const Feed &f, uint8_t *smem, int s) {
+// Issues iteration f.j into stage s, completing on its full barrier.  A null
+// source (an entry outside the store) is never copied: the error word
+// records it and the stage stays empty, so its consumers time out instead.
+__device__ __forceinline__ void feed_issue(const GemvParams &p, const FeedCtx &fc, const Feed &f,
+                                           uint8_t *smem, int s) {
     RingHead *h = reinterpret_cast<RingHead *>(smem);
+    if (!f.src) {
+        set_error(p.err, kErrItemList);
+        return;
+    }
     const uint32_t bytes = (uint32_t)min(kStageKT, fc.KT - f.ks * kStageKT) * kUnitBytes;
     mbar_arrive_expect_tx(&h->full[s], bytes);
     bulk_g2s(smem + kRingOff + (size_t)s * kStageBytes, f.src, bytes, &h->full[s]);
 }
 
 // N-tiles (of 8 pairs) the consumers run for a chunk of nq pairs.  Two
-// regimes, chosen per launch from the batch: few pairs per expert (decode)
-// runs one, two or four n-tiles; many (prefill) one or four, the set whose
-// four-tile path keeps every value in registers (three shapes in one kernel
-// spill a little, which the wide path feels and the narrow one does not).
+// regimes, chosen per launch from the batch (wide_batch): chunks of up to 16
+// pairs (decode) run one or two n-tiles, chunks of up to 32 (prefill) one or
+// four.  Two shapes a kernel keep every value in registers; three spilled.
 __host__ __device__ inline int n_tiles(int nq, bool wide) {
-    return nq <= 8 ? 1 : (!wide && nq <= 16) ? 2 : 4;
+    return nq <= 8 ? 1 : wide ? 4 : 2;
 }
 
 // Bytes of the activation region for chunks of up to nq pairs: nq int8 rows
@@ -277,35 +268,54 @@ __host__ __device__ inline uint32_t region_size(int nq, bool wide, uint32_t x_st
 // of a block as one f32 pair.
 //   gate/up: xq[token(pair)] and dx[token] (quantized by the router);
 //   down:    hq[pair] and hs[pair] (quantized by k_swiglu_q8).
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void *dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.commit_group;\ncp.async.wait_all;" ::: "memory");
+}
+
+// Called by all consumer threads between two CTA barriers.  Every copy is an
+// asynchronous global-to-shared copy issued before the first wait, so a fill
+// costs one round trip for the data (plus one for the token rows of gate/up)
+// however many vectors each thread moves.
 template <bool kGU>
 __device__ void fill_region(const GemvParams &p, uint8_t *region, int rows_cap, int seg0, int t0,
-                            int n, int row_bytes, int nscale) {
+                            int n, int row_bytes, int nscale, int *tok) {
     const int srow = (int)smem_stride((uint32_t)nscale * 8);  // scale row of a pair of pairs
     uint8_t *rs = region + (size_t)rows_cap * p.x_stride;
     const int8_t *q_src = kGU ? p.xq : p.hq;
     const float *s_src = kGU ? p.dx : p.hs;
-    const int qv = row_bytes / 16, sv = nscale / 4;  // 16-byte vectors per row / scale row
-    const int per = qv + sv;
-    for (int v = threadIdx.x; v < n * per; v += kConsumers) {
-        const int j = v / per, k = v % per;
-        int t = seg0 + t0 + j;
-        if (kGU) {
-            const int pr = __ldg(p.perm + t);
-            t = p.pair_row ? __ldg(p.pair_row + pr) : pr / p.m.K;
+    if (kGU) {  // the chunk's activation rows
+        if ((int)threadIdx.x < n) {
+            const int pr = __ldg(p.perm + seg0 + t0 + threadIdx.x);
+            int t = p.pair_row ? __ldg(p.pair_row + pr) : pr / p.m.K;
             if (t < 0 || t >= p.n_rows) {  // a caller's row index out of range
                 set_error(p.err, kErrBadExpert);
                 t = 0;
             }
+            tok[threadIdx.x] = t;
         }
-        if (k < qv)
-            *reinterpret_cast<int4 *>(region + (size_t)j * p.x_stride + 16 * k) =
-                __ldcg(reinterpret_cast<const int4 *>(q_src + (size_t)t * row_bytes) + k);
-        else {
-            const float4 v4 = __ldcg(reinterpret_cast<const float4 *>(s_src + (size_t)t * nscale) + (k - qv));
+        consumer_sync();
+    }
+    const int qv = row_bytes / 16, sv = nscale / 4;  // 16-byte vectors per row / scale row
+    const int per = qv + sv, total = n * per;
+    for (int v = threadIdx.x; v < total; v += kConsumers) {
+        const int j = v / per, k = v - j * per;
+        const int t = kGU ? tok[j] : seg0 + t0 + j;
+        if (k < qv) {
+            cp_async16(region + (size_t)j * p.x_stride + 16 * k, q_src + (size_t)t * row_bytes + 16 * k);
+        } else {
+            const float *src = s_src + (size_t)t * nscale + 4 * (k - qv);
             float *dst = reinterpret_cast<float *>(rs + (size_t)(j >> 1) * srow) + 8 * (k - qv) + (j & 1);
-            dst[0] = v4.x, dst[2] = v4.y, dst[4] = v4.z, dst[6] = v4.w;
+#pragma unroll
+            for (int i = 0; i < 4; i++) cp_async4(dst + 2 * i, src + i);
         }
     }
+    cp_async_wait_all();
 }
 
 // h = silu(gate) * up (forward.c:188-191) for every pair, quantized to Q8_0
@@ -458,7 +468,6 @@ struct ItemCtx {
     uint32_t x_rows, x_scl;  // shared addresses of the activation rows / scale rows
     uint32_t xpp_bytes;      // stride of the scale rows (one per pair of pairs)
     int S, KT, NS, nb, rows;
-    int total;               // iterations this CTA streams
     int rt, seg0, t0, nq;    // the item: row tile, expert segment, first pair, pairs
 };
 
@@ -533,10 +542,10 @@ __device__ __forceinline__ void run_item(const GemvParams &p, const ItemCtx &ic,
             // release the stage; the eighth release of a round refills it
             __threadfence_block();
             const uint32_t done = atomicAdd(&head->released[s], 1u);
-            if ((done % kConsumerWarps) == kConsumerWarps - 1 && fd.j < ic.total) {
+            if ((done % kConsumerWarps) == kConsumerWarps - 1 && fd.k < fc.n_items) {
                 __threadfence_block();
                 fence_proxy_async_smem();
-                feed_issue(fc, fd, smem, s);
+                feed_issue(p, fc, fd, smem, s);
             }
         }
         feed_next(p, fc, fd);
@@ -582,6 +591,11 @@ __device__ __forceinline__ void run_item(const GemvParams &p, const ItemCtx &ic,
 }
 
 // gate+up (kGU) or down: one launch over all items of all active experts.
+// Items (row tile, pair chunk) are numbered chunk by chunk, experts
+// ascending; CTA c runs a contiguous share, so consecutive items share their
+// activations.  (Handing the last 15-30 % of the items out one by one from
+// an atomic counter evened out the CTAs' end times but cost more in
+// activation stagings than it saved, at every batch size measured.)
 template <bool kGU, bool kWide>
 __global__ void __launch_bounds__(kGemvThreads, 1) k_expert_mma(GemvParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -592,30 +606,24 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_expert_mma(GemvParams p) {
     const int rows = kGU ? 2 * eh : d;       // matrix rows
     const int nb = Kb / MIAG_QK, xs = scale_pad(nb);
     const int NS = (KT + kStageKT - 1) / kStageKT;  // stages per item
-    const int nact = __ldg(p.n_active);
-    const int n_items = __ldg(p.chunk_pre + nact) * RT;
-    const int first = (int)((long)n_items * blockIdx.x / gridDim.x);
-    const int last = (int)((long)n_items * (blockIdx.x + 1) / gridDim.x);
+    const int n_items = __ldg(p.chunk_pre + __ldg(p.n_active)) * RT;
+    const int G = gridDim.x;
+
+    // The activation region holds the largest chunk of the launch; the rest
+    // of shared memory deepens the ring.
+    const int nq_max = max(1, __ldg(p.max_chunk));
+    const uint32_t region_bytes = region_size(nq_max, kWide, p.x_stride, xs);
+    const int S = min(kMaxStages, (int)((kSmemBudget - kRingOff - (int)region_bytes) / kStageBytes));
+
+    const int first = (int)((long)n_items * blockIdx.x / G);
+    const int n_mine = (int)((long)n_items * (blockIdx.x + 1) / G) - first;
 
     RingHead *head = reinterpret_cast<RingHead *>(smem);
     uint8_t *stages = smem + kRingOff;
     int4 *table = reinterpret_cast<int4 *>(smem + kBarBytes);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n_mine = last - first;
-    if (threadIdx.x == 0) head->nq_max = 1;
-    __syncthreads();
-    // Decode this CTA's items and find its largest pair chunk: the activation
-    // region is sized for that, and the rest of shared memory deepens the ring.
-    int my_nq = 1;
-    for (int k = threadIdx.x; k < n_mine; k += kGemvThreads) {
-        const ItemInfo ii = decode_item(p, nact, RT, first + k);
-        if (k < kItemTable) table[k] = pack_item(ii);
-        my_nq = max(my_nq, ii.nq);
-    }
-    atomicMax(&head->nq_max, my_nq);
-    __syncthreads();
-    const uint32_t region_bytes = region_size(head->nq_max, kWide, p.x_stride, xs);
-    const int S = min(kMaxStages, (int)((kSmemBudget - kRingOff - (int)region_bytes) / kStageBytes));
+    for (int k = threadIdx.x; k < min(n_mine, kItemTable); k += kGemvThreads)
+        table[k] = pack_item(decode_item(p, RT, first + k));
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; s++) {
             mbar_init(&head->full[s], 1);
@@ -627,11 +635,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_expert_mma(GemvParams p) {
     FeedCtx fc;
     fc.weights = p.experts + (kGU ? p.lay.gu_off : p.lay.dn_off);
     fc.table = table, fc.expert_bytes = p.lay.expert_bytes;
-    fc.first = first, fc.n_mine = n_mine, fc.nact = nact, fc.RT = RT, fc.KT = KT, fc.NS = NS;
-    const int total = n_mine * NS;
+    fc.first = first, fc.RT = RT, fc.KT = KT, fc.NS = NS, fc.E = p.m.E, fc.n_items = n_mine;
     if (threadIdx.x == 0) {
         Feed f = feed_at(p, fc, 0);
-        for (int j = 0; j < min(S, total); j++, feed_next(p, fc, f)) feed_issue(fc, f, smem, j);
+        for (int j = 0; j < min(S, n_mine * NS); j++, feed_next(p, fc, f)) feed_issue(p, fc, f, smem, j);
     }
     Feed fd = feed_at(p, fc, S);  // the refill of iteration 0
 
@@ -641,33 +648,31 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_expert_mma(GemvParams p) {
     ItemCtx ic;
     ic.stages = smem_addr(stages);
     ic.x_rows = smem_addr(region);
-    ic.x_scl = ic.x_rows + (uint32_t)head->nq_max * p.x_stride;
+    ic.x_scl = ic.x_rows + (uint32_t)nq_max * p.x_stride;
     ic.xpp_bytes = smem_stride((uint32_t)xs * 8);
-    ic.S = S, ic.KT = KT, ic.NS = NS, ic.nb = nb, ic.rows = rows, ic.total = total;
+    ic.S = S, ic.KT = KT, ic.NS = NS, ic.nb = nb, ic.rows = rows;
 
     int cur_e = -1, cur_tc = -1;
     RingPos rp{0, 0, 0u};
     bool failed = false;
-    for (int item = first; item < last; item++) {
-        const ItemInfo ii = item_at(p, table, first, nact, RT, item);
-        const int seg0 = ii.seg0, t0 = ii.tc * kTokChunk, nq = ii.nq;
+    for (int k = 0; k < n_mine; k++) {
+        const ItemInfo ii = unpack_item(item_entry(p, table, first, RT, k));
+        const int seg0 = ii.seg0, t0 = ii.tc * p.chunk, nq = ii.nq;
         if (ii.e != cur_e || ii.tc != cur_tc) {
             consumer_sync();  // nobody still reads the region
-            fill_region<kGU>(p, region, head->nq_max, seg0, t0, nq, Kb, xs);
+            fill_region<kGU>(p, region, nq_max, seg0, t0, nq, Kb, xs, head->tok);
             cur_e = ii.e, cur_tc = ii.tc;
             consumer_sync();
         }
         ic.rt = ii.rt, ic.seg0 = seg0, ic.t0 = t0, ic.nq = nq;
-        // Two tile shapes (more do not fit the registers without spilling):
-        // one n-tile of 8 pairs, or four (32 pairs; columns past nq are
-        // computed on repeated rows and not written).
-        const int nt = n_tiles(nq, kWide);
-        if (nt == 1) run_item<kGU, 1>(p, ic, ln, smem, rp, fc, fd, failed);
-        else if (!kWide && nt == 2) run_item<kGU, kWide ? 4 : 2>(p, ic, ln, smem, rp, fc, fd, failed);
-        else run_item<kGU, 4>(p, ic, ln, smem, rp, fc, fd, failed);
+        // Two tile shapes (n_tiles): one n-tile of 8 pairs, or the chunk's
+        // full width (columns past nq run on repeated rows, not written).
+        if (nq <= 8) run_item<kGU, 1>(p, ic, ln, smem, rp, fc, fd, failed);
+        else run_item<kGU, kWide ? 4 : 2>(p, ic, ln, smem, rp, fc, fd, failed);
     }
     // After a timed-out wait, let every issued copy land (bounded) before the
     // CTA's shared memory goes away.  All refills are issued by now.
+    const int total = n_mine * NS;
     if (__syncthreads_or(failed) && threadIdx.x == 0) {
         for (int j = total - 1; j >= 0 && j >= total - S; j--)
             mbar_wait(&head->full[j % S], (j / S) & 1);
@@ -717,10 +722,11 @@ static void fill_params(GemvParams &p, const Dims &m, const StoreLayout &lay, co
                         const Work &w, int *err) {
     p.m = m, p.lay = lay, p.experts = L.experts;
     p.offsets = w.offsets, p.perm = w.perm, p.active = w.active, p.n_active = w.n_active;
-    p.chunk_pre = w.chunk_pre;
+    p.chunk_pre = w.chunk_pre, p.chunk_info = w.chunk_info, p.max_chunk = w.max_chunk;
     p.xq = w.xq, p.dx = w.dx, p.h = w.h, p.hq = w.hq, p.hs = w.hs, p.y = w.y, p.err = err;
     p.pair_row = w.pair_row, p.n_rows = w.pair_row ? w.n_rows : w.T;
     p.one = 1.0f;
+    p.chunk = tok_chunk(w.P, m.E);
 }
 
 // Shared memory: head | item table | ring | activation region.  Every CTA
@@ -755,11 +761,11 @@ int gemv_setup_attributes(const Dims &m, const StoreLayout &lay) {
 
 // The prefill regime once an expert gets more than one n-tile of pairs on
 // average.
-static bool wide_regime(const Dims &m, const Work &w) { return (long)w.P > 8L * m.E; }
+static bool wide_regime(const Dims &m, const Work &w) { return wide_batch(w.P, m.E); }
 
 static int grid_for(const Dims &m, int RT, int num_sms, int P) {
-    // items <= RT * (chunks), chunks <= P / kTokChunk + (active experts)
-    const long max_items = (long)RT * ((long)P / kTokChunk + m.E);
+    // items <= RT * (chunks), chunks <= P / kTokChunkNarrow + (active experts)
+    const long max_items = (long)RT * ((long)P / kTokChunkNarrow + m.E);
     return (int)(max_items < num_sms ? max_items : num_sms);
 }
 

@@ -20,7 +20,10 @@ struct Work {
     int32_t *offsets;      // [E+1]
     int32_t *active;       // [E]           experts with >= 1 pair, ascending
     int32_t *n_active;     // [1]
-    int32_t *chunk_pre;    // [E+1]         exclusive prefix over active experts of ceil(n_e / kTokChunk)
+    int32_t *chunk_pre;    // [E+1]         exclusive prefix over active experts of ceil(n_e / chunk)
+    int4 *chunk_info;      // [chunks]      per pair chunk: (expert, chunk of it, its first sorted
+                           //               position, pairs); chunks <= P / kTokChunkNarrow + E
+    int32_t *max_chunk;    // [1]           largest chunk (pairs)
     int32_t *perm;         // [P]           pair id at each sorted position
     int32_t *inv;          // [P]           sorted position of each pair
     float *h;              // [P][2 eh]     gate/up products (gate even, up odd), sorted order
@@ -46,7 +49,15 @@ struct Dims {
 };
 
 constexpr int kPermChunk = 1024;
-constexpr int kTokChunk = 32;  // pairs of one expert handled per expert-GEMV item
+// Pairs of one expert handled per expert-GEMV item: 32 once experts average
+// more than 8 pairs (the wide regime), 16 below that, where the expert
+// launches then need no four-n-tile path and keep every value in registers.
+constexpr int kTokChunk = 32;
+constexpr int kTokChunkNarrow = 16;
+__host__ __device__ inline bool wide_batch(int P, int E) { return (long)P > 8L * E; }
+__host__ __device__ inline int tok_chunk(int P, int E) {
+    return wide_batch(P, E) ? kTokChunk : kTokChunkNarrow;
+}
 
 // Device-side view of one layer of a context (api.cu), for launch sequences
 // that bring their own workspace.

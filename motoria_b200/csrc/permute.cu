@@ -91,10 +91,21 @@ __device__ int block_excl_scan(int v, int *total, int *sh /* >= 33 ints */) {
     return r;
 }
 
+// The pair chunks of one active expert (n pairs from sorted position off),
+// numbered from cpos in the list the expert launches walk: (e, chunk, first
+// sorted position of the expert, pairs in the chunk).
+__device__ __forceinline__ void write_chunks(int4 *chunk_info, int cpos, int e, int off, int n,
+                                             int chunk) {
+    for (int tc = 0; tc * chunk < n; tc++)
+        chunk_info[cpos + tc] = make_int4(e, tc, off, min(chunk, n - tc * chunk));
+}
+
 __global__ void __launch_bounds__(1024)
 k_perm_scan(int nchunks, int E, const int32_t *chunk_cnt, int32_t *chunk_base, int32_t *counts,
-            int32_t *offsets, int32_t *active, int32_t *n_active, int32_t *chunk_pre) {
+            int32_t *offsets, int32_t *active, int32_t *n_active, int32_t *chunk_pre,
+            int4 *chunk_info, int32_t *max_chunk, int chunk) {
     __shared__ int sh[33];
+    __shared__ int smax;
     const int e = threadIdx.x;
     int run = 0;
     if (e < E) {
@@ -109,19 +120,25 @@ k_perm_scan(int nchunks, int E, const int32_t *chunk_cnt, int32_t *chunk_base, i
     const int off = block_excl_scan(e < E ? run : 0, &total, sh);
     int nact, nchk;
     const int apos = block_excl_scan((e < E && run > 0) ? 1 : 0, &nact, sh);
-    const int cpos = block_excl_scan(e < E ? (run + kTokChunk - 1) / kTokChunk : 0, &nchk, sh);
+    const int cpos = block_excl_scan(e < E ? (run + chunk - 1) / chunk : 0, &nchk, sh);
+    if (e == 0) smax = 0;
+    __syncthreads();
     if (e < E) {
         offsets[e] = off;
         if (run > 0) {
             active[apos] = e;
             chunk_pre[apos] = cpos;
+            write_chunks(chunk_info, cpos, e, off, run, chunk);
+            atomicMax(&smax, min(chunk, run));
         }
         for (int c = 0; c < nchunks; c++) chunk_base[(size_t)c * E + e] += off;
     }
+    __syncthreads();
     if (e == 0) {
         offsets[E] = total;
         *n_active = nact;
         chunk_pre[nact] = nchk;
+        *max_chunk = smax;
     }
 }
 
@@ -140,14 +157,16 @@ __global__ void k_perm_scatter(const int32_t *idx, int P, int E, const int32_t *
 // pairs, in one CTA of 1024 threads (one pair each).
 __global__ void __launch_bounds__(1024)
 k_permute_small(const int32_t *idx, int P, int E, int32_t *counts, int32_t *offsets,
-                int32_t *active, int32_t *n_active, int32_t *chunk_pre, int32_t *perm,
-                int32_t *inv, int *err) {
+                int32_t *active, int32_t *n_active, int32_t *chunk_pre, int4 *chunk_info,
+                int32_t *max_chunk, int chunk, int32_t *perm, int32_t *inv, int *err) {
     extern __shared__ int32_t sm_i[];  // wcnt [32][E], base [E]
     __shared__ int sh[33];
+    __shared__ int smax;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     int32_t *wcnt = sm_i;
     int32_t *base = wcnt + 32 * E;
     for (int i = tid; i < 32 * E; i += 1024) wcnt[i] = 0;
+    if (tid == 0) smax = 0;
     __syncthreads();
     const int p = tid;
     int e = -1;
@@ -174,21 +193,24 @@ k_permute_small(const int32_t *idx, int P, int E, int32_t *counts, int32_t *offs
     int total, nact, nchk;
     const int off = block_excl_scan(tid < E ? run : 0, &total, sh);
     const int apos = block_excl_scan((tid < E && run > 0) ? 1 : 0, &nact, sh);
-    const int cpos = block_excl_scan(tid < E ? (run + kTokChunk - 1) / kTokChunk : 0, &nchk, sh);
+    const int cpos = block_excl_scan(tid < E ? (run + chunk - 1) / chunk : 0, &nchk, sh);
     if (tid < E) {
         offsets[tid] = off;
         base[tid] = off;
         if (run > 0) {
             active[apos] = tid;
             chunk_pre[apos] = cpos;
+            write_chunks(chunk_info, cpos, tid, off, run, chunk);
+            atomicMax(&smax, min(chunk, run));
         }
     }
+    __syncthreads();
     if (tid == 0) {
         offsets[E] = total;
         *n_active = nact;
         chunk_pre[nact] = nchk;
+        *max_chunk = smax;
     }
-    __syncthreads();
     if (e >= 0) {
         const int pos = base[e] + wcnt[warp * E + e] + lr;
         perm[pos] = p;
@@ -203,7 +225,9 @@ void launch_permute(const Dims &m, const Work &w, int *err, cudaStream_t s) {
         cudaFuncSetAttribute(k_permute_small, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)small_smem);
         k_permute_small<<<1, 1024, small_smem, s>>>(w.idx, P, E, w.counts, w.offsets, w.active,
-                                                     w.n_active, w.chunk_pre, w.perm, w.inv, err);
+                                                     w.n_active, w.chunk_pre, w.chunk_info,
+                                                     w.max_chunk, tok_chunk(P, E), w.perm,
+                                                     w.inv, err);
         return;
     }
     const size_t smem = sizeof(int32_t) * (size_t)E * (1 + kPermWarps);
@@ -212,7 +236,8 @@ void launch_permute(const Dims &m, const Work &w, int *err, cudaStream_t s) {
     k_perm_count<<<w.nchunks, kPermThreads, smem, s>>>(w.idx, P, E, w.rank, w.chunk_cnt, err);
     const int st = ((E + 31) / 32) * 32;
     k_perm_scan<<<1, st < 64 ? 64 : st, 0, s>>>(w.nchunks, E, w.chunk_cnt, w.chunk_base, w.counts,
-                                                w.offsets, w.active, w.n_active, w.chunk_pre);
+                                                w.offsets, w.active, w.n_active, w.chunk_pre,
+                                                w.chunk_info, w.max_chunk, tok_chunk(P, E));
     k_perm_scatter<<<(P + 255) / 256, 256, 0, s>>>(w.idx, P, E, w.rank, w.chunk_base, w.perm,
                                                    w.inv);
 }
