@@ -372,6 +372,7 @@ static size_t ws_layout(miag_ctx *c, int T, uint8_t *base, Work *w, float **x_de
     Work v{};
     v.T = T, v.P = (int)P, v.nchunks = nchunks;
     v.tg_count = (int32_t *)bump(p, (size_t)T * 4);  // zeroed with the workspace, kept zero by the router
+    v.shares = (uint8_t *)bump(p, kShareKinds * sizeof(ShareState));  // zero at creation
     v.xq = (int8_t *)bump(p, (size_t)T * m.d);
     v.dx = (float *)bump(p, (size_t)T * xs * 4);
     v.logits = (float *)bump(p, (size_t)T * m.E * 4);

@@ -51,6 +51,8 @@ struct GemvParams {
     const int32_t *offsets, *perm, *active, *n_active, *chunk_pre;
     const int4 *chunk_info;    // per pair chunk: (expert, chunk of it, segment start, pairs)
     const int32_t *max_chunk;  // largest chunk
+    ShareState *share;         // this launch kind's SM shares
+    int num_sms;
     const int8_t *xq;  // [rows][d]
     const float *dx;   // [rows][xs]
     const int32_t *pair_row;  // [P] activation row of each pair, or null: pair / K
@@ -143,7 +145,7 @@ struct ItemInfo {
 // Item `item` of the launch: row tile item % RT of pair chunk item / RT in
 // the permutation's chunk list (experts ascending, chunks in order).
 __device__ __forceinline__ ItemInfo decode_item(const GemvParams &p, int RT, int item) {
-    const int4 c = __ldg(p.chunk_info + item / RT);
+    const int4 c = __ldcg(p.chunk_info + item / RT);
     ItemInfo it;
     it.e = c.x, it.tc = c.y, it.seg0 = c.z, it.nq = c.w;
     it.rt = item % RT;
@@ -166,6 +168,9 @@ struct RingHead {
     uint64_t full[kMaxStages];      // stage holds its k tiles (TMA complete_tx)
     uint32_t released[kMaxStages];  // warps done with the stage, summed over rounds
     int tok[kTokChunk];             // activation rows of the pairs being staged
+    int slot, first, n_mine;        // this CTA's share of the items
+    int parity;                     // rate buffer read (-1: shares not weighted)
+    unsigned long long t_start;     // when the share's work began
 };
 static_assert(sizeof(RingHead) <= kBarBytes, "ring head");
 
@@ -325,6 +330,10 @@ __device__ void fill_region(const GemvParams &p, uint8_t *region, int rows_cap, 
 // exp runs in double precision (expf_cr): at full occupancy its latency
 // hides; in the expert launches' eight warps per SM it did not.
 __global__ void k_swiglu_q8(const float *gu, int P, int eh, int xs, int8_t *hq, float *hs) {
+    // lets down start its prologue (see k_expert_mma) before the products
+    // are complete
+    pdl_launch_dependents();
+    pdl_wait();
     const int nb = eh / MIAG_QK;
     const long task = (long)blockIdx.x * blockDim.x + threadIdx.x;
     if (task >= (long)P * nb) return;
@@ -590,12 +599,60 @@ __device__ __forceinline__ void run_item(const GemvParams &p, const ItemCtx &ic,
     }
 }
 
+// SM shares.  On B200 some SMs stream and compute the same items 15-35 %
+// slower than others, and the same SMs every launch; with equal shares the
+// launch ends with them.  So a launch with one CTA per SM gives slot s (the
+// CTA on SM s, normally) a contiguous share in proportion to rate[s], the
+// items a microsecond slot s achieved in earlier launches, and measures it
+// again (in the narrow regime, where items cost alike).  Every slot is
+// claimed exactly once whichever SMs the CTAs land on,
+// and every CTA derives the shares the same way from the same rates, so the
+// shares always partition the items; placement only decides how even the
+// end is.
+
+// Slot of this CTA: its SM's, else the next free one (thread 0).
+__device__ int claim_slot(ShareState *sh, int G, int *err) {
+    const int s0 = (int)(sm_id() % (unsigned)G);
+    for (int i = 0; i < G; i++) {
+        const int c = (s0 + i) % G;
+        if (atomicExch(&sh->taken[c], 1) == 0) return c;
+    }
+    set_error(err, kErrItemList);  // no free slot: the state was not reset
+    return -1;
+}
+
+// Sum of the rates of slots [0, j), the same float in every CTA and
+// nondecreasing in j: lane l holds slots [5l, 5l + 5); the sums of lanes
+// below the slot's lane are added one by one in lane order, then the slot's
+// first j - 5l rates in order.  Every prefix is so a sequential sum of the
+// one before it and a nonnegative term, and rounding is monotone.
+__device__ float rate_prefix(const float (&r)[kMaxSlots / 32], int j) {
+    constexpr int per = kMaxSlots / 32;
+    float own = 0.0f;
+#pragma unroll
+    for (int i = 0; i < per; i++) own = __fadd_rn(own, r[i]);
+    const int l = min(j / per, 32);
+    float e = 0.0f;
+    for (int q = 0; q < 32; q++) {
+        const float o = __shfl_sync(0xffffffffu, own, q);
+        if (q < l) e = __fadd_rn(e, o);
+    }
+    if (l >= 32) return e;
+    float blk = 0.0f;
+#pragma unroll
+    for (int i = 0; i < per; i++) {
+        const float v = __shfl_sync(0xffffffffu, r[i], l);
+        if (i < j - per * l) blk = __fadd_rn(blk, v);
+    }
+    return j > per * l ? __fadd_rn(e, blk) : e;
+}
+
 // gate+up (kGU) or down: one launch over all items of all active experts.
 // Items (row tile, pair chunk) are numbered chunk by chunk, experts
-// ascending; CTA c runs a contiguous share, so consecutive items share their
-// activations.  (Handing the last 15-30 % of the items out one by one from
-// an atomic counter evened out the CTAs' end times but cost more in
-// activation stagings than it saved, at every batch size measured.)
+// ascending; each CTA runs a contiguous share (see SM shares above), so
+// consecutive items share their activations.  (Handing the last 15-30 % of
+// the items out one by one from an atomic counter evened out the end times
+// too, but cost more in activation stagings than it saved.)
 template <bool kGU, bool kWide>
 __global__ void __launch_bounds__(kGemvThreads, 1) k_expert_mma(GemvParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -606,22 +663,66 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_expert_mma(GemvParams p) {
     const int rows = kGU ? 2 * eh : d;       // matrix rows
     const int nb = Kb / MIAG_QK, xs = scale_pad(nb);
     const int NS = (KT + kStageKT - 1) / kStageKT;  // stages per item
-    const int n_items = __ldg(p.chunk_pre + __ldg(p.n_active)) * RT;
+    // gate/up reads what the router and the permutation just wrote; down,
+    // whose items and weights were settled before gate/up began (gate/up
+    // lets it start only after its own wait), decodes them and fills its
+    // ring while gate/up and the SwiGLU finish, and waits only before its
+    // activations.  Reads of the permutation go through L2.
+    if (kGU) pdl_wait();
+    const int n_items = __ldcg(p.chunk_pre + __ldcg(p.n_active)) * RT;
     const int G = gridDim.x;
 
     // The activation region holds the largest chunk of the launch; the rest
     // of shared memory deepens the ring.
-    const int nq_max = max(1, __ldg(p.max_chunk));
+    const int nq_max = max(1, __ldcg(p.max_chunk));
     const uint32_t region_bytes = region_size(nq_max, kWide, p.x_stride, xs);
     const int S = min(kMaxStages, (int)((kSmemBudget - kRingOff - (int)region_bytes) / kStageBytes));
-
-    const int first = (int)((long)n_items * blockIdx.x / G);
-    const int n_mine = (int)((long)n_items * (blockIdx.x + 1) / G) - first;
 
     RingHead *head = reinterpret_cast<RingHead *>(smem);
     uint8_t *stages = smem + kRingOff;
     int4 *table = reinterpret_cast<int4 *>(smem + kBarBytes);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // this CTA's share
+    ShareState *sh = p.share;
+    // (the wide regime keeps equal shares: there an item's cost follows its
+    // pair count, and rates measured on one launch's mix misled the next)
+    const bool weighted = !kWide && sh && G == p.num_sms && G <= kMaxSlots && n_items >= 4 * G;
+    const int parity = weighted ? (__ldcg(&sh->launches) & 1) : 0;
+    if (warp == 0) {
+        int slot = blockIdx.x;
+        if (weighted) {
+            if (lane == 0) slot = claim_slot(sh, G, p.err);
+            slot = __shfl_sync(0xffffffffu, slot, 0);
+        }
+        int first = (int)((long)n_items * blockIdx.x / G);
+        int last = (int)((long)n_items * (blockIdx.x + 1) / G);
+        if (weighted && slot >= 0) {
+            constexpr int per = kMaxSlots / 32;
+            float r[per];
+            bool ok = true;
+#pragma unroll
+            for (int i = 0; i < per; i++) {
+                const int c = per * lane + i;
+                r[i] = c < G ? __ldcg(&sh->rate[parity][c]) : 0.0f;
+                if (c < G && !(r[i] > 0.0f && r[i] < 1e30f)) ok = false;
+            }
+            if (__all_sync(0xffffffffu, ok)) {
+                const double total = rate_prefix(r, G);
+                const double a = rate_prefix(r, slot), b = rate_prefix(r, slot + 1);
+                first = (int)((double)n_items * a / total);
+                last = slot + 1 == G ? n_items : (int)((double)n_items * b / total);
+            } else {  // no rates yet: equal shares
+                first = (int)((long)n_items * slot / G);
+                last = (int)((long)n_items * (slot + 1) / G);
+            }
+        }
+        if (lane == 0) {
+            head->slot = slot, head->first = first, head->n_mine = max(0, last - first);
+            head->parity = weighted && slot >= 0 ? parity : -1;
+        }
+    }
+    __syncthreads();
+    const int first = head->first, n_mine = head->n_mine;
     for (int k = threadIdx.x; k < min(n_mine, kItemTable); k += kGemvThreads)
         table[k] = pack_item(decode_item(p, RT, first + k));
     if (threadIdx.x == 0) {
@@ -641,6 +742,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_expert_mma(GemvParams p) {
         for (int j = 0; j < min(S, n_mine * NS); j++, feed_next(p, fc, f)) feed_issue(p, fc, f, smem, j);
     }
     Feed fd = feed_at(p, fc, S);  // the refill of iteration 0
+    if (!kGU) pdl_wait();
+    pdl_launch_dependents();
 
     // ---- consumers
     uint8_t *region = smem + kRingOff + (size_t)S * kStageBytes;
@@ -655,6 +758,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_expert_mma(GemvParams p) {
     int cur_e = -1, cur_tc = -1;
     RingPos rp{0, 0, 0u};
     bool failed = false;
+    if (threadIdx.x == 0) head->t_start = global_ns();
     for (int k = 0; k < n_mine; k++) {
         const ItemInfo ii = unpack_item(item_entry(p, table, first, RT, k));
         const int seg0 = ii.seg0, t0 = ii.tc * p.chunk, nq = ii.nq;
@@ -677,6 +781,26 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_expert_mma(GemvParams p) {
         for (int j = total - 1; j >= 0 && j >= total - S; j--)
             mbar_wait(&head->full[j % S], (j / S) & 1);
     }
+    if (threadIdx.x == 0 && head->parity >= 0) {
+        // this share's rate, into the buffer the next launch reads
+        const int parity = head->parity, slot = head->slot;
+        ShareState *sh = p.share;
+        const float old = __ldcg(&sh->rate[parity][slot]);
+        const float us = (float)(global_ns() - head->t_start) * 1e-3f;
+        float rate = old;
+        if (n_mine > 0 && us > 0.5f) {
+            const float now = (float)n_mine / us;
+            rate = old > 0.0f ? 0.75f * old + 0.25f * now : now;
+        }
+        sh->rate[parity ^ 1][slot] = rate;
+        __threadfence();
+        if (atomicAdd(&sh->done, 1) == G - 1) {  // the last CTA: clear for the next launch
+            for (int c = 0; c < G; c++) sh->taken[c] = 0;
+            sh->done = 0;
+            __threadfence();
+            atomicAdd(&sh->launches, 1);
+        }
+    }
 }
 
 // x[t] += w_j * y_j for j = 0..K-1 in order (forward.c:194).
@@ -686,6 +810,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_expert_mma(GemvParams p) {
 constexpr int kCombineMaxK = 16;
 __global__ void k_combine(float *x, int d, int K, const float *w, const float *y,
                           const int32_t *pos) {
+    pdl_wait();
+    pdl_launch_dependents();
     const int t = blockIdx.x;
     const int i = 4 * (blockIdx.y * blockDim.x + threadIdx.x);
     if (i >= d) return;
@@ -769,34 +895,42 @@ static int grid_for(const Dims &m, int RT, int num_sms, int P) {
     return (int)(max_items < num_sms ? max_items : num_sms);
 }
 
+// The SM-share state of launch kind `kind` (gate/up, down x narrow, wide).
+static void set_share(GemvParams &p, const Work &w, int num_sms, int kind) {
+    p.share = w.shares ? reinterpret_cast<ShareState *>(w.shares) + kind : nullptr;
+    p.num_sms = num_sms;
+}
+
 void launch_gateup(const Dims &m, const StoreLayout &lay, const LayerDev &L, const Work &w,
                    int num_sms, int *err, cudaStream_t s) {
     GemvParams p{};
     fill_params(p, m, lay, L, w, err);
     geometry(p, true);
+    set_share(p, w, num_sms, 0 + (wide_regime(m, w) ? 1 : 0));
     const dim3 grid(grid_for(m, lay.gu_rt, num_sms, w.P));
-    if (wide_regime(m, w)) k_expert_mma<true, true><<<grid, kGemvThreads, kSmemBudget, s>>>(p);
-    else k_expert_mma<true, false><<<grid, kGemvThreads, kSmemBudget, s>>>(p);
+    launch_dependent(wide_regime(m, w) ? k_expert_mma<true, true> : k_expert_mma<true, false>, grid,
+                     dim3(kGemvThreads), kSmemBudget, s, p);
 }
 
 void launch_down(const Dims &m, const StoreLayout &lay, const LayerDev &L, const Work &w,
                  int num_sms, int *err, cudaStream_t s) {
     if (w.P > 0) {
         const long tasks = (long)w.P * (m.eh / MIAG_QK);
-        k_swiglu_q8<<<(unsigned)((tasks + 127) / 128), 128, 0, s>>>(
-            w.h, w.P, m.eh, scale_pad(m.eh / MIAG_QK), w.hq, w.hs);
+        launch_dependent(k_swiglu_q8, dim3((unsigned)((tasks + 127) / 128)), dim3(128), 0, s, w.h,
+                         w.P, m.eh, scale_pad(m.eh / MIAG_QK), w.hq, w.hs);
     }
     GemvParams p{};
     fill_params(p, m, lay, L, w, err);
     geometry(p, false);
+    set_share(p, w, num_sms, 2 + (wide_regime(m, w) ? 1 : 0));
     const dim3 grid(grid_for(m, lay.dn_rt, num_sms, w.P));
-    if (wide_regime(m, w)) k_expert_mma<false, true><<<grid, kGemvThreads, kSmemBudget, s>>>(p);
-    else k_expert_mma<false, false><<<grid, kGemvThreads, kSmemBudget, s>>>(p);
+    launch_dependent(wide_regime(m, w) ? k_expert_mma<false, true> : k_expert_mma<false, false>,
+                     grid, dim3(kGemvThreads), kSmemBudget, s, p);
 }
 
 void launch_combine(const Dims &m, const Work &w, float *x, cudaStream_t s) {
     dim3 grid(w.T, (m.d / 4 + 127) / 128);
-    k_combine<<<grid, 128, 0, s>>>(x, m.d, m.K, w.w, w.y, w.y_pos);
+    launch_dependent(k_combine, grid, dim3(128), 0, s, x, m.d, m.K, w.w, w.y, w.y_pos);
 }
 
 }  // namespace miag

@@ -24,6 +24,8 @@ struct Work {
     int4 *chunk_info;      // [chunks]      per pair chunk: (expert, chunk of it, its first sorted
                            //               position, pairs); chunks <= P / kTokChunkNarrow + E
     int32_t *max_chunk;    // [1]           largest chunk (pairs)
+    uint8_t *shares;       // [kShareKinds] ShareState: the expert launches' SM shares; zero at
+                           //               creation, kept by the launches themselves
     int32_t *perm;         // [P]           pair id at each sorted position
     int32_t *inv;          // [P]           sorted position of each pair
     float *h;              // [P][2 eh]     gate/up products (gate even, up odd), sorted order
@@ -49,6 +51,19 @@ struct Dims {
 };
 
 constexpr int kPermChunk = 1024;
+
+// How an expert launch (gate/up or down, narrow or wide regime) splits its
+// items over the SMs: shares in proportion to each SM's measured item rate.
+// A launch reads rate[launches & 1] and writes the other buffer; the last
+// CTA to finish clears `taken`, `done` and counts the launch.
+constexpr int kMaxSlots = 160;
+constexpr int kShareKinds = 4;
+struct ShareState {
+    int launches;              // launches finished
+    int done;                  // CTAs finished in the running launch
+    int taken[kMaxSlots];      // slot claimed in the running launch
+    float rate[2][kMaxSlots];  // items a microsecond, a running average (0: none yet)
+};
 // Pairs of one expert handled per expert-GEMV item: 32 once experts average
 // more than 8 pairs (the wide regime), 16 below that, where the expert
 // launches then need no four-n-tile path and keep every value in registers.

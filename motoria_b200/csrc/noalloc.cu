@@ -87,6 +87,7 @@ size_t layout(const Dims &m, int T, uint8_t *base, Work *w) {
     Work v{};
     v.T = T, v.P = (int)P, v.nchunks = nchunks;
     v.tg_count = reinterpret_cast<int32_t *>(bump(p, (size_t)kNoAllocGroups * 4));
+    v.shares = reinterpret_cast<uint8_t *>(bump(p, kShareKinds * sizeof(ShareState)));  // fixed offset too
     v.xq = reinterpret_cast<int8_t *>(bump(p, (size_t)T * m.d));
     v.dx = reinterpret_cast<float *>(bump(p, (size_t)T * xs * 4));
     v.logits = reinterpret_cast<float *>(bump(p, (size_t)T * m.E * 4));

@@ -23,6 +23,8 @@ constexpr int kPermWarps = kPermThreads / 32;
 
 __global__ void __launch_bounds__(kPermThreads)
 k_perm_count(const int32_t *idx, int P, int E, int32_t *rank, int32_t *chunk_cnt, int *err) {
+    pdl_wait();
+    pdl_launch_dependents();
     extern __shared__ int32_t sh[];  // cnt[E], wcnt[kPermWarps][E]
     int32_t *cnt = sh;
     int32_t *wcnt = sh + E;
@@ -104,6 +106,8 @@ __global__ void __launch_bounds__(1024)
 k_perm_scan(int nchunks, int E, const int32_t *chunk_cnt, int32_t *chunk_base, int32_t *counts,
             int32_t *offsets, int32_t *active, int32_t *n_active, int32_t *chunk_pre,
             int4 *chunk_info, int32_t *max_chunk, int chunk) {
+    pdl_wait();
+    pdl_launch_dependents();
     __shared__ int sh[33];
     __shared__ int smax;
     const int e = threadIdx.x;
@@ -144,6 +148,8 @@ k_perm_scan(int nchunks, int E, const int32_t *chunk_cnt, int32_t *chunk_base, i
 
 __global__ void k_perm_scatter(const int32_t *idx, int P, int E, const int32_t *rank,
                                const int32_t *chunk_base, int32_t *perm, int32_t *inv) {
+    pdl_wait();
+    pdl_launch_dependents();
     const int p = blockIdx.x * blockDim.x + threadIdx.x;
     if (p >= P) return;
     const int e = idx[p];
@@ -159,6 +165,8 @@ __global__ void __launch_bounds__(1024)
 k_permute_small(const int32_t *idx, int P, int E, int32_t *counts, int32_t *offsets,
                 int32_t *active, int32_t *n_active, int32_t *chunk_pre, int4 *chunk_info,
                 int32_t *max_chunk, int chunk, int32_t *perm, int32_t *inv, int *err) {
+    pdl_wait();
+    pdl_launch_dependents();
     extern __shared__ int32_t sm_i[];  // wcnt [32][E], base [E]
     __shared__ int sh[33];
     __shared__ int smax;
@@ -224,22 +232,22 @@ void launch_permute(const Dims &m, const Work &w, int *err, cudaStream_t s) {
     if (P <= kPermChunk && small_smem <= 200 * 1024) {
         cudaFuncSetAttribute(k_permute_small, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)small_smem);
-        k_permute_small<<<1, 1024, small_smem, s>>>(w.idx, P, E, w.counts, w.offsets, w.active,
-                                                     w.n_active, w.chunk_pre, w.chunk_info,
-                                                     w.max_chunk, tok_chunk(P, E), w.perm,
-                                                     w.inv, err);
+        launch_dependent(k_permute_small, dim3(1), dim3(1024), small_smem, s, w.idx, P, E, w.counts,
+                         w.offsets, w.active, w.n_active, w.chunk_pre, w.chunk_info, w.max_chunk,
+                         tok_chunk(P, E), w.perm, w.inv, err);
         return;
     }
     const size_t smem = sizeof(int32_t) * (size_t)E * (1 + kPermWarps);
     if (smem > 48 * 1024)
         cudaFuncSetAttribute(k_perm_count, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    k_perm_count<<<w.nchunks, kPermThreads, smem, s>>>(w.idx, P, E, w.rank, w.chunk_cnt, err);
+    launch_dependent(k_perm_count, dim3(w.nchunks), dim3(kPermThreads), smem, s, w.idx, P, E, w.rank,
+                     w.chunk_cnt, err);
     const int st = ((E + 31) / 32) * 32;
-    k_perm_scan<<<1, st < 64 ? 64 : st, 0, s>>>(w.nchunks, E, w.chunk_cnt, w.chunk_base, w.counts,
-                                                w.offsets, w.active, w.n_active, w.chunk_pre,
-                                                w.chunk_info, w.max_chunk, tok_chunk(P, E));
-    k_perm_scatter<<<(P + 255) / 256, 256, 0, s>>>(w.idx, P, E, w.rank, w.chunk_base, w.perm,
-                                                   w.inv);
+    launch_dependent(k_perm_scan, dim3(1), dim3(st < 64 ? 64 : st), 0, s, w.nchunks, E, w.chunk_cnt,
+                     w.chunk_base, w.counts, w.offsets, w.active, w.n_active, w.chunk_pre,
+                     w.chunk_info, w.max_chunk, tok_chunk(P, E));
+    launch_dependent(k_perm_scatter, dim3((P + 255) / 256), dim3(256), 0, s, w.idx, P, E, w.rank,
+                     w.chunk_base, w.perm, w.inv);
 }
 
 int permute_launches(int P, int E) {

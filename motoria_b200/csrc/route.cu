@@ -137,8 +137,11 @@ __global__ void __launch_bounds__(9 * 32, 1) k_route(RouteParams p, int W, int s
         fence_barrier_init();
     }
     __syncthreads();
+    pdl_launch_dependents();
 
     if (warp == W) {
+        // (the router is the layer's own: streamed before the previous
+        // kernel of the stream has finished)
         // Producer: the router chunks, 32 KiB bulk copies (on B200 a bulk copy
         // occupies the copy engine ~0.26 us whatever its size up to ~8 KiB,
         // so small chunks cap the SM's ingest).
@@ -161,6 +164,7 @@ __global__ void __launch_bounds__(9 * 32, 1) k_route(RouteParams p, int W, int s
         return;
     }
 
+    pdl_wait();  // x, and the counters and outputs the previous call used
     const int tw0 = tg0 + warp * R;  // this warp's first token
     const int nt = max(0, min(R, p.T - tw0));
     float *xw = xs_all + (size_t)warp * R * d;  // this warp's rows: x, then xn in place
@@ -368,7 +372,7 @@ template <int R>
 static void launch_r(const RouteParams &p, dim3 grid, int W, int stages, size_t smem,
                      cudaStream_t s) {
     cudaFuncSetAttribute(k_route<R>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    k_route<R><<<grid, (W + 1) * 32, smem, s>>>(p, W, stages);
+    launch_dependent(k_route<R>, grid, dim3((W + 1) * 32), smem, s, p, W, stages);
 }
 
 void launch_route(const Dims &m, const LayerDev &L, const float *x, const Work &w, int *err,

@@ -228,6 +228,31 @@ def test_batch_invariance_and_determinism(qwen):
         assert np.array_equal(part.view(np.uint32), full[lo:hi].view(np.uint32))
 
 
+def test_sm_shares_leave_results_unchanged(torch_cuda):
+    """The expert launches split their items over the SMs by rates measured
+    in earlier launches, so shares differ from call to call.  Whatever the
+    split, every output bit must equal the first call on a fresh context
+    (equal shares); both regimes, and Zipf routing with its hot experts."""
+    build.build()
+    cases = [(layer, T, 50 + i) for i, (layer, T) in
+             enumerate([(0, 64), (1, 64), (0, 200), (0, 1500), (1, 1500)])]
+    with MoEEngine(QWEN, n_layers=2) as eng:
+        eng.load_layer(0, get_layer(QWEN, False))
+        eng.load_layer(1, get_layer(QWEN, True))
+        first = {c: eng.moe(synth.tokens(QWEN, c[2], c[1]), layer=c[0]) for c in cases[:1]}
+    with MoEEngine(QWEN, n_layers=2) as eng:
+        eng.load_layer(0, get_layer(QWEN, False))
+        eng.load_layer(1, get_layer(QWEN, True))
+        for c in cases[1:]:  # each on a fresh context first: equal shares
+            with MoEEngine(QWEN, n_layers=2) as fresh:
+                fresh.load_layer(c[0], get_layer(QWEN, c[0] == 1))
+                first[c] = fresh.moe(synth.tokens(QWEN, c[2], c[1]), layer=c[0])
+        for rep in range(6):  # the same context again and again: weighted shares
+            for c in cases:
+                got = eng.moe(synth.tokens(QWEN, c[2], c[1]), layer=c[0])
+                assert np.array_equal(got.view(np.uint32), first[c].view(np.uint32)), (rep, c)
+
+
 def test_hot_experts_take_every_token(torch_cuda, orc):
     """A bias that pushes experts 3 and 77 into every token's top-k gives them
     T pairs each, exercising many pair rounds per staged weight tile."""
