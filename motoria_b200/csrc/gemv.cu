@@ -324,11 +324,11 @@ __device__ void fill_region(const GemvParams &p, uint8_t *region, int rows_cap, 
 }
 
 // h = silu(gate) * up (forward.c:188-191) for every pair, quantized to Q8_0
-// exactly as mia_matvec quantizes its input (matmul.c:93, quant.c:11-27):
-// one thread per (pair, 32-block), its sixteen 16-byte loads of the block's
-// (gate, up) values issued together.  A launch of its own because the SiLU's
-// exp runs in double precision (expf_cr): at full occupancy its latency
-// hides; in the expert launches' eight warps per SM it did not.
+// exactly as mia_matvec quantizes its input (matmul.c:93, quant.c:11-27).
+// A launch of its own because the SiLU's exp runs in double precision
+// (expf_cr), whose latency only many threads hide: four threads per
+// (pair, 32-block), eight values each, their loads issued together; the
+// block maximum is combined over the four lanes (max is exact in any order).
 __global__ void k_swiglu_q8(const float *gu, int P, int eh, int xs, int8_t *hq, float *hs) {
     // lets down start its prologue (see k_expert_mma) before the products
     // are complete
@@ -336,39 +336,39 @@ __global__ void k_swiglu_q8(const float *gu, int P, int eh, int xs, int8_t *hq, 
     pdl_wait();
     const int nb = eh / MIAG_QK;
     const long task = (long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (task >= (long)P * nb) return;
-    const int j = (int)(task / nb), b = (int)(task % nb);
-    const float4 *src = reinterpret_cast<const float4 *>(gu + (size_t)j * 2 * eh + (size_t)b * 2 * MIAG_QK);
-    float4 g[16];
+    const long n_tasks = (long)P * nb * 4;
+    const bool live = task < n_tasks;  // whole quads are live or not (n_tasks % 4 == 0)
+    const long blk = live ? task >> 2 : 0;
+    const int j = (int)(blk / nb), b = (int)(blk % nb), q = (int)(task & 3);
+    // values 8q .. 8q+7 of the block: (gate, up) floats 16q .. 16q+15
+    const float4 *src = reinterpret_cast<const float4 *>(gu + (size_t)j * 2 * eh + (size_t)b * 2 * MIAG_QK) + 4 * q;
+    float4 g[4];
 #pragma unroll
-    for (int k = 0; k < 16; k++) g[k] = __ldg(src + k);
-    float4 v[8];
+    for (int k = 0; k < 4; k++) g[k] = live ? __ldg(src + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+    float v[8];
 #pragma unroll
-    for (int k = 0; k < 8; k++) {
-        v[k].x = swiglu_ref(g[2 * k].x, g[2 * k].y);
-        v[k].y = swiglu_ref(g[2 * k].z, g[2 * k].w);
-        v[k].z = swiglu_ref(g[2 * k + 1].x, g[2 * k + 1].y);
-        v[k].w = swiglu_ref(g[2 * k + 1].z, g[2 * k + 1].w);
+    for (int k = 0; k < 4; k++) {
+        v[2 * k] = swiglu_ref(g[k].x, g[k].y);
+        v[2 * k + 1] = swiglu_ref(g[k].z, g[k].w);
     }
     float a = 0.0f;
 #pragma unroll
-    for (int k = 0; k < 8; k++)
-        a = fmaxf(a, fmaxf(fmaxf(fabsf(v[k].x), fabsf(v[k].y)), fmaxf(fabsf(v[k].z), fabsf(v[k].w))));
+    for (int k = 0; k < 8; k++) a = fmaxf(a, fabsf(v[k]));
+    a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 1));
+    a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 2));
+    if (!live) return;
     const float dq = __fdiv_rn(a, 127.0f);
     const float id = dq != 0.0f ? __fdiv_rn(1.0f, dq) : 0.0f;
-    uint32_t q[8];
+    uint32_t w[2];
 #pragma unroll
-    for (int k = 0; k < 8; k++) {
-        const uint32_t q0 = (uint8_t)(int8_t)roundf(__fmul_rn(v[k].x, id));
-        const uint32_t q1 = (uint8_t)(int8_t)roundf(__fmul_rn(v[k].y, id));
-        const uint32_t q2 = (uint8_t)(int8_t)roundf(__fmul_rn(v[k].z, id));
-        const uint32_t q3 = (uint8_t)(int8_t)roundf(__fmul_rn(v[k].w, id));
-        q[k] = q0 | (q1 << 8) | (q2 << 16) | (q3 << 24);
+    for (int h = 0; h < 2; h++) {
+        uint32_t u = 0;
+#pragma unroll
+        for (int k = 0; k < 4; k++) u |= (uint32_t)(uint8_t)(int8_t)roundf(__fmul_rn(v[4 * h + k], id)) << (8 * k);
+        w[h] = u;
     }
-    uint4 *dst = reinterpret_cast<uint4 *>(hq + (size_t)j * eh + (size_t)b * MIAG_QK);
-    dst[0] = make_uint4(q[0], q[1], q[2], q[3]);
-    dst[1] = make_uint4(q[4], q[5], q[6], q[7]);
-    hs[(size_t)j * xs + b] = dq;
+    *reinterpret_cast<uint2 *>(hq + (size_t)j * eh + (size_t)b * MIAG_QK + 8 * q) = make_uint2(w[0], w[1]);
+    if (q == 0) hs[(size_t)j * xs + b] = dq;
 }
 
 __device__ __forceinline__ float4 lds128(uint32_t addr) {
@@ -915,7 +915,7 @@ void launch_gateup(const Dims &m, const StoreLayout &lay, const LayerDev &L, con
 void launch_down(const Dims &m, const StoreLayout &lay, const LayerDev &L, const Work &w,
                  int num_sms, int *err, cudaStream_t s) {
     if (w.P > 0) {
-        const long tasks = (long)w.P * (m.eh / MIAG_QK);
+        const long tasks = (long)w.P * (m.eh / MIAG_QK) * 4;
         launch_dependent(k_swiglu_q8, dim3((unsigned)((tasks + 127) / 128)), dim3(128), 0, s, w.h,
                          w.P, m.eh, scale_pad(m.eh / MIAG_QK), w.hq, w.hs);
     }

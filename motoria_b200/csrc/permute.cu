@@ -159,21 +159,52 @@ __global__ void k_perm_scatter(const int32_t *idx, int P, int E, const int32_t *
     inv[p] = pos;
 }
 
+// Exclusive block scan of one 64-bit value per thread (blockDim.x <= 1024).
+__device__ long long block_excl_scan64(long long v, long long *total, long long *sh /* >= 33 */) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    long long incl = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const long long n = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += n;
+    }
+    if (lane == 31) sh[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+        const int nw = (blockDim.x + 31) >> 5;
+        const long long s = lane < nw ? sh[lane] : 0;
+        long long si = s;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const long long n = __shfl_up_sync(0xffffffffu, si, o);
+            if (lane >= o) si += n;
+        }
+        sh[lane] = si - s;
+        if (lane == 31) sh[32] = si;
+    }
+    __syncthreads();
+    const long long r = sh[warp] + incl - v;
+    *total = sh[32];
+    __syncthreads();
+    return r;
+}
+
 // Everything between the top-k and the expert products, for at most 1024
-// pairs, in one CTA of 1024 threads (one pair each).
+// pairs, in one CTA of max(P, E) threads rounded to warps (one pair each;
+// thread e < E also owns expert e).
 __global__ void __launch_bounds__(1024)
 k_permute_small(const int32_t *idx, int P, int E, int32_t *counts, int32_t *offsets,
                 int32_t *active, int32_t *n_active, int32_t *chunk_pre, int4 *chunk_info,
                 int32_t *max_chunk, int chunk, int32_t *perm, int32_t *inv, int *err) {
     pdl_wait();
     pdl_launch_dependents();
-    extern __shared__ int32_t sm_i[];  // wcnt [32][E], base [E]
-    __shared__ int sh[33];
+    extern __shared__ int32_t sm_i[];  // wcnt [warps][E], base [E]
+    __shared__ long long sh[33];
     __shared__ int smax;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
     int32_t *wcnt = sm_i;
-    int32_t *base = wcnt + 32 * E;
-    for (int i = tid; i < 32 * E; i += 1024) wcnt[i] = 0;
+    int32_t *base = wcnt + nw * E;
+    for (int i = tid; i < nw * E; i += blockDim.x) wcnt[i] = 0;
     if (tid == 0) smax = 0;
     __syncthreads();
     const int p = tid;
@@ -191,17 +222,23 @@ k_permute_small(const int32_t *idx, int P, int E, int32_t *counts, int32_t *offs
     __syncthreads();
     int run = 0;
     if (tid < E) {
-        for (int ww = 0; ww < 32; ww++) {
+        for (int ww = 0; ww < nw; ww++) {
             const int c = wcnt[ww * E + tid];
             wcnt[ww * E + tid] = run;
             run += c;
         }
         counts[tid] = run;
     }
-    int total, nact, nchk;
-    const int off = block_excl_scan(tid < E ? run : 0, &total, sh);
-    const int apos = block_excl_scan((tid < E && run > 0) ? 1 : 0, &nact, sh);
-    const int cpos = block_excl_scan(tid < E ? (run + chunk - 1) / chunk : 0, &nchk, sh);
+    // the three scans at once, in 21-bit fields (each total is at most
+    // P + E + P / chunk < 2^21): pairs, active experts, chunks
+    constexpr long long kF = (1ll << 21) - 1;
+    const long long v = tid < E ? (long long)run | ((long long)(run > 0) << 21) |
+                                      ((long long)((run + chunk - 1) / chunk) << 42)
+                                : 0ll;
+    long long tot;
+    const long long ex = block_excl_scan64(v, &tot, sh);
+    const int off = (int)(ex & kF), apos = (int)((ex >> 21) & kF), cpos = (int)(ex >> 42);
+    const int total = (int)(tot & kF), nact = (int)((tot >> 21) & kF), nchk = (int)(tot >> 42);
     if (tid < E) {
         offsets[tid] = off;
         base[tid] = off;
@@ -228,11 +265,12 @@ k_permute_small(const int32_t *idx, int P, int E, int32_t *counts, int32_t *offs
 
 void launch_permute(const Dims &m, const Work &w, int *err, cudaStream_t s) {
     const int P = w.P, E = m.E;
-    const size_t small_smem = (size_t)(32 * E) * 4 + (size_t)E * 4;
-    if (P <= kPermChunk && small_smem <= 200 * 1024) {
+    const int threads = ((P > E ? P : E) + 31) / 32 * 32;
+    const size_t small_smem = (size_t)(threads / 32 * E) * 4 + (size_t)E * 4;
+    if (P <= kPermChunk && E <= 1024 && small_smem <= 200 * 1024) {
         cudaFuncSetAttribute(k_permute_small, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)small_smem);
-        launch_dependent(k_permute_small, dim3(1), dim3(1024), small_smem, s, w.idx, P, E, w.counts,
+        launch_dependent(k_permute_small, dim3(1), dim3(threads), small_smem, s, w.idx, P, E, w.counts,
                          w.offsets, w.active, w.n_active, w.chunk_pre, w.chunk_info, w.max_chunk,
                          tok_chunk(P, E), w.perm, w.inv, err);
         return;
@@ -251,7 +289,10 @@ void launch_permute(const Dims &m, const Work &w, int *err, cudaStream_t s) {
 }
 
 int permute_launches(int P, int E) {
-    return (P <= kPermChunk && (size_t)(32 * E) * 4 + (size_t)E * 4 <= 200 * 1024) ? 1 : 3;
+    const int threads = ((P > E ? P : E) + 31) / 32 * 32;
+    return (P <= kPermChunk && E <= 1024 && (size_t)(threads / 32 * E) * 4 + (size_t)E * 4 <= 200 * 1024)
+               ? 1
+               : 3;
 }
 
 }  // namespace miag
