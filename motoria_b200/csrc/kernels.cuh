@@ -40,7 +40,7 @@ struct Work {
 
 struct LayerDev {
     const float *ffn_norm;  // [d]
-    const float *router_t;  // [ceil(E/32)][d][32]  router, 32-expert groups contiguous
+    const float *router_t;  // [ceil(E/32)][d/4][32][4]  router, 32-expert groups contiguous
     const float *bias;      // [E] or nullptr
     const uint8_t *experts; // E * layout.expert_bytes
 };

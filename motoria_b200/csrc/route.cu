@@ -14,7 +14,7 @@
 //   3. lane e computes the router logit of expert 32*eg + e for the warp's
 //      tokens as the reference's serial fp32 sum (rounded multiply, then
 //      rounded add, i = 0..d-1 in order).  The group's router slice, stored
-//      [group][i][32] so it is contiguous, streams through a ring of
+//      [group][i/4][32][4] so it is contiguous, streams through a ring of
 //      shared-memory chunks that the producer fills with 1-D TMA bulk copies
 //      and all consumer warps read;
 //   4. the last CTA of a token group to finish (a counter per group) runs
@@ -84,29 +84,53 @@ __host__ __device__ inline size_t route_smem(int d, int R, int W, int stages) {
            (size_t)d * 4;
 }
 
-// Router rows [u, u + 64) of a chunk for R tokens: acc[r] += w_i * xn[r][i]
-// in order, each product and sum rounded (matmul.c:13-17), with scalar
-// round-to-nearest intrinsics, which the compiler never fuses.  Written as
-// one straight run (loads at compile-time offsets): on B200 this measured
-// ~6.4 cycles a row for one token and ~4.5 a token-row for two, against
-// ~7.5 and ~4.9 for a software-pipelined form.
-template <int R>
-__device__ __forceinline__ void router_rows64(float (&acc)[R], const float *wc, const float *xc,
-                                              int d) {
-#pragma unroll
-    for (int k4 = 0; k4 < 64; k4 += 4) {
-        float4 xv[R];
-#pragma unroll
-        for (int r = 0; r < R; r++) xv[r] = *reinterpret_cast<const float4 *>(xc + (size_t)r * d + k4);
-        const float w0 = wc[(k4 + 0) * 32], w1 = wc[(k4 + 1) * 32];
-        const float w2 = wc[(k4 + 2) * 32], w3 = wc[(k4 + 3) * 32];
+// Router rows of a chunk for R tokens, `groups` groups of four rows:
+// acc[r] += w_i * xn[r][i] in order, each product and sum rounded
+// (matmul.c:13-17), with scalar round-to-nearest intrinsics, which the
+// compiler never fuses.  w4: this lane's weights of row group g at w4[32 g]
+// (one 16-byte load).  The chain of adds is serial, so the products of the
+// next group are formed between the adds of this one: on B200 the loop alone
+// measured 5.8 cycles a row for one token, against 9 with the four rows'
+// loads and products in line and 5.2 for the bare chain of adds.
+template <int R, int kGroups = 0>  // kGroups > 0: a compile-time group count, fully unrolled
+__device__ __forceinline__ void router_chunk(float (&acc)[R], const float4 *w4, const float *xc,
+                                             int d, int groups_rt) {
+    const int groups = kGroups > 0 ? kGroups : groups_rt;
+    float p[R][4];
+    {
+        const float4 w = w4[0];
 #pragma unroll
         for (int r = 0; r < R; r++) {
-            acc[r] = __fadd_rn(acc[r], __fmul_rn(w0, xv[r].x));
-            acc[r] = __fadd_rn(acc[r], __fmul_rn(w1, xv[r].y));
-            acc[r] = __fadd_rn(acc[r], __fmul_rn(w2, xv[r].z));
-            acc[r] = __fadd_rn(acc[r], __fmul_rn(w3, xv[r].w));
+            const float4 xv = *reinterpret_cast<const float4 *>(xc + (size_t)r * d);
+            p[r][0] = __fmul_rn(w.x, xv.x), p[r][1] = __fmul_rn(w.y, xv.y);
+            p[r][2] = __fmul_rn(w.z, xv.z), p[r][3] = __fmul_rn(w.w, xv.w);
         }
+    }
+#pragma unroll (kGroups > 0 ? kGroups : 16)
+    for (int g = 1; g < groups; g++) {
+        const float4 w = w4[g * 32];
+        float4 xv[R];
+#pragma unroll
+        for (int r = 0; r < R; r++) xv[r] = *reinterpret_cast<const float4 *>(xc + (size_t)r * d + 4 * g);
+#pragma unroll
+        for (int r = 0; r < R; r++) {
+            acc[r] = __fadd_rn(acc[r], p[r][0]);
+            const float q0 = __fmul_rn(w.x, xv[r].x);
+            acc[r] = __fadd_rn(acc[r], p[r][1]);
+            const float q1 = __fmul_rn(w.y, xv[r].y);
+            acc[r] = __fadd_rn(acc[r], p[r][2]);
+            const float q2 = __fmul_rn(w.z, xv[r].z);
+            acc[r] = __fadd_rn(acc[r], p[r][3]);
+            const float q3 = __fmul_rn(w.w, xv[r].w);
+            p[r][0] = q0, p[r][1] = q1, p[r][2] = q2, p[r][3] = q3;
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < R; r++) {
+        acc[r] = __fadd_rn(acc[r], p[r][0]);
+        acc[r] = __fadd_rn(acc[r], p[r][1]);
+        acc[r] = __fadd_rn(acc[r], p[r][2]);
+        acc[r] = __fadd_rn(acc[r], p[r][3]);
     }
 }
 
@@ -172,18 +196,18 @@ __global__ void __launch_bounds__(9 * 32, 1) k_route(RouteParams p, int W, int s
     // The warp's token rows and the shared ffn_norm come in through plain
     // coalesced loads: with these rows bulk-copied instead, the norm and the
     // router loop that follow measured 2-2.5x slower on B200.
-    // Loads go out eight at a time before their stores, so a row costs about
-    // one memory latency rather than one per float4.
+    // Loads go out sixteen at a time before their stores, so a row of up to
+    // 2048 costs one memory latency.
     for (int r = 0; r < nt; r++) {
         const float4 *src = reinterpret_cast<const float4 *>(p.x + (size_t)(tw0 + r) * d);
         float4 *dst = reinterpret_cast<float4 *>(xw + (size_t)r * d);
-        for (int i0 = lane; i0 < d / 4; i0 += 8 * 32) {
-            float4 v[8];
+        for (int i0 = lane; i0 < d / 4; i0 += 16 * 32) {
+            float4 v[16];
 #pragma unroll
-            for (int u = 0; u < 8; u++)
+            for (int u = 0; u < 16; u++)
                 if (i0 + 32 * u < d / 4) v[u] = __ldg(src + i0 + 32 * u);
 #pragma unroll
-            for (int u = 0; u < 8; u++)
+            for (int u = 0; u < 16; u++)
                 if (i0 + 32 * u < d / 4) dst[i0 + 32 * u] = v[u];
         }
     }
@@ -305,24 +329,15 @@ __global__ void __launch_bounds__(9 * 32, 1) k_route(RouteParams p, int W, int s
                 failed = true;
             }
         }
-        const float *wc = ring + (size_t)s * kRouteChunk * 32 + lane;
+        const float4 *w4 = reinterpret_cast<const float4 *>(ring + (size_t)s * kRouteChunk * 32) + lane;
         const float *xc = xw + (size_t)ch * kRouteChunk;
-        // a warp past the last token only keeps the ring turning
+        // a warp past the last token only keeps the ring turning; rows is a
+        // multiple of four (d is a multiple of 32)
         const int rows = nt > 0 ? min(kRouteChunk, d - ch * kRouteChunk) : 0;
-        int u = 0;
-        for (; u + 64 <= rows; u += 64) router_rows64<R>(acc, wc + u * 32, xc + u, d);
-        for (; u < rows; u += 4) {  // d % 64 tail, rows of four (d is a multiple of 32)
-            float4 xv[R];
-#pragma unroll
-            for (int r = 0; r < R; r++) xv[r] = *reinterpret_cast<const float4 *>(xc + (size_t)r * d + u);
-#pragma unroll
-            for (int r = 0; r < R; r++) {
-                acc[r] = __fadd_rn(acc[r], __fmul_rn(wc[(u + 0) * 32], xv[r].x));
-                acc[r] = __fadd_rn(acc[r], __fmul_rn(wc[(u + 1) * 32], xv[r].y));
-                acc[r] = __fadd_rn(acc[r], __fmul_rn(wc[(u + 2) * 32], xv[r].z));
-                acc[r] = __fadd_rn(acc[r], __fmul_rn(wc[(u + 3) * 32], xv[r].w));
-            }
-        }
+        // full chunks in straight-line code: with a remainder loop after an
+        // unrolled body the loop ran at ~9.7 cycles a row on B200
+        if (rows == kRouteChunk) router_chunk<R, kRouteChunk / 4>(acc, w4, xc, d, kRouteChunk / 4);
+        else if (rows > 0) router_chunk<R>(acc, w4, xc, d, rows / 4);
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
     }

@@ -49,8 +49,9 @@ __global__ void k_repack(const uint8_t *aos, size_t aos_stride, size_t off_up, s
     }
 }
 
-// router [E][d] -> grouped [ceil(E/32)][d][32]: a group of 32 experts is one
-// contiguous slice, row i holding those experts' weights for input i.
+// router [E][d] -> grouped [ceil(E/32)][d/4][32][4]: a group of 32 experts is
+// one contiguous slice; within it, the weights of expert 32g + l for inputs
+// 4j .. 4j+3 are one 16-byte vector, lane l's in a row of 32.
 __global__ void k_group_router(const float *in, float *out, int E, int d) {
     __shared__ float tile[32][33];
     const int i0 = blockIdx.x * 32, g = blockIdx.y;
@@ -61,7 +62,7 @@ __global__ void k_group_router(const float *in, float *out, int E, int d) {
     __syncthreads();
     for (int k = threadIdx.y; k < 32; k += blockDim.y) {
         const int i = i0 + k;
-        if (i < d) out[((size_t)g * d + i) * 32 + threadIdx.x] = tile[threadIdx.x][k];
+        if (i < d) out[(((size_t)g * (d / 4) + i / 4) * 32 + threadIdx.x) * 4 + (i & 3)] = tile[threadIdx.x][k];
     }
 }
 
