@@ -388,6 +388,7 @@ static size_t ws_layout(miag_ctx *c, int T, uint8_t *base, Work *w, float **x_de
     v.chunk_pre = (int32_t *)bump(p, (size_t)(m.E + 1) * 4);
     v.chunk_info = (int4 *)bump(p, (P / kTokChunkNarrow + m.E + 1) * 16);
     v.max_chunk = (int32_t *)bump(p, 4);
+    v.chunk_done = (int32_t *)bump(p, (P / kTokChunkNarrow + m.E + 1) * 4);
     v.perm = (int32_t *)bump(p, P * 4);
     v.inv = (int32_t *)bump(p, P * 4);
     v.h = (float *)bump(p, P * 2 * m.eh * 4);
@@ -440,7 +441,7 @@ static int enqueue_moe(miag_ctx *c, int layer, float *x_dev, int T, cudaStream_t
               [&] { launch_permute(c->dims, w, c->d_err, s); });
     run_stage(c, kGateUp, 1, s,
               [&] { launch_gateup(c->dims, c->lay, L, w, c->num_sms, c->d_err, s); });
-    run_stage(c, kDown, 2, s,
+    run_stage(c, kDown, down_launches(c->dims, w.P), s,
               [&] { launch_down(c->dims, c->lay, L, w, c->num_sms, c->d_err, s); });
     run_stage(c, kCombine, 1, s, [&] { launch_combine(c->dims, w, x_dev, s); });
     c->last_T = T;
@@ -568,7 +569,7 @@ extern "C" int miag_experts_async(miag_ctx *c, int layer, const int8_t *xq, cons
               [&] { launch_permute(c->dims, w, c->d_err, s); });
     run_stage(c, kGateUp, 1, s,
               [&] { launch_gateup(c->dims, c->lay, L, w, c->num_sms, c->d_err, s); });
-    run_stage(c, kDown, 2, s,
+    run_stage(c, kDown, down_launches(c->dims, w.P), s,
               [&] { launch_down(c->dims, c->lay, L, w, c->num_sms, c->d_err, s); });
     CU(cudaGetLastError());
     return 0;

@@ -51,6 +51,7 @@ struct GemvParams {
     const int32_t *offsets, *perm, *active, *n_active, *chunk_pre;
     const int4 *chunk_info;    // per pair chunk: (expert, chunk of it, segment start, pairs)
     const int32_t *max_chunk;  // largest chunk
+    int32_t *chunk_done;       // decode regime: gate/up row tiles finished per chunk
     ShareState *share;         // this launch kind's SM shares
     int num_sms;
     const int8_t *xq;  // [rows][d]
@@ -321,6 +322,77 @@ __device__ void fill_region(const GemvParams &p, uint8_t *region, int rows_cap, 
         }
     }
     cp_async_wait_all();
+}
+
+// Decode regime, down: stage the activations of pairs [t0, t0+n) of the
+// expert segment at seg0 straight from gate/up's products, forming
+// h = silu(gate) * up (forward.c:188-191) and quantizing it to Q8_0 as
+// mia_matvec quantizes its input (matmul.c:93, quant.c:11-27) -- the work of
+// k_swiglu_q8 for these pairs, four threads per 32-block, eight values
+// each; the block maximum is combined over the four lanes.  Layout as
+// fill_region.  Whole warps run every round (the shuffles need them).
+__device__ void fill_region_swiglu(const GemvParams &p, uint8_t *region, int rows_cap, int seg0,
+                                   int t0, int n, int eh, int nscale) {
+    const int srow = (int)smem_stride((uint32_t)nscale * 8);
+    uint8_t *rs = region + (size_t)rows_cap * p.x_stride;
+    const int nb = eh / MIAG_QK, total = n * nb * 4;
+    for (int v0 = 0; v0 < total; v0 += kConsumers) {
+        const int v = v0 + (int)threadIdx.x;
+        const bool live = v < total;  // whole quads (total % 4 == 0)
+        const int blk = live ? v >> 2 : 0, q = v & 3;
+        const int j = blk / nb, b = blk - j * nb;
+        const float4 *src = reinterpret_cast<const float4 *>(
+            p.h + (size_t)(seg0 + t0 + j) * 2 * eh + (size_t)b * 2 * MIAG_QK) + 4 * q;
+        float4 g[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) g[k] = live ? __ldcg(src + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+        float h[8];
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            h[2 * k] = swiglu_ref(g[k].x, g[k].y);
+            h[2 * k + 1] = swiglu_ref(g[k].z, g[k].w);
+        }
+        float a = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 8; k++) a = fmaxf(a, fabsf(h[k]));
+        a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 1));
+        a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 2));
+        if (!live) continue;
+        const float dq = __fdiv_rn(a, 127.0f);
+        const float id = dq != 0.0f ? __fdiv_rn(1.0f, dq) : 0.0f;
+        uint32_t w[2];
+#pragma unroll
+        for (int hh = 0; hh < 2; hh++) {
+            uint32_t u = 0;
+#pragma unroll
+            for (int k = 0; k < 4; k++)
+                u |= (uint32_t)(uint8_t)(int8_t)roundf(__fmul_rn(h[4 * hh + k], id)) << (8 * k);
+            w[hh] = u;
+        }
+        *reinterpret_cast<uint2 *>(region + (size_t)j * p.x_stride + (size_t)b * MIAG_QK + 8 * q) =
+            make_uint2(w[0], w[1]);
+        if (q == 0) reinterpret_cast<float *>(rs + (size_t)(j >> 1) * srow)[2 * b + (j & 1)] = dq;
+    }
+}
+
+// Decode regime: chunk c's gate/up products are complete once all its row
+// tiles are counted (gate/up adds a CTA's tiles of a chunk when it leaves
+// the chunk, after a CTA barrier and a fence).  Thread 0 waits (bounded).
+__device__ __forceinline__ int ld_acquire(const int32_t *p) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ void wait_chunk(const GemvParams &p, int c) {
+    const int target = p.lay.gu_rt;
+    const long long t0 = clock64();
+    while (ld_acquire(p.chunk_done + c) < target) {
+        if (clock64() - t0 > kWaitCycles) {
+            set_error(p.err, kErrWaitFull);
+            return;
+        }
+        __nanosleep(64);
+    }
 }
 
 // h = silu(gate) * up (forward.c:188-191) for every pair, quantized to Q8_0
@@ -621,30 +693,41 @@ __device__ int claim_slot(ShareState *sh, int G, int *err) {
     return -1;
 }
 
-// Sum of the rates of slots [0, j), the same float in every CTA and
-// nondecreasing in j: lane l holds slots [5l, 5l + 5); the sums of lanes
-// below the slot's lane are added one by one in lane order, then the slot's
-// first j - 5l rates in order.  Every prefix is so a sequential sum of the
-// one before it and a nonnegative term, and rounding is monotone.
-__device__ float rate_prefix(const float (&r)[kMaxSlots / 32], int j) {
+// Sums of the rates of slots [0, ja), [0, jb) and [0, G): the same floats in
+// every CTA and nondecreasing in j.  Lane l holds slots [5l, 5l + 5); the
+// lane sums below a slot's lane are added one by one in lane order, then
+// the slot's first j - 5l rates in order, so every prefix is a sequential
+// sum of the one before it and a nonnegative term, and rounding is
+// monotone.  One pass over the lanes serves all three.
+struct RatePrefix {
+    float a, b, total;
+};
+__device__ RatePrefix rate_prefixes(const float (&r)[kMaxSlots / 32], int ja, int jb) {
     constexpr int per = kMaxSlots / 32;
     float own = 0.0f;
 #pragma unroll
     for (int i = 0; i < per; i++) own = __fadd_rn(own, r[i]);
-    const int l = min(j / per, 32);
-    float e = 0.0f;
+    const int la = min(ja / per, 32), lb = min(jb / per, 32);
+    float ea = 0.0f, eb = 0.0f, et = 0.0f;
     for (int q = 0; q < 32; q++) {
         const float o = __shfl_sync(0xffffffffu, own, q);
-        if (q < l) e = __fadd_rn(e, o);
+        if (q < la) ea = __fadd_rn(ea, o);
+        if (q < lb) eb = __fadd_rn(eb, o);
+        et = __fadd_rn(et, o);
     }
-    if (l >= 32) return e;
-    float blk = 0.0f;
+    float ba = 0.0f, bb = 0.0f;
 #pragma unroll
     for (int i = 0; i < per; i++) {
-        const float v = __shfl_sync(0xffffffffu, r[i], l);
-        if (i < j - per * l) blk = __fadd_rn(blk, v);
+        const float va = __shfl_sync(0xffffffffu, r[i], min(la, 31));
+        const float vb = __shfl_sync(0xffffffffu, r[i], min(lb, 31));
+        if (la < 32 && i < ja - per * la) ba = __fadd_rn(ba, va);
+        if (lb < 32 && i < jb - per * lb) bb = __fadd_rn(bb, vb);
     }
-    return j > per * l ? __fadd_rn(e, blk) : e;
+    RatePrefix rp;
+    rp.a = la < 32 && ja > per * la ? __fadd_rn(ea, ba) : ea;
+    rp.b = lb < 32 && jb > per * lb ? __fadd_rn(eb, bb) : eb;
+    rp.total = et;
+    return rp;
 }
 
 // gate+up (kGU) or down: one launch over all items of all active experts.
@@ -690,28 +773,30 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_expert_mma(GemvParams p) {
     const int parity = weighted ? (__ldcg(&sh->launches) & 1) : 0;
     if (warp == 0) {
         int slot = blockIdx.x;
-        if (weighted) {
-            if (lane == 0) slot = claim_slot(sh, G, p.err);
-            slot = __shfl_sync(0xffffffffu, slot, 0);
-        }
         int first = (int)((long)n_items * blockIdx.x / G);
         int last = (int)((long)n_items * (blockIdx.x + 1) / G);
-        if (weighted && slot >= 0) {
+        if (weighted) {
+            // the rates load while the slot is claimed (neither needs the other)
             constexpr int per = kMaxSlots / 32;
             float r[per];
-            bool ok = true;
 #pragma unroll
             for (int i = 0; i < per; i++) {
                 const int c = per * lane + i;
                 r[i] = c < G ? __ldcg(&sh->rate[parity][c]) : 0.0f;
-                if (c < G && !(r[i] > 0.0f && r[i] < 1e30f)) ok = false;
             }
-            if (__all_sync(0xffffffffu, ok)) {
-                const double total = rate_prefix(r, G);
-                const double a = rate_prefix(r, slot), b = rate_prefix(r, slot + 1);
-                first = (int)((double)n_items * a / total);
-                last = slot + 1 == G ? n_items : (int)((double)n_items * b / total);
-            } else {  // no rates yet: equal shares
+            if (lane == 0) slot = claim_slot(sh, G, p.err);
+            slot = __shfl_sync(0xffffffffu, slot, 0);
+            bool ok = true;
+#pragma unroll
+            for (int i = 0; i < per; i++)
+                if (per * lane + i < G && !(r[i] > 0.0f && r[i] < 1e30f)) ok = false;
+            if (slot >= 0 && __all_sync(0xffffffffu, ok)) {
+                const RatePrefix rp = rate_prefixes(r, slot, slot + 1);
+                const float n = (float)n_items;
+                first = (int)__fdiv_rn(__fmul_rn(n, rp.a), rp.total);
+                last = slot + 1 == G ? n_items : (int)__fdiv_rn(__fmul_rn(n, rp.b), rp.total);
+                first = min(first, n_items), last = min(last, n_items);
+            } else if (slot >= 0) {  // no rates yet: equal shares
                 first = (int)((long)n_items * slot / G);
                 last = (int)((long)n_items * (slot + 1) / G);
             }
@@ -723,8 +808,17 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_expert_mma(GemvParams p) {
     }
     __syncthreads();
     const int first = head->first, n_mine = head->n_mine;
+    // Decode down works its share from the first chunk that starts inside
+    // it: the chunk it shares with the previous slot, whose gate/up rows
+    // another SM may still be producing, goes last.  (The list is rotated by
+    // k0 items; only when the whole list fits the table.)
+    int k0 = 0;
+    if (!kGU && !kWide && n_mine <= kItemTable) {
+        const int lead = (RT - first % RT) % RT;
+        if (lead < n_mine) k0 = lead;
+    }
     for (int k = threadIdx.x; k < min(n_mine, kItemTable); k += kGemvThreads)
-        table[k] = pack_item(decode_item(p, RT, first + k));
+        table[k] = pack_item(decode_item(p, RT, first + (k + k0) % n_mine));
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; s++) {
             mbar_init(&head->full[s], 1);
@@ -742,7 +836,13 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_expert_mma(GemvParams p) {
         for (int j = 0; j < min(S, n_mine * NS); j++, feed_next(p, fc, f)) feed_issue(p, fc, f, smem, j);
     }
     Feed fd = feed_at(p, fc, S);  // the refill of iteration 0
-    if (!kGU) pdl_wait();
+    // Decode regime: gate/up counts each chunk's finished row tiles and down
+    // waits chunk by chunk, so down's CTAs (on the SMs gate/up has left, and
+    // on the chunks those SMs just finished) start before gate/up ends; down
+    // forms the SwiGLU itself while staging.  Prefill: the SwiGLU launch sits
+    // between, and down waits for it as a whole.
+    constexpr bool kSignal = kGU && !kWide, kChunkWait = !kGU && !kWide;
+    if (!kGU && kWide) pdl_wait();
     pdl_launch_dependents();
 
     // ---- consumers
@@ -756,6 +856,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_expert_mma(GemvParams p) {
     ic.S = S, ic.KT = KT, ic.NS = NS, ic.nb = nb, ic.rows = rows;
 
     int cur_e = -1, cur_tc = -1;
+    int cur_c = -1, tiles_c = 0;  // chunk being worked on, its row tiles done here (kSignal)
     RingPos rp{0, 0, 0u};
     bool failed = false;
     if (threadIdx.x == 0) head->t_start = global_ns();
@@ -763,16 +864,35 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_expert_mma(GemvParams p) {
         const ItemInfo ii = unpack_item(item_entry(p, table, first, RT, k));
         const int seg0 = ii.seg0, t0 = ii.tc * p.chunk, nq = ii.nq;
         if (ii.e != cur_e || ii.tc != cur_tc) {
-            consumer_sync();  // nobody still reads the region
-            fill_region<kGU>(p, region, nq_max, seg0, t0, nq, Kb, xs, head->tok);
-            cur_e = ii.e, cur_tc = ii.tc;
+            consumer_sync();  // nobody still reads the region (or writes the last chunk)
+            const int c = (first + (k + k0) % n_mine) / RT;  // its chunk in the permutation's list
+            if (kSignal && threadIdx.x == 0 && cur_c >= 0) {
+                __threadfence();  // the CTA's products of chunk cur_c, before they are counted
+                atomicAdd(p.chunk_done + cur_c, tiles_c);
+            }
+            if (kChunkWait) {
+                if (threadIdx.x == 0) wait_chunk(p, c);
+                consumer_sync();
+                fill_region_swiglu(p, region, nq_max, seg0, t0, nq, eh, xs);
+            } else {
+                fill_region<kGU>(p, region, nq_max, seg0, t0, nq, Kb, xs, head->tok);
+            }
+            cur_e = ii.e, cur_tc = ii.tc, cur_c = c, tiles_c = 0;
             consumer_sync();
         }
+        tiles_c++;
         ic.rt = ii.rt, ic.seg0 = seg0, ic.t0 = t0, ic.nq = nq;
         // Two tile shapes (n_tiles): one n-tile of 8 pairs, or the chunk's
         // full width (columns past nq run on repeated rows, not written).
         if (nq <= 8) run_item<kGU, 1>(p, ic, ln, smem, rp, fc, fd, failed);
         else run_item<kGU, kWide ? 4 : 2>(p, ic, ln, smem, rp, fc, fd, failed);
+    }
+    if (kSignal) {
+        consumer_sync();
+        if (threadIdx.x == 0 && cur_c >= 0) {
+            __threadfence();
+            atomicAdd(p.chunk_done + cur_c, tiles_c);
+        }
     }
     // After a timed-out wait, let every issued copy land (bounded) before the
     // CTA's shared memory goes away.  All refills are issued by now.
@@ -801,6 +921,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_expert_mma(GemvParams p) {
             atomicAdd(&sh->launches, 1);
         }
     }
+    // decode down waited per chunk only; its end must still imply gate/up's
+    if (kChunkWait) pdl_wait();
 }
 
 // x[t] += w_j * y_j for j = 0..K-1 in order (forward.c:194).
@@ -849,6 +971,7 @@ static void fill_params(GemvParams &p, const Dims &m, const StoreLayout &lay, co
     p.m = m, p.lay = lay, p.experts = L.experts;
     p.offsets = w.offsets, p.perm = w.perm, p.active = w.active, p.n_active = w.n_active;
     p.chunk_pre = w.chunk_pre, p.chunk_info = w.chunk_info, p.max_chunk = w.max_chunk;
+    p.chunk_done = w.chunk_done;
     p.xq = w.xq, p.dx = w.dx, p.h = w.h, p.hq = w.hq, p.hs = w.hs, p.y = w.y, p.err = err;
     p.pair_row = w.pair_row, p.n_rows = w.pair_row ? w.n_rows : w.T;
     p.one = 1.0f;
@@ -912,9 +1035,11 @@ void launch_gateup(const Dims &m, const StoreLayout &lay, const LayerDev &L, con
                      dim3(kGemvThreads), kSmemBudget, s, p);
 }
 
+int down_launches(const Dims &m, int P) { return P > 0 && wide_batch(P, m.E) ? 2 : 1; }
+
 void launch_down(const Dims &m, const StoreLayout &lay, const LayerDev &L, const Work &w,
                  int num_sms, int *err, cudaStream_t s) {
-    if (w.P > 0) {
+    if (w.P > 0 && wide_regime(m, w)) {  // decode: down forms the SwiGLU while staging
         const long tasks = (long)w.P * (m.eh / MIAG_QK) * 4;
         launch_dependent(k_swiglu_q8, dim3((unsigned)((tasks + 127) / 128)), dim3(128), 0, s, w.h,
                          w.P, m.eh, scale_pad(m.eh / MIAG_QK), w.hq, w.hs);

@@ -24,6 +24,8 @@ struct Work {
     int4 *chunk_info;      // [chunks]      per pair chunk: (expert, chunk of it, its first sorted
                            //               position, pairs); chunks <= P / kTokChunkNarrow + E
     int32_t *max_chunk;    // [1]           largest chunk (pairs)
+    int32_t *chunk_done;   // [chunks]      decode regime: gate/up warp-tiles finished per chunk
+                           //               (zeroed by the permutation)
     uint8_t *shares;       // [kShareKinds] ShareState: the expert launches' SM shares; zero at
                            //               creation, kept by the launches themselves
     int32_t *perm;         // [P]           pair id at each sorted position
@@ -97,6 +99,7 @@ void launch_gateup(const Dims &m, const StoreLayout &lay, const LayerDev &L, con
 void launch_down(const Dims &m, const StoreLayout &lay, const LayerDev &L, const Work &w,
                  int num_sms, int *err, cudaStream_t s);
 void launch_combine(const Dims &m, const Work &w, float *x, cudaStream_t s);
+int down_launches(const Dims &m, int P);  // kernels launch_down issues
 int gemv_setup_attributes(const Dims &m, const StoreLayout &lay);
 // store.cu
 void launch_repack(const Dims &m, const StoreLayout &lay, const uint8_t *aos, size_t aos_stride,

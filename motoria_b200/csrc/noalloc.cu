@@ -103,6 +103,7 @@ size_t layout(const Dims &m, int T, uint8_t *base, Work *w) {
     v.chunk_pre = reinterpret_cast<int32_t *>(bump(p, (size_t)(m.E + 1) * 4));
     v.chunk_info = reinterpret_cast<int4 *>(bump(p, (P / kTokChunkNarrow + m.E + 1) * 16));
     v.max_chunk = reinterpret_cast<int32_t *>(bump(p, 4));
+    v.chunk_done = reinterpret_cast<int32_t *>(bump(p, (P / kTokChunkNarrow + m.E + 1) * 4));
     v.perm = reinterpret_cast<int32_t *>(bump(p, P * 4));
     v.inv = reinterpret_cast<int32_t *>(bump(p, P * 4));
     v.h = reinterpret_cast<float *>(bump(p, P * 2 * m.eh * 4));

@@ -95,17 +95,20 @@ __device__ int block_excl_scan(int v, int *total, int *sh /* >= 33 ints */) {
 
 // The pair chunks of one active expert (n pairs from sorted position off),
 // numbered from cpos in the list the expert launches walk: (e, chunk, first
-// sorted position of the expert, pairs in the chunk).
-__device__ __forceinline__ void write_chunks(int4 *chunk_info, int cpos, int e, int off, int n,
-                                             int chunk) {
-    for (int tc = 0; tc * chunk < n; tc++)
+// sorted position of the expert, pairs in the chunk); each chunk's
+// completion counter (gate/up tiles done) starts at zero.
+__device__ __forceinline__ void write_chunks(int4 *chunk_info, int32_t *chunk_done, int cpos, int e,
+                                             int off, int n, int chunk) {
+    for (int tc = 0; tc * chunk < n; tc++) {
         chunk_info[cpos + tc] = make_int4(e, tc, off, min(chunk, n - tc * chunk));
+        chunk_done[cpos + tc] = 0;
+    }
 }
 
 __global__ void __launch_bounds__(1024)
 k_perm_scan(int nchunks, int E, const int32_t *chunk_cnt, int32_t *chunk_base, int32_t *counts,
             int32_t *offsets, int32_t *active, int32_t *n_active, int32_t *chunk_pre,
-            int4 *chunk_info, int32_t *max_chunk, int chunk) {
+            int4 *chunk_info, int32_t *chunk_done, int32_t *max_chunk, int chunk) {
     pdl_wait();
     pdl_launch_dependents();
     __shared__ int sh[33];
@@ -132,7 +135,7 @@ k_perm_scan(int nchunks, int E, const int32_t *chunk_cnt, int32_t *chunk_base, i
         if (run > 0) {
             active[apos] = e;
             chunk_pre[apos] = cpos;
-            write_chunks(chunk_info, cpos, e, off, run, chunk);
+            write_chunks(chunk_info, chunk_done, cpos, e, off, run, chunk);
             atomicMax(&smax, min(chunk, run));
         }
         for (int c = 0; c < nchunks; c++) chunk_base[(size_t)c * E + e] += off;
@@ -195,7 +198,8 @@ __device__ long long block_excl_scan64(long long v, long long *total, long long 
 __global__ void __launch_bounds__(1024)
 k_permute_small(const int32_t *idx, int P, int E, int32_t *counts, int32_t *offsets,
                 int32_t *active, int32_t *n_active, int32_t *chunk_pre, int4 *chunk_info,
-                int32_t *max_chunk, int chunk, int32_t *perm, int32_t *inv, int *err) {
+                int32_t *chunk_done, int32_t *max_chunk, int chunk, int32_t *perm, int32_t *inv,
+                int *err) {
     pdl_wait();
     pdl_launch_dependents();
     extern __shared__ int32_t sm_i[];  // wcnt [warps][E], base [E]
@@ -245,7 +249,7 @@ k_permute_small(const int32_t *idx, int P, int E, int32_t *counts, int32_t *offs
         if (run > 0) {
             active[apos] = tid;
             chunk_pre[apos] = cpos;
-            write_chunks(chunk_info, cpos, tid, off, run, chunk);
+            write_chunks(chunk_info, chunk_done, cpos, tid, off, run, chunk);
             atomicMax(&smax, min(chunk, run));
         }
     }
@@ -271,8 +275,8 @@ void launch_permute(const Dims &m, const Work &w, int *err, cudaStream_t s) {
         cudaFuncSetAttribute(k_permute_small, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)small_smem);
         launch_dependent(k_permute_small, dim3(1), dim3(threads), small_smem, s, w.idx, P, E, w.counts,
-                         w.offsets, w.active, w.n_active, w.chunk_pre, w.chunk_info, w.max_chunk,
-                         tok_chunk(P, E), w.perm, w.inv, err);
+                         w.offsets, w.active, w.n_active, w.chunk_pre, w.chunk_info, w.chunk_done,
+                         w.max_chunk, tok_chunk(P, E), w.perm, w.inv, err);
         return;
     }
     const size_t smem = sizeof(int32_t) * (size_t)E * (1 + kPermWarps);
@@ -283,7 +287,7 @@ void launch_permute(const Dims &m, const Work &w, int *err, cudaStream_t s) {
     const int st = ((E + 31) / 32) * 32;
     launch_dependent(k_perm_scan, dim3(1), dim3(st < 64 ? 64 : st), 0, s, w.nchunks, E, w.chunk_cnt,
                      w.chunk_base, w.counts, w.offsets, w.active, w.n_active, w.chunk_pre,
-                     w.chunk_info, w.max_chunk, tok_chunk(P, E));
+                     w.chunk_info, w.chunk_done, w.max_chunk, tok_chunk(P, E));
     launch_dependent(k_perm_scatter, dim3((P + 255) / 256), dim3(256), 0, s, w.idx, P, E, w.rank,
                      w.chunk_base, w.perm, w.inv);
 }
