@@ -139,6 +139,13 @@ int miag_dx_stride(const miag_shape *s);
  * any device-side error (a bounded wait that gave up, a bad index). */
 int miag_sync(miag_ctx *c, void *stream, char *err, size_t errlen);
 
+/* Self-test of the failure path (no reference counterpart): runs one bounded
+ * wait on a barrier that never completes, with a limit of timeout_us
+ * (1..100000), and reports it as the block's kernels report a tile that
+ * never lands.  Returns -1 with "device error 1: ... timed out ..." in err
+ * when the wait gave up, as it always should; the context stays usable. */
+int miag_selftest_wait_timeout(miag_ctx *c, int timeout_us, char *err, size_t errlen);
+
 /* Routing of the most recent miag_moe / miag_moe_async call, copied to host
  * (any pointer may be NULL): idx, w [n_tokens][n_active]; counts [E];
  * offsets [E+1]; perm [n_tokens*n_active] (pair id t*K+j at each position of

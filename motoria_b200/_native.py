@@ -55,6 +55,7 @@ SIGNATURES = {
                                      C.c_void_p, C.c_void_p, C.c_char_p, C.c_size_t]),
     "miag_dx_stride": (C.c_int, [C.POINTER(Shape)]),
     "miag_sync": (C.c_int, [C.c_void_p, C.c_void_p, C.c_char_p, C.c_size_t]),
+    "miag_selftest_wait_timeout": (C.c_int, [C.c_void_p, C.c_int, C.c_char_p, C.c_size_t]),
     "miag_routing": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                C.c_void_p, C.c_char_p, C.c_size_t]),
     "miag_router_logits": (C.c_int, [C.c_void_p, C.c_void_p, C.c_char_p, C.c_size_t]),

@@ -481,6 +481,34 @@ static int read_device_error(miag_ctx *c, char *err, size_t errlen) {
     return -1;
 }
 
+// One thread waits, bounded, on an mbarrier that nothing arrives on: the
+// same wait and error path the block's kernels take when a staged tile
+// never lands, run on purpose.  No copy is in flight and the barrier lives
+// in the CTA's own shared memory, so giving up leaves nothing behind.
+static __global__ void k_wait_selftest(int *err, long long limit) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_barrier_init();
+        if (!mbar_wait_for(&bar, 0, limit)) set_error(err, kErrWaitFull);
+    }
+}
+
+extern "C" int miag_selftest_wait_timeout(miag_ctx *c, int timeout_us, char *err, size_t errlen) {
+    if (!c || timeout_us <= 0 || timeout_us > 100000) {
+        set_err(err, errlen, "miag_selftest_wait_timeout: null context or timeout outside 1..100000 us");
+        return -1;
+    }
+    CU(cudaSetDevice(c->device));
+    int khz = 0;
+    CU(cudaDeviceGetAttribute(&khz, cudaDevAttrClockRate, c->device));
+    const long long limit = (long long)timeout_us * (khz / 1000);
+    k_wait_selftest<<<1, 32, 0, c->stream>>>(c->d_err, limit);
+    CU(cudaGetLastError());
+    CU(cudaStreamSynchronize(c->stream));
+    return read_device_error(c, err, errlen);
+}
+
 extern "C" int miag_sync(miag_ctx *c, void *stream, char *err, size_t errlen) {
     if (!c) {
         set_err(err, errlen, "null context");

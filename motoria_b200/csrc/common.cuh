@@ -153,14 +153,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Waits for the phase of `parity` to complete; false after ~1 s.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+// Waits for the phase of `parity` to complete; false after `limit` cycles.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t *bar, uint32_t parity, long long limit) {
     if (mbar_try_wait(bar, parity)) return true;
     long long t0 = clock64();
     while (!mbar_try_wait(bar, parity)) {
-        if (clock64() - t0 > kWaitCycles) return false;
+        if (clock64() - t0 > limit) return false;
     }
     return true;
+}
+
+// Waits for the phase of `parity` to complete; false after ~1 s.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+    return mbar_wait_for(bar, parity, kWaitCycles);
 }
 
 // Global -> shared bulk copy completing on `bar` (16-B aligned, bytes % 16 == 0).

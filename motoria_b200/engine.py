@@ -179,6 +179,13 @@ class MoEEngine:
         N.check(self._lib.miag_sync(self._ctx, C.c_void_p(stream or 0), err, len(err)), err,
                 "miag_sync")
 
+    def selftest_wait_timeout(self, timeout_us: int = 2000) -> str:
+        """Runs the library's bounded wait on a barrier that never completes;
+        returns the error text it reported ('' if it did not report)."""
+        err = N.errbuf()
+        rc = self._lib.miag_selftest_wait_timeout(self._ctx, timeout_us, err, len(err))
+        return err.value.decode(errors="replace") if rc != 0 else ""
+
     def routing(self, n_tokens: int) -> dict:
         """Routing of the last call: idx, w [T][K]; counts [E]; offsets [E+1]; perm [T*K]."""
         K, E = self.shape.n_active, self.shape.n_experts

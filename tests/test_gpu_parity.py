@@ -361,3 +361,19 @@ def test_loader_failure_reports_the_expert(torch_cuda):
             eng.moe(np.zeros((1, TINY.dim), np.float32), layer=3)
     finally:
         eng.close()
+
+
+def test_wait_timeout_is_reported_and_context_survives(torch_cuda):
+    """Failure detection without a fault: a bounded wait on a barrier nothing
+    completes gives up after its limit, the error comes back through the
+    context's error word, and the context then runs the block as before."""
+    build.build()
+    with MoEEngine(TINY, n_layers=1) as eng:
+        eng.load_layer(0, get_layer(TINY, False))
+        x = synth.tokens(TINY, 5, 9)
+        before = eng.moe(x.copy())
+        msg = eng.selftest_wait_timeout(2000)
+        assert "timed out" in msg, msg
+        after = eng.moe(x.copy())
+        assert np.array_equal(before.view(np.uint32), after.view(np.uint32))
+        eng.sync()  # the error word was cleared when it was reported
