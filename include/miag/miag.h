@@ -135,6 +135,35 @@ int miag_combine_async(miag_ctx *c, float *x_dev, int n_tokens, const float *w,
 /* f32 scales per row of dx: dim/32 rounded up to a multiple of four. */
 int miag_dx_stride(const miag_shape *s);
 
+/* The exchange of expert parallelism (no reference counterpart: the
+ * reference runs on one device).  Experts are split over n_ranks ranks
+ * (1..8), experts_per_rank each: expert e lives on rank e / experts_per_rank,
+ * or on e % n_ranks when strided is nonzero.  Order on every rank: rows
+ * grouped by destination rank, tokens ascending; pairs grouped by
+ * destination, pair id t*n_active + j ascending.
+ * miag_ep_plan_async: from idx [n_tokens][n_active] (miag_route_async),
+ *   counts [n_ranks][2] int64 (rows, pairs) to each rank; send_rows
+ *   [n_tokens*n_ranks] the token of each row to send (the first
+ *   sum(rows) are used); pair_meta [n_tokens*n_active][2] (row within the
+ *   destination's block from this rank, expert) in pair order as above;
+ *   y_pos [n_tokens*n_active] the place of pair t*n_active + j in that
+ *   order, for miag_combine_async.
+ * miag_ep_pack_async: the send buffers of rank `rank`.  rec [n_rows] records
+ *   of dim int8 values then miag_dx_stride f32 scales, the rows of xq/dx
+ *   named by send_rows; meta_out [n_pairs][2] the pair records with each row
+ *   renumbered in the receiver's buffer, where lower ranks' rows come first.
+ *   all_counts [n_ranks][n_ranks][2] holds every rank's counts, in rank
+ *   order (an all-gather of counts). */
+int miag_ep_plan_async(miag_ctx *c, const int32_t *idx, int n_tokens, int n_ranks,
+                       int experts_per_rank, int strided, int64_t *counts,
+                       int32_t *send_rows, int32_t *pair_meta, int32_t *y_pos,
+                       void *stream, char *err, size_t errlen);
+int miag_ep_pack_async(miag_ctx *c, const int8_t *xq, const float *dx,
+                       const int32_t *send_rows, int n_rows, const int32_t *pair_meta,
+                       int n_pairs, const int64_t *all_counts, int rank, int n_ranks,
+                       uint8_t *rec, int32_t *meta_out, void *stream, char *err,
+                       size_t errlen);
+
 /* Waits for the context's work on `stream` (NULL = own stream) and reports
  * any device-side error (a bounded wait that gave up, a bad index). */
 int miag_sync(miag_ctx *c, void *stream, char *err, size_t errlen);

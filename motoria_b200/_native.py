@@ -54,6 +54,13 @@ SIGNATURES = {
     "miag_combine_async": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p,
                                      C.c_void_p, C.c_void_p, C.c_char_p, C.c_size_t]),
     "miag_dx_stride": (C.c_int, [C.POINTER(Shape)]),
+    "miag_ep_plan_async": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
+                                     C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                     C.c_char_p, C.c_size_t]),
+    "miag_ep_pack_async": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
+                                     C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int,
+                                     C.c_void_p, C.c_void_p, C.c_void_p, C.c_char_p,
+                                     C.c_size_t]),
     "miag_sync": (C.c_int, [C.c_void_p, C.c_void_p, C.c_char_p, C.c_size_t]),
     "miag_selftest_wait_timeout": (C.c_int, [C.c_void_p, C.c_int, C.c_char_p, C.c_size_t]),
     "miag_routing": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,

@@ -51,9 +51,9 @@ struct miag_ctx {
 };
 
 namespace {
-enum Stage { kRoute = 0, kPermute, kGateUp, kDown, kCombine, kNumStages };
-const char *const kStageNames[kNumStages] = {"route", "permute", "gateup", "down",
-                                             "combine"};
+enum Stage { kRoute = 0, kPermute, kGateUp, kDown, kCombine, kEpPlan, kEpPack, kNumStages };
+const char *const kStageNames[kNumStages] = {"route",   "permute", "gateup", "down",
+                                             "combine", "ep_plan", "ep_pack"};
 
 cudaEvent_t take_event(miag_ctx *c) {
     if (!c->event_pool.empty()) {
@@ -626,6 +626,75 @@ extern "C" int miag_combine_async(miag_ctx *c, float *x_dev, int n_tokens, const
     Work w{};
     w.T = n_tokens, w.w = const_cast<float *>(wts), w.y = const_cast<float *>(y), w.y_pos = y_pos;
     run_stage(c, kCombine, 1, s, [&] { launch_combine(c->dims, w, x_dev, s); });
+    CU(cudaGetLastError());
+    return 0;
+}
+
+extern "C" int miag_ep_plan_async(miag_ctx *c, const int32_t *idx, int n_tokens, int n_ranks,
+                                  int experts_per_rank, int strided, int64_t *counts,
+                                  int32_t *send_rows, int32_t *pair_meta, int32_t *y_pos,
+                                  void *stream, char *err, size_t errlen) {
+    if (!c) {
+        set_err(err, errlen, "null context");
+        return -1;
+    }
+    if (n_ranks < 1 || n_ranks > kEpMaxRanks || experts_per_rank < 1 ||
+        (long)n_ranks * experts_per_rank != c->dims.E) {
+        set_err(err, errlen, "%d ranks x %d experts: need 1..%d ranks holding all %d experts",
+                n_ranks, experts_per_rank, kEpMaxRanks, c->dims.E);
+        return -1;
+    }
+    if (c->dims.K > 32) {  // the plan's per-tile pair prefixes are 16-bit fields
+        set_err(err, errlen, "expert parallelism supports at most 32 active experts");
+        return -1;
+    }
+    if (n_tokens < 0 || !counts || (n_tokens > 0 && (!idx || !send_rows || !pair_meta || !y_pos)) ||
+        ((uintptr_t)pair_meta & 7u)) {
+        set_err(err, errlen, "bad buffers (device pointers; pair_meta 8-byte aligned)");
+        return -1;
+    }
+    c->last_launches = 0;
+    CU(cudaSetDevice(c->device));
+    const cudaStream_t s = stream ? (cudaStream_t)stream : c->stream;
+    run_stage(c, kEpPlan, 1, s, [&] {
+        launch_ep_plan(idx, n_tokens, c->dims.K, n_ranks, experts_per_rank, strided != 0,
+                       reinterpret_cast<long long *>(counts), send_rows, pair_meta, y_pos, c->d_err,
+                       s);
+    });
+    CU(cudaGetLastError());
+    return 0;
+}
+
+extern "C" int miag_ep_pack_async(miag_ctx *c, const int8_t *xq, const float *dx,
+                                  const int32_t *send_rows, int n_rows, const int32_t *pair_meta,
+                                  int n_pairs, const int64_t *all_counts, int rank, int n_ranks,
+                                  uint8_t *rec, int32_t *meta_out, void *stream, char *err,
+                                  size_t errlen) {
+    if (!c) {
+        set_err(err, errlen, "null context");
+        return -1;
+    }
+    if (n_ranks < 1 || n_ranks > kEpMaxRanks || rank < 0 || rank >= n_ranks) {
+        set_err(err, errlen, "rank %d of %d: need 1..%d ranks", rank, n_ranks, kEpMaxRanks);
+        return -1;
+    }
+    if (n_rows < 0 || n_pairs < 0 || (n_rows > 0 && (!xq || !dx || !send_rows || !rec)) ||
+        (n_pairs > 0 && (!pair_meta || !meta_out || !all_counts)) || ((uintptr_t)xq & 15u) ||
+        ((uintptr_t)dx & 15u) || ((uintptr_t)rec & 15u) || ((uintptr_t)pair_meta & 7u) ||
+        ((uintptr_t)meta_out & 7u)) {
+        set_err(err, errlen,
+                "bad buffers (device pointers; xq, dx, rec 16-byte and pair records 8-byte aligned)");
+        return -1;
+    }
+    c->last_launches = 0;
+    if (n_rows == 0 && n_pairs == 0) return 0;
+    CU(cudaSetDevice(c->device));
+    const cudaStream_t s = stream ? (cudaStream_t)stream : c->stream;
+    run_stage(c, kEpPack, 1, s, [&] {
+        launch_ep_pack(xq, dx, c->dims.d, scale_pad(c->dims.d / MIAG_QK), send_rows, n_rows,
+                       pair_meta, n_pairs, reinterpret_cast<const long long *>(all_counts), rank,
+                       n_ranks, rec, meta_out, c->num_sms, s);
+    });
     CU(cudaGetLastError());
     return 0;
 }

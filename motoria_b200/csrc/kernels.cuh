@@ -101,6 +101,15 @@ void launch_down(const Dims &m, const StoreLayout &lay, const LayerDev &L, const
 void launch_combine(const Dims &m, const Work &w, float *x, cudaStream_t s);
 int down_launches(const Dims &m, int P);  // kernels launch_down issues
 int gemv_setup_attributes(const Dims &m, const StoreLayout &lay);
+
+// Expert parallelism (ep.cu): the dispatch plan and the send records.
+constexpr int kEpMaxRanks = 8;  // one node
+void launch_ep_plan(const int32_t *idx, int T, int K, int G, int per_rank, bool strided,
+                    long long *counts, int32_t *send_rows, int32_t *pair_meta, int32_t *y_pos,
+                    int *err, cudaStream_t s);
+void launch_ep_pack(const int8_t *xq, const float *dx, int d, int xs, const int32_t *send_rows,
+                    int n_rows, const int32_t *pair_meta, int n_pairs, const long long *all_counts,
+                    int me, int G, uint8_t *rec, int32_t *meta_out, int num_sms, cudaStream_t s);
 // store.cu
 void launch_repack(const Dims &m, const StoreLayout &lay, const uint8_t *aos, size_t aos_stride,
                    int n, uint8_t *dst, cudaStream_t s);

@@ -174,6 +174,34 @@ class MoEEngine:
                                           err, len(err))
         N.check(rc, err, "miag_combine_async")
 
+    def ep_plan_device(self, idx_ptr: int, n_tokens: int, n_ranks: int, experts_per_rank: int,
+                       strided: bool, counts_ptr: int, send_rows_ptr: int, pair_meta_ptr: int,
+                       y_pos_ptr: int, stream: int | None = None) -> None:
+        """Enqueues the expert-parallel dispatch plan of idx [n][K]: counts
+        [G][2] int64 (rows, pairs) per rank, send_rows [n*G], pair_meta
+        [n*K][2], y_pos [n*K] (miag_ep_plan_async)."""
+        err = N.errbuf()
+        rc = self._lib.miag_ep_plan_async(self._ctx, C.c_void_p(idx_ptr), n_tokens, n_ranks,
+                                          experts_per_rank, int(strided), C.c_void_p(counts_ptr),
+                                          C.c_void_p(send_rows_ptr), C.c_void_p(pair_meta_ptr),
+                                          C.c_void_p(y_pos_ptr), C.c_void_p(stream or 0), err,
+                                          len(err))
+        N.check(rc, err, "miag_ep_plan_async")
+
+    def ep_pack_device(self, xq_ptr: int, dx_ptr: int, send_rows_ptr: int, n_rows: int,
+                       pair_meta_ptr: int, n_pairs: int, all_counts_ptr: int, rank: int,
+                       n_ranks: int, rec_ptr: int, meta_out_ptr: int,
+                       stream: int | None = None) -> None:
+        """Enqueues the send records of rank `rank` (miag_ep_pack_async)."""
+        err = N.errbuf()
+        rc = self._lib.miag_ep_pack_async(self._ctx, C.c_void_p(xq_ptr), C.c_void_p(dx_ptr),
+                                          C.c_void_p(send_rows_ptr), n_rows,
+                                          C.c_void_p(pair_meta_ptr), n_pairs,
+                                          C.c_void_p(all_counts_ptr), rank, n_ranks,
+                                          C.c_void_p(rec_ptr), C.c_void_p(meta_out_ptr),
+                                          C.c_void_p(stream or 0), err, len(err))
+        N.check(rc, err, "miag_ep_pack_async")
+
     def sync(self, stream: int | None = None) -> None:
         err = N.errbuf()
         N.check(self._lib.miag_sync(self._ctx, C.c_void_p(stream or 0), err, len(err)), err,

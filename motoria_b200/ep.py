@@ -21,8 +21,12 @@ Because the combine keeps the reference's order of adds (x + w_0 y_0 + w_1 y_1
 a partial sum would reassociate the adds.  The outputs therefore equal the
 single-GPU block bit for bit.
 
-The plan (who sends what where) is built with device tensor operations; the
-collectives are torch.distributed's (NCCL on GPUs, gloo in the CPU tests).
+The plan (who sends what where) and the send records are built by two
+kernels of the library (miag_ep_plan_async, miag_ep_pack_async), so the
+host reads only the per-rank counts that the collectives' split sizes need;
+plan_dispatch and pack_records state the same in torch operations for the
+CPU tests.  The collectives are torch.distributed's (NCCL on GPUs, gloo in
+the CPU tests).
 """
 
 from __future__ import annotations
@@ -35,20 +39,24 @@ import torch
 @dataclass
 class DispatchPlan:
     """What one rank sends, for G ranks and its T tokens of K pairs each.
-    Built with device operations only (no host synchronisation)."""
+    Order, the same on every rank: rows grouped by destination, tokens
+    ascending within a destination; pairs grouped by destination, pair id
+    t*K + j ascending within a destination."""
 
-    row_keys: torch.Tensor       # [T*G] g*T + t of every (token, destination) row to send,
-                                 #   ascending; the first rows_per_dest.sum() are real
-    rows_per_dest: torch.Tensor  # [G] rows to each destination
-    pair_order: torch.Tensor     # [P] pair ids (t*K + j) grouped by destination, ascending
-    pairs_per_dest: torch.Tensor  # [G]
-    pair_dest: torch.Tensor      # [P] destination of each pair in pair_order
-    pair_meta: torch.Tensor      # [P, 2] int32: (row within the destination's block from
-                                 #   this rank, expert)
+    counts: torch.Tensor     # [G, 2] int64: rows and pairs to each destination
+    send_rows: torch.Tensor  # [T*G] int32: the token of each row to send; the first
+                             #   counts[:, 0].sum() are used
+    pair_meta: torch.Tensor  # [T*K, 2] int32: (row within the destination's block from
+                             #   this rank, expert), in pair order
+    y_pos: torch.Tensor      # [T*K] int32: the place of pair t*K + j in pair order
 
-    def send_rows(self, n: int, T: int) -> torch.Tensor:
-        """The first n row keys as token indices (n = rows_per_dest.sum())."""
-        return self.row_keys[:n] % max(T, 1)
+    @property
+    def rows_per_dest(self) -> torch.Tensor:
+        return self.counts[:, 0]
+
+    @property
+    def pairs_per_dest(self) -> torch.Tensor:
+        return self.counts[:, 1]
 
 
 def owner(expert: torch.Tensor, experts_per_rank: int, world: int, placement: str) -> torch.Tensor:
@@ -62,31 +70,48 @@ def owner(expert: torch.Tensor, experts_per_rank: int, world: int, placement: st
 
 def plan_dispatch(idx: torch.Tensor, experts_per_rank: int, world: int,
                   placement: str = "contiguous") -> DispatchPlan:
-    """idx [T][K] int32 top-k experts -> the rows and pair records to send.
+    """idx [T][K] int32 top-k experts -> the rows and pair records to send,
+    in torch operations: the statement of the plan that EngineOps.plan
+    computes in one kernel (miag_ep_plan_async), used by the CPU tests.
 
     A row goes to a destination once however many of the token's experts
-    live there; within a destination rows keep token order and pairs keep
-    pair order, so every rank sees the same canonical ordering."""
+    live there."""
     T, K = idx.shape
     dev = idx.device
     dest = owner(idx.long(), experts_per_rank, world, placement)      # [T, K]
     hit = torch.zeros((T, world), dtype=torch.bool, device=dev)
     hit.scatter_(1, dest, True)
-    rows_per_dest = hit.sum(0)                                       # [G]
     # (g, t) keys of the hits first, ascending; misses after them
     key = torch.arange(world, device=dev)[:, None] * T + torch.arange(T, device=dev)[None, :]
     key = torch.where(hit.t(), key, torch.full_like(key, world * T))
-    row_keys = torch.sort(key.reshape(-1)).values
+    send_rows = (torch.sort(key.reshape(-1)).values % max(T, 1)).to(torch.int32)
     row_in_block = hit.long().cumsum(0) - 1                          # [T, G] index of t in g's block
     pair_ids = torch.arange(T * K, device=dev)
-    pkey = dest.reshape(-1) * (T * K) + pair_ids                    # g-major, then pair order
-    pair_order = torch.argsort(pkey)
+    pair_order = torch.argsort(dest.reshape(-1) * (T * K) + pair_ids)  # g-major, then pair order
     d_sorted = dest.reshape(-1)[pair_order]
-    pairs_per_dest = torch.bincount(d_sorted, minlength=world)
     t_sorted = pair_order // K
     meta = torch.stack([row_in_block[t_sorted, d_sorted], idx.reshape(-1)[pair_order].long()], 1)
-    return DispatchPlan(row_keys, rows_per_dest, pair_order, pairs_per_dest, d_sorted,
-                        meta.to(torch.int32))
+    y_pos = torch.empty(T * K, dtype=torch.int32, device=dev)
+    y_pos[pair_order] = torch.arange(T * K, dtype=torch.int32, device=dev)
+    counts = torch.stack([hit.sum(0), torch.bincount(d_sorted, minlength=world)], 1)
+    return DispatchPlan(counts.to(torch.int64), send_rows, meta.to(torch.int32), y_pos)
+
+
+def pack_records(xq: torch.Tensor, dx: torch.Tensor, plan: DispatchPlan,
+                 all_counts: torch.Tensor, me: int, n_rows: int, n_pairs: int):
+    """The send buffers of rank `me`, in torch operations (the statement of
+    miag_ep_pack_async): one record per row to send (its int8 values, then
+    its f32 scales as bytes), and the pair records with each row renumbered
+    in the receiver's buffer, where the rows of lower ranks come first.
+    all_counts [G][G][2]: every rank's plan.counts, in rank order."""
+    rows = plan.send_rows[:n_rows].long()
+    rec = torch.cat([xq[rows].view(torch.uint8), dx[rows].view(torch.uint8)], 1)
+    G = all_counts.shape[0]
+    dest = torch.repeat_interleave(torch.arange(G, device=xq.device), all_counts[me, :, 1])
+    row_start = (all_counts[:, :, 0].cumsum(0) - all_counts[:, :, 0])[me]
+    meta = plan.pair_meta[:n_pairs].clone()
+    meta[:, 0] += row_start[dest].to(torch.int32)
+    return rec, meta
 
 
 class EngineOps:
@@ -115,6 +140,33 @@ class EngineOps:
         self.eng.route_device(x.data_ptr(), T, idx.data_ptr(), w.data_ptr(), xq.data_ptr(),
                               dx.data_ptr(), layer=self.layer, stream=self._stream(x))
         return idx, w, xq, dx
+
+    def plan(self, idx: torch.Tensor, experts_per_rank: int, world: int,
+             placement: str = "contiguous") -> DispatchPlan:
+        """plan_dispatch in one kernel (miag_ep_plan_async)."""
+        T, dev = idx.shape[0], idx.device
+        plan = DispatchPlan(torch.empty((world, 2), dtype=torch.int64, device=dev),
+                            torch.empty(T * world, dtype=torch.int32, device=dev),
+                            torch.empty((T * self.K, 2), dtype=torch.int32, device=dev),
+                            torch.empty(T * self.K, dtype=torch.int32, device=dev))
+        self.eng.ep_plan_device(idx.data_ptr(), T, world, experts_per_rank,
+                                placement == "strided", plan.counts.data_ptr(),
+                                plan.send_rows.data_ptr(), plan.pair_meta.data_ptr(),
+                                plan.y_pos.data_ptr(), stream=self._stream(idx))
+        return plan
+
+    def pack(self, xq: torch.Tensor, dx: torch.Tensor, plan: DispatchPlan,
+             all_counts: torch.Tensor, me: int, n_rows: int, n_pairs: int):
+        """pack_records in one kernel (miag_ep_pack_async)."""
+        dev = xq.device
+        rec = torch.empty((n_rows, xq.shape[1] + 4 * dx.shape[1]), dtype=torch.uint8, device=dev)
+        meta = torch.empty((n_pairs, 2), dtype=torch.int32, device=dev)
+        counts = all_counts.contiguous()
+        self.eng.ep_pack_device(xq.data_ptr(), dx.data_ptr(), plan.send_rows.data_ptr(), n_rows,
+                                plan.pair_meta.data_ptr(), n_pairs, counts.data_ptr(), me,
+                                counts.shape[0], rec.data_ptr(), meta.data_ptr(),
+                                stream=self._stream(xq))
+        return rec, meta
 
     def experts(self, xq: torch.Tensor, dx: torch.Tensor, pair_row: torch.Tensor,
                 pair_expert: torch.Tensor) -> torch.Tensor:
@@ -170,16 +222,12 @@ class ExpertParallelMoE:
         dist, ops, G, me = self.dist, self.ops, self.world, self.rank
         T, K, dev = x.shape[0], ops.K, x.device
         idx, w, xq, dx = ops.route(x)
-        plan = plan_dispatch(idx, self.per_rank, G, self.placement)
+        plan = ops.plan(idx, self.per_rank, G, self.placement)
 
         # Every rank's (rows, pairs) per destination: one all_gather, one
         # host synchronisation for the collectives' split sizes.
-        cnt = torch.stack([plan.rows_per_dest, plan.pairs_per_dest], 1).to(torch.int64)  # [G, 2]
-        M = torch.empty((G * G, 2), dtype=torch.int64, device=dev)
-        dist.all_gather_into_tensor(M, cnt, group=self.group)
-        M = M.view(G, G, 2)                                              # [src, dst, (rows, pairs)]
-        # where this rank's rows start in each destination's receive buffer
-        row_start = (M[:, :, 0].cumsum(0) - M[:, :, 0])[me]              # [G]
+        M = torch.empty((G, G, 2), dtype=torch.int64, device=dev)      # [src, dst, (rows, pairs)]
+        dist.all_gather_into_tensor(M.view(G * G, 2), plan.counts, group=self.group)
         Mh = M.cpu()
         rows_out, pairs_out = Mh[me, :, 0].tolist(), Mh[me, :, 1].tolist()
         rows_in, pairs_in = Mh[:, me, 0].tolist(), Mh[:, me, 1].tolist()
@@ -187,13 +235,8 @@ class ExpertParallelMoE:
 
         # dispatch: each row as one record (int8 values, then the f32 block
         # scales), and the pair records with rows numbered in the receiver
-        rows = plan.send_rows(R_out, T)
-        rec_w = xq.shape[1] + dx.shape[1] * 4
-        rec = torch.empty((R_out, rec_w), dtype=torch.uint8, device=dev)
-        rec[:, :xq.shape[1]] = xq[rows].view(torch.uint8)
-        rec[:, xq.shape[1]:] = dx[rows].view(torch.uint8)
-        meta = plan.pair_meta.clone()
-        meta[:, 0] += row_start[plan.pair_dest].to(torch.int32)
+        rec, meta = ops.pack(xq, dx, plan, M, me, R_out, T * K)
+        rec_w = rec.shape[1]
         rec_in = torch.empty((R_in, rec_w), dtype=torch.uint8, device=dev)
         meta_in = torch.empty((P_in, 2), dtype=torch.int32, device=dev)
         _a2a(dist, rec_in, rec, rows_in, rows_out, self.group)
@@ -209,9 +252,7 @@ class ExpertParallelMoE:
         # row y_pos[p] of it
         y_back = torch.empty((T * K, y_in.shape[1]), dtype=y_in.dtype, device=dev)
         _a2a(dist, y_back, y_in, pairs_out, pairs_in, self.group)
-        y_pos = torch.empty(T * K, dtype=torch.int32, device=dev)
-        y_pos[plan.pair_order] = torch.arange(T * K, dtype=torch.int32, device=dev)
-        ops.combine(x, w, y_back, y_pos)
+        ops.combine(x, w, y_back, plan.y_pos)
         return x
 
 
@@ -225,7 +266,7 @@ def simulate(ops, x: torch.Tensor, world: int, placement: str = "contiguous") ->
     routed = []
     for r in range(G):
         idx, w, xq, dx = ops.route(x[r])
-        routed.append((w, xq, dx, plan_dispatch(idx, per, G, placement)))
+        routed.append((w, xq, dx, ops.plan(idx, per, G, placement)))
     y_back = [None] * G
     parts = [[] for _ in range(G)]
     for g in range(G):  # destination g receives from every source, in source order
@@ -234,7 +275,7 @@ def simulate(ops, x: torch.Tensor, world: int, placement: str = "contiguous") ->
             w, xq, dx, plan = routed[s]
             r0 = int(plan.rows_per_dest[:g].sum()); r1 = r0 + int(plan.rows_per_dest[g])
             p0 = int(plan.pairs_per_dest[:g].sum()); p1 = p0 + int(plan.pairs_per_dest[g])
-            sel = plan.send_rows(int(plan.rows_per_dest.sum()), T)[r0:r1]
+            sel = plan.send_rows[r0:r1].long()
             xq_in.append(xq[sel]); dx_in.append(dx[sel])
             rows.append(plan.pair_meta[p0:p1, 0].long() + base)
             exps.append(plan.pair_meta[p0:p1, 1])
@@ -249,7 +290,5 @@ def simulate(ops, x: torch.Tensor, world: int, placement: str = "contiguous") ->
     for r in range(G):
         w, xq, dx, plan = routed[r]
         y_back[r] = torch.cat(parts[r])  # destination-major: the plan's pair order
-        y = torch.empty_like(y_back[r])
-        y[plan.pair_order] = y_back[r]
-        ops.combine(x[r], w, y)
+        ops.combine(x[r], w, y_back[r], plan.y_pos)
     return x

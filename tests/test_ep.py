@@ -17,7 +17,7 @@ import numpy as np
 import pytest
 import torch
 
-from motoria_b200.ep import ExpertParallelMoE, plan_dispatch
+from motoria_b200.ep import ExpertParallelMoE, pack_records, plan_dispatch
 
 D, E, K, XS = 16, 8, 3, 4
 
@@ -40,6 +40,9 @@ class FakeOps:
         xq = torch.clamp(torch.round(x * 20), -127, 127).to(torch.int8)
         dx = torch.stack([x.abs().amax(1), x.sum(1), x[:, 0], x[:, 1]], 1)
         return idx.to(torch.int32), w, xq, dx
+
+    plan = staticmethod(plan_dispatch)
+    pack = staticmethod(pack_records)
 
     def experts(self, xq, dx, pair_row, pair_expert):
         r = pair_row.long()
@@ -79,13 +82,14 @@ def test_plan_sends_each_row_once_per_destination():
         plan = plan_dispatch(idx, per, world, placement)
         dest = idx.long() // per if placement == "contiguous" else idx.long() % world
         assert int(plan.pairs_per_dest.sum()) == idx.numel()
-        assert int((plan.row_keys < world * x.shape[0]).sum()) == int(plan.rows_per_dest.sum())
+        pair_order = torch.argsort(plan.y_pos.long())
+        assert torch.equal(torch.sort(plan.y_pos.long()).values, torch.arange(idx.numel()))
         r0 = p0 = 0
         for g in range(world):
-            rows = plan.send_rows(int(plan.rows_per_dest.sum()), x.shape[0])[r0:r0 + int(plan.rows_per_dest[g])]
+            rows = plan.send_rows[r0:r0 + int(plan.rows_per_dest[g])].long()
             want = torch.nonzero((dest == g).any(1)).flatten()
             assert torch.equal(rows, want)              # each token once, ascending
-            pairs = plan.pair_order[p0:p0 + int(plan.pairs_per_dest[g])]
+            pairs = pair_order[p0:p0 + int(plan.pairs_per_dest[g])]
             assert torch.equal(pairs, torch.sort(pairs).values)
             meta = plan.pair_meta[p0:p0 + int(plan.pairs_per_dest[g])]
             assert torch.equal(rows[meta[:, 0].long()], pairs // K)   # record -> its row

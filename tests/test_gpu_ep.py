@@ -4,6 +4,8 @@ miag_moe on the same tokens: sharding must not change a single bit.
 
 * the split steps on one GPU (pair p of token t is row t of the router's
   Q8_0 output, against expert idx[t][j]);
+* the dispatch plan and send records of the library's kernels against their
+  torch statement (ep.plan_dispatch, ep.pack_records), at ragged sizes;
 * G = 2, 4, 8 ranks played by one process on one GPU (ep.simulate), with the
   Zipf-biased router of config 3 so the ranks see skewed loads;
 * with two or more GPUs visible, two NCCL ranks under torchrun, each engine
@@ -21,7 +23,7 @@ import pytest
 
 from conftest import get_layer
 from motoria_b200 import MoEEngine, synth
-from motoria_b200.ep import EngineOps, simulate
+from motoria_b200.ep import EngineOps, pack_records, plan_dispatch, simulate
 
 pytestmark = pytest.mark.gpu
 QWEN = synth.QWEN3_30B_A3B
@@ -48,6 +50,65 @@ def test_split_steps_equal_the_block(torch_cuda, T):
         torch.cuda.synchronize()
         eng.sync()
         assert np.array_equal(_bits(x.cpu().numpy()), _bits(want))
+
+
+TOKENS = (3001, 0, 1, 1024, 37, 4100, 5, 2048)  # per source rank: ragged, 0, several tiles
+
+
+def _routing(torch, T, seed):
+    """T rows of K distinct experts, skewed toward low expert ids."""
+    g = torch.Generator().manual_seed(seed)
+    p = 1.0 / torch.arange(1, QWEN.n_experts + 1, dtype=torch.float64) ** 0.8
+    if T == 0:
+        return torch.empty((0, QWEN.n_active), dtype=torch.int32)
+    return torch.multinomial(p.expand(T, -1), QWEN.n_active, generator=g).to(torch.int32)
+
+
+@pytest.mark.parametrize("G,placement", [(1, "contiguous"), (2, "contiguous"), (4, "strided"),
+                                         (8, "contiguous"), (8, "strided")])
+def test_plan_and_records_equal_their_statement(torch_cuda, G, placement):
+    torch = torch_cuda
+    per = QWEN.n_experts // G
+    with MoEEngine(QWEN, n_layers=1) as eng:
+        ops = EngineOps(eng)
+        idx = [_routing(torch, TOKENS[r], 10 * G + r).cuda() for r in range(G)]
+        got = [ops.plan(i, per, G, placement) for i in idx]
+        want = [plan_dispatch(i, per, G, placement) for i in idx]
+        torch.cuda.synchronize()
+        eng.sync()
+        for a, b in zip(got, want):
+            n = int(b.counts[:, 0].sum())
+            assert torch.equal(a.counts, b.counts)
+            assert torch.equal(a.send_rows[:n], b.send_rows[:n])
+            assert torch.equal(a.pair_meta, b.pair_meta)
+            assert torch.equal(a.y_pos, b.y_pos)
+        all_counts = torch.stack([b.counts for b in want])
+        g = torch.Generator().manual_seed(G)
+        for me in range(G):
+            T = TOKENS[me]
+            xq = torch.randint(-128, 128, (T, QWEN.dim), generator=g, dtype=torch.int8).cuda()
+            dx = torch.randn((T, ops.xs), generator=g).cuda()
+            n_rows, n_pairs = int(all_counts[me, :, 0].sum()), T * QWEN.n_active
+            rec, meta = ops.pack(xq, dx, got[me], all_counts, me, n_rows, n_pairs)
+            rec_w, meta_w = pack_records(xq, dx, want[me], all_counts, me, n_rows, n_pairs)
+            torch.cuda.synchronize()
+            eng.sync()
+            assert torch.equal(rec, rec_w)
+            assert torch.equal(meta, meta_w)
+
+
+def test_plan_reports_an_expert_out_of_range(torch_cuda):
+    torch = torch_cuda
+    with MoEEngine(QWEN, n_layers=1) as eng:
+        ops = EngineOps(eng)
+        idx = _routing(torch, 40, 5).cuda()
+        idx[3, 2] = QWEN.n_experts
+        ops.plan(idx, QWEN.n_experts // 2, 2)
+        torch.cuda.synchronize()
+        with pytest.raises(Exception, match="routing index|expert"):
+            eng.sync()
+        ops.plan(_routing(torch, 40, 6).cuda(), QWEN.n_experts // 2, 2)  # the context still works
+        eng.sync()
 
 
 @pytest.mark.parametrize("G,placement", [(2, "contiguous"), (4, "contiguous"), (8, "contiguous"),
