@@ -39,6 +39,7 @@ struct miag_ctx {
     Work ws{};
     float *x_dev = nullptr;
     int *d_err = nullptr;
+    int *h_err = nullptr;  // pinned: the error word, read back with a call's results
     int last_T = 0, last_launches = 0;
     // upload staging
     uint8_t *stage_dev = nullptr, *stage_host = nullptr;
@@ -183,6 +184,8 @@ extern "C" int miag_open(miag_ctx **out, const miag_shape *shape, int device, ch
     if ((e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking)) != cudaSuccess)
         return fail("cudaStreamCreate", e);
     if ((e = cudaMalloc(&c->d_err, sizeof(int))) != cudaSuccess) return fail("cudaMalloc(err)", e);
+    if ((e = cudaHostAlloc(&c->h_err, sizeof(int), cudaHostAllocDefault)) != cudaSuccess)
+        return fail("cudaHostAlloc(err)", e);
     // Zero-fills go on the context stream: it is non-blocking, so a plain
     // cudaMemset (legacy default stream) would not be ordered with its kernels.
     if ((e = cudaMemsetAsync(c->d_err, 0, sizeof(int), c->stream)) != cudaSuccess)
@@ -223,6 +226,7 @@ extern "C" void miag_close(miag_ctx *c) {
     for (cudaEvent_t e : c->event_pool) cudaEventDestroy(e);
     cudaFree(c->ws_mem);
     cudaFree(c->d_err);
+    if (c->h_err) cudaFreeHost(c->h_err);
     cudaFree(c->stage_dev);
     if (c->stage_host) cudaFreeHost(c->stage_host);
     if (c->stream) cudaStreamDestroy(c->stream);
@@ -466,9 +470,11 @@ extern "C" int miag_moe_async(miag_ctx *c, int layer, float *x_dev, int n_tokens
                        errlen);
 }
 
-static int read_device_error(miag_ctx *c, char *err, size_t errlen) {
-    int code = 0;
-    CU(cudaMemcpy(&code, c->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+// The error word, as a call that has just synchronised its stream left it:
+// `code` when the caller already copied the word back with its results
+// (pinned h_err, same stream), else read now.
+static int read_device_error(miag_ctx *c, char *err, size_t errlen, int code = -1) {
+    if (code < 0) CU(cudaMemcpy(&code, c->d_err, sizeof(int), cudaMemcpyDeviceToHost));
     if (code == 0) return 0;
     CU(cudaMemsetAsync(c->d_err, 0, sizeof(int), c->stream));
     CU(cudaStreamSynchronize(c->stream));
@@ -535,8 +541,9 @@ extern "C" int miag_moe(miag_ctx *c, int layer, float *x, int n_tokens, char *er
     CU(cudaMemcpyAsync(c->x_dev, x, bytes, cudaMemcpyHostToDevice, c->stream));
     if (enqueue_moe(c, layer, c->x_dev, n_tokens, c->stream, err, errlen)) return -1;
     CU(cudaMemcpyAsync(x, c->x_dev, bytes, cudaMemcpyDeviceToHost, c->stream));
-    CU(cudaStreamSynchronize(c->stream));
-    return read_device_error(c, err, errlen);
+    CU(cudaMemcpyAsync(c->h_err, c->d_err, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
+    CU(cudaStreamSynchronize(c->stream));  // one wait for the results and the error word
+    return read_device_error(c, err, errlen, *c->h_err);
 }
 
 // ---- The block in three device steps, for callers that move pairs between
