@@ -27,8 +27,9 @@ Multi-GPU (torchrun, N>1), scaling weak (tokens per GPU fixed):
   config5, the expert-parallel configuration: motoria_b200.ep.  Each rank
     holds E/N experts (--ep-placement contiguous, as specified, or strided)
     and routes its own tokens; (row, expert) pairs go to the experts' ranks
-    and the results come back over NCCL all-to-all; outputs equal the one-GPU
-    block bit for bit.
+    and the results come back stored by the down launch straight into the
+    origin rank's memory over NVLink (--ep-exchange peer, the default) or by
+    NCCL all-to-all (collective); outputs equal the one-GPU block bit for bit.
   config1-3: replicas.  Every rank holds all experts and serves its own
     batch; the block is independent per token, so there is no data-path
     collective.
@@ -254,7 +255,8 @@ def run_ours(args, T_desc, T, rms, zipf):
         # expert parallelism: this rank holds E/N experts (placement below)
         from motoria_b200.ep import EngineOps, ExpertParallelMoE
 
-        ep = ExpertParallelMoE(EngineOps(eng), placement=args.ep_placement)
+        ep = ExpertParallelMoE(EngineOps(eng), placement=args.ep_placement,
+                               exchange=args.ep_exchange)
         eng.set_layer(0, lay.ffn_norm, lay.router, lay.bias)
         for e in ep.experts_of(rank):
             eng.upload_experts(0, lay.blobs[e:e + 1], first=e)
@@ -394,7 +396,9 @@ def run_ours(args, T_desc, T, rms, zipf):
                        "expert_hidden": shape.expert_hidden, "active_experts": n_act,
                        "weights": "Q8_0 HBM-resident",
                        "l2": "flushed between steps outside the timed events (256 MiB written, then read back)",
-                       "parallelism": (f"ep{world} ({args.ep_placement})" if ep else
+                       "parallelism": (f"ep{world} ({args.ep_placement}, y back by "
+                                       f"{'peer stores' if args.ep_exchange == 'peer' else 'all-to-all'})"
+                                       if ep else
                                        "replicas" if world > 1 else "single"),
                        "experts_per_gpu": shape.n_experts // world if ep else shape.n_experts},
             "e2e": {"value": e2e_value, "unit": UNIT,
@@ -432,6 +436,9 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ep-placement", choices=["contiguous", "strided"], default="contiguous",
                     help="expert placement of the expert-parallel run (config5, N>1)")
+    ap.add_argument("--ep-exchange", choices=["peer", "collective"], default="peer",
+                    help="how the expert results return (config5, N>1): stored by the down "
+                         "launch into the origin rank's memory over NVLink, or NCCL all-to-all")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -164,6 +164,42 @@ int miag_ep_pack_async(miag_ctx *c, const int8_t *xq, const float *dx,
                        uint8_t *rec, int32_t *meta_out, void *stream, char *err,
                        size_t errlen);
 
+/* The return of the y rows over NVLink peer memory (no reference
+ * counterpart).  Each rank's exchange buffer holds the y rows of its own
+ * pairs, in its send order, and one completion flag per rank; the peers map
+ * it through CUDA IPC, so the ranks must be processes on distinct GPUs of
+ * one node.
+ * miag_ep_buffer: allocates (or grows) this rank's buffer for y_rows rows of
+ *   dim f32; returns the rows, the flags [8] (zeroed when allocated) and a
+ *   64-byte cudaIpcMemHandle_t for the peers.  Growing frees the old buffer:
+ *   every peer must have closed its mapping first (miag_ep_close_peers).
+ * miag_ep_open_peer: maps a peer's buffer (its handle); returns its rows and
+ *   flags.  miag_ep_close_peers unmaps every peer buffer opened.
+ * miag_experts_to_ranks_async: miag_experts_async, except that the y row of
+ *   pair p, received from rank s (pairs [src_end[s-1], src_end[s]), in rank
+ *   order), is stored at dst[s] + (p - src_end[s-1]) rows on rank s; when
+ *   all rows are stored, flags[r][rank] = seq on every rank r.  src_end,
+ *   dst and flags are host arrays of n_ranks entries (dst, flags: device
+ *   addresses as miag_ep_buffer / miag_ep_open_peer gave them).  With no
+ *   pairs it only sets the flags.
+ * miag_ep_wait_async: enqueues a wait until flags[r] >= seq for every rank
+ *   r < n_ranks (this rank's own flags); then every row stored for this rank
+ *   has landed.  The wait gives up after two seconds and reports it as a
+ *   device error at the next miag_sync. */
+int miag_ep_buffer(miag_ctx *c, size_t y_rows, void **y_dev, unsigned **flags_dev,
+                   void *ipc_handle, char *err, size_t errlen);
+int miag_ep_open_peer(miag_ctx *c, const void *ipc_handle, void **y_dev,
+                      unsigned **flags_dev, char *err, size_t errlen);
+int miag_ep_close_peers(miag_ctx *c, char *err, size_t errlen);
+int miag_experts_to_ranks_async(miag_ctx *c, int layer, const int8_t *xq, const float *dx,
+                                int n_rows, const int32_t *pair_row,
+                                const int32_t *pair_expert, int n_pairs, int n_ranks,
+                                int rank, const int32_t *src_end, float *const *dst,
+                                unsigned *const *flags, unsigned seq, void *stream,
+                                char *err, size_t errlen);
+int miag_ep_wait_async(miag_ctx *c, const unsigned *flags, int n_ranks, unsigned seq,
+                       void *stream, char *err, size_t errlen);
+
 /* Waits for the context's work on `stream` (NULL = own stream) and reports
  * any device-side error (a bounded wait that gave up, a bad index). */
 int miag_sync(miag_ctx *c, void *stream, char *err, size_t errlen);

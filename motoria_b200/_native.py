@@ -61,6 +61,17 @@ SIGNATURES = {
                                      C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int,
                                      C.c_void_p, C.c_void_p, C.c_void_p, C.c_char_p,
                                      C.c_size_t]),
+    "miag_ep_buffer": (C.c_int, [C.c_void_p, C.c_size_t, C.c_void_p, C.c_void_p, C.c_void_p,
+                                 C.c_char_p, C.c_size_t]),
+    "miag_ep_open_peer": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_char_p,
+                                    C.c_size_t]),
+    "miag_ep_close_peers": (C.c_int, [C.c_void_p, C.c_char_p, C.c_size_t]),
+    "miag_experts_to_ranks_async": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_int,
+                                              C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int,
+                                              C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint,
+                                              C.c_void_p, C.c_char_p, C.c_size_t]),
+    "miag_ep_wait_async": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_uint, C.c_void_p,
+                                     C.c_char_p, C.c_size_t]),
     "miag_sync": (C.c_int, [C.c_void_p, C.c_void_p, C.c_char_p, C.c_size_t]),
     "miag_selftest_wait_timeout": (C.c_int, [C.c_void_p, C.c_int, C.c_char_p, C.c_size_t]),
     "miag_routing": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,

@@ -40,6 +40,11 @@ struct miag_ctx {
     float *x_dev = nullptr;
     int *d_err = nullptr;
     int *h_err = nullptr;  // pinned: the error word, read back with a call's results
+    // expert parallelism: this rank's exchange buffer (flags | CTA counter |
+    // y rows) and the peers' buffers mapped here
+    uint8_t *ep_buf = nullptr;
+    size_t ep_rows = 0;
+    std::vector<void *> ep_peers;
     int last_T = 0, last_launches = 0;
     // upload staging
     uint8_t *stage_dev = nullptr, *stage_host = nullptr;
@@ -225,6 +230,8 @@ extern "C" void miag_close(miag_ctx *c) {
         for (auto &pr : v) c->event_pool.push_back(pr.first), c->event_pool.push_back(pr.second);
     for (cudaEvent_t e : c->event_pool) cudaEventDestroy(e);
     cudaFree(c->ws_mem);
+    for (void *q : c->ep_peers) cudaIpcCloseMemHandle(q);
+    cudaFree(c->ep_buf);
     cudaFree(c->d_err);
     if (c->h_err) cudaFreeHost(c->h_err);
     cudaFree(c->stage_dev);
@@ -482,6 +489,7 @@ static int read_device_error(miag_ctx *c, char *err, size_t errlen, int code = -
                        : code == kErrWaitEmpty ? "the producer timed out waiting for a free stage"
                        : code == kErrBadExpert ? "a routing index was out of range"
                        : code == kErrItemList  ? "an expert launch's work list named a tile outside the store"
+                       : code == kErrWaitPeer  ? "timed out waiting for another rank's expert results"
                                                : "unknown device error";
     set_err(err, errlen, "device error %d: %s", code, what);
     return -1;
@@ -606,6 +614,141 @@ extern "C" int miag_experts_async(miag_ctx *c, int layer, const int8_t *xq, cons
               [&] { launch_gateup(c->dims, c->lay, L, w, c->num_sms, c->d_err, s); });
     run_stage(c, kDown, down_launches(c->dims, w.P), s,
               [&] { launch_down(c->dims, c->lay, L, w, c->num_sms, c->d_err, s); });
+    CU(cudaGetLastError());
+    return 0;
+}
+
+// ---- Expert parallelism over peer memory: down stores each y row at the
+// pair's origin rank, and a flag per rank says when all of them have landed.
+
+namespace {
+constexpr size_t kEpFlagsOff = 0, kEpDoneOff = 64, kEpRowsOff = 256;
+}
+
+extern "C" int miag_ep_buffer(miag_ctx *c, size_t y_rows, void **y_dev, unsigned **flags_dev,
+                              void *ipc_handle, char *err, size_t errlen) {
+    if (!c || !y_dev || !flags_dev || !ipc_handle) {
+        set_err(err, errlen, "null argument");
+        return -1;
+    }
+    CU(cudaSetDevice(c->device));
+    if (!c->ep_buf || y_rows > c->ep_rows) {
+        CU(cudaStreamSynchronize(c->stream));
+        cudaFree(c->ep_buf);
+        c->ep_buf = nullptr, c->ep_rows = 0;
+        const size_t bytes = kEpRowsOff + y_rows * (size_t)c->dims.d * sizeof(float);
+        CU(cudaMalloc(&c->ep_buf, bytes));
+        CU(cudaMemset(c->ep_buf, 0, kEpRowsOff));  // flags and counter start at zero
+        CU(cudaDeviceSynchronize());
+        c->ep_rows = y_rows;
+    }
+    cudaIpcMemHandle_t h;
+    CU(cudaIpcGetMemHandle(&h, c->ep_buf));
+    memcpy(ipc_handle, &h, sizeof h);
+    *y_dev = c->ep_buf + kEpRowsOff;
+    *flags_dev = reinterpret_cast<unsigned *>(c->ep_buf + kEpFlagsOff);
+    return 0;
+}
+
+extern "C" int miag_ep_open_peer(miag_ctx *c, const void *ipc_handle, void **y_dev,
+                                 unsigned **flags_dev, char *err, size_t errlen) {
+    if (!c || !ipc_handle || !y_dev || !flags_dev) {
+        set_err(err, errlen, "null argument");
+        return -1;
+    }
+    CU(cudaSetDevice(c->device));
+    cudaIpcMemHandle_t h;
+    memcpy(&h, ipc_handle, sizeof h);
+    void *q = nullptr;
+    CU(cudaIpcOpenMemHandle(&q, h, cudaIpcMemLazyEnablePeerAccess));
+    c->ep_peers.push_back(q);
+    *y_dev = static_cast<uint8_t *>(q) + kEpRowsOff;
+    *flags_dev = reinterpret_cast<unsigned *>(static_cast<uint8_t *>(q) + kEpFlagsOff);
+    return 0;
+}
+
+extern "C" int miag_ep_close_peers(miag_ctx *c, char *err, size_t errlen) {
+    if (!c) {
+        set_err(err, errlen, "null context");
+        return -1;
+    }
+    CU(cudaSetDevice(c->device));
+    CU(cudaStreamSynchronize(c->stream));
+    for (void *q : c->ep_peers) CU(cudaIpcCloseMemHandle(q));
+    c->ep_peers.clear();
+    return 0;
+}
+
+extern "C" int miag_experts_to_ranks_async(miag_ctx *c, int layer, const int8_t *xq,
+                                           const float *dx, int n_rows, const int32_t *pair_row,
+                                           const int32_t *pair_expert, int n_pairs, int n_ranks,
+                                           int rank, const int32_t *src_end, float *const *dst,
+                                           unsigned *const *flags, unsigned seq, void *stream,
+                                           char *err, size_t errlen) {
+    if (check_layer(c, layer, err, errlen)) return -1;
+    if (n_ranks < 1 || n_ranks > kEpMaxRanks || rank < 0 || rank >= n_ranks || !src_end || !dst ||
+        !flags || !c->ep_buf) {
+        set_err(err, errlen, "bad ranks or routes (1..%d ranks; miag_ep_buffer first)", kEpMaxRanks);
+        return -1;
+    }
+    if (n_pairs < 0 || n_rows < 0 ||
+        (n_pairs > 0 && (!xq || !dx || !pair_row || !pair_expert || n_rows == 0)) ||
+        ((uintptr_t)xq & 15u) || ((uintptr_t)dx & 15u)) {
+        set_err(err, errlen, "bad buffers (device pointers; xq, dx 16-byte aligned)");
+        return -1;
+    }
+    YRoute yr{};
+    yr.n = n_ranks, yr.me = rank, yr.seq = seq;
+    yr.done = reinterpret_cast<unsigned *>(c->ep_buf + kEpDoneOff);
+    int prev = 0;
+    for (int r = 0; r < n_ranks; r++) {
+        if (src_end[r] < prev || !flags[r] || (src_end[r] > prev && !dst[r])) {
+            set_err(err, errlen, "rank %d: bad pair range or destination", r);
+            return -1;
+        }
+        yr.end[r] = prev = src_end[r], yr.dst[r] = dst[r], yr.flags[r] = flags[r];
+    }
+    if (prev != n_pairs) {
+        set_err(err, errlen, "the ranks' pair ranges cover %d pairs, not %d", prev, n_pairs);
+        return -1;
+    }
+    c->last_launches = 0;
+    CU(cudaSetDevice(c->device));
+    const cudaStream_t s = stream ? (cudaStream_t)stream : c->stream;
+    if (n_pairs == 0) {  // nothing to compute: the other ranks still wait for this one
+        launch_ep_signal(yr, s);
+        c->last_launches = 1;
+        CU(cudaGetLastError());
+        return 0;
+    }
+    if (ensure_ws(c, (n_pairs + c->dims.K - 1) / c->dims.K, err, errlen)) return -1;
+    const LayerState &Ls = c->layers[(size_t)layer];
+    const LayerDev L{Ls.ffn_norm, Ls.router_t, Ls.has_bias ? Ls.bias : nullptr, Ls.experts};
+    Work w = c->ws;
+    w.P = n_pairs, w.nchunks = (n_pairs + kPermChunk - 1) / kPermChunk;
+    w.idx = const_cast<int32_t *>(pair_expert);
+    w.xq = const_cast<int8_t *>(xq), w.dx = const_cast<float *>(dx);
+    w.pair_row = pair_row, w.n_rows = n_rows, w.y = nullptr, w.yr = yr;
+    run_stage(c, kPermute, permute_launches(w.P, c->dims.E), s,
+              [&] { launch_permute(c->dims, w, c->d_err, s); });
+    run_stage(c, kGateUp, 1, s,
+              [&] { launch_gateup(c->dims, c->lay, L, w, c->num_sms, c->d_err, s); });
+    run_stage(c, kDown, down_launches(c->dims, w.P), s,
+              [&] { launch_down(c->dims, c->lay, L, w, c->num_sms, c->d_err, s); });
+    CU(cudaGetLastError());
+    return 0;
+}
+
+extern "C" int miag_ep_wait_async(miag_ctx *c, const unsigned *flags, int n_ranks, unsigned seq,
+                                  void *stream, char *err, size_t errlen) {
+    if (!c || !flags || n_ranks < 1 || n_ranks > kEpMaxRanks) {
+        set_err(err, errlen, "bad flags or ranks (1..%d)", kEpMaxRanks);
+        return -1;
+    }
+    CU(cudaSetDevice(c->device));
+    const cudaStream_t s = stream ? (cudaStream_t)stream : c->stream;
+    launch_ep_wait(flags, n_ranks, seq, 2000000000LL, c->d_err, s);  // gives up after 2 s
+    c->last_launches = 1;
     CU(cudaGetLastError());
     return 0;
 }

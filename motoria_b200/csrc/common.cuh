@@ -23,6 +23,7 @@ enum : int {
     kErrWaitEmpty = 2,    // the producer gave up waiting for a free stage
     kErrBadExpert = 3,    // a routing index outside [0, E)
     kErrItemList = 4,     // an expert launch's work list named a tile outside the store
+    kErrWaitPeer = 5,     // a rank gave up waiting for another rank's expert results
 };
 
 // Bounded spin: about one second at B200 clocks.
@@ -187,6 +188,17 @@ __device__ __forceinline__ unsigned long long global_ns() {
     unsigned long long t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
+}
+
+// A flag between GPUs: stored with release, loaded with acquire, both at
+// system scope (the other side may be a peer GPU).
+__device__ __forceinline__ void st_release_sys(unsigned *p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
 }
 
 // bar.sync on a named barrier shared by `threads` threads (a multiple of 32).

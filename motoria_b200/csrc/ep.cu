@@ -233,7 +233,39 @@ __global__ void k_ep_pack(const int8_t *xq, const float *dx, int d, int xs,
     meta_out[i] = make_int2(m.x + start, m.y);
 }
 
+// A rank that received no pairs runs no down launch: it still tells every
+// rank that it has stored all it had for them (one thread).
+__global__ void k_ep_signal(YRoute yr) {
+    __threadfence_system();
+    for (int r = 0; r < yr.n; r++) st_release_sys(yr.flags[r] + yr.me, yr.seq);
+}
+
+// Waits until every rank's flag here has reached seq: then every y row that
+// the ranks' down launches stored for this rank has landed.  One lane per
+// rank; gives up after timeout_ns (the error word says so) rather than spin
+// on a rank that will never signal.
+__global__ void k_ep_wait(const unsigned *flags, int n_ranks, unsigned seq, long long timeout_ns,
+                          int *err) {
+    const int r = threadIdx.x;
+    if (r >= n_ranks) return;
+    const unsigned long long t0 = global_ns();
+    while ((int)(ld_acquire_sys(flags + r) - seq) < 0) {
+        if ((long long)(global_ns() - t0) > timeout_ns) {
+            set_error(err, kErrWaitPeer);
+            return;
+        }
+        __nanosleep(200);
+    }
+}
+
 }  // namespace
+
+void launch_ep_signal(const YRoute &yr, cudaStream_t s) { k_ep_signal<<<1, 1, 0, s>>>(yr); }
+
+void launch_ep_wait(const unsigned *flags, int n_ranks, unsigned seq, long long timeout_ns,
+                    int *err, cudaStream_t s) {
+    k_ep_wait<<<1, 32, 0, s>>>(flags, n_ranks, seq, timeout_ns, err);
+}
 
 void launch_ep_plan(const int32_t *idx, int T, int K, int G, int per_rank, bool strided,
                     long long *counts, int32_t *send_rows, int32_t *pair_meta, int32_t *y_pos,

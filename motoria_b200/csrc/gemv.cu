@@ -62,6 +62,7 @@ struct GemvParams {
     const int8_t *hq;  // [P][eh]   Q8_0 h = silu(gate) * up, sorted order (down's input)
     const float *hs;   // [P][xs]   its block scales
     float *y;          // [P][d], pair order
+    YRoute yr;         // expert parallelism: y rows stored at their origin ranks instead
     int stages;
     int chunk;                 // pairs per chunk (tok_chunk)
     uint32_t x_stride;         // row stride of the staged activations
@@ -544,6 +545,21 @@ __device__ __forceinline__ void k_tile(uint64_t (&acc)[NT][2], uint32_t tile, ui
 }
 
 // What one item needs besides the kernel parameters.
+// The row of pair `pid` (pair order) in y: this rank's y, or under expert
+// parallelism the row at the pair's origin rank (YRoute).  The source rank is
+// found by compares on compile-time indices, so the route stays in the
+// parameter bank.
+__device__ __forceinline__ float *y_row(const GemvParams &p, int pid) {
+    const size_t d = (size_t)p.m.d;
+    if (p.yr.n == 0) return p.y + (size_t)pid * d;
+    float *base = p.yr.dst[0];
+    int start = 0;
+#pragma unroll
+    for (int i = 0; i < kEpMaxRanks - 1; i++)
+        if (i + 1 < p.yr.n && pid >= p.yr.end[i]) base = p.yr.dst[i + 1], start = p.yr.end[i];
+    return base + (size_t)(pid - start) * d;
+}
+
 struct ItemCtx {
     uint32_t stages;         // shared address of stage 0
     uint32_t x_rows, x_scl;  // shared addresses of the activation rows / scale rows
@@ -656,14 +672,13 @@ __device__ __forceinline__ void run_item(const GemvParams &p, const ItemCtx &ic,
         } else {
             // y goes out in pair order, so the combine (and a remote caller)
             // finds pair t*K + j's row without the permutation
-            const int d = p.m.d;
             if (qa < nq) {
-                float *yp = p.y + (size_t)__ldg(p.perm + ic.seg0 + ic.t0 + qa) * d;
+                float *yp = y_row(p, __ldg(p.perm + ic.seg0 + ic.t0 + qa));
                 if (R0 < rows) yp[R0] = o[0];
                 if (R1 < rows) yp[R1] = o[2];
             }
             if (qb < nq) {
-                float *yp = p.y + (size_t)__ldg(p.perm + ic.seg0 + ic.t0 + qb) * d;
+                float *yp = y_row(p, __ldg(p.perm + ic.seg0 + ic.t0 + qb));
                 if (R0 < rows) yp[R0] = o[1];
                 if (R1 < rows) yp[R1] = o[3];
             }
@@ -736,6 +751,20 @@ __device__ RatePrefix rate_prefixes(const float (&r)[kMaxSlots / 32], int ja, in
 // consecutive items share their activations.  (Handing the last 15-30 % of
 // the items out one by one from an atomic counter evened out the end times
 // too, but cost more in activation stagings than it saved.)
+// Expert parallelism: after the CTA's y rows (stores to peer memory among
+// them) the CTA is counted, and the launch's last CTA sets this rank's flag
+// on every rank (st.release.sys), so a rank that sees its flags at seq may
+// read every row stored for it.
+__device__ __forceinline__ void ep_signal_done(const YRoute &yr) {
+    __threadfence_system();  // this thread's y stores, before the CTA is counted
+    __syncthreads();
+    if (threadIdx.x == 0 && atomicAdd(yr.done, 1u) == gridDim.x - 1) {
+        __threadfence_system();
+        *yr.done = 0;  // for the next launch
+        for (int r = 0; r < yr.n; r++) st_release_sys(yr.flags[r] + yr.me, yr.seq);
+    }
+}
+
 template <bool kGU, bool kWide>
 __global__ void __launch_bounds__(kGemvThreads, 1) k_expert_mma(GemvParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -923,6 +952,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_expert_mma(GemvParams p) {
     }
     // decode down waited per chunk only; its end must still imply gate/up's
     if (kChunkWait) pdl_wait();
+    if (!kGU && p.yr.n > 0) ep_signal_done(p.yr);
 }
 
 // x[t] += w_j * y_j for j = 0..K-1 in order (forward.c:194).
@@ -973,6 +1003,7 @@ static void fill_params(GemvParams &p, const Dims &m, const StoreLayout &lay, co
     p.chunk_pre = w.chunk_pre, p.chunk_info = w.chunk_info, p.max_chunk = w.max_chunk;
     p.chunk_done = w.chunk_done;
     p.xq = w.xq, p.dx = w.dx, p.h = w.h, p.hq = w.hq, p.hs = w.hs, p.y = w.y, p.err = err;
+    p.yr = w.yr;
     p.pair_row = w.pair_row, p.n_rows = w.pair_row ? w.n_rows : w.T;
     p.one = 1.0f;
     p.chunk = tok_chunk(w.P, m.E);

@@ -6,6 +6,23 @@
 namespace miag {
 
 // Device workspace of one MoE call over T tokens, P = T*K pairs.
+constexpr int kEpMaxRanks = 8;  // one node
+
+// Expert parallelism: where the down launch stores the y row of each pair
+// it received.  Pairs arrive grouped by source rank: pairs [end[s-1], end[s])
+// came from rank s (end[-1] = 0), and pair p's row goes to
+// dst[s] + (p - end[s-1]) rows, in rank s's memory (a peer mapping).  When
+// every CTA's rows are stored, the launch's last CTA sets flags[r][me] = seq
+// on every rank r.  n == 0: y in pair order in Work::y, no flags.
+struct YRoute {
+    int n, me;
+    unsigned seq;
+    int end[kEpMaxRanks];
+    float *dst[kEpMaxRanks];
+    unsigned *flags[kEpMaxRanks];
+    unsigned *done;  // CTAs of the launch done so far; zero between launches
+};
+
 struct Work {
     int T, P, nchunks;
     int8_t *xq;            // [T][d]        quantized normalised input (Q8_0 values)
@@ -35,6 +52,7 @@ struct Work {
     float *hs;             // [P][xs_h]     its block scales (xs_h = scale_pad(eh / 32))
     float *y;              // [P][d]        down projections, pair order
     int32_t *tg_count;     // [T]           route: CTAs done per token group; zero between calls
+    YRoute yr;                // down's stores to other ranks (n == 0: none)
     const int32_t *pair_row;  // [P]        expert products over given pairs: each pair's row of
     int n_rows;               //              xq/dx (null: pair p is row p / K, the moe() case)
     const int32_t *y_pos;     // [P]        combine: row of y holding pair p (null: row p)
@@ -102,10 +120,13 @@ void launch_combine(const Dims &m, const Work &w, float *x, cudaStream_t s);
 int down_launches(const Dims &m, int P);  // kernels launch_down issues
 int gemv_setup_attributes(const Dims &m, const StoreLayout &lay);
 
-// Expert parallelism (ep.cu): the dispatch plan and the send records.
-constexpr int kEpMaxRanks = 8;  // one node
+// Expert parallelism (ep.cu): the dispatch plan, the send records, and the
+// completion flags of the y rows that down stores at their origin ranks.
 void launch_ep_plan(const int32_t *idx, int T, int K, int G, int per_rank, bool strided,
                     long long *counts, int32_t *send_rows, int32_t *pair_meta, int32_t *y_pos,
+                    int *err, cudaStream_t s);
+void launch_ep_signal(const YRoute &yr, cudaStream_t s);
+void launch_ep_wait(const unsigned *flags, int n_ranks, unsigned seq, long long timeout_ns,
                     int *err, cudaStream_t s);
 void launch_ep_pack(const int8_t *xq, const float *dx, int d, int xs, const int32_t *send_rows,
                     int n_rows, const int32_t *pair_meta, int n_pairs, const long long *all_counts,

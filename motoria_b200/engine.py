@@ -202,6 +202,53 @@ class MoEEngine:
                                           C.c_void_p(stream or 0), err, len(err))
         N.check(rc, err, "miag_ep_pack_async")
 
+    def ep_buffer(self, y_rows: int) -> tuple[int, int, bytes]:
+        """This rank's exchange buffer for y_rows rows (grown when needed):
+        (rows address, flags address, IPC handle bytes) (miag_ep_buffer)."""
+        y, fl, h = C.c_void_p(), C.c_void_p(), C.create_string_buffer(64)
+        err = N.errbuf()
+        rc = self._lib.miag_ep_buffer(self._ctx, y_rows, C.byref(y), C.byref(fl), h, err, len(err))
+        N.check(rc, err, "miag_ep_buffer")
+        return int(y.value), int(fl.value), bytes(h.raw)
+
+    def ep_open_peer(self, handle: bytes) -> tuple[int, int]:
+        """Maps a peer's exchange buffer: (rows address, flags address)."""
+        y, fl = C.c_void_p(), C.c_void_p()
+        err = N.errbuf()
+        rc = self._lib.miag_ep_open_peer(self._ctx, C.c_char_p(handle), C.byref(y), C.byref(fl),
+                                         err, len(err))
+        N.check(rc, err, "miag_ep_open_peer")
+        return int(y.value), int(fl.value)
+
+    def ep_close_peers(self) -> None:
+        err = N.errbuf()
+        N.check(self._lib.miag_ep_close_peers(self._ctx, err, len(err)), err, "miag_ep_close_peers")
+
+    def experts_to_ranks_device(self, xq_ptr: int, dx_ptr: int, n_rows: int, pair_row_ptr: int,
+                                pair_expert_ptr: int, n_pairs: int, rank: int, src_end, dst,
+                                flags, seq: int, layer: int = 0,
+                                stream: int | None = None) -> None:
+        """Expert products whose y rows go to the pairs' origin ranks
+        (miag_experts_to_ranks_async); src_end, dst, flags: one per rank."""
+        G = len(src_end)
+        ends = (C.c_int32 * G)(*src_end)
+        dsts = (C.c_void_p * G)(*dst)
+        fls = (C.c_void_p * G)(*flags)
+        err = N.errbuf()
+        rc = self._lib.miag_experts_to_ranks_async(
+            self._ctx, layer, C.c_void_p(xq_ptr), C.c_void_p(dx_ptr), n_rows,
+            C.c_void_p(pair_row_ptr), C.c_void_p(pair_expert_ptr), n_pairs, G, rank, ends, dsts,
+            fls, seq, C.c_void_p(stream or 0), err, len(err))
+        N.check(rc, err, "miag_experts_to_ranks_async")
+
+    def ep_wait_device(self, flags_ptr: int, n_ranks: int, seq: int,
+                       stream: int | None = None) -> None:
+        """Enqueues the wait for every rank's flag here to reach seq."""
+        err = N.errbuf()
+        rc = self._lib.miag_ep_wait_async(self._ctx, C.c_void_p(flags_ptr), n_ranks, seq,
+                                          C.c_void_p(stream or 0), err, len(err))
+        N.check(rc, err, "miag_ep_wait_async")
+
     def sync(self, stream: int | None = None) -> None:
         err = N.errbuf()
         N.check(self._lib.miag_sync(self._ctx, C.c_void_p(stream or 0), err, len(err)), err,

@@ -177,6 +177,27 @@ class EngineOps:
                                 stream=self._stream(xq))
         return y
 
+    def experts_to_ranks(self, xq: torch.Tensor, dx: torch.Tensor, pair_row: torch.Tensor,
+                         pair_expert: torch.Tensor, rank: int, src_end, dst, flags,
+                         seq: int) -> None:
+        """Expert products whose y rows are stored at the pairs' origin ranks
+        (peer memory), then flagged there (miag_experts_to_ranks_async)."""
+        P = pair_row.numel()
+        self.eng.experts_to_ranks_device(xq.data_ptr() if P else 0, dx.data_ptr() if P else 0,
+                                         xq.shape[0], pair_row.data_ptr() if P else 0,
+                                         pair_expert.data_ptr() if P else 0, P, rank, src_end,
+                                         dst, flags, seq, layer=self.layer,
+                                         stream=self._stream(xq))
+
+    def wait(self, flags: int, world: int, seq: int, like: torch.Tensor) -> None:
+        """Enqueues the wait for every rank's y rows to have landed here."""
+        self.eng.ep_wait_device(flags, world, seq, stream=self._stream(like))
+
+    def combine_rows(self, x: torch.Tensor, w: torch.Tensor, y: int, y_pos: torch.Tensor) -> None:
+        """combine() over y rows at a device address (the exchange buffer)."""
+        self.eng.combine_device(x.data_ptr(), x.shape[0], w.data_ptr(), y, y_pos.data_ptr(),
+                                stream=self._stream(x))
+
     def combine(self, x: torch.Tensor, w: torch.Tensor, y: torch.Tensor,
                 y_pos: torch.Tensor | None = None) -> None:
         """x[t] += sum_j w[t][j] * y[row(t*K + j)]; row(p) = y_pos[p], or p."""
@@ -195,13 +216,22 @@ class ExpertParallelMoE:
     `ops` runs the three device steps (EngineOps over this rank's MoEEngine,
     whose store must hold at least this rank's experts).  forward() updates
     the residual x [T][dim] (f32) in place, like miag_moe.
+
+    exchange: how the y rows come back.  "collective": all_to_all_single.
+    "peer": the down launch stores each row straight into the origin rank's
+    exchange buffer over NVLink (CUDA IPC mappings), so the return overlaps
+    the expert products, and a bounded device-side wait on per-rank flags
+    orders the combine after it.  Peer needs one GPU per rank on one node.
     """
 
-    def __init__(self, ops, group=None, placement: str = "contiguous"):
+    def __init__(self, ops, group=None, placement: str = "contiguous",
+                 exchange: str = "collective"):
         import torch.distributed as dist
 
         if placement not in ("contiguous", "strided"):
             raise ValueError(f"unknown placement {placement!r}")
+        if exchange not in ("collective", "peer"):
+            raise ValueError(f"unknown exchange {exchange!r}")
         self.dist = dist
         self.ops = ops
         self.group = group
@@ -211,6 +241,39 @@ class ExpertParallelMoE:
         if ops.E % self.world:
             raise ValueError(f"{ops.E} experts do not split evenly over {self.world} ranks")
         self.per_rank = ops.E // self.world
+        self.exchange = exchange
+        self._cap, self._seq = 0, 0
+        if exchange == "peer":
+            # every rank on a GPU of its own: the flag waits of two ranks
+            # must never share one GPU
+            dev = torch.cuda.current_device()
+            uuid = str(torch.cuda.get_device_properties(dev).uuid)
+            ids = [None] * self.world
+            dist.all_gather_object(ids, uuid, group=group)
+            if len(set(ids)) != self.world:
+                raise ValueError("exchange='peer' needs one GPU per rank")
+
+    def _ensure_buffers(self, rows: int) -> None:
+        """Exchange buffers of at least `rows` y rows on every rank, mapped
+        by every peer.  Every rank calls this with the same `rows` (derived
+        from the all-gathered counts), so all grow together."""
+        if rows <= self._cap:
+            return
+        dist, eng, G, me = self.dist, self.ops.eng, self.world, self.rank
+        cap = max(rows, 2 * self._cap)
+        torch.cuda.synchronize()
+        if self._cap:
+            eng.ep_close_peers()
+        dist.barrier(group=self.group)  # nobody maps or writes the old buffers now
+        y, flags, handle = eng.ep_buffer(cap)
+        handles = [None] * G
+        dist.all_gather_object(handles, handle, group=self.group)
+        maps = [(y, flags) if r == me else eng.ep_open_peer(handles[r]) for r in range(G)]
+        self._peer_y = [m[0] for m in maps]
+        self._peer_flags = [m[1] for m in maps]
+        self._own_y, self._own_flags = y, flags
+        self._cap = cap
+        dist.barrier(group=self.group)
 
     def experts_of(self, rank: int) -> list[int]:
         """The experts this placement puts on `rank` (its store must hold them)."""
@@ -246,6 +309,18 @@ class ExpertParallelMoE:
         pair_row = meta_in[:, 0].contiguous()
         pair_expert = meta_in[:, 1].contiguous()
         self.last_received = (R_in, P_in, pair_expert)
+        if self.exchange == "peer":
+            # rows from source s go to rank s's buffer, after the rows that
+            # s sends to lower ranks (its send order, the one y_pos indexes)
+            self._ensure_buffers(int(Mh[:, :, 1].sum(1).max()))
+            src_end = [int(v) for v in torch.tensor(pairs_in).cumsum(0)] if G else []
+            dst = [self._peer_y[s] + int(Mh[s, :me, 1].sum()) * ops.dim * 4 for s in range(G)]
+            self._seq += 1
+            ops.experts_to_ranks(xq_in, dx_in, pair_row, pair_expert, me, src_end, dst,
+                                 self._peer_flags, self._seq)
+            ops.wait(self._own_flags, G, self._seq, x)
+            ops.combine_rows(x, w, self._own_y, plan.y_pos)
+            return x
         y_in = ops.experts(xq_in, dx_in, pair_row, pair_expert)
 
         # results back in this rank's send order; the combine finds pair p at

@@ -26,7 +26,8 @@ def main():
     T = int(os.environ.get("EP_TOKENS", "300"))
     lay = synth.layer(shape, 1234, zipf=True)
     ep_eng = MoEEngine(shape, n_layers=1, device=local)
-    ep = ExpertParallelMoE(EngineOps(ep_eng), placement=os.environ.get("EP_PLACEMENT", "contiguous"))
+    ep = ExpertParallelMoE(EngineOps(ep_eng), placement=os.environ.get("EP_PLACEMENT", "contiguous"),
+                           exchange=os.environ.get("EP_EXCHANGE", "peer"))
     ep_eng.set_layer(0, lay.ffn_norm, lay.router, lay.bias)
     for e in ep.experts_of(rank):  # only this rank's experts
         ep_eng.upload_experts(0, lay.blobs[e:e + 1], first=e)
@@ -34,12 +35,14 @@ def main():
     full.load_layer(0, lay)
     x_host = synth.tokens(shape, 500 + rank, T)
     want = full.moe(x_host.copy())
-    x = torch.from_numpy(x_host).cuda()
-    ep.forward(x)
-    torch.cuda.synchronize()
-    ep_eng.sync()  # reports any device-side error of the sharded steps
-    got = x.cpu().numpy()
-    ok = np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    ok = True
+    for _ in range(2):  # twice: the second call reuses the exchange buffers and flags
+        x = torch.from_numpy(x_host).cuda()
+        ep.forward(x)
+        torch.cuda.synchronize()
+        ep_eng.sync()  # reports any device-side error of the sharded steps
+        got = x.cpu().numpy()
+        ok = ok and np.array_equal(got.view(np.uint32), want.view(np.uint32))
     flags = torch.tensor([int(ok)], device="cuda")
     dist.all_reduce(flags, op=dist.ReduceOp.MIN)
     if rank == 0:
