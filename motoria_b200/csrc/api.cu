@@ -44,6 +44,8 @@ struct miag_ctx {
     // y rows) and the peers' buffers mapped here
     uint8_t *ep_buf = nullptr;
     size_t ep_rows = 0;
+    int *ep_tiles = nullptr;  // the dispatch plan's per-tile counts
+    int ep_tiles_cap = 0;
     std::vector<void *> ep_peers;
     int last_T = 0, last_launches = 0;
     // upload staging
@@ -232,6 +234,7 @@ extern "C" void miag_close(miag_ctx *c) {
     cudaFree(c->ws_mem);
     for (void *q : c->ep_peers) cudaIpcCloseMemHandle(q);
     cudaFree(c->ep_buf);
+    cudaFree(c->ep_tiles);
     cudaFree(c->d_err);
     if (c->h_err) cudaFreeHost(c->h_err);
     cudaFree(c->stage_dev);
@@ -806,10 +809,18 @@ extern "C" int miag_ep_plan_async(miag_ctx *c, const int32_t *idx, int n_tokens,
     c->last_launches = 0;
     CU(cudaSetDevice(c->device));
     const cudaStream_t s = stream ? (cudaStream_t)stream : c->stream;
-    run_stage(c, kEpPlan, 1, s, [&] {
+    const int n_tiles = std::max(1, ep_plan_tiles(n_tokens));
+    if (n_tiles > c->ep_tiles_cap) {
+        CU(cudaStreamSynchronize(s));  // an earlier plan may still read the old counts
+        cudaFree(c->ep_tiles);
+        c->ep_tiles = nullptr, c->ep_tiles_cap = 0;
+        CU(cudaMalloc(&c->ep_tiles, (size_t)n_tiles * 2 * kEpMaxRanks * sizeof(int)));
+        c->ep_tiles_cap = n_tiles;
+    }
+    run_stage(c, kEpPlan, 2, s, [&] {
         launch_ep_plan(idx, n_tokens, c->dims.K, n_ranks, experts_per_rank, strided != 0,
-                       reinterpret_cast<long long *>(counts), send_rows, pair_meta, y_pos, c->d_err,
-                       s);
+                       c->ep_tiles, reinterpret_cast<long long *>(counts), send_rows, pair_meta,
+                       y_pos, c->d_err, s);
     });
     CU(cudaGetLastError());
     return 0;

@@ -5,8 +5,8 @@
 // (row, expert) record per (token, expert) pair; the expert products come
 // back one f32 row per pair and are combined in top-k order, so the results
 // equal the one-device block (src/model/forward.c:167-197) bit for bit.
-// The reference has no multi-device path; these two kernels compute the
-// plan of motoria_b200/ep.py:plan_dispatch and the records it sends, so
+// The reference has no multi-device path; these kernels compute the plan
+// of motoria_b200/ep.py:plan_dispatch and the records it sends, so
 // that the host only reads the per-rank counts its collectives need.
 //
 // Order (the one every rank agrees on): rows grouped by destination rank,
@@ -21,7 +21,7 @@ namespace miag {
 
 namespace {
 
-constexpr int kPlanThreads = 1024;  // one CTA: the plan is a few hundred KB of indices
+constexpr int kPlanThreads = 1024;  // tokens a plan CTA places (one tile)
 
 __device__ __forceinline__ int dest_of(int e, int per_rank, int G, bool strided) {
     return strided ? e % G : e / per_rank;
@@ -86,115 +86,104 @@ __device__ __forceinline__ void add_field(uint64_t (&v)[4], int f) {
         if ((f >> 2) == i) v[i] += 1ull << (16 * (f & 3));
 }
 
-__global__ void __launch_bounds__(kPlanThreads, 1)
-    k_ep_plan(const int32_t *idx, int T, int K, int G, int per_rank, int strided,
-              long long *counts, int32_t *send_rows, int2 *pair_meta, int32_t *y_pos, int *err) {
-    __shared__ int tot_rows[kEpMaxRanks], tot_pairs[kEpMaxRanks];
-    __shared__ int row_off[kEpMaxRanks], pair_off[kEpMaxRanks];  // where each block starts
-    __shared__ int run_rows[kEpMaxRanks], run_pairs[kEpMaxRanks];  // in earlier tiles
-    __shared__ uint64_t warp_sums[32][4];
-    const int E = per_rank * G;
-    const bool str = strided != 0;
-    if (threadIdx.x < kEpMaxRanks) {
-        tot_rows[threadIdx.x] = tot_pairs[threadIdx.x] = 0;
-        run_rows[threadIdx.x] = run_pairs[threadIdx.x] = 0;
+// The destinations of token t's pairs: per destination rank g, whether the
+// token goes there (bit g of hit) and its pairs to g (field 2g + 1 of v);
+// field 2g of v gets the hit.  A routing index outside [0, E) is placed
+// as expert 0 (in bounds) and reported.
+__device__ __forceinline__ unsigned token_dests(const int32_t *idx, int t, int K, int E,
+                                                int per_rank, int G, bool strided, uint64_t (&v)[4],
+                                                int *err) {
+    unsigned hit = 0;
+    for (int j = 0; j < K; j++) {
+        int e = __ldg(idx + (size_t)t * K + j);
+        if ((unsigned)e >= (unsigned)E) {
+            if (err) set_error(err, kErrBadExpert);
+            e = 0;
+        }
+        const int g = dest_of(e, per_rank, G, strided);
+        hit |= 1u << g;
+        add_field(v, 2 * g + 1);
     }
-    __syncthreads();
+#pragma unroll
+    for (int g = 0; g < kEpMaxRanks; g++)
+        if ((hit >> g) & 1u) add_field(v, 2 * g);
+    return hit;
+}
 
-    // pass 1: rows and pairs to each destination
-    {
-        int rows[kEpMaxRanks], pairs[kEpMaxRanks];
-#pragma unroll
-        for (int g = 0; g < kEpMaxRanks; g++) rows[g] = pairs[g] = 0;
-        for (int t = threadIdx.x; t < T; t += kPlanThreads) {
-            unsigned hit = 0;
-            for (int j = 0; j < K; j++) {
-                int e = __ldg(idx + (size_t)t * K + j);
-                if ((unsigned)e >= (unsigned)E) set_error(err, kErrBadExpert), e = 0;
-                const int g = dest_of(e, per_rank, G, str);
-                hit |= 1u << g;
-#pragma unroll
-                for (int gg = 0; gg < kEpMaxRanks; gg++) pairs[gg] += gg == g;
+// Pass 1, one CTA per tile of 1024 tokens: the tile's rows and pairs to each
+// destination, into tiles[tile][2g] and [2g + 1].
+__global__ void __launch_bounds__(kPlanThreads, 1)
+    k_ep_count(const int32_t *idx, int T, int K, int G, int per_rank, int strided, int *tiles,
+               int *err) {
+    __shared__ uint64_t warp_sums[32][4];
+    const int t = blockIdx.x * kPlanThreads + (int)threadIdx.x;
+    uint64_t v[4] = {0, 0, 0, 0};
+    if (t < T) token_dests(idx, t, K, per_rank * G, per_rank, G, strided != 0, v, err);
+    uint64_t total[4];
+    block_scan4(v, total, warp_sums);
+    if (threadIdx.x < 2 * kEpMaxRanks)
+        tiles[blockIdx.x * 2 * kEpMaxRanks + threadIdx.x] = field(total, (int)threadIdx.x);
+}
+
+// Pass 2, one CTA per tile: each token's rows and pairs at their places.
+// Every CTA derives the blocks' starts (and its tile's place in them) from
+// all tiles' counts; CTA 0 also writes the per-destination counts.
+__global__ void __launch_bounds__(kPlanThreads, 1)
+    k_ep_place(const int32_t *idx, int T, int K, int G, int per_rank, int strided,
+               const int *tiles, int n_tiles, long long *counts, int32_t *send_rows,
+               int2 *pair_meta, int32_t *y_pos) {
+    __shared__ int row_off[kEpMaxRanks], pair_off[kEpMaxRanks];  // where each block starts
+    __shared__ int row_pre[kEpMaxRanks], pair_pre[kEpMaxRanks];  // in earlier tiles
+    __shared__ uint64_t warp_sums[32][4];
+    if (threadIdx.x < kEpMaxRanks) {
+        const int g = threadIdx.x;
+        int rows = 0, pairs = 0, rb = 0, pb = 0;
+        if (g < G) {
+            for (int i = 0; i < n_tiles; i++) {
+                const int r = tiles[i * 2 * kEpMaxRanks + 2 * g];
+                const int q = tiles[i * 2 * kEpMaxRanks + 2 * g + 1];
+                if (i < (int)blockIdx.x) rb += r, pb += q;
+                rows += r, pairs += q;
             }
-#pragma unroll
-            for (int gg = 0; gg < kEpMaxRanks; gg++) rows[gg] += (hit >> gg) & 1u;
         }
-#pragma unroll
-        for (int g = 0; g < kEpMaxRanks; g++) {
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                rows[g] += __shfl_xor_sync(0xffffffffu, rows[g], o);
-                pairs[g] += __shfl_xor_sync(0xffffffffu, pairs[g], o);
-            }
-        }
-        if ((threadIdx.x & 31) == 0) {
-#pragma unroll
-            for (int g = 0; g < kEpMaxRanks; g++)
-                if (g < G) atomicAdd(&tot_rows[g], rows[g]), atomicAdd(&tot_pairs[g], pairs[g]);
-        }
+        row_pre[g] = rb, pair_pre[g] = pb;
+        row_off[g] = rows, pair_off[g] = pairs;  // totals; made exclusive below
+        if (blockIdx.x == 0 && g < G) counts[2 * g] = rows, counts[2 * g + 1] = pairs;
     }
     __syncthreads();
     if (threadIdx.x == 0) {
         int r = 0, q = 0;
-        for (int g = 0; g < G; g++) {
+        for (int g = 0; g < kEpMaxRanks; g++) {
+            const int tr = row_off[g], tq = pair_off[g];
             row_off[g] = r, pair_off[g] = q;
-            counts[2 * g] = tot_rows[g], counts[2 * g + 1] = tot_pairs[g];
-            r += tot_rows[g], q += tot_pairs[g];
+            r += tr, q += tq;
         }
     }
-    __syncthreads();
-
-    // pass 2: each token's rows and pairs at their places, a tile at a time
-    for (int base = 0; base < T; base += kPlanThreads) {
-        const int t = base + (int)threadIdx.x;
-        uint64_t v[4] = {0, 0, 0, 0};
-        unsigned hit = 0;
-        if (t < T) {
-            for (int j = 0; j < K; j++) {
-                int e = __ldg(idx + (size_t)t * K + j);
-                if ((unsigned)e >= (unsigned)E) e = 0;
-                const int g = dest_of(e, per_rank, G, str);
-                hit |= 1u << g;
-                add_field(v, 2 * g + 1);
-            }
+    const int t = blockIdx.x * kPlanThreads + (int)threadIdx.x;
+    const int E = per_rank * G;
+    const bool str = strided != 0;
+    uint64_t v[4] = {0, 0, 0, 0};
+    unsigned hit = 0;
+    if (t < T) hit = token_dests(idx, t, K, E, per_rank, G, str, v, nullptr);
+    const uint64_t own[4] = {v[0], v[1], v[2], v[3]};
+    uint64_t total[4];
+    block_scan4(v, total, warp_sums);  // its barriers also publish row_off / pair_off
+    if (t >= T) return;
+    uint64_t ex[4];
 #pragma unroll
-            for (int g = 0; g < kEpMaxRanks; g++)
-                if ((hit >> g) & 1u) add_field(v, 2 * g);
-        }
-        const uint64_t own[4] = {v[0], v[1], v[2], v[3]};
-        uint64_t total[4];
-        block_scan4(v, total, warp_sums);
-        if (t < T) {
-            // exclusive prefixes: the token's row within each destination's
-            // block, and the place of its first pair to each destination
-            uint64_t ex[4];
+    for (int i = 0; i < 4; i++) ex[i] = v[i] - own[i];
 #pragma unroll
-            for (int i = 0; i < 4; i++) ex[i] = v[i] - own[i];
-            int row_in[kEpMaxRanks], next[kEpMaxRanks];
-#pragma unroll
-            for (int g = 0; g < kEpMaxRanks; g++) {
-                const bool live = g < G;
-                row_in[g] = live ? run_rows[g] + field(ex, 2 * g) : 0;
-                next[g] = live ? pair_off[g] + run_pairs[g] + field(ex, 2 * g + 1) : 0;
-                if (live && ((hit >> g) & 1u)) send_rows[row_off[g] + row_in[g]] = t;
-            }
-            for (int j = 0; j < K; j++) {
-                const int e = __ldg(idx + (size_t)t * K + j);
-                const int g = dest_of((unsigned)e >= (unsigned)E ? 0 : e, per_rank, G, str);
-                int pos = 0, row = 0;
-#pragma unroll
-                for (int gg = 0; gg < kEpMaxRanks; gg++)
-                    if (gg == g) pos = next[gg]++, row = row_in[gg];
-                y_pos[(size_t)t * K + j] = pos;
-                pair_meta[pos] = make_int2(row, e);
-            }
-        }
-        __syncthreads();  // every thread has read run_rows / run_pairs
-        if (threadIdx.x < kEpMaxRanks && (int)threadIdx.x < G) {
-            run_rows[threadIdx.x] += field(total, 2 * threadIdx.x);
-            run_pairs[threadIdx.x] += field(total, 2 * threadIdx.x + 1);
-        }
-        __syncthreads();
+    for (int g = 0; g < kEpMaxRanks; g++)
+        if (g < G && ((hit >> g) & 1u)) send_rows[row_off[g] + row_pre[g] + field(ex, 2 * g)] = t;
+    uint64_t seen = 0;  // 8-bit fields: this token's pairs to each rank so far
+    for (int j = 0; j < K; j++) {
+        const int e = __ldg(idx + (size_t)t * K + j);
+        const int g = dest_of((unsigned)e >= (unsigned)E ? 0 : e, per_rank, G, str);
+        const int c = (int)((seen >> (8 * g)) & 0xffu);
+        seen += 1ull << (8 * g);
+        const int pos = pair_off[g] + pair_pre[g] + field(ex, 2 * g + 1) + c;
+        y_pos[(size_t)t * K + j] = pos;
+        pair_meta[pos] = make_int2(row_pre[g] + field(ex, 2 * g), e);
     }
 }
 
@@ -267,11 +256,16 @@ void launch_ep_wait(const unsigned *flags, int n_ranks, unsigned seq, long long 
     k_ep_wait<<<1, 32, 0, s>>>(flags, n_ranks, seq, timeout_ns, err);
 }
 
+int ep_plan_tiles(int T) { return (T + kPlanThreads - 1) / kPlanThreads; }
+
 void launch_ep_plan(const int32_t *idx, int T, int K, int G, int per_rank, bool strided,
-                    long long *counts, int32_t *send_rows, int32_t *pair_meta, int32_t *y_pos,
-                    int *err, cudaStream_t s) {
-    k_ep_plan<<<1, kPlanThreads, 0, s>>>(idx, T, K, G, per_rank, strided ? 1 : 0, counts, send_rows,
-                                         reinterpret_cast<int2 *>(pair_meta), y_pos, err);
+                    int *tiles, long long *counts, int32_t *send_rows, int32_t *pair_meta,
+                    int32_t *y_pos, int *err, cudaStream_t s) {
+    const int n = std::max(1, ep_plan_tiles(T));  // one CTA even for no tokens: it writes counts
+    k_ep_count<<<n, kPlanThreads, 0, s>>>(idx, T, K, G, per_rank, strided ? 1 : 0, tiles, err);
+    k_ep_place<<<n, kPlanThreads, 0, s>>>(idx, T, K, G, per_rank, strided ? 1 : 0, tiles, n,
+                                          counts, send_rows, reinterpret_cast<int2 *>(pair_meta),
+                                          y_pos);
 }
 
 void launch_ep_pack(const int8_t *xq, const float *dx, int d, int xs, const int32_t *send_rows,

@@ -544,7 +544,6 @@ __device__ __forceinline__ void k_tile(uint64_t (&acc)[NT][2], uint32_t tile, ui
     }
 }
 
-// What one item needs besides the kernel parameters.
 // The row of pair `pid` (pair order) in y: this rank's y, or under expert
 // parallelism the row at the pair's origin rank (YRoute).  The source rank is
 // found by compares on compile-time indices, so the route stays in the
@@ -560,6 +559,7 @@ __device__ __forceinline__ float *y_row(const GemvParams &p, int pid) {
     return base + (size_t)(pid - start) * d;
 }
 
+// What one item needs besides the kernel parameters.
 struct ItemCtx {
     uint32_t stages;         // shared address of stage 0
     uint32_t x_rows, x_scl;  // shared addresses of the activation rows / scale rows

@@ -122,9 +122,10 @@ int gemv_setup_attributes(const Dims &m, const StoreLayout &lay);
 
 // Expert parallelism (ep.cu): the dispatch plan, the send records, and the
 // completion flags of the y rows that down stores at their origin ranks.
+int ep_plan_tiles(int T);  // tiles of the plan: tiles[] holds 2 * kEpMaxRanks ints each
 void launch_ep_plan(const int32_t *idx, int T, int K, int G, int per_rank, bool strided,
-                    long long *counts, int32_t *send_rows, int32_t *pair_meta, int32_t *y_pos,
-                    int *err, cudaStream_t s);
+                    int *tiles, long long *counts, int32_t *send_rows, int32_t *pair_meta,
+                    int32_t *y_pos, int *err, cudaStream_t s);
 void launch_ep_signal(const YRoute &yr, cudaStream_t s);
 void launch_ep_wait(const unsigned *flags, int n_ranks, unsigned seq, long long timeout_ns,
                     int *err, cudaStream_t s);
