@@ -114,6 +114,20 @@ def pack_records(xq: torch.Tensor, dx: torch.Tensor, plan: DispatchPlan,
     return rec, meta
 
 
+def peer_routes(counts: torch.Tensor, me: int, peer_rows: list[int], row_bytes: int):
+    """Where the y rows of the pairs rank `me` received go, for the peer
+    exchange.  counts [G][G][2]: every rank's (rows, pairs) per destination,
+    all-gathered.  The pairs arrive grouped by source rank; those from rank s
+    go to s's exchange buffer (rows at address peer_rows[s]), after the pairs
+    s sends to lower ranks: the place s's y_pos gives them.  Returns
+    (src_end, dst): the end of each source's pairs in the received list, and
+    the address of each source's first row."""
+    G = counts.shape[0]
+    src_end = [int(v) for v in counts[:, me, 1].cumsum(0)]
+    dst = [peer_rows[s] + int(counts[s, :me, 1].sum()) * row_bytes for s in range(G)]
+    return src_end, dst
+
+
 class EngineOps:
     """The three device steps of a MoEEngine on torch tensors, enqueued on the
     tensors' device's current stream."""
@@ -313,8 +327,7 @@ class ExpertParallelMoE:
             # rows from source s go to rank s's buffer, after the rows that
             # s sends to lower ranks (its send order, the one y_pos indexes)
             self._ensure_buffers(int(Mh[:, :, 1].sum(1).max()))
-            src_end = [int(v) for v in torch.tensor(pairs_in).cumsum(0)] if G else []
-            dst = [self._peer_y[s] + int(Mh[s, :me, 1].sum()) * ops.dim * 4 for s in range(G)]
+            src_end, dst = peer_routes(Mh, me, self._peer_y, ops.dim * 4)
             self._seq += 1
             ops.experts_to_ranks(xq_in, dx_in, pair_row, pair_expert, me, src_end, dst,
                                  self._peer_flags, self._seq)

@@ -17,7 +17,7 @@ import numpy as np
 import pytest
 import torch
 
-from motoria_b200.ep import ExpertParallelMoE, pack_records, plan_dispatch
+from motoria_b200.ep import ExpertParallelMoE, pack_records, peer_routes, plan_dispatch
 
 D, E, K, XS = 16, 8, 3, 4
 
@@ -97,6 +97,37 @@ def test_plan_sends_each_row_once_per_destination():
             assert bool((dest.reshape(-1)[pairs] == g).all())
             r0 += int(plan.rows_per_dest[g])
             p0 += int(plan.pairs_per_dest[g])
+
+
+@pytest.mark.parametrize("world,placement", [(2, "contiguous"), (4, "strided"), (8, "contiguous")])
+def test_peer_routes_land_where_the_origin_looks(world, placement):
+    """The peer exchange: rank r stores the y row of each pair it received at
+    an address from peer_routes; decoded, that must be the origin rank and
+    the place its y_pos gives the pair (its send order)."""
+    ops = FakeOps()
+    T = (23, 0, 9, 31, 4, 17, 2, 11)[:world]
+    plans = [plan_dispatch(ops.route(tokens(r, T[r]))[0], E // world, world, placement)
+             for r in range(world)]
+    counts = torch.stack([p.counts for p in plans])            # [src, dst, (rows, pairs)]
+    BIG = 1 << 20                                              # rank s's rows at s * BIG
+    for me in range(world):
+        src_end, dst = peer_routes(counts, me, [s * BIG for s in range(world)], 1)
+        start = 0
+        for s in range(world):
+            assert src_end[s] - start == int(counts[s, me, 1])
+            order = torch.argsort(plans[s].y_pos.long())           # s's pairs in send order
+            first = int(counts[s, :me, 1].sum())                   # s's pairs to lower ranks
+            for i in range(src_end[s] - start):
+                addr = dst[s] + i
+                assert addr // BIG == s                            # stored at the origin
+                pair = int(order[first + i])                       # the i-th pair s sent to me
+                assert int(plans[s].y_pos[pair]) == addr % BIG     # where s's combine reads it
+            start = src_end[s]
+
+
+def test_peer_exchange_is_checked_at_construction():
+    with pytest.raises(ValueError, match="exchange"):
+        ExpertParallelMoE(FakeOps(), exchange="nvshmem")
 
 
 def _free_port():
