@@ -377,3 +377,23 @@ def test_wait_timeout_is_reported_and_context_survives(torch_cuda):
         after = eng.moe(x.copy())
         assert np.array_equal(before.view(np.uint32), after.view(np.uint32))
         eng.sync()  # the error word was cleared when it was reported
+
+
+def test_peer_wait_timeout_is_reported_and_context_survives(torch_cuda):
+    """Failure detection for the expert-parallel exchange, on one GPU and
+    without a fault: the wait for the ranks' flags (miag_ep_wait_async) on a
+    flag that no rank will raise gives up after its limit (two seconds), the
+    next miag_sync reports it, and the context then runs the block as
+    before."""
+    build.build()
+    with MoEEngine(TINY, n_layers=1) as eng:
+        eng.load_layer(0, get_layer(TINY, False))
+        x = synth.tokens(TINY, 5, 9)
+        before = eng.moe(x.copy())
+        _, flags, _ = eng.ep_buffer(4)  # this rank's flags, zero: nothing has stored here
+        eng.ep_wait_device(flags, 1, 1)
+        with pytest.raises(MiagError, match="another rank"):
+            eng.sync()
+        after = eng.moe(x.copy())
+        assert np.array_equal(before.view(np.uint32), after.view(np.uint32))
+        eng.sync()  # the error word was cleared when it was reported
