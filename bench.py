@@ -326,6 +326,7 @@ def run_ours(args, T_desc, T, rms, zipf):
     eng.sync(sp)
     prof = eng.profile_read()
     eng.profile(False)
+    prof = {k: v for k, v in prof.items() if v[1] > 0}  # stages that launched something
     launches_per_step = sum(v[1] for v in prof.values()) // args.steps
     t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
     if dist:
@@ -373,7 +374,7 @@ def run_ours(args, T_desc, T, rms, zipf):
 
     hbm_gbs, tflops, peak_kind = load_peaks()
     stage_ms = {k: v[0] / args.steps for k, v in prof.items()}  # mean ms per step
-    top = max(stage_ms, key=stage_ms.get)
+    top = max((k for k in stage_ms if k in per_stage_bytes), key=stage_ms.get)
     achieved = per_stage_bytes[top] / (stage_ms[top] / 1e3) / 1e9
     block_bytes = sum(per_stage_bytes.values())
 
