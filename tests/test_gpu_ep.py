@@ -8,9 +8,9 @@ miag_moe on the same tokens: sharding must not change a single bit.
   torch statement (ep.plan_dispatch, ep.pack_records), at ragged sizes;
 * G = 2, 4, 8 ranks played by one process on one GPU (ep.simulate), with the
   Zipf-biased router of config 3 so the ranks see skewed loads;
-* with two or more GPUs visible, two NCCL ranks under torchrun, each engine
-  holding only its own 64 experts (tests/ep_worker.py), with the y rows
-  returned by peer stores and by all-to-all, two calls each.
+* with two (four) or more GPUs visible, two (four) NCCL ranks under
+  torchrun, each engine holding only its own experts (tests/ep_worker.py),
+  with the y rows returned by peer stores and by all-to-all, two calls each.
 """
 
 from __future__ import annotations
@@ -129,15 +129,17 @@ def test_simulated_ranks_equal_the_block(torch_cuda, G, placement):
         assert np.array_equal(_bits(x.cpu().numpy()), _bits(want))
 
 
-@pytest.mark.parametrize("exchange,tokens,port", [("peer", 300, 29517), ("peer", 40, 29518),
-                                                  ("collective", 300, 29519)])
-def test_nccl_ranks_equal_the_block(torch_cuda, exchange, tokens, port):
+@pytest.mark.parametrize("world,exchange,tokens,port", [(2, "peer", 300, 29517),
+                                                        (2, "peer", 40, 29518),
+                                                        (2, "collective", 300, 29519),
+                                                        (4, "peer", 300, 29520)])
+def test_nccl_ranks_equal_the_block(torch_cuda, world, exchange, tokens, port):
     torch = torch_cuda
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     here = os.path.dirname(os.path.abspath(__file__))
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run",
-           "--nnodes=1", "--nproc-per-node=2", "--master-addr", "127.0.0.1",
+           "--nnodes=1", f"--nproc-per-node={world}", "--master-addr", "127.0.0.1",
            "--master-port", str(port), os.path.join(here, "ep_worker.py")]
     env = dict(os.environ, NCCL_NVLS_ENABLE="0", EP_EXCHANGE=exchange, EP_TOKENS=str(tokens))
     r = subprocess.run(cmd, capture_output=True, text=True, env=env, timeout=360)
