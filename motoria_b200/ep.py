@@ -271,6 +271,7 @@ class ExpertParallelMoE:
         """Exchange buffers of at least `rows` y rows on every rank, mapped
         by every peer.  Every rank calls this with the same `rows` (derived
         from the all-gathered counts), so all grow together."""
+        rows = max(rows, 1)  # buffers exist even when no rank has tokens yet
         if rows <= self._cap:
             return
         dist, eng, G, me = self.dist, self.ops.eng, self.world, self.rank
