@@ -1,38 +1,49 @@
 #!/usr/bin/env python
 """MoE-block tokens/s of the B200 (sm_100a) Qwen3-30B-A3B MoE FFN block.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload config2]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload config5]
                     [--impl ours|reference]
 
 A step is one MoE block call (router, top-8, dispatch, Q8_0 SwiGLU experts,
 weighted combine) over one batch of synthetic tokens with seeded
-random-init Q8_0 weights (motoria_b200.synth).  Default workload: config2,
-batched decode of 64 tokens per GPU.  Prints ONE JSON line on rank 0.
+random-init Q8_0 weights (motoria_b200.synth).  Prints ONE JSON line on
+rank 0.
+
+Default workload: config5, 4096 tokens per GPU with the Zipf-biased router
+(the largest single-GPU configuration, and the expert-parallel one):
+  N = 1   one GPU holds all 128 experts;
+  N > 1   expert parallelism (motoria_b200.ep): rank g holds experts
+          [g*128/N, (g+1)*128/N) (contiguous, as specified); each rank routes
+          its own tokens, (row, expert) pairs go to the experts' ranks over
+          NCCL, and the down launch stores each result straight into the
+          origin rank's memory over NVLink.  Outputs equal the one-GPU block
+          bit for bit.  The strided placement (expert e on rank e mod N) is
+          reported beside it under "ep_strided".
+Scaling is weak: tokens per GPU are fixed as N grows.
 
   value      tokens/s of the whole job, inputs resident in HBM, device-timed
              (CUDA events around each step on the launching stream, L2
              flushed between steps outside the events -- a 256 MiB buffer
              written, then read back -- max over ranks)
-  e2e        the same metric through the public host API (miag_moe with
-             pinned host buffers: H2D of x and D2H of the result every step)
-  roofline   the dominant kernel's algorithmic bytes / its mean duration,
-             from CUDA events around each kernel on its stream in a second
-             pass of the same steps (the timed pass carries no such events)
+  e2e        the same metric through the public host API with pinned host
+             buffers, H2D of x and D2H of the result every step (N = 1:
+             miag_moe; N > 1: H2D, the sharded block, D2H on each rank);
+             "e2e_pageable" repeats it from ordinary (malloc'd) host memory,
+             as the reference engine's own buffers are
+  roofline   the dominant kernel, from CUDA events around each kernel on its
+             stream in a second pass of the same steps (the timed pass has
+             none).  Prefill-size batches (config3, config5): tensor FLOP/s of
+             the expert products against the measured bf16 peak, and the
+             FP32 operations of the reference's exact Q8_0 steps against the
+             chip's FP32 lane rate ("epilogue"); decode: HBM bytes/s against
+             the measured copy bandwidth
+  decode     (N = 1) config2 (64 tokens) and config1 (1 token) measured the
+             same way: value, e2e and the HBM roofline
   cpu_baseline  the reference engine built from its sources (oracle/_ref)
-             or the oracle port, on this host's cores, rank 0 at N=1
+             or the oracle port, on this host's cores, rank 0 at N = 1, on a
+             bounded sample of the workload's tokens
   --impl reference  times the reference CPU implementation (all host threads)
-             on the same workload and prints its own line.
-
-Multi-GPU (torchrun, N>1), scaling weak (tokens per GPU fixed):
-  config5, the expert-parallel configuration: motoria_b200.ep.  Each rank
-    holds E/N experts (--ep-placement contiguous, as specified, or strided)
-    and routes its own tokens; (row, expert) pairs go to the experts' ranks
-    and the results come back stored by the down launch straight into the
-    origin rank's memory over NVLink (--ep-exchange peer, the default) or by
-    NCCL all-to-all (collective); outputs equal the one-GPU block bit for bit.
-  config1-3: replicas.  Every rank holds all experts and serves its own
-    batch; the block is independent per token, so there is no data-path
-    collective.
+             on a bounded sample of the same workload and prints its own line.
 """
 
 from __future__ import annotations
@@ -58,21 +69,30 @@ METRIC = "MoE-block tokens/s"
 UNIT = "tokens/s"
 DTYPE = "int8 dot / f32 accumulate (Q8_0)"
 
+# name: (description, tokens per GPU, RMS-normalised inputs, Zipf-biased router)
 WORKLOADS = {
     "config1": ("MoE block, decode of 1 token (Qwen3-30B-A3B shapes)", 1, True, False),
     "config2": ("MoE block, batched decode of 64 tokens (Qwen3-30B-A3B shapes)", 64, True, False),
     "config3": ("MoE block, prefill of 2048 tokens, Zipf-biased router", 2048, False, True),
-    "config5": ("MoE block, 4096 tokens per GPU, Zipf-biased router", 4096, False, True),
+    "config5": ("MoE block, 4096 tokens per GPU, Zipf-biased router; expert-parallel over "
+                "the GPUs when N > 1", 4096, False, True),
 }
-EP_WORKLOADS = ("config5",)  # the expert-parallel configuration; the others run replicas
+DEFAULT_WORKLOAD = "config5"
+EP_WORKLOADS = ("config5",)       # expert-parallel at N > 1; the others run replicas
+PREFILL_WORKLOADS = ("config3", "config5")
+DECODE_EXTRAS = ("config2", "config1")
+CPU_SAMPLE_TOKENS = 512           # reference-arm tokens per step for the big batches
 
 
 def load_peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
-    return 6650.0, 1590.0, "fallback"
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16": float(d["bf16_tflops"]),
+                "bf16_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
+                "sm_max_mhz": float(d.get("sm_max_mhz", 1965.0)), "kind": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16": 1590.0, "bf16_sustained": 1400.0, "sm_max_mhz": 1965.0,
+            "kind": "fallback"}
 
 
 def host_cores() -> int:
@@ -80,6 +100,10 @@ def host_cores() -> int:
         return len(os.sched_getaffinity(0))
     except AttributeError:
         return os.cpu_count() or 1
+
+
+def cpu_sample(T: int) -> int:
+    return min(T, CPU_SAMPLE_TOKENS)
 
 
 # ---------------------------------------------------------------------------
@@ -109,7 +133,8 @@ def run_reference(args, T_desc, T, rms, zipf):
         return
     shape = synth.QWEN3_30B_A3B
     lay = synth.layer(shape, SEED, zipf=zipf)
-    x = synth.tokens(shape, XSEED, T, rms_normalise=rms)
+    Ts = cpu_sample(T)
+    x = synth.tokens(shape, XSEED, T, rms_normalise=rms)[:Ts]
     from oracle import oracle as O
 
     O.build()
@@ -121,9 +146,11 @@ def run_reference(args, T_desc, T, rms, zipf):
     for _ in range(args.steps):
         impl.moe(shape, lay.ffn_norm, lay.router, lay.bias, lay.blobs, x, threads=cores)
     el = time.perf_counter() - t0
-    value = args.steps * T / el
+    value = args.steps * Ts / el
     arch = os.uname().machine
-    sample = (f"{args.steps} steps x {T} tokens of {args.workload}; "
+    sample = (f"{args.steps} steps x {Ts} tokens"
+              f"{f' (the first {Ts} of the {T} tokens a GPU holds)' if Ts < T else ''}"
+              f" of {args.workload} on {cores} threads; "
               f"{'reference built from source' if impl.kind == 'reference' else 'oracle port'}"
               f"{' (x86 scalar path: the NEON path needs an aarch64 host)' if arch == 'x86_64' else ''}")
     line = {
@@ -131,8 +158,8 @@ def run_reference(args, T_desc, T, rms, zipf):
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": el / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": DTYPE, "data": "synthetic",
-        "config": {"workload": f"{args.workload}: {T_desc}", "tokens_per_step": T,
-                   "threads": cores},
+        "config": {"workload": f"{args.workload}: {T_desc}", "tokens_per_step": Ts,
+                   "tokens_per_gpu": T, "threads": cores},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": impl.kind,
                          "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -153,6 +180,7 @@ class ClockSampler:
     def __init__(self, device: int):
         self.device = device
         self.proc = None
+        self.out = ""
 
     def __enter__(self):
         try:
@@ -175,8 +203,6 @@ class ClockSampler:
                 self.proc.kill()
                 out, _ = self.proc.communicate()
             self.out = out
-        else:
-            self.out = ""
 
     def summary(self):
         rows = [r.split(", ") for r in self.out.strip().splitlines() if r.count(",") >= 8]
@@ -191,25 +217,30 @@ class ClockSampler:
                 "samples": len(rows)}
 
 
-def stage_bytes(shape, T, counts, rows=None, pairs=None):
-    """Algorithmic HBM bytes per launch of each stage (weights streamed once
-    per active expert; activations read/written once).  T tokens are routed
-    and combined here; the expert kernels see `pairs` pairs over `rows`
-    activation rows (T*K and T on one GPU; what arrived, under expert
-    parallelism)."""
+def stage_work(shape, T, counts, rows=None, pairs=None):
+    """Algorithmic work per launch of each stage: HBM bytes (weights streamed
+    once per active expert; activations read/written once), tensor FLOPs of
+    the expert products, and the FP32 operations of the reference's exact
+    Q8_0 steps (four per row, pair and 32-block: the exact int-to-float, two
+    rounded products, a rounded add).  T tokens are routed and combined
+    here; the expert kernels see `pairs` pairs over `rows` activation rows
+    (T*K and T on one GPU; what arrived, under expert parallelism)."""
     d, eh, E, K = shape.dim, shape.expert_hidden, shape.n_experts, shape.n_active
     P = T * K if pairs is None else pairs
     R = T if rows is None else rows
     n_act = int((counts > 0).sum())
     gu_w = 2 * eh * (d + d // 32 * 4)    # gate + up: int8 rows + f32 block scales
     dn_w = d * (eh + eh // 32 * 4)
-    return {
+    nbytes = {
         "route": E * d * 4 + T * d * 4 + T * (d + d // 8) + T * K * 8,
         "permute": P * 4 * 6 + E * 16,
-        "gateup": n_act * gu_w + R * (d + d // 8) + P * eh * 4,
-        "down": n_act * dn_w + P * eh * 4 + P * d * 4,
+        "gateup": n_act * gu_w + R * (d + d // 8) + P * 2 * eh * 4,
+        "down": n_act * dn_w + P * 2 * eh * 4 + P * d * 4,
         "combine": T * K * d * 4 + 2 * T * d * 4 + T * K * 8,
-    }, n_act
+    }
+    flops = {"gateup": 2.0 * P * 2 * eh * d, "down": 2.0 * P * d * eh}
+    fp32_ops = {"gateup": 4.0 * P * 2 * eh * (d // 32), "down": 4.0 * P * d * (eh // 32)}
+    return nbytes, flops, fp32_ops, n_act
 
 
 def ncu_traffic(workload: str, kernel: str):
@@ -225,222 +256,375 @@ def ncu_traffic(workload: str, kernel: str):
     return None
 
 
+class Ctx:
+    """Process-wide GPU plumbing of one bench run (torch as plumbing only)."""
+
+    def __init__(self):
+        import torch
+
+        self.torch = torch
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(self.local)
+        self.dist = None
+        if self.world > 1:
+            import datetime
+
+            import torch.distributed as dist
+
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                    device_id=torch.device("cuda", self.local))
+            self.dist = dist
+        self.dev = torch.device("cuda", self.local)
+        self.flush = torch.empty(256 << 20, dtype=torch.uint8, device=self.dev)  # > 126 MB L2
+        self.flush_sink = torch.zeros((), dtype=torch.int64, device=self.dev)
+        # A dedicated stream: the kernels, the restore/flush copies and the
+        # timing events all go to it (a NULL handle would mean the library's
+        # own stream).
+        self.stream = torch.cuda.Stream(self.dev)
+        torch.cuda.set_stream(self.stream)
+        self.num_sms = torch.cuda.get_device_properties(self.dev).multi_processor_count
+
+    def barrier(self):
+        self.torch.cuda.synchronize(self.dev)
+        if self.dist:
+            self.dist.barrier()
+            self.torch.cuda.synchronize(self.dev)
+
+    def max_over_ranks(self, v: float) -> float:
+        t = self.torch.tensor([v], dtype=self.torch.float64, device=self.dev)
+        if self.dist:
+            self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def flush_l2(self):
+        # write a buffer larger than L2, then read it: the L2 holds none of
+        # the step's data and no dirty lines whose write-back the step would pay
+        self.flush.zero_()
+        self.flush_sink.add_(self.flush.sum())
+
+
+class SingleRunner:
+    """One GPU holding every expert (or a replica): miag_moe_async on the
+    device, miag_moe through host buffers."""
+
+    def __init__(self, eng, layer: int):
+        self.eng, self.layer = eng, layer
+
+    def device(self, x, sp):
+        self.eng.moe_device(x.data_ptr(), x.shape[0], layer=self.layer, stream=sp)
+
+    def host(self, xp_np, x, stream):
+        self.eng.moe_inplace(xp_np, layer=self.layer)
+
+    def received(self):
+        return None
+
+
+class EPRunner:
+    """Expert parallelism over the process group (motoria_b200.ep)."""
+
+    def __init__(self, ep, eng):
+        self.ep, self.eng = ep, eng
+
+    def device(self, x, sp):
+        self.ep.forward(x)
+
+    def host(self, xp_np, x, stream):
+        xp = self._pinned.get(id(xp_np))
+        x.copy_(xp, non_blocking=True)
+        self.ep.forward(x)
+        xp.copy_(x, non_blocking=True)
+        stream.synchronize()
+
+    def received(self):
+        return self.ep.last_received
+
+
+def measure(ctx: Ctx, runner, x_host, steps: int, warmup: int, e2e: bool = True,
+            pageable: bool = False, clocks: bool = False):
+    """Times `steps` block steps after `warmup` untimed ones.  Returns a dict:
+    total_ms (max over ranks), per-stage mean ms and launches of this rank,
+    e2e seconds (max over ranks) and the clock summary."""
+    torch, dev, stream = ctx.torch, ctx.dev, ctx.stream
+    sp = stream.cuda_stream
+    T = x_host.shape[0]
+    x0 = torch.from_numpy(x_host).to(dev)
+    x = x0.clone()
+
+    def one_step(ev=None):
+        x.copy_(x0)
+        ctx.flush_l2()
+        if ev:
+            ev[0].record(stream)
+        runner.device(x, sp)
+        if ev:
+            ev[1].record(stream)
+
+    for _ in range(warmup):
+        one_step()
+    runner.eng.sync(sp)
+    events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(steps)]
+    ctx.barrier()
+    clk = ClockSampler(ctx.local) if clocks else None
+    if clk:
+        clk.__enter__()
+    for i in range(steps):
+        one_step(events[i])
+    ctx.barrier()
+    if clk:
+        clk.__exit__(None, None, None)
+    runner.eng.sync(sp)
+    total_ms = sum(a.elapsed_time(b) for a, b in events)
+    # Per-kernel durations: the same steps again, each kernel bracketed by
+    # CUDA events on the stream it is launched on.
+    runner.eng.profile(True)
+    runner.eng.profile_read()
+    for _ in range(steps):
+        one_step()
+    runner.eng.sync(sp)
+    prof = runner.eng.profile_read()
+    runner.eng.profile(False)
+    prof = {k: v for k, v in prof.items() if v[1] > 0}
+    out = {"total_ms": ctx.max_over_ranks(total_ms),
+           "stage_ms": {k: v[0] / steps for k, v in prof.items()},
+           "launches_per_step": sum(v[1] for v in prof.values()) // steps,
+           "received": runner.received(),
+           "clocks": clk.summary() if clk else None}
+    if not e2e:
+        return out
+
+    # e2e: the public host API, pinned host buffers, H2D + D2H every step.
+    # Each step's input sits in its own host buffer, written before the timed
+    # region (the block updates its input in place); up to 1 GiB of them,
+    # past which a buffer is rewritten inside the step.
+    def e2e_pass(pinned: bool):
+        n_e2e = warmup + steps
+        nbuf = max(1, min(n_e2e, (1 << 30) // max(1, x_host.nbytes)))
+        if pinned:
+            bufs = [torch.empty(x_host.shape, dtype=torch.float32, pin_memory=True)
+                    for _ in range(nbuf)]
+            arrs = [b.numpy() for b in bufs]
+            runner._pinned = {id(a): b for a, b in zip(arrs, bufs)}
+        else:
+            arrs = [np.empty(x_host.shape, np.float32) for _ in range(nbuf)]
+            runner._pinned = {id(a): torch.from_numpy(a) for a in arrs}
+        for a in arrs:
+            a[:] = x_host
+        i = [0]
+
+        def step():
+            a = arrs[i[0] % nbuf]
+            if i[0] >= nbuf:
+                a[:] = x_host
+            i[0] += 1
+            runner.host(a, x, stream)
+
+        for _ in range(warmup):
+            step()
+        ctx.barrier()
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            step()
+        el = time.perf_counter() - t0
+        return ctx.max_over_ranks(el), nbuf >= n_e2e
+
+    out["e2e_s"], out["e2e_own_buffers"] = e2e_pass(True)
+    if pageable:
+        out["e2e_pageable_s"], _ = e2e_pass(False)
+    return out
+
+
+def roofline(kind, m, work, peaks, num_sms, workload):
+    """The dominant kernel's roofline.  kind "tensor" (prefill-size batches)
+    or "hbm" (decode)."""
+    nbytes, flops, fp32_ops, _ = work
+    st = m["stage_ms"]
+    top = max((k for k in st if k in nbytes), key=st.get)
+    t = st[top] / 1e3
+    hbm = nbytes[top] / t / 1e9
+    if kind == "hbm" or top not in flops:
+        return {"bound": "hbm", "kernel": top, "achieved": hbm, "peak": peaks["hbm_gbs"],
+                "unit": "GB/s", "frac": hbm / peaks["hbm_gbs"],
+                "traffic": ncu_traffic(workload, top),
+                "peak_source": f"{peaks['kind']} hbm_gbs"}
+    tf = flops[top] / t / 1e12
+    lane_rate = num_sms * 128 * peaks["sm_max_mhz"] * 1e6 / 1e12  # FP32 lanes x clock, T op/s
+    ep = fp32_ops[top] / t / 1e12
+    return {"bound": "tensor", "kernel": top, "achieved": tf, "peak": peaks["bf16_sustained"],
+            "unit": "TFLOP/s", "frac": tf / peaks["bf16_sustained"],
+            "traffic": ncu_traffic(workload, top),
+            "peak_source": f"{peaks['kind']} bf16_tflops_sustained (int8 MMA FLOPs of the "
+                           "expert products)",
+            "epilogue": {"achieved": ep, "peak": lane_rate, "unit": "T FP32 op/s",
+                         "frac": ep / lane_rate,
+                         "what": "4 rounded FP32 operations per (row, pair, 32-block): the "
+                                 "reference's exact Q8_0 step; peak = SMs x 128 FP32 lanes x "
+                                 "max SM clock"},
+            "hbm": {"achieved": hbm, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                    "frac": hbm / peaks["hbm_gbs"]}}
+
+
+def summarise(ctx, args, name, T, m, work, peaks, n_act, dim=2048):
+    steps = args.steps
+    kind = "tensor" if name in PREFILL_WORKLOADS else "hbm"
+    block_bytes = sum(work[0].values())
+    r = {"value": ctx.world * T * steps / (m["total_ms"] / 1e3),
+         "ms_per_step": m["total_ms"] / steps,
+         "roofline": roofline(kind, m, work, peaks, ctx.num_sms, name),
+         "block_achieved_gbs": block_bytes / (m["total_ms"] / steps / 1e3) / 1e9,
+         "active_experts": n_act,
+         "stages_ms": {k: round(v, 5) for k, v in m["stage_ms"].items()},
+         "gpu_launches": m["launches_per_step"] * steps}
+    if "e2e_s" in m:
+        r["e2e"] = {"value": ctx.world * T * steps / m["e2e_s"], "unit": UNIT,
+                    "h2d_bytes_per_step": T * dim * 4, "d2h_bytes_per_step": T * dim * 4,
+                    "inputs": ("each step's own pinned buffer, written before the timed region"
+                               if m["e2e_own_buffers"] else
+                               "pinned buffers written before the timed region, rewritten in "
+                               "the step past 1 GiB of them")}
+    if "e2e_pageable_s" in m:
+        r["e2e_pageable"] = {"value": ctx.world * T * steps / m["e2e_pageable_s"], "unit": UNIT,
+                             "inputs": "ordinary (pageable) host memory, like the reference "
+                                       "engine's malloc'd buffers"}
+    return r
+
+
+def work_of(shape, T, m, eng, layer):
+    rec = m["received"]
+    if rec is not None:
+        import torch
+
+        R_in, P_in, pe = rec
+        counts = torch.bincount(pe.long(), minlength=shape.n_experts).cpu().numpy()
+        return stage_work(shape, T, counts, rows=R_in, pairs=P_in)
+    routing = eng.routing(T)
+    return stage_work(shape, T, routing["counts"])
+
+
+def make_ep(ctx, shape, lay, placement):
+    from motoria_b200 import MoEEngine
+    from motoria_b200.ep import EngineOps, ExpertParallelMoE
+
+    eng = MoEEngine(shape, n_layers=1, device=ctx.local)
+    ep = ExpertParallelMoE(EngineOps(eng), placement=placement, exchange="peer")
+    eng.set_layer(0, lay.ffn_norm, lay.router, lay.bias)
+    for e in ep.experts_of(ctx.rank):
+        eng.upload_experts(0, lay.blobs[e:e + 1], first=e)
+    return EPRunner(ep, eng), eng
+
+
 def run_ours(args, T_desc, T, rms, zipf):
-    import torch
-
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    dist = None
-    if world > 1:
-        import datetime
-
-        import torch.distributed as dist
-
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=torch.device("cuda", local))
-    else:
-        torch.cuda.set_device(local)
-
+    ctx = Ctx()
     from motoria_b200 import MoEEngine, build
 
     build.build()
     shape = synth.QWEN3_30B_A3B
+    peaks = load_peaks()
+    name = args.workload
     lay = synth.layer(shape, SEED, zipf=zipf)
-    x_host = synth.tokens(shape, XSEED + 1000 * rank, T, rms_normalise=rms)
-    eng = MoEEngine(shape, n_layers=1, device=local)
-    ep = None
-    if world > 1 and args.workload in EP_WORKLOADS:
-        # expert parallelism: this rank holds E/N experts (placement below)
-        from motoria_b200.ep import EngineOps, ExpertParallelMoE
-
-        ep = ExpertParallelMoE(EngineOps(eng), placement=args.ep_placement,
-                               exchange=args.ep_exchange)
-        eng.set_layer(0, lay.ffn_norm, lay.router, lay.bias)
-        for e in ep.experts_of(rank):
-            eng.upload_experts(0, lay.blobs[e:e + 1], first=e)
+    x_host = synth.tokens(shape, XSEED + 1000 * ctx.rank, T, rms_normalise=rms)
+    use_ep = ctx.world > 1 and name in EP_WORKLOADS
+    engines = []
+    if use_ep:
+        runner, eng = make_ep(ctx, shape, lay, args.ep_placement)
     else:  # one GPU, or replicas: every rank holds all experts and serves its own batch
+        eng = MoEEngine(shape, n_layers=1, device=ctx.local)
         eng.load_layer(0, lay)
+        runner = SingleRunner(eng, 0)
+    engines.append(eng)
+    m = measure(ctx, runner, x_host, args.steps, args.warmup, pageable=ctx.world == 1,
+                clocks=True)
+    work = work_of(shape, T, m, eng, 0)
+    main = summarise(ctx, args, name, T, m, work, peaks, work[3], shape.dim)
 
-    dev = torch.device("cuda", local)
-    x0 = torch.from_numpy(x_host).to(dev)
-    x = x0.clone()
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # > 126 MB L2
-    # A dedicated stream: the kernels, the restore/flush copies and the timing
-    # events all go to it (a NULL handle would mean the library's own stream).
-    stream = torch.cuda.Stream(dev)
-    torch.cuda.set_stream(stream)
-    sp = stream.cuda_stream
+    extras = {}
+    if use_ep:  # the other placement, device-timed
+        other = "strided" if args.ep_placement == "contiguous" else "contiguous"
+        r2, e2 = make_ep(ctx, shape, lay, other)
+        engines.append(e2)
+        m2 = measure(ctx, r2, x_host, args.steps, args.warmup, e2e=False)
+        extras[f"ep_{other}"] = {"value": ctx.world * T * args.steps / (m2["total_ms"] / 1e3),
+                                 "ms_per_step": m2["total_ms"] / args.steps,
+                                 "stages_ms_rank0": {k: round(v, 5) for k, v in
+                                                     m2["stage_ms"].items()}}
+    if ctx.world == 1 and name == DEFAULT_WORKLOAD and not args.no_extras:
+        decode = {}
+        for dn in DECODE_EXTRAS:
+            ddesc, dT, drms, dzipf = WORKLOADS[dn]
+            dlay = synth.layer(shape, SEED, zipf=dzipf)
+            deng = MoEEngine(shape, n_layers=1, device=ctx.local)
+            deng.load_layer(0, dlay)
+            engines.append(deng)
+            dx = synth.tokens(shape, XSEED, dT, rms_normalise=drms)
+            dm = measure(ctx, SingleRunner(deng, 0), dx, max(args.steps, 50), args.warmup)
+            dwork = work_of(shape, dT, dm, deng, 0)
+            s = summarise(ctx, args, dn, dT, dm, dwork, peaks, dwork[3], shape.dim)
+            s["steps"] = max(args.steps, 50)
+            s["workload"] = f"{dn}: {ddesc}"
+            decode[dn] = s
+        extras["decode"] = decode
 
-    def barrier():
-        torch.cuda.synchronize(dev)
-        if dist:
-            dist.barrier()
-            torch.cuda.synchronize(dev)
-
-    flush_sink = torch.zeros((), dtype=torch.int64, device=dev)
-
-    def one_step(ev=None):
-        x.copy_(x0)
-        # write a buffer larger than L2, then read it: the L2 holds none of the
-        # step's data and no dirty lines whose write-back the step would pay
-        flush.zero_()
-        flush_sink.add_(flush.sum())
-        if ev:
-            ev[0].record(stream)
-        if ep:
-            ep.forward(x)
-        else:
-            eng.moe_device(x.data_ptr(), T, stream=sp)
-        if ev:
-            ev[1].record(stream)
-
-    for _ in range(args.warmup):
-        one_step()
-    eng.sync(sp)
-    if ep:
-        R_in, P_in, pe = ep.last_received
-        counts = torch.bincount(pe.long(), minlength=shape.n_experts).cpu().numpy()
-        per_stage_bytes, n_act = stage_bytes(shape, T, counts, rows=R_in, pairs=P_in)
-    else:
-        routing = eng.routing(T)
-        per_stage_bytes, n_act = stage_bytes(shape, T, routing["counts"])
-
-    events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-              for _ in range(args.steps)]
-    barrier()
-    with ClockSampler(local) as clk:
-        for i in range(args.steps):
-            one_step(events[i])
-        barrier()
-    eng.sync(sp)
-    total_ms = sum(a.elapsed_time(b) for a, b in events)
-    # Per-kernel durations: the same steps again, each kernel bracketed by
-    # CUDA events on the stream it is launched on (kept out of the timed pass
-    # above so the brackets do not stretch the step).
-    eng.profile(True)
-    eng.profile_read()
-    for i in range(args.steps):
-        one_step()
-    eng.sync(sp)
-    prof = eng.profile_read()
-    eng.profile(False)
-    prof = {k: v for k, v in prof.items() if v[1] > 0}  # stages that launched something
-    launches_per_step = sum(v[1] for v in prof.values()) // args.steps
-    t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
-    if dist:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    total_ms = float(t.item())
-    value = world * T * args.steps / (total_ms / 1e3)
-
-    # e2e: the public host API, pinned host buffers, H2D + D2H every step.
-    # Each step's input sits in its own pinned buffer, written before the
-    # timed region (the block updates its input in place); up to 1 GiB of
-    # them, past which a buffer is rewritten inside the step.
-    n_e2e = args.warmup + args.steps
-    nbuf = max(1, min(n_e2e, (1 << 30) // max(1, x_host.nbytes)))
-    bufs = [torch.empty((T, shape.dim), dtype=torch.float32, pin_memory=True) for _ in range(nbuf)]
-    for b in bufs:
-        b.numpy()[:] = x_host
-    e2e_i = [0]
-
-    def e2e_step():
-        xp = bufs[e2e_i[0] % nbuf]
-        xp_np = xp.numpy()
-        if e2e_i[0] >= nbuf:
-            xp_np[:] = x_host
-        e2e_i[0] += 1
-        if ep:  # H2D, the sharded block, D2H, on this rank's stream
-            x.copy_(xp, non_blocking=True)
-            ep.forward(x)
-            xp.copy_(x, non_blocking=True)
-            stream.synchronize()
-        else:
-            eng.moe_inplace(xp_np)
-
-    for _ in range(args.warmup):
-        e2e_step()
-    barrier()
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        e2e_step()
-    e2e_s = time.perf_counter() - t0
-    te = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
-    if dist:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_s = float(te.item())
-    e2e_value = world * T * args.steps / e2e_s
-
-    hbm_gbs, tflops, peak_kind = load_peaks()
-    stage_ms = {k: v[0] / args.steps for k, v in prof.items()}  # mean ms per step
-    top = max((k for k in stage_ms if k in per_stage_bytes), key=stage_ms.get)
-    achieved = per_stage_bytes[top] / (stage_ms[top] / 1e3) / 1e9
-    block_bytes = sum(per_stage_bytes.values())
-
-    line = None
-    if rank == 0:
+    if ctx.rank == 0:
         cpu = None
-        if world == 1 and not args.no_cpu_baseline:
-            v, cores, kind, steps, el = cpu_arm(shape, lay, x_host, args.cpu_seconds)
+        if ctx.world == 1 and not args.no_cpu_baseline:
+            Ts = cpu_sample(T)
+            v, cores, kind, steps, el = cpu_arm(shape, lay, x_host[:Ts], args.cpu_seconds)
             cpu = {"value": v, "unit": UNIT, "cores": cores, "kind": kind,
-                   "sample": f"{steps} x {T} tokens of {args.workload} ({el:.1f} s on "
+                   "sample": f"{steps} x {Ts} tokens of {name}"
+                             f"{f' (the first {Ts} of {T})' if Ts < T else ''} ({el:.1f} s on "
                              f"{cores} threads, {os.uname().machine})"}
         line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": DTYPE,
+            "metric": METRIC, "value": main["value"], "unit": UNIT, "n_gpus": ctx.world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": main["ms_per_step"],
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": DTYPE,
             "data": "synthetic (seeded random-init Q8_0 weights and N(0,1) tokens)",
-            "config": {"workload": f"{args.workload}: {T_desc}", "tokens_per_gpu": T,
+            "config": {"workload": f"{name}: {T_desc}", "tokens_per_gpu": T,
                        "experts": shape.n_experts, "top_k": shape.n_active, "dim": shape.dim,
-                       "expert_hidden": shape.expert_hidden, "active_experts": n_act,
+                       "expert_hidden": shape.expert_hidden,
+                       "active_experts": main["active_experts"],
                        "weights": "Q8_0 HBM-resident",
-                       "l2": "flushed between steps outside the timed events (256 MiB written, then read back)",
-                       "parallelism": (f"ep{world} ({args.ep_placement}, y back by "
-                                       f"{'peer stores' if args.ep_exchange == 'peer' else 'all-to-all'})"
-                                       if ep else
-                                       "replicas" if world > 1 else "single"),
-                       "experts_per_gpu": shape.n_experts // world if ep else shape.n_experts},
-            "e2e": {"value": e2e_value, "unit": UNIT,
-                    "h2d_bytes_per_step": T * shape.dim * 4,
-                    "d2h_bytes_per_step": T * shape.dim * 4,
-                    "inputs": ("each step's own pinned buffer, written before the timed region"
-                               if nbuf >= n_e2e else
-                               f"{nbuf} pinned buffers written before the timed region, "
-                               "rewritten in the step past them")},
-            "roofline": {"bound": "hbm", "kernel": top, "achieved": achieved, "peak": hbm_gbs,
-                         "unit": "GB/s", "frac": achieved / hbm_gbs,
-                         "traffic": ncu_traffic(args.workload, top),
-                         "peak_source": f"{peak_kind} hbm_gbs",
-                         "block_achieved_gbs": block_bytes / (total_ms / args.steps / 1e3) / 1e9},
-            "stages_ms": {k: round(v, 5) for k, v in stage_ms.items()},
-            "gpu_launches": launches_per_step * args.steps,
+                       "l2": "flushed between steps outside the timed events (256 MiB "
+                             "written, then read back)",
+                       "parallelism": (f"ep{ctx.world} ({args.ep_placement}, y back by peer "
+                                       "stores over NVLink)" if use_ep else
+                                       "replicas" if ctx.world > 1 else "single"),
+                       "experts_per_gpu": shape.n_experts // ctx.world if use_ep
+                       else shape.n_experts},
+            "e2e": main.get("e2e"),
+            "roofline": main["roofline"],
+            "stages_ms": main["stages_ms"],
+            "gpu_launches": main["gpu_launches"],
             "cpu_baseline": cpu,
-            "clocks": clk.summary(),
+            "clocks": m["clocks"],
         }
+        if "e2e_pageable" in main:
+            line["e2e_pageable"] = main["e2e_pageable"]
+        line.update(extras)
         print(json.dumps(line), flush=True)
-    eng.close()
-    if dist:
-        dist.barrier()
-        dist.destroy_process_group()
-    return line
+    for e in engines:
+        e.close()
+    if ctx.dist:
+        ctx.dist.barrier()
+        ctx.dist.destroy_process_group()
 
 
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="config2")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default=DEFAULT_WORKLOAD)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ep-placement", choices=["contiguous", "strided"], default="contiguous",
-                    help="expert placement of the expert-parallel run (config5, N>1)")
-    ap.add_argument("--ep-exchange", choices=["peer", "collective"], default="peer",
-                    help="how the expert results return (config5, N>1): stored by the down "
-                         "launch into the origin rank's memory over NVLink, or NCCL all-to-all")
+                    help="expert placement of the expert-parallel run (config5, N>1); the "
+                         "other placement is reported beside it")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the decode figures (config2, config1) of the default run")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

@@ -99,8 +99,12 @@ int miag_moe_async(miag_ctx *c, int layer, float *x_dev, int n_tokens,
  * libmiag until the process exits, which bounds a batch to 92 tokens at
  * Qwen3-30B-A3B shapes; larger batches return -1 with a message.  The
  * first call on a device looks the array's address up (make it before any
- * stream capture).  All calls share the array, so calls whose work overlaps
- * on the GPU race on it and must be serialised by the caller. */
+ * stream capture) and keeps it for the life of the process, so a device
+ * reset while libmiag is loaded is not supported.  All calls share the
+ * array, so calls whose work overlaps on the GPU race on it and must be
+ * serialised by the caller.  When a call reports a device error
+ * (miag_sync), the counters at the head of the array, which every call
+ * expects at zero, are cleared again before miag_sync returns. */
 int miag_moe_noalloc(miag_ctx *c, int layer, float *x_dev, int n_tokens,
                      void *stream, char *err, size_t errlen);
 
@@ -121,7 +125,9 @@ int miag_moe_noalloc(miag_ctx *c, int layer, float *x_dev, int n_tokens,
  *   (forward.c:186-193, SwiGLU included): y [n_pairs][dim] f32, in pair order.
  * miag_combine_async: x[t] += sum_j w[t][j] * y[row(t*n_active + j)], j in
  *   order (forward.c:194), for t < n_tokens; row(p) = y_pos[p], or p when
- *   y_pos is NULL (y in pair order). */
+ *   y_pos is NULL (y in pair order).  While the context's device error word
+ *   is set (an earlier step failed and miag_sync has not reported it yet),
+ *   the combine leaves x unchanged. */
 int miag_route_async(miag_ctx *c, int layer, const float *x_dev, int n_tokens,
                      int32_t *idx, float *w, int8_t *xq, float *dx, void *stream,
                      char *err, size_t errlen);
@@ -185,7 +191,11 @@ int miag_ep_pack_async(miag_ctx *c, const int8_t *xq, const float *dx,
  * miag_ep_wait_async: enqueues a wait until flags[r] >= seq for every rank
  *   r < n_ranks (this rank's own flags); then every row stored for this rank
  *   has landed.  The wait gives up after two seconds and reports it as a
- *   device error at the next miag_sync. */
+ *   device error at the next miag_sync.  After such an error the combine
+ *   leaves x as it was (every combine skips while the error word is set),
+ *   and a late peer store may still land in the buffer: close the peers,
+ *   re-create the buffers (zeroed flags) and re-open them on every rank
+ *   before the exchange is used again. */
 int miag_ep_buffer(miag_ctx *c, size_t y_rows, void **y_dev, unsigned **flags_dev,
                    void *ipc_handle, char *err, size_t errlen);
 int miag_ep_open_peer(miag_ctx *c, const void *ipc_handle, void **y_dev,

@@ -457,7 +457,7 @@ static int enqueue_moe(miag_ctx *c, int layer, float *x_dev, int T, cudaStream_t
               [&] { launch_gateup(c->dims, c->lay, L, w, c->num_sms, c->d_err, s); });
     run_stage(c, kDown, down_launches(c->dims, w.P), s,
               [&] { launch_down(c->dims, c->lay, L, w, c->num_sms, c->d_err, s); });
-    run_stage(c, kCombine, 1, s, [&] { launch_combine(c->dims, w, x_dev, s); });
+    run_stage(c, kCombine, 1, s, [&] { launch_combine(c->dims, w, x_dev, c->d_err, s); });
     c->last_T = T;
     CU(cudaGetLastError());
     return 0;
@@ -487,6 +487,14 @@ static int read_device_error(miag_ctx *c, char *err, size_t errlen, int code = -
     if (code < 0) CU(cudaMemcpy(&code, c->d_err, sizeof(int), cudaMemcpyDeviceToHost));
     if (code == 0) return 0;
     CU(cudaMemsetAsync(c->d_err, 0, sizeof(int), c->stream));
+    // A call cut short may have left counters that every call expects at
+    // zero (the router's token-group counters, the SM-share claims): clear
+    // them, in the workspace and in the no-allocation array of this device.
+    if (c->ws_mem) {
+        CU(cudaMemsetAsync(c->ws.tg_count, 0, (size_t)c->ws_cap * sizeof(int32_t), c->stream));
+        CU(cudaMemsetAsync(c->ws.shares, 0, kShareKinds * sizeof(ShareState), c->stream));
+    }
+    noalloc_clear_counters(c->device, c->stream);
     CU(cudaStreamSynchronize(c->stream));
     const char *what = code == kErrWaitFull    ? "a consumer timed out waiting for a staged tile"
                        : code == kErrWaitEmpty ? "the producer timed out waiting for a free stage"
@@ -778,7 +786,7 @@ extern "C" int miag_combine_async(miag_ctx *c, float *x_dev, int n_tokens, const
     const cudaStream_t s = stream ? (cudaStream_t)stream : c->stream;
     Work w{};
     w.T = n_tokens, w.w = const_cast<float *>(wts), w.y = const_cast<float *>(y), w.y_pos = y_pos;
-    run_stage(c, kCombine, 1, s, [&] { launch_combine(c->dims, w, x_dev, s); });
+    run_stage(c, kCombine, 1, s, [&] { launch_combine(c->dims, w, x_dev, c->d_err, s); });
     CU(cudaGetLastError());
     return 0;
 }

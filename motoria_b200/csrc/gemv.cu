@@ -958,12 +958,16 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_expert_mma(GemvParams p) {
 // x[t] += w_j * y_j for j = 0..K-1 in order (forward.c:194).
 // Pair t*K + j is token t's j-th expert; its row of y is pos[t*K + j]
 // (pos null: y is in pair order).  A thread owns four columns (d % 4 == 0)
-// and loads all K of its y rows before the ordered adds.
+// and loads all K of its y rows before the ordered adds.  When an earlier
+// step of the call has set the error word (a wait that gave up, a bad index),
+// y may be partly written: x is then left as it was, and the caller learns of
+// the error at its next miag_sync.
 constexpr int kCombineMaxK = 16;
 __global__ void k_combine(float *x, int d, int K, const float *w, const float *y,
-                          const int32_t *pos) {
+                          const int32_t *pos, const int *err) {
     pdl_wait();
     pdl_launch_dependents();
+    if (err && __ldcg(err) != kErrNone) return;
     const int t = blockIdx.x;
     const int i = 4 * (blockIdx.y * blockDim.x + threadIdx.x);
     if (i >= d) return;
@@ -1084,9 +1088,10 @@ void launch_down(const Dims &m, const StoreLayout &lay, const LayerDev &L, const
                      grid, dim3(kGemvThreads), kSmemBudget, s, p);
 }
 
-void launch_combine(const Dims &m, const Work &w, float *x, cudaStream_t s) {
+void launch_combine(const Dims &m, const Work &w, float *x, int *err, cudaStream_t s) {
     dim3 grid(w.T, (m.d / 4 + 127) / 128);
-    launch_dependent(k_combine, grid, dim3(128), 0, s, x, m.d, m.K, w.w, w.y, w.y_pos);
+    launch_dependent(k_combine, grid, dim3(128), 0, s, x, m.d, m.K, w.w, w.y, w.y_pos,
+                     (const int *)err);
 }
 
 }  // namespace miag

@@ -116,7 +116,7 @@ void launch_gateup(const Dims &m, const StoreLayout &lay, const LayerDev &L, con
                    int num_sms, int *err, cudaStream_t s);
 void launch_down(const Dims &m, const StoreLayout &lay, const LayerDev &L, const Work &w,
                  int num_sms, int *err, cudaStream_t s);
-void launch_combine(const Dims &m, const Work &w, float *x, cudaStream_t s);
+void launch_combine(const Dims &m, const Work &w, float *x, int *err, cudaStream_t s);
 int down_launches(const Dims &m, int P);  // kernels launch_down issues
 int gemv_setup_attributes(const Dims &m, const StoreLayout &lay);
 
@@ -132,6 +132,9 @@ void launch_ep_wait(const unsigned *flags, int n_ranks, unsigned seq, long long 
 void launch_ep_pack(const int8_t *xq, const float *dx, int d, int xs, const int32_t *send_rows,
                     int n_rows, const int32_t *pair_meta, int n_pairs, const long long *all_counts,
                     int me, int G, uint8_t *rec, int32_t *meta_out, int num_sms, cudaStream_t s);
+// noalloc.cu: zeroes the counters at the head of the no-allocation array on
+// `device` (a no-op where it was never set up)
+void noalloc_clear_counters(int device, cudaStream_t s);
 // store.cu
 void launch_repack(const Dims &m, const StoreLayout &lay, const uint8_t *aos, size_t aos_stride,
                    int n, uint8_t *dst, cudaStream_t s);

@@ -16,12 +16,18 @@
 // before any stream capture that contains later calls.
 //
 // All calls share the one array and it keeps whatever the last call left
-// there.  One thing in it must start at zero: the router's per-token-group
-// counters, which sit first, at a fixed place for every batch size; the array
-// starts zeroed when the library loads and every call leaves them at zero
-// again.  Every other buffer of the block is written before it is read.  Two
-// calls whose work overlaps on the GPU (other streams, other contexts on the
-// same device) race on the array and must be serialised by the caller.
+// there.  Two things in it must start at zero: the router's per-token-group
+// counters and the expert launches' SM-share claims, which sit first, at a
+// fixed place for every batch size.  The array starts zeroed when the
+// library loads and every call that runs to its end leaves them at zero
+// again; when a call reports a device error (miag_sync, miag_moe), the
+// library clears them once more on that device, so a call cut short cannot
+// corrupt the next one.  Every other buffer of the block is written before it
+// is read.  Two calls whose work overlaps on the GPU (other streams, other
+// contexts on the same device) race on the array and must be serialised by
+// the caller.  The address looked up at set-up is kept for the life of the
+// process: a device reset (cudaDeviceReset) while libmiag is loaded is not
+// supported.
 #include <cstdio>
 #include <mutex>
 
@@ -116,6 +122,26 @@ size_t layout(const Dims &m, int T, uint8_t *base, Work *w) {
 
 }  // namespace
 
+namespace miag {
+// Zeroes the counters at the head of the array on `device` (after a call
+// reported a device error), if the array was ever set up there.  Enqueued on
+// `s`; allocates nothing.
+void noalloc_clear_counters(int device, cudaStream_t s) {
+    if (device < 0 || device >= kMaxDevices) return;
+    void *ptr;
+    {
+        std::lock_guard<std::mutex> lock(g_setup_mutex);
+        ptr = g_scratch_dev[device];
+    }
+    if (!ptr) return;
+    uint8_t *base = nullptr;
+    Work w;
+    layout(Dims{}, 0, base, &w);  // offsets of the counters from the array's start
+    const size_t head = reinterpret_cast<size_t>(w.shares) + kShareKinds * sizeof(ShareState);
+    cudaMemsetAsync(ptr, 0, head, s);
+}
+}  // namespace miag
+
 extern "C" int miag_moe_noalloc(miag_ctx *c, int layer, float *x_dev, int n_tokens, void *stream,
                                 char *err, size_t errlen) {
     CtxView v;
@@ -152,7 +178,7 @@ extern "C" int miag_moe_noalloc(miag_ctx *c, int layer, float *x_dev, int n_toke
     launch_permute(v.dims, w, v.d_err, s);
     launch_gateup(v.dims, v.lay, v.layer, w, v.num_sms, v.d_err, s);
     launch_down(v.dims, v.lay, v.layer, w, v.num_sms, v.d_err, s);
-    launch_combine(v.dims, w, x_dev, s);
+    launch_combine(v.dims, w, x_dev, v.d_err, s);
     e = cudaGetLastError();
     if (e != cudaSuccess) {
         if (err && errlen) snprintf(err, errlen, "miag_moe_noalloc: launch: %s",

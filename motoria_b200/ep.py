@@ -224,6 +224,66 @@ def _a2a(dist, out: torch.Tensor, inp: torch.Tensor, out_splits, in_splits, grou
     return out
 
 
+class _PeerExchange:
+    """The peer exchange of one engine: its buffer (y rows and one flag per
+    rank, owned by the library context), the peers' buffers mapped here, and
+    the step counter the flags are compared with.  All of it belongs to the
+    context, so every ExpertParallelMoE over the same engine (one per layer,
+    say) shares this one object: a second counter starting again at 1 would
+    find the flags already at the first one's count and pass its wait before
+    the rows land, and a second set of mappings would be freed under the
+    first."""
+
+    def __init__(self, eng, dist, group, world: int, rank: int):
+        self.eng, self.dist, self.group, self.world, self.rank = eng, dist, group, world, rank
+        self.cap, self.seq = 0, 0
+        # every rank on a GPU of its own: the flag waits of two ranks must
+        # never share one GPU
+        dev = torch.cuda.current_device()
+        uuid = str(torch.cuda.get_device_properties(dev).uuid)
+        ids = [None] * world
+        dist.all_gather_object(ids, uuid, group=group)
+        if len(set(ids)) != world:
+            raise ValueError("exchange='peer' needs one GPU per rank")
+
+    @classmethod
+    def of(cls, eng, dist, group, world: int, rank: int) -> "_PeerExchange":
+        px = getattr(eng, "_peer_exchange", None)
+        if px is None:
+            px = cls(eng, dist, group, world, rank)
+            eng._peer_exchange = px
+        elif (px.world, px.rank) != (world, rank) or px.group is not group:
+            raise ValueError("this engine's peer exchange belongs to another process group")
+        return px
+
+    def next_seq(self) -> int:
+        self.seq += 1
+        return self.seq
+
+    def ensure(self, rows: int) -> None:
+        """Buffers of at least `rows` y rows on every rank, mapped by every
+        peer.  Every rank calls this with the same `rows` (derived from the
+        all-gathered counts), so all grow together."""
+        rows = max(rows, 1)  # buffers exist even when no rank has tokens yet
+        if rows <= self.cap:
+            return
+        dist, eng, G, me = self.dist, self.eng, self.world, self.rank
+        cap = max(rows, 2 * self.cap)
+        torch.cuda.synchronize()
+        if self.cap:
+            eng.ep_close_peers()
+        dist.barrier(group=self.group)  # nobody maps or writes the old buffers now
+        y, flags, handle = eng.ep_buffer(cap)
+        handles = [None] * G
+        dist.all_gather_object(handles, handle, group=self.group)
+        maps = [(y, flags) if r == me else eng.ep_open_peer(handles[r]) for r in range(G)]
+        self.peer_y = [m[0] for m in maps]
+        self.peer_flags = [m[1] for m in maps]
+        self.own_y, self.own_flags = y, flags
+        self.cap = cap
+        dist.barrier(group=self.group)
+
+
 class ExpertParallelMoE:
     """The MoE block over the ranks of a process group, one GPU each.
 
@@ -256,39 +316,9 @@ class ExpertParallelMoE:
             raise ValueError(f"{ops.E} experts do not split evenly over {self.world} ranks")
         self.per_rank = ops.E // self.world
         self.exchange = exchange
-        self._cap, self._seq = 0, 0
+        self._px = None
         if exchange == "peer":
-            # every rank on a GPU of its own: the flag waits of two ranks
-            # must never share one GPU
-            dev = torch.cuda.current_device()
-            uuid = str(torch.cuda.get_device_properties(dev).uuid)
-            ids = [None] * self.world
-            dist.all_gather_object(ids, uuid, group=group)
-            if len(set(ids)) != self.world:
-                raise ValueError("exchange='peer' needs one GPU per rank")
-
-    def _ensure_buffers(self, rows: int) -> None:
-        """Exchange buffers of at least `rows` y rows on every rank, mapped
-        by every peer.  Every rank calls this with the same `rows` (derived
-        from the all-gathered counts), so all grow together."""
-        rows = max(rows, 1)  # buffers exist even when no rank has tokens yet
-        if rows <= self._cap:
-            return
-        dist, eng, G, me = self.dist, self.ops.eng, self.world, self.rank
-        cap = max(rows, 2 * self._cap)
-        torch.cuda.synchronize()
-        if self._cap:
-            eng.ep_close_peers()
-        dist.barrier(group=self.group)  # nobody maps or writes the old buffers now
-        y, flags, handle = eng.ep_buffer(cap)
-        handles = [None] * G
-        dist.all_gather_object(handles, handle, group=self.group)
-        maps = [(y, flags) if r == me else eng.ep_open_peer(handles[r]) for r in range(G)]
-        self._peer_y = [m[0] for m in maps]
-        self._peer_flags = [m[1] for m in maps]
-        self._own_y, self._own_flags = y, flags
-        self._cap = cap
-        dist.barrier(group=self.group)
+            self._px = _PeerExchange.of(ops.eng, dist, group, self.world, self.rank)
 
     def experts_of(self, rank: int) -> list[int]:
         """The experts this placement puts on `rank` (its store must hold them)."""
@@ -327,13 +357,14 @@ class ExpertParallelMoE:
         if self.exchange == "peer":
             # rows from source s go to rank s's buffer, after the rows that
             # s sends to lower ranks (its send order, the one y_pos indexes)
-            self._ensure_buffers(int(Mh[:, :, 1].sum(1).max()))
-            src_end, dst = peer_routes(Mh, me, self._peer_y, ops.dim * 4)
-            self._seq += 1
+            px = self._px
+            px.ensure(int(Mh[:, :, 1].sum(1).max()))
+            src_end, dst = peer_routes(Mh, me, px.peer_y, ops.dim * 4)
+            seq = px.next_seq()
             ops.experts_to_ranks(xq_in, dx_in, pair_row, pair_expert, me, src_end, dst,
-                                 self._peer_flags, self._seq)
-            ops.wait(self._own_flags, G, self._seq, x)
-            ops.combine_rows(x, w, self._own_y, plan.y_pos)
+                                 px.peer_flags, seq)
+            ops.wait(px.own_flags, G, seq, x)
+            ops.combine_rows(x, w, px.own_y, plan.y_pos)
             return x
         y_in = ops.experts(xq_in, dx_in, pair_row, pair_expert)
 

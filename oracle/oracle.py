@@ -29,8 +29,29 @@ class OShape(C.Structure):
                 ("expert_hidden", C.c_int32), ("norm_topk", C.c_int32), ("norm_eps", C.c_float)]
 
 
+def reference_tree() -> str | None:
+    """Where the reference sources lie: $MIA_REFERENCE, else BASELINE.json's
+    reference_path; None when neither names an existing tree (the GPU box)."""
+    import json
+    import os
+
+    cand = os.environ.get("MIA_REFERENCE")
+    if not cand:
+        try:
+            cand = json.loads((HERE.parent / "BASELINE.json").read_text()).get("reference_path")
+        except (OSError, ValueError):
+            cand = None
+    if cand and (Path(cand) / "src" / "model" / "forward.c").exists():
+        return cand
+    return None
+
+
 def build() -> None:
-    r = subprocess.run(["make", "-s", "-C", str(HERE)], capture_output=True, text=True)
+    cmd = ["make", "-s", "-C", str(HERE)]
+    tree = reference_tree()
+    if tree:
+        cmd.append(f"REF={tree}")
+    r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"oracle build failed:\n{r.stdout}\n{r.stderr}")
 

@@ -18,6 +18,7 @@ from __future__ import annotations
 import os
 import subprocess
 import sys
+import warnings
 
 import numpy as np
 import pytest
@@ -132,11 +133,17 @@ def test_simulated_ranks_equal_the_block(torch_cuda, G, placement):
 @pytest.mark.parametrize("world,exchange,tokens,port", [(2, "peer", 300, 29517),
                                                         (2, "peer", 40, 29518),
                                                         (2, "collective", 300, 29519),
-                                                        (4, "peer", 300, 29520)])
+                                                        (4, "peer", 300, 29520),
+                                                        (8, "peer", 300, 29521)])
 def test_nccl_ranks_equal_the_block(torch_cuda, world, exchange, tokens, port):
     torch = torch_cuda
-    if torch.cuda.device_count() < world:
-        pytest.skip(f"needs {world} GPUs")
+    n = torch.cuda.device_count()
+    if n < world:
+        msg = (f"NOT CHECKED: {world} NCCL ranks need {world} GPUs and {n} are visible; "
+               "the sharded block over real ranks was not compared here")
+        warnings.warn(msg)
+        print(msg, file=sys.stderr)
+        pytest.skip(msg)
     here = os.path.dirname(os.path.abspath(__file__))
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run",
            "--nnodes=1", f"--nproc-per-node={world}", "--master-addr", "127.0.0.1",

@@ -172,7 +172,7 @@ def test_config2_full_batch_matches_oracle(qwen, orc):
     assert exact >= 0.5
 
 
-def test_config3_routing_permutation_exact_and_sampled_outputs(qwen, orc):
+def test_config3_routing_permutation_and_every_output(qwen, orc):
     eng, _, zipf = qwen
     T = 2048
     x = synth.tokens(QWEN, XSEED + 2, T, rms_normalise=False)
@@ -186,13 +186,14 @@ def test_config3_routing_permutation_exact_and_sampled_outputs(qwen, orc):
     assert np.array_equal(r["offsets"], p["offsets"])
     assert np.array_equal(r["counts"], p["counts"])
     assert r["counts"][0] > 4 * r["counts"][-1]  # the Zipf bias skews the load
-    sample = np.random.default_rng(0).choice(T, 48, replace=False)
-    want, _, _ = orc.moe(QWEN, zipf.ffn_norm, zipf.router, zipf.bias, zipf.blobs, x[sample],
+    # every one of the 2048 tokens against the oracle (threaded on the host)
+    want, _, _ = orc.moe(QWEN, zipf.ffn_norm, zipf.router, zipf.bias, zipf.blobs, x,
                          threads=n_threads())
-    check_block(x[sample], out[sample], want, "config3-sampled")
+    exact = check_block(x, out, want, "config3-all-2048")
+    assert exact >= 0.8  # the rest differ through glibc's expf (rare misroundings)
 
 
-def test_config5_size_permutation_invariants(qwen, orc):
+def test_config5_size_permutation_invariants_and_every_output(qwen, orc):
     eng, _, zipf = qwen
     T = 4096
     x = synth.tokens(QWEN, XSEED + 3, T, rms_normalise=False)
@@ -208,11 +209,12 @@ def test_config5_size_permutation_invariants(qwen, orc):
         assert np.all(np.diff(seg) > 0)
     assert np.array_equal(np.cumsum(r["counts"]), r["offsets"][1:])
     assert np.allclose(r["w"].sum(1), 1.0, atol=2e-6)
-    sample = np.random.default_rng(1).choice(T, 16, replace=False)
-    want, idx, _ = orc.moe(QWEN, zipf.ffn_norm, zipf.router, zipf.bias, zipf.blobs, x[sample],
+    # every one of the 4096 tokens against the oracle (threaded on the host)
+    want, idx, _ = orc.moe(QWEN, zipf.ffn_norm, zipf.router, zipf.bias, zipf.blobs, x,
                            threads=n_threads())
-    assert np.array_equal(r["idx"][sample], idx)
-    check_block(x[sample], out[sample], want, "config5-size-sampled")
+    assert np.array_equal(r["idx"], idx)
+    exact = check_block(x, out, want, "config5-size-all-4096")
+    assert exact >= 0.8
 
 
 # ---- size-independent properties -------------------------------------------

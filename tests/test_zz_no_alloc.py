@@ -47,10 +47,11 @@ def test_noalloc_matches_the_allocating_entry_point_on_consecutive_calls(torch_c
             assert rc == 0, msg
             eng.sync()  # NULL stream = the context's stream; also reports device errors
             got = xd.cpu().numpy()
+            # the same kernels on the same bytes: identical bits, like the
+            # expert-parallel checks; the block tolerance is only reported
             errs = [rel_l2(g - a, w - a) for g, w, a in zip(got, want, x)]
-            assert max(errs) <= RTOL_L2, max(errs)
-            print(f"T={T}: max rel-L2 {max(errs):.1e}, identical bits "
-                  f"{np.array_equal(got.view(np.uint32), want.view(np.uint32))}")
+            print(f"T={T}: max rel-L2 {max(errs):.1e} (block tolerance {RTOL_L2})")
+            assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), max(errs)
 
 
 def test_noalloc_refuses_batches_beyond_its_array(torch_cuda):
