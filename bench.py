@@ -237,6 +237,9 @@ def stage_work(shape, T, counts, rows=None, pairs=None):
         "gateup": n_act * gu_w + R * (d + d // 8) + P * 2 * eh * 4,
         "down": n_act * dn_w + P * 2 * eh * 4 + P * d * 4,
         "combine": T * K * d * 4 + 2 * T * d * 4 + T * K * 8,
+        # tcgen05 prefill only: the activations laid out as pair tiles
+        "gather": P * (d + d // 8) * 2,
+        "swiglu": P * 2 * eh * 4 + P * (eh + eh // 8),
     }
     flops = {"gateup": 2.0 * P * 2 * eh * d, "down": 2.0 * P * d * eh}
     fp32_ops = {"gateup": 4.0 * P * 2 * eh * (d // 32), "down": 4.0 * P * d * (eh // 32)}
@@ -467,8 +470,8 @@ def roofline(kind, m, work, peaks, num_sms, workload):
                     "frac": hbm / peaks["hbm_gbs"]}}
 
 
-def summarise(ctx, args, name, T, m, work, peaks, n_act, dim=2048):
-    steps = args.steps
+def summarise(ctx, args, name, T, m, work, peaks, n_act, dim=2048, steps=None):
+    steps = steps or args.steps
     kind = "tensor" if name in PREFILL_WORKLOADS else "hbm"
     block_bytes = sum(work[0].values())
     r = {"value": ctx.world * T * steps / (m["total_ms"] / 1e3),
@@ -559,10 +562,11 @@ def run_ours(args, T_desc, T, rms, zipf):
             deng.load_layer(0, dlay)
             engines.append(deng)
             dx = synth.tokens(shape, XSEED, dT, rms_normalise=drms)
-            dm = measure(ctx, SingleRunner(deng, 0), dx, max(args.steps, 50), args.warmup)
+            dsteps = max(args.steps, 50)
+            dm = measure(ctx, SingleRunner(deng, 0), dx, dsteps, args.warmup)
             dwork = work_of(shape, dT, dm, deng, 0)
-            s = summarise(ctx, args, dn, dT, dm, dwork, peaks, dwork[3], shape.dim)
-            s["steps"] = max(args.steps, 50)
+            s = summarise(ctx, args, dn, dT, dm, dwork, peaks, dwork[3], shape.dim, steps=dsteps)
+            s["steps"] = dsteps
             s["workload"] = f"{dn}: {ddesc}"
             decode[dn] = s
         extras["decode"] = decode

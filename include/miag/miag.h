@@ -247,6 +247,20 @@ int miag_matvec(float *out, const void *w, int wtype, const float *x,
 /* Number of kernels the most recent miag_moe / miag_moe_async launched. */
 int miag_last_launch_count(const miag_ctx *c);
 
+/* Which kernels run the expert products of prefill-size batches (more than
+ * 8 (token, expert) pairs per expert on average; no reference counterpart --
+ * the reference has one scalar matvec, src/tensor/matmul.c:19-28).  Both
+ * give the same bits.  MIAG_PREFILL_MMA (the default): the mma.sync kernels
+ * of the decode regime.  MIAG_PREFILL_TCGEN05 (where the shape allows: dim
+ * and expert_hidden multiples of 256): the block dots on the tcgen05 tensor
+ * cores into tensor memory, the exact FP32 steps in separate epilogue
+ * warps, weights read from HBM once per launch.  miag_set_prefill_kernel
+ * waits for the context's stream. */
+#define MIAG_PREFILL_MMA 0
+#define MIAG_PREFILL_TCGEN05 1
+int miag_set_prefill_kernel(miag_ctx *c, int kind, char *err, size_t errlen);
+int miag_prefill_kernel(const miag_ctx *c);
+
 /* Per-kernel timing (no reference counterpart; the reference only has
  * wall-clock stats, src/app/main.c:146-158).  While enabled, every kernel of
  * the block is bracketed by CUDA events on the stream it is launched on.

@@ -6,6 +6,8 @@ reference interface (engine.py) plus seeded synthetic inputs (synth.py).
 """
 
 from . import synth  # noqa: F401
-from .engine import MIA_F32, MIA_Q8_0, MoEEngine, blob_bytes, matvec, quantize_row_q8  # noqa: F401
+from .engine import (MIA_F32, MIA_Q8_0, PREFILL_MMA, PREFILL_TCGEN05, MoEEngine,  # noqa: F401
+                     blob_bytes, matvec, quantize_row_q8)
 
-__all__ = ["MoEEngine", "blob_bytes", "matvec", "quantize_row_q8", "MIA_F32", "MIA_Q8_0", "synth"]
+__all__ = ["MoEEngine", "blob_bytes", "matvec", "quantize_row_q8", "MIA_F32", "MIA_Q8_0",
+           "PREFILL_MMA", "PREFILL_TCGEN05", "synth"]

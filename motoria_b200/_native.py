@@ -81,6 +81,8 @@ SIGNATURES = {
     "miag_matvec": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_int,
                               C.c_int, C.c_void_p]),
     "miag_last_launch_count": (C.c_int, [C.c_void_p]),
+    "miag_set_prefill_kernel": (C.c_int, [C.c_void_p, C.c_int, C.c_char_p, C.c_size_t]),
+    "miag_prefill_kernel": (C.c_int, [C.c_void_p]),
     "miag_profile": (C.c_int, [C.c_void_p, C.c_int]),
     "miag_profile_stages": (C.c_int, []),
     "miag_profile_stage_name": (C.c_char_p, [C.c_int]),

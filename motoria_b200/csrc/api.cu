@@ -47,21 +47,27 @@ struct miag_ctx {
     int *ep_tiles = nullptr;  // the dispatch plan's per-tile counts
     int ep_tiles_cap = 0;
     std::vector<void *> ep_peers;
+    const void *ep_owner = nullptr;  // the expert-parallel block using the exchange buffer
     int last_T = 0, last_launches = 0;
+    // prefill-size batches on the tcgen05 kernels (tc.cu), else on the
+    // mma.sync kernels of the decode regime (gemv.cu)
+    bool prefill_tc = false;
     // upload staging
     uint8_t *stage_dev = nullptr, *stage_host = nullptr;
     size_t stage_bytes = 0;
     // per-kernel profiling: event pairs recorded around each stage
     bool profiling = false;
     std::vector<cudaEvent_t> event_pool;
-    std::vector<std::pair<cudaEvent_t, cudaEvent_t>> prof_events[8];
-    int prof_launches[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    std::vector<std::pair<cudaEvent_t, cudaEvent_t>> prof_events[16];
+    int prof_launches[16] = {};
 };
 
 namespace {
-enum Stage { kRoute = 0, kPermute, kGateUp, kDown, kCombine, kEpPlan, kEpPack, kNumStages };
-const char *const kStageNames[kNumStages] = {"route",   "permute", "gateup", "down",
-                                             "combine", "ep_plan", "ep_pack"};
+enum Stage {
+    kRoute = 0, kPermute, kGateUp, kDown, kCombine, kEpPlan, kEpPack, kGather, kSwiglu, kNumStages
+};
+const char *const kStageNames[kNumStages] = {"route",   "permute", "gateup", "down",  "combine",
+                                             "ep_plan", "ep_pack", "gather", "swiglu"};
 
 cudaEvent_t take_event(miag_ctx *c) {
     if (!c->event_pool.empty()) {
@@ -213,6 +219,11 @@ extern "C" int miag_open(miag_ctx **out, const miag_shape *shape, int device, ch
         miag_close(c);
         return -1;
     }
+    // The tcgen05 prefill kernels are built and exact, but the mma.sync ones
+    // are still faster end to end (the tensor-memory epilogue issues about
+    // twice the instructions its steps need): opt in with
+    // miag_set_prefill_kernel(c, MIAG_PREFILL_TCGEN05).
+    c->prefill_tc = false;
     if ((e = cudaStreamSynchronize(c->stream)) != cudaSuccess) return fail("zero-fill", e);
     *out = c;
     return 0;
@@ -387,6 +398,7 @@ static size_t ws_layout(miag_ctx *c, int T, uint8_t *base, Work *w, float **x_de
     v.T = T, v.P = (int)P, v.nchunks = nchunks;
     v.tg_count = (int32_t *)bump(p, (size_t)T * 4);  // zeroed with the workspace, kept zero by the router
     v.shares = (uint8_t *)bump(p, kShareKinds * sizeof(ShareState));  // zero at creation
+    v.tc_sched = (int32_t *)bump(p, 4 * sizeof(int32_t));             // zero at creation
     v.xq = (int8_t *)bump(p, (size_t)T * m.d);
     v.dx = (float *)bump(p, (size_t)T * xs * 4);
     v.logits = (float *)bump(p, (size_t)T * m.E * 4);
@@ -403,6 +415,11 @@ static size_t ws_layout(miag_ctx *c, int T, uint8_t *base, Work *w, float **x_de
     v.chunk_info = (int4 *)bump(p, (P / kTokChunkNarrow + m.E + 1) * 16);
     v.max_chunk = (int32_t *)bump(p, 4);
     v.chunk_done = (int32_t *)bump(p, (P / kTokChunkNarrow + m.E + 1) * 4);
+    v.chunk_brow = (int32_t *)bump(p, (P / kTokChunkNarrow + m.E + 1) * 4);
+    if (tc_supported(m)) {  // pair tiles of the tcgen05 prefill kernels
+        v.bx = (uint8_t *)bump(p, tc_tile_bytes(m, (int)P, true));
+        v.bh = (uint8_t *)bump(p, tc_tile_bytes(m, (int)P, false));
+    }
     v.perm = (int32_t *)bump(p, P * 4);
     v.inv = (int32_t *)bump(p, P * 4);
     v.h = (float *)bump(p, P * 2 * m.eh * 4);
@@ -440,6 +457,30 @@ static int ensure_ws(miag_ctx *c, int T, char *err, size_t errlen) {
     return 0;
 }
 
+// The regime of a call over w.P pairs: prefill-size batches (more than 8
+// pairs per expert on average) on the tcgen05 kernels when the context uses
+// them, in chunks of 128 pairs; otherwise the mma.sync kernels.
+static void set_regime(const miag_ctx *c, Work &w) {
+    w.tc = (c->prefill_tc && w.bx && w.bh && w.tc_sched && wide_batch(w.P, c->dims.E)) ? 1 : 0;
+    w.chunk = w.tc ? kTcChunk : tok_chunk(w.P, c->dims.E);
+}
+
+// The expert products of a call: gate/up then down, each preceded on the
+// tcgen05 path by the launch that lays its activations out as pair tiles.
+template <class Run>
+static void launch_experts(miag_ctx *c, const LayerDev &L, const Work &w, cudaStream_t s, Run run) {
+    if (w.tc) {
+        run(kGather, 1, [&] { launch_tc_gather(c->dims, c->lay, w, c->num_sms, c->d_err, s); });
+        run(kGateUp, 1, [&] { launch_gateup_tc(c->dims, c->lay, L, w, c->num_sms, c->d_err, s); });
+        run(kSwiglu, 1, [&] { launch_tc_swiglu(c->dims, c->lay, w, c->num_sms, c->d_err, s); });
+        run(kDown, 1, [&] { launch_down_tc(c->dims, c->lay, L, w, c->num_sms, c->d_err, s); });
+    } else {
+        run(kGateUp, 1, [&] { launch_gateup(c->dims, c->lay, L, w, c->num_sms, c->d_err, s); });
+        run(kDown, down_launches(c->dims, w.P),
+            [&] { launch_down(c->dims, c->lay, L, w, c->num_sms, c->d_err, s); });
+    }
+}
+
 static int enqueue_moe(miag_ctx *c, int layer, float *x_dev, int T, cudaStream_t s, char *err,
                        size_t errlen) {
     const LayerState &Ls = c->layers[(size_t)layer];
@@ -448,15 +489,13 @@ static int enqueue_moe(miag_ctx *c, int layer, float *x_dev, int T, cudaStream_t
         return -1;
     }
     LayerDev L{Ls.ffn_norm, Ls.router_t, Ls.has_bias ? Ls.bias : nullptr, Ls.experts};
+    set_regime(c, c->ws);
     const Work &w = c->ws;
     c->last_launches = 0;
     run_stage(c, kRoute, 1, s, [&] { launch_route(c->dims, L, x_dev, w, c->d_err, s); });
     run_stage(c, kPermute, permute_launches(w.P, c->dims.E), s,
               [&] { launch_permute(c->dims, w, c->d_err, s); });
-    run_stage(c, kGateUp, 1, s,
-              [&] { launch_gateup(c->dims, c->lay, L, w, c->num_sms, c->d_err, s); });
-    run_stage(c, kDown, down_launches(c->dims, w.P), s,
-              [&] { launch_down(c->dims, c->lay, L, w, c->num_sms, c->d_err, s); });
+    launch_experts(c, L, w, s, [&](int st, int n, auto f) { run_stage(c, st, n, s, f); });
     run_stage(c, kCombine, 1, s, [&] { launch_combine(c->dims, w, x_dev, c->d_err, s); });
     c->last_T = T;
     CU(cudaGetLastError());
@@ -493,6 +532,7 @@ static int read_device_error(miag_ctx *c, char *err, size_t errlen, int code = -
     if (c->ws_mem) {
         CU(cudaMemsetAsync(c->ws.tg_count, 0, (size_t)c->ws_cap * sizeof(int32_t), c->stream));
         CU(cudaMemsetAsync(c->ws.shares, 0, kShareKinds * sizeof(ShareState), c->stream));
+        CU(cudaMemsetAsync(c->ws.tc_sched, 0, 4 * sizeof(int32_t), c->stream));
     }
     noalloc_clear_counters(c->device, c->stream);
     CU(cudaStreamSynchronize(c->stream));
@@ -619,12 +659,10 @@ extern "C" int miag_experts_async(miag_ctx *c, int layer, const int8_t *xq, cons
     w.idx = const_cast<int32_t *>(pair_expert);  // read only by the permutation
     w.xq = const_cast<int8_t *>(xq), w.dx = const_cast<float *>(dx);
     w.pair_row = pair_row, w.n_rows = n_rows, w.y = y;
+    set_regime(c, w);
     run_stage(c, kPermute, permute_launches(w.P, c->dims.E), s,
               [&] { launch_permute(c->dims, w, c->d_err, s); });
-    run_stage(c, kGateUp, 1, s,
-              [&] { launch_gateup(c->dims, c->lay, L, w, c->num_sms, c->d_err, s); });
-    run_stage(c, kDown, down_launches(c->dims, w.P), s,
-              [&] { launch_down(c->dims, c->lay, L, w, c->num_sms, c->d_err, s); });
+    launch_experts(c, L, w, s, [&](int st, int n, auto f) { run_stage(c, st, n, s, f); });
     CU(cudaGetLastError());
     return 0;
 }
@@ -690,12 +728,15 @@ extern "C" int miag_ep_close_peers(miag_ctx *c, char *err, size_t errlen) {
     return 0;
 }
 
-extern "C" int miag_experts_to_ranks_async(miag_ctx *c, int layer, const int8_t *xq,
-                                           const float *dx, int n_rows, const int32_t *pair_row,
-                                           const int32_t *pair_expert, int n_pairs, int n_ranks,
-                                           int rank, const int32_t *src_end, float *const *dst,
-                                           unsigned *const *flags, unsigned seq, void *stream,
-                                           char *err, size_t errlen) {
+namespace miag {
+// miag_experts_to_ranks_async with the activation rows at any stride (the
+// expert-parallel block of ep_comm.cu reads them straight from the received
+// records: values then scales, one record a row).
+int ctx_experts_to_ranks(miag_ctx *c, int layer, const int8_t *xq, size_t x_stride,
+                         const float *dx, size_t dx_stride, int n_rows, const int32_t *pair_row,
+                         const int32_t *pair_expert, int n_pairs, int n_ranks, int rank,
+                         const int32_t *src_end, float *const *dst, unsigned *const *flags,
+                         unsigned seq, cudaStream_t s, char *err, size_t errlen) {
     if (check_layer(c, layer, err, errlen)) return -1;
     if (n_ranks < 1 || n_ranks > kEpMaxRanks || rank < 0 || rank >= n_ranks || !src_end || !dst ||
         !flags || !c->ep_buf) {
@@ -704,8 +745,8 @@ extern "C" int miag_experts_to_ranks_async(miag_ctx *c, int layer, const int8_t 
     }
     if (n_pairs < 0 || n_rows < 0 ||
         (n_pairs > 0 && (!xq || !dx || !pair_row || !pair_expert || n_rows == 0)) ||
-        ((uintptr_t)xq & 15u) || ((uintptr_t)dx & 15u)) {
-        set_err(err, errlen, "bad buffers (device pointers; xq, dx 16-byte aligned)");
+        ((uintptr_t)xq & 15u) || ((uintptr_t)dx & 15u) || (x_stride & 15u) || (dx_stride & 3u)) {
+        set_err(err, errlen, "bad buffers (device pointers; xq, dx and row strides 16-byte aligned)");
         return -1;
     }
     YRoute yr{};
@@ -725,7 +766,6 @@ extern "C" int miag_experts_to_ranks_async(miag_ctx *c, int layer, const int8_t 
     }
     c->last_launches = 0;
     CU(cudaSetDevice(c->device));
-    const cudaStream_t s = stream ? (cudaStream_t)stream : c->stream;
     if (n_pairs == 0) {  // nothing to compute: the other ranks still wait for this one
         launch_ep_signal(yr, s);
         c->last_launches = 1;
@@ -739,15 +779,46 @@ extern "C" int miag_experts_to_ranks_async(miag_ctx *c, int layer, const int8_t 
     w.P = n_pairs, w.nchunks = (n_pairs + kPermChunk - 1) / kPermChunk;
     w.idx = const_cast<int32_t *>(pair_expert);
     w.xq = const_cast<int8_t *>(xq), w.dx = const_cast<float *>(dx);
+    w.x_stride = x_stride, w.dx_stride = dx_stride / sizeof(float);
     w.pair_row = pair_row, w.n_rows = n_rows, w.y = nullptr, w.yr = yr;
+    set_regime(c, w);
     run_stage(c, kPermute, permute_launches(w.P, c->dims.E), s,
               [&] { launch_permute(c->dims, w, c->d_err, s); });
-    run_stage(c, kGateUp, 1, s,
-              [&] { launch_gateup(c->dims, c->lay, L, w, c->num_sms, c->d_err, s); });
-    run_stage(c, kDown, down_launches(c->dims, w.P), s,
-              [&] { launch_down(c->dims, c->lay, L, w, c->num_sms, c->d_err, s); });
+    launch_experts(c, L, w, s, [&](int st, int n, auto f) { run_stage(c, st, n, s, f); });
     CU(cudaGetLastError());
     return 0;
+}
+
+// The exchange buffer of a context belongs to at most one expert-parallel
+// block (ep_comm.cu) at a time: its sequence numbers and peer mappings
+// would otherwise interleave.
+bool ctx_claim_ep(miag_ctx *c, const void *owner) {
+    if (c->ep_owner && c->ep_owner != owner) return false;
+    c->ep_owner = owner;
+    return true;
+}
+void ctx_release_ep(miag_ctx *c, const void *owner) {
+    if (c->ep_owner == owner) c->ep_owner = nullptr;
+}
+int ctx_device(const miag_ctx *c) { return c->device; }
+const miag_shape *ctx_shape(const miag_ctx *c) { return &c->shape; }
+cudaStream_t ctx_stream(const miag_ctx *c) { return c->stream; }
+}  // namespace miag
+
+extern "C" int miag_experts_to_ranks_async(miag_ctx *c, int layer, const int8_t *xq,
+                                           const float *dx, int n_rows, const int32_t *pair_row,
+                                           const int32_t *pair_expert, int n_pairs, int n_ranks,
+                                           int rank, const int32_t *src_end, float *const *dst,
+                                           unsigned *const *flags, unsigned seq, void *stream,
+                                           char *err, size_t errlen) {
+    if (!c) {
+        set_err(err, errlen, "null context");
+        return -1;
+    }
+    return ctx_experts_to_ranks(c, layer, xq, (size_t)c->dims.d, dx,
+                                (size_t)scale_pad(c->dims.d / MIAG_QK) * sizeof(float), n_rows,
+                                pair_row, pair_expert, n_pairs, n_ranks, rank, src_end, dst, flags,
+                                seq, stream ? (cudaStream_t)stream : c->stream, err, errlen);
 }
 
 extern "C" int miag_ep_wait_async(miag_ctx *c, const unsigned *flags, int n_ranks, unsigned seq,
@@ -898,6 +969,28 @@ extern "C" int miag_router_logits(miag_ctx *c, float *logits, char *err, size_t 
 }
 
 extern "C" int miag_last_launch_count(const miag_ctx *c) { return c ? c->last_launches : 0; }
+
+extern "C" int miag_set_prefill_kernel(miag_ctx *c, int kind, char *err, size_t errlen) {
+    if (!c || (kind != MIAG_PREFILL_MMA && kind != MIAG_PREFILL_TCGEN05)) {
+        set_err(err, errlen, "null context or unknown prefill kernel %d", kind);
+        return -1;
+    }
+    if (kind == MIAG_PREFILL_TCGEN05) {
+        CU(cudaSetDevice(c->device));
+        if (!tc_supported(c->dims) || tc_setup_attributes() != 0) {
+            set_err(err, errlen, "the tcgen05 prefill kernels do not take this shape (dim and "
+                                 "expert_hidden must be multiples of 256)");
+            return -1;
+        }
+    }
+    CU(cudaStreamSynchronize(c->stream));
+    c->prefill_tc = kind == MIAG_PREFILL_TCGEN05;
+    return 0;
+}
+
+extern "C" int miag_prefill_kernel(const miag_ctx *c) {
+    return c && c->prefill_tc ? MIAG_PREFILL_TCGEN05 : MIAG_PREFILL_MMA;
+}
 
 extern "C" int miag_profile(miag_ctx *c, int enable) {
     if (!c) return -1;

@@ -179,6 +179,22 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
         : "memory");
 }
 
+// 4 bytes from shared memory (a shared-window address).
+__device__ __forceinline__ float lds32(uint32_t addr) {
+    float v;
+    asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr));
+    return v;
+}
+
+// 16 bytes from shared memory (a shared-window address).
+__device__ __forceinline__ float4 lds128(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(addr));
+    return v;
+}
+
 __device__ __forceinline__ unsigned sm_id() {
     unsigned r;
     asm volatile("mov.u32 %0, %%smid;" : "=r"(r));
@@ -238,6 +254,53 @@ __device__ __forceinline__ void set_error(int *err, int code) {
 // One reference Q8_0 step: s += ((float)acc * dw) * dx (matmul.c:25).
 __device__ __forceinline__ float q8_step(float s, int acc, float dw, float dx) {
     return __fadd_rn(s, __fmul_rn(__fmul_rn(__int2float_rn(acc), dw), dx));
+}
+
+
+// ---------------------------------------------------------------------------
+// Exact Q8_0 steps on int8 tensor-core dots.
+
+// The int8 MMA accumulates onto kMagicBits, the bit pattern of 1.5 * 2^23.
+// A Q8_0 block dot satisfies |dot| <= 32 * 127 * 127 < 2^22, so the int32
+// result, read as a float, is exactly 12582912 + dot (same binade, unit ulp)
+// and one exact subtraction gives (float)dot.  The conversion so runs on the
+// FMA pipe; as an int-to-float conversion it saturated the conversion unit.
+constexpr int kMagicBits = 0x4B400000;
+constexpr float kMagic = 12582912.0f;
+
+// Two f32 lanes in one 64-bit register: the packed FP32 instructions of
+// sm_100 (FADD2, FMUL2, FFMA2) do one operation on both.
+__device__ __forceinline__ uint64_t pack2(float lo, float hi) {
+    uint64_t v;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(v) : "f"(lo), "f"(hi));
+    return v;
+}
+__device__ __forceinline__ uint64_t pack2i(int lo, int hi) {
+    uint64_t v;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(v) : "r"(lo), "r"(hi));
+    return v;
+}
+__device__ __forceinline__ float2 unpack2(uint64_t v) {
+    float2 r;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+    return r;
+}
+
+// The reference step s += ((float)dot * dw) * dx (matmul.c:25) for two
+// accumulators at once, on magic MMA results m = kMagicBits + dot.  Each
+// operation is rounded on its own, as in the reference: the dot is exact,
+// then two rounded products.  The product is added as fma(v, one, s) with
+// one = 1.0 from a kernel argument: v * 1 is exact, so this rounds once like
+// the add -- and the compiler, which contracts a packed multiply feeding a
+// packed add into one FFMA2 even when both are written with .rn (measured on
+// sm_100a), finds no multiply-add pair here to contract.
+__device__ __forceinline__ void q8_step_x2(uint64_t &s, uint64_t m, uint64_t w2, uint64_t x2,
+                                           uint64_t neg_magic2, uint64_t one2) {
+    uint64_t t;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(t) : "l"(m), "l"(neg_magic2));
+    asm("mul.rn.f32x2 %0, %0, %1;" : "+l"(t) : "l"(w2));
+    asm("mul.rn.f32x2 %0, %0, %1;" : "+l"(t) : "l"(x2));
+    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(s) : "l"(t), "l"(one2));
 }
 
 }  // namespace miag

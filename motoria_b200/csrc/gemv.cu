@@ -58,6 +58,8 @@ struct GemvParams {
     const float *dx;   // [rows][xs]
     const int32_t *pair_row;  // [P] activation row of each pair, or null: pair / K
     int n_rows;        // rows of xq / dx
+    size_t x_row;      // bytes between rows of xq
+    size_t dx_row;     // floats between rows of dx
     float *h;          // [P][2 eh] gate/up products (gate even, up odd), sorted order
     const int8_t *hq;  // [P][eh]   Q8_0 h = silu(gate) * up, sorted order (down's input)
     const float *hs;   // [P][xs]   its block scales
@@ -85,14 +87,6 @@ __device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t &r0, uint32_t &r
                  : "r"(addr));
 }
 
-// The int8 MMA accumulates onto kMagicBits, the bit pattern of 1.5 * 2^23.
-// A Q8_0 block dot satisfies |dot| <= 32 * 127 * 127 < 2^22, so the int32
-// result, read as a float, is exactly 12582912 + dot (same binade, unit ulp)
-// and one exact subtraction gives (float)dot.  The conversion so runs on the
-// FMA pipe; as an int-to-float conversion it saturated the conversion unit.
-constexpr int kMagicBits = 0x4B400000;
-constexpr float kMagic = 12582912.0f;
-
 // D = A(16x32 s8, row) * B(32x8 s8, col) + kMagicBits, int32, exact.
 __device__ __forceinline__ void mma_s8(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                        uint32_t a3, uint32_t b0, uint32_t b1) {
@@ -101,41 +95,6 @@ __device__ __forceinline__ void mma_s8(int (&c)[4], uint32_t a0, uint32_t a1, ui
         "{%8, %9}, {%10, %10, %10, %10};"
         : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(kMagicBits));
-}
-
-// Two f32 lanes in one 64-bit register: the packed FP32 instructions of
-// sm_100 (FADD2, FMUL2, FFMA2) do one operation on both.
-__device__ __forceinline__ uint64_t pack2(float lo, float hi) {
-    uint64_t v;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(v) : "f"(lo), "f"(hi));
-    return v;
-}
-__device__ __forceinline__ uint64_t pack2i(int lo, int hi) {
-    uint64_t v;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(v) : "r"(lo), "r"(hi));
-    return v;
-}
-__device__ __forceinline__ float2 unpack2(uint64_t v) {
-    float2 r;
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
-    return r;
-}
-
-// The reference step s += ((float)dot * dw) * dx (matmul.c:25) for two
-// accumulators at once, on magic MMA results m = kMagicBits + dot.  Each
-// operation is rounded on its own, as in the reference: the dot is exact,
-// then two rounded products.  The product is added as fma(v, one, s) with
-// one = 1.0 from a kernel argument: v * 1 is exact, so this rounds once like
-// the add -- and the compiler, which contracts a packed multiply feeding a
-// packed add into one FFMA2 even when both are written with .rn (measured on
-// sm_100a), finds no multiply-add pair here to contract.
-__device__ __forceinline__ void q8_step_x2(uint64_t &s, uint64_t m, uint64_t w2, uint64_t x2,
-                                           uint64_t neg_magic2, uint64_t one2) {
-    uint64_t t;
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(t) : "l"(m), "l"(neg_magic2));
-    asm("mul.rn.f32x2 %0, %0, %1;" : "+l"(t) : "l"(w2));
-    asm("mul.rn.f32x2 %0, %0, %1;" : "+l"(t) : "l"(x2));
-    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(s) : "l"(t), "l"(one2));
 }
 
 // An item: expert e, row tile rt, pair chunk tc, which covers pairs
@@ -313,10 +272,12 @@ __device__ void fill_region(const GemvParams &p, uint8_t *region, int rows_cap, 
     for (int v = threadIdx.x; v < total; v += kConsumers) {
         const int j = v / per, k = v - j * per;
         const int t = kGU ? tok[j] : seg0 + t0 + j;
+        const size_t q_row = kGU ? p.x_row : (size_t)row_bytes;
+        const size_t s_row = kGU ? p.dx_row : (size_t)nscale;
         if (k < qv) {
-            cp_async16(region + (size_t)j * p.x_stride + 16 * k, q_src + (size_t)t * row_bytes + 16 * k);
+            cp_async16(region + (size_t)j * p.x_stride + 16 * k, q_src + (size_t)t * q_row + 16 * k);
         } else {
-            const float *src = s_src + (size_t)t * nscale + 4 * (k - qv);
+            const float *src = s_src + (size_t)t * s_row + 4 * (k - qv);
             float *dst = reinterpret_cast<float *>(rs + (size_t)(j >> 1) * srow) + 8 * (k - qv) + (j & 1);
 #pragma unroll
             for (int i = 0; i < 4; i++) cp_async4(dst + 2 * i, src + i);
@@ -444,14 +405,6 @@ __global__ void k_swiglu_q8(const float *gu, int P, int eh, int xs, int8_t *hq, 
     if (q == 0) hs[(size_t)j * xs + b] = dq;
 }
 
-__device__ __forceinline__ float4 lds128(uint32_t addr) {
-    float4 v;
-    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
-                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-                 : "r"(addr));
-    return v;
-}
-
 // Per-lane roles in the warp's 16-row slice of a tile, as shared-memory
 // byte offsets fixed for the whole kernel.
 struct Lanes {
@@ -544,19 +497,9 @@ __device__ __forceinline__ void k_tile(uint64_t (&acc)[NT][2], uint32_t tile, ui
     }
 }
 
-// The row of pair `pid` (pair order) in y: this rank's y, or under expert
-// parallelism the row at the pair's origin rank (YRoute).  The source rank is
-// found by compares on compile-time indices, so the route stays in the
-// parameter bank.
+// The row of pair `pid` (pair order) in y (see y_route_row).
 __device__ __forceinline__ float *y_row(const GemvParams &p, int pid) {
-    const size_t d = (size_t)p.m.d;
-    if (p.yr.n == 0) return p.y + (size_t)pid * d;
-    float *base = p.yr.dst[0];
-    int start = 0;
-#pragma unroll
-    for (int i = 0; i < kEpMaxRanks - 1; i++)
-        if (i + 1 < p.yr.n && pid >= p.yr.end[i]) base = p.yr.dst[i + 1], start = p.yr.end[i];
-    return base + (size_t)(pid - start) * d;
+    return y_route_row(p.yr, p.y, p.m.d, pid);
 }
 
 // What one item needs besides the kernel parameters.
@@ -751,20 +694,6 @@ __device__ RatePrefix rate_prefixes(const float (&r)[kMaxSlots / 32], int ja, in
 // consecutive items share their activations.  (Handing the last 15-30 % of
 // the items out one by one from an atomic counter evened out the end times
 // too, but cost more in activation stagings than it saved.)
-// Expert parallelism: after the CTA's y rows (stores to peer memory among
-// them) the CTA is counted, and the launch's last CTA sets this rank's flag
-// on every rank (st.release.sys), so a rank that sees its flags at seq may
-// read every row stored for it.
-__device__ __forceinline__ void ep_signal_done(const YRoute &yr) {
-    __threadfence_system();  // this thread's y stores, before the CTA is counted
-    __syncthreads();
-    if (threadIdx.x == 0 && atomicAdd(yr.done, 1u) == gridDim.x - 1) {
-        __threadfence_system();
-        *yr.done = 0;  // for the next launch
-        for (int r = 0; r < yr.n; r++) st_release_sys(yr.flags[r] + yr.me, yr.seq);
-    }
-}
-
 template <bool kGU, bool kWide>
 __global__ void __launch_bounds__(kGemvThreads, 1) k_expert_mma(GemvParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -1009,6 +938,8 @@ static void fill_params(GemvParams &p, const Dims &m, const StoreLayout &lay, co
     p.xq = w.xq, p.dx = w.dx, p.h = w.h, p.hq = w.hq, p.hs = w.hs, p.y = w.y, p.err = err;
     p.yr = w.yr;
     p.pair_row = w.pair_row, p.n_rows = w.pair_row ? w.n_rows : w.T;
+    p.x_row = w.x_stride ? w.x_stride : (size_t)m.d;
+    p.dx_row = w.dx_stride ? w.dx_stride : (size_t)scale_pad(m.d / MIAG_QK);
     p.one = 1.0f;
     p.chunk = tok_chunk(w.P, m.E);
 }

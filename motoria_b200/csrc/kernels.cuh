@@ -23,6 +23,35 @@ struct YRoute {
     unsigned *done;  // CTAs of the launch done so far; zero between launches
 };
 
+
+// Row of pair `pid` (pair order) of the down projections: y itself, or under
+// expert parallelism the row at the pair's origin rank (YRoute).  The source
+// rank is found by compares on compile-time indices, so the route stays in
+// the parameter bank.
+__device__ __forceinline__ float *y_route_row(const YRoute &yr, float *y, int d, int pid) {
+    if (yr.n == 0) return y + (size_t)pid * d;
+    float *base = yr.dst[0];
+    int start = 0;
+#pragma unroll
+    for (int i = 0; i < kEpMaxRanks - 1; i++)
+        if (i + 1 < yr.n && pid >= yr.end[i]) base = yr.dst[i + 1], start = yr.end[i];
+    return base + (size_t)(pid - start) * d;
+}
+
+// Expert parallelism: after the CTA's y rows (stores to peer memory among
+// them) the CTA is counted, and the launch's last CTA sets this rank's flag
+// on every rank (st.release.sys), so a rank that sees its flags at seq may
+// read every row stored for it.
+__device__ __forceinline__ void ep_signal_done(const YRoute &yr) {
+    __threadfence_system();  // this thread's y stores, before the CTA is counted
+    __syncthreads();
+    if (threadIdx.x == 0 && atomicAdd(yr.done, 1u) == gridDim.x - 1) {
+        __threadfence_system();
+        *yr.done = 0;  // for the next launch
+        for (int r = 0; r < yr.n; r++) st_release_sys(yr.flags[r] + yr.me, yr.seq);
+    }
+}
+
 struct Work {
     int T, P, nchunks;
     int8_t *xq;            // [T][d]        quantized normalised input (Q8_0 values)
@@ -43,6 +72,14 @@ struct Work {
     int32_t *max_chunk;    // [1]           largest chunk (pairs)
     int32_t *chunk_done;   // [chunks]      decode regime: gate/up warp-tiles finished per chunk
                            //               (zeroed by the permutation)
+    int32_t *chunk_brow;   // [chunks]      first row of each chunk in the pair-tile buffers bx / bh:
+                           //               the pairs of earlier chunks, each chunk rounded up to 16
+    int chunk;             // pairs per chunk (0: tok_chunk(P, E))
+    int tc;                // prefill regime on the tcgen05 kernels (tc.cu)
+    uint8_t *bx;           // tcgen05 prefill: gate/up activations as swizzled pair tiles (tc.cu)
+    uint8_t *bh;           // tcgen05 prefill: down activations (Q8_0 h) as pair tiles
+    int32_t *tc_sched;     // [4] tcgen05 launches' item counters (gate/up, down): zero between
+                           //               launches (kept by the launches; zero at creation)
     uint8_t *shares;       // [kShareKinds] ShareState: the expert launches' SM shares; zero at
                            //               creation, kept by the launches themselves
     int32_t *perm;         // [P]           pair id at each sorted position
@@ -56,6 +93,9 @@ struct Work {
     const int32_t *pair_row;  // [P]        expert products over given pairs: each pair's row of
     int n_rows;               //              xq/dx (null: pair p is row p / K, the moe() case)
     const int32_t *y_pos;     // [P]        combine: row of y holding pair p (null: row p)
+    size_t x_stride;          // bytes between rows of xq (0: d)
+    size_t dx_stride;         // floats between rows of dx (0: scale_pad(d / 32)); records that
+                              //            carry a row's values and scales together set both
 };
 
 struct LayerDev {
@@ -89,6 +129,7 @@ struct ShareState {
 // launches then need no four-n-tile path and keep every value in registers.
 constexpr int kTokChunk = 32;
 constexpr int kTokChunkNarrow = 16;
+constexpr int kTcChunk = 128;  // pairs per chunk of the tcgen05 prefill kernels (one MMA's N)
 __host__ __device__ inline bool wide_batch(int P, int E) { return (long)P > 8L * E; }
 __host__ __device__ inline int tok_chunk(int P, int E) {
     return wide_batch(P, E) ? kTokChunk : kTokChunkNarrow;
@@ -105,6 +146,18 @@ struct CtxView {
     int *d_err;
 };
 
+// tc.cu: the prefill regime on the 5th-generation tensor cores
+bool tc_supported(const Dims &m);              // shapes the tcgen05 kernels take
+size_t tc_tile_bytes(const Dims &m, int P, bool gu);  // bytes of bx (gu) or bh
+void launch_tc_gather(const Dims &m, const StoreLayout &lay, const Work &w, int num_sms, int *err,
+                      cudaStream_t s);  // gate/up's pair tiles (bx)
+void launch_tc_swiglu(const Dims &m, const StoreLayout &lay, const Work &w, int num_sms, int *err,
+                      cudaStream_t s);  // h = silu(gate) * up as Q8_0 pair tiles (bh)
+void launch_gateup_tc(const Dims &m, const StoreLayout &lay, const LayerDev &L, const Work &w,
+                      int num_sms, int *err, cudaStream_t s);
+void launch_down_tc(const Dims &m, const StoreLayout &lay, const LayerDev &L, const Work &w,
+                    int num_sms, int *err, cudaStream_t s);
+int tc_setup_attributes();
 // route.cu
 void launch_route(const Dims &m, const LayerDev &L, const float *x, const Work &w,
                   int *err, cudaStream_t s);

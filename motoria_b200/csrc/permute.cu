@@ -96,19 +96,26 @@ __device__ int block_excl_scan(int v, int *total, int *sh /* >= 33 ints */) {
 // The pair chunks of one active expert (n pairs from sorted position off),
 // numbered from cpos in the list the expert launches walk: (e, chunk, first
 // sorted position of the expert, pairs in the chunk); each chunk's
-// completion counter (gate/up tiles done) starts at zero.
-__device__ __forceinline__ void write_chunks(int4 *chunk_info, int32_t *chunk_done, int cpos, int e,
-                                             int off, int n, int chunk) {
+// completion counter (gate/up tiles done) starts at zero, and its first row
+// in the pair-tile buffers is brow0 (the expert's, the sum of the earlier
+// experts' pairs each rounded up to 16) plus the chunks before it (chunk is
+// a multiple of 16, so only an expert's last chunk is ragged).  Workspaces
+// without pair tiles pass no chunk_brow.
+__device__ __forceinline__ void write_chunks(int4 *chunk_info, int32_t *chunk_done,
+                                             int32_t *chunk_brow, int cpos, int e, int off, int n,
+                                             int chunk, int brow0) {
     for (int tc = 0; tc * chunk < n; tc++) {
         chunk_info[cpos + tc] = make_int4(e, tc, off, min(chunk, n - tc * chunk));
         chunk_done[cpos + tc] = 0;
+        if (chunk_brow) chunk_brow[cpos + tc] = brow0 + tc * chunk;
     }
 }
 
 __global__ void __launch_bounds__(1024)
 k_perm_scan(int nchunks, int E, const int32_t *chunk_cnt, int32_t *chunk_base, int32_t *counts,
             int32_t *offsets, int32_t *active, int32_t *n_active, int32_t *chunk_pre,
-            int4 *chunk_info, int32_t *chunk_done, int32_t *max_chunk, int chunk) {
+            int4 *chunk_info, int32_t *chunk_done, int32_t *chunk_brow, int32_t *max_chunk,
+            int chunk) {
     pdl_wait();
     pdl_launch_dependents();
     __shared__ int sh[33];
@@ -128,6 +135,8 @@ k_perm_scan(int nchunks, int E, const int32_t *chunk_cnt, int32_t *chunk_base, i
     int nact, nchk;
     const int apos = block_excl_scan((e < E && run > 0) ? 1 : 0, &nact, sh);
     const int cpos = block_excl_scan(e < E ? (run + chunk - 1) / chunk : 0, &nchk, sh);
+    int nrow;
+    const int brow = block_excl_scan(e < E ? (run + 15) & ~15 : 0, &nrow, sh);
     if (e == 0) smax = 0;
     __syncthreads();
     if (e < E) {
@@ -135,7 +144,7 @@ k_perm_scan(int nchunks, int E, const int32_t *chunk_cnt, int32_t *chunk_base, i
         if (run > 0) {
             active[apos] = e;
             chunk_pre[apos] = cpos;
-            write_chunks(chunk_info, chunk_done, cpos, e, off, run, chunk);
+            write_chunks(chunk_info, chunk_done, chunk_brow, cpos, e, off, run, chunk, brow);
             atomicMax(&smax, min(chunk, run));
         }
         for (int c = 0; c < nchunks; c++) chunk_base[(size_t)c * E + e] += off;
@@ -198,8 +207,8 @@ __device__ long long block_excl_scan64(long long v, long long *total, long long 
 __global__ void __launch_bounds__(1024)
 k_permute_small(const int32_t *idx, int P, int E, int32_t *counts, int32_t *offsets,
                 int32_t *active, int32_t *n_active, int32_t *chunk_pre, int4 *chunk_info,
-                int32_t *chunk_done, int32_t *max_chunk, int chunk, int32_t *perm, int32_t *inv,
-                int *err) {
+                int32_t *chunk_done, int32_t *chunk_brow, int32_t *max_chunk, int chunk,
+                int32_t *perm, int32_t *inv, int *err) {
     pdl_wait();
     pdl_launch_dependents();
     extern __shared__ int32_t sm_i[];  // wcnt [warps][E], base [E]
@@ -243,13 +252,15 @@ k_permute_small(const int32_t *idx, int P, int E, int32_t *counts, int32_t *offs
     const long long ex = block_excl_scan64(v, &tot, sh);
     const int off = (int)(ex & kF), apos = (int)((ex >> 21) & kF), cpos = (int)(ex >> 42);
     const int total = (int)(tot & kF), nact = (int)((tot >> 21) & kF), nchk = (int)(tot >> 42);
+    long long nrow;
+    const int brow = (int)block_excl_scan64(tid < E ? (long long)((run + 15) & ~15) : 0ll, &nrow, sh);
     if (tid < E) {
         offsets[tid] = off;
         base[tid] = off;
         if (run > 0) {
             active[apos] = tid;
             chunk_pre[apos] = cpos;
-            write_chunks(chunk_info, chunk_done, cpos, tid, off, run, chunk);
+            write_chunks(chunk_info, chunk_done, chunk_brow, cpos, tid, off, run, chunk, brow);
             atomicMax(&smax, min(chunk, run));
         }
     }
@@ -269,6 +280,7 @@ k_permute_small(const int32_t *idx, int P, int E, int32_t *counts, int32_t *offs
 
 void launch_permute(const Dims &m, const Work &w, int *err, cudaStream_t s) {
     const int P = w.P, E = m.E;
+    const int chunk = w.chunk > 0 ? w.chunk : tok_chunk(P, E);
     const int threads = ((P > E ? P : E) + 31) / 32 * 32;
     const size_t small_smem = (size_t)(threads / 32 * E) * 4 + (size_t)E * 4;
     if (P <= kPermChunk && E <= 1024 && small_smem <= 200 * 1024) {
@@ -276,7 +288,7 @@ void launch_permute(const Dims &m, const Work &w, int *err, cudaStream_t s) {
                              (int)small_smem);
         launch_dependent(k_permute_small, dim3(1), dim3(threads), small_smem, s, w.idx, P, E, w.counts,
                          w.offsets, w.active, w.n_active, w.chunk_pre, w.chunk_info, w.chunk_done,
-                         w.max_chunk, tok_chunk(P, E), w.perm, w.inv, err);
+                         w.chunk_brow, w.max_chunk, chunk, w.perm, w.inv, err);
         return;
     }
     const size_t smem = sizeof(int32_t) * (size_t)E * (1 + kPermWarps);
@@ -287,7 +299,7 @@ void launch_permute(const Dims &m, const Work &w, int *err, cudaStream_t s) {
     const int st = ((E + 31) / 32) * 32;
     launch_dependent(k_perm_scan, dim3(1), dim3(st < 64 ? 64 : st), 0, s, w.nchunks, E, w.chunk_cnt,
                      w.chunk_base, w.counts, w.offsets, w.active, w.n_active, w.chunk_pre,
-                     w.chunk_info, w.chunk_done, w.max_chunk, tok_chunk(P, E));
+                     w.chunk_info, w.chunk_done, w.chunk_brow, w.max_chunk, chunk);
     launch_dependent(k_perm_scatter, dim3((P + 255) / 256), dim3(256), 0, s, w.idx, P, E, w.rank,
                      w.chunk_base, w.perm, w.inv);
 }

@@ -23,6 +23,7 @@ from . import _native as N
 from .synth import Shape
 
 MIA_F32, MIA_Q8_0 = 0, 1
+PREFILL_MMA, PREFILL_TCGEN05 = 0, 1  # MIAG_PREFILL_* of miag.h
 
 
 def _shape(shape: Shape, n_layers: int) -> N.Shape:
@@ -285,6 +286,15 @@ class MoEEngine:
 
     def last_launch_count(self) -> int:
         return int(self._lib.miag_last_launch_count(self._ctx))
+
+    def set_prefill_kernel(self, kind: int) -> None:
+        """PREFILL_TCGEN05 or PREFILL_MMA for prefill-size batches (same bits)."""
+        err = N.errbuf()
+        N.check(self._lib.miag_set_prefill_kernel(self._ctx, kind, err, len(err)), err,
+                "miag_set_prefill_kernel")
+
+    def prefill_kernel(self) -> int:
+        return int(self._lib.miag_prefill_kernel(self._ctx))
 
     def profile(self, enable: bool = True) -> None:
         """Brackets every kernel stage of later calls with CUDA events."""

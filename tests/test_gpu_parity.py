@@ -19,7 +19,8 @@ import numpy as np
 import pytest
 
 from conftest import SEED, XSEED, get_layer, n_threads, rel_l2
-from motoria_b200 import MIA_F32, MIA_Q8_0, MoEEngine, build, matvec, quantize_row_q8, synth
+from motoria_b200 import (MIA_F32, MIA_Q8_0, PREFILL_MMA, PREFILL_TCGEN05, MoEEngine, build, matvec,
+                          quantize_row_q8, synth)
 from motoria_b200._native import MiagError
 
 pytestmark = pytest.mark.gpu
@@ -215,6 +216,27 @@ def test_config5_size_permutation_invariants_and_every_output(qwen, orc):
     assert np.array_equal(r["idx"], idx)
     exact = check_block(x, out, want, "config5-size-all-4096")
     assert exact >= 0.8
+
+
+@pytest.mark.parametrize("T,layer", [(129, 1), (700, 0), (1500, 1), (4096, 1)])
+def test_prefill_kernels_agree_bit_for_bit(qwen, T, layer):
+    """The tcgen05 prefill kernels (tensor-memory block dots, separate
+    epilogue warps) against the mma.sync kernels on the same batch: every
+    output bit equal.  129 tokens is just past the prefill threshold (1032
+    pairs over 128 experts: many chunks of 1-16 pairs); 4096 with the Zipf
+    bias gives full 128-pair chunks and one expert with thousands of pairs."""
+    eng, _, _ = qwen
+    x = synth.tokens(QWEN, 300 + T, T, rms_normalise=layer == 0)
+    default = eng.prefill_kernel()
+    try:
+        eng.set_prefill_kernel(PREFILL_TCGEN05)
+        got = eng.moe(x, layer=layer)
+        eng.set_prefill_kernel(PREFILL_MMA)
+        want = eng.moe(x, layer=layer)
+    finally:
+        eng.set_prefill_kernel(default)
+    same = np.all(got.view(np.uint32) == want.view(np.uint32), axis=1)
+    assert same.all(), f"{int((~same).sum())} of {T} tokens differ"
 
 
 # ---- size-independent properties -------------------------------------------
