@@ -16,8 +16,8 @@ Default workload: config5, 4096 tokens per GPU with the Zipf-biased router
           [g*128/N, (g+1)*128/N) (contiguous, as specified); each rank routes
           its own tokens, (row, expert) pairs go to the experts' ranks over
           NCCL, and the down launch stores each result straight into the
-          origin rank's memory over NVLink.  Outputs equal the one-GPU block
-          bit for bit.  The strided placement (expert e on rank e mod N) is
+          origin rank's memory over NVLink -- all inside libmiag
+          (miag_moe_ep_async).  Outputs equal the one-GPU block bit for bit.  The strided placement (expert e on rank e mod N) is
           reported beside it under "ep_strided".
 Scaling is weak: tokens per GPU are fixed as N grows.
 
@@ -288,6 +288,7 @@ class Ctx:
         self.stream = torch.cuda.Stream(self.dev)
         torch.cuda.set_stream(self.stream)
         self.num_sms = torch.cuda.get_device_properties(self.dev).multi_processor_count
+        self.closers = []  # expert-parallel blocks and communicators, closed before the engines
 
     def barrier(self):
         self.torch.cuda.synchronize(self.dev)
@@ -326,23 +327,21 @@ class SingleRunner:
 
 
 class EPRunner:
-    """Expert parallelism over the process group (motoria_b200.ep)."""
+    """libmiag's expert-parallel block (miag_moe_ep_async / miag_moe_ep):
+    NCCL, dispatch, the expert products and the peer-memory return all run
+    inside the library."""
 
-    def __init__(self, ep, eng):
-        self.ep, self.eng = ep, eng
+    def __init__(self, block, eng):
+        self.block, self.eng = block, eng
 
     def device(self, x, sp):
-        self.ep.forward(x)
+        self.block.forward_device(x.data_ptr(), x.shape[0], stream=sp)
 
     def host(self, xp_np, x, stream):
-        xp = self._pinned.get(id(xp_np))
-        x.copy_(xp, non_blocking=True)
-        self.ep.forward(x)
-        xp.copy_(x, non_blocking=True)
-        stream.synchronize()
+        self.block.forward_host(xp_np)
 
     def received(self):
-        return self.ep.last_received
+        return self.block.last_received()
 
 
 def measure(ctx: Ctx, runner, x_host, steps: int, warmup: int, e2e: bool = True,
@@ -495,28 +494,35 @@ def summarise(ctx, args, name, T, m, work, peaks, n_act, dim=2048, steps=None):
     return r
 
 
-def work_of(shape, T, m, eng, layer):
+def work_of(shape, T, m, eng, layer, experts_here=None):
     rec = m["received"]
     if rec is not None:
-        import torch
-
-        R_in, P_in, pe = rec
-        counts = torch.bincount(pe.long(), minlength=shape.n_experts).cpu().numpy()
+        R_in, P_in = rec
+        counts = np.zeros(shape.n_experts, np.int64)
+        counts[:experts_here] = 1  # the rank's experts (each has pairs at these batch sizes)
         return stage_work(shape, T, counts, rows=R_in, pairs=P_in)
     routing = eng.routing(T)
     return stage_work(shape, T, routing["counts"])
 
 
 def make_ep(ctx, shape, lay, placement):
+    """This rank's share of the experts and libmiag's expert-parallel block
+    over an NCCL communicator of its own (rank 0's id shared through the
+    process group: plumbing, no data)."""
     from motoria_b200 import MoEEngine
-    from motoria_b200.ep import EngineOps, ExpertParallelMoE
+    from motoria_b200.ep_native import ExpertParallelBlock, NcclComm, nccl_unique_id
 
+    uid = [nccl_unique_id() if ctx.rank == 0 else None]
+    ctx.dist.broadcast_object_list(uid, src=0)
+    comm = NcclComm(uid[0], ctx.world, ctx.rank, ctx.local)
     eng = MoEEngine(shape, n_layers=1, device=ctx.local)
-    ep = ExpertParallelMoE(EngineOps(eng), placement=placement, exchange="peer")
+    block = ExpertParallelBlock(eng, comm, placement)
     eng.set_layer(0, lay.ffn_norm, lay.router, lay.bias)
-    for e in ep.experts_of(ctx.rank):
+    for e in block.experts():
         eng.upload_experts(0, lay.blobs[e:e + 1], first=e)
-    return EPRunner(ep, eng), eng
+    ctx.closers.append(block.close)
+    ctx.closers.append(comm.close)
+    return EPRunner(block, eng), eng
 
 
 def run_ours(args, T_desc, T, rms, zipf):
@@ -540,7 +546,7 @@ def run_ours(args, T_desc, T, rms, zipf):
     engines.append(eng)
     m = measure(ctx, runner, x_host, args.steps, args.warmup, pageable=ctx.world == 1,
                 clocks=True)
-    work = work_of(shape, T, m, eng, 0)
+    work = work_of(shape, T, m, eng, 0, experts_here=shape.n_experts // ctx.world)
     main = summarise(ctx, args, name, T, m, work, peaks, work[3], shape.dim)
 
     extras = {}
@@ -608,6 +614,8 @@ def run_ours(args, T_desc, T, rms, zipf):
             line["e2e_pageable"] = main["e2e_pageable"]
         line.update(extras)
         print(json.dumps(line), flush=True)
+    for f in ctx.closers:
+        f()
     for e in engines:
         e.close()
     if ctx.dist:

@@ -210,6 +210,52 @@ int miag_experts_to_ranks_async(miag_ctx *c, int layer, const int8_t *xq, const 
 int miag_ep_wait_async(miag_ctx *c, const unsigned *flags, int n_ranks, unsigned seq,
                        void *stream, char *err, size_t errlen);
 
+/* The expert-parallel block in one call (no reference counterpart: the
+ * reference runs moe(), src/model/forward.c:167-197, on one device).  The
+ * ranks of an NCCL communicator, one GPU each on one node (2..8; 1 works
+ * too), each hold E / N experts of every layer in their context's store:
+ * rank r the experts r*E/N .. (r+1)*E/N - 1 (contiguous), or r, r+N,
+ * r+2N, ... when strided is nonzero; the caller uploads them (miag_ep_rank
+ * says which).  Each rank brings its own tokens.  miag_moe_ep_async is then
+ * moe() for n_tokens rows of x on every rank at once: route here, the
+ * (row, expert) pairs to the ranks that hold the experts (NCCL send/recv,
+ * after one all-gather of the per-rank counts, the one host
+ * synchronisation of a step), the expert products there, each result row
+ * stored back into this rank's memory over NVLink, the combine here.  The
+ * outputs equal miag_moe's bit for bit.  Every rank must make the same
+ * sequence of calls (collectives inside), with any n_tokens >= 0.
+ * NCCL is loaded at run time (libnccl.so.2).  The context's exchange buffer
+ * (miag_ep_buffer) belongs to the block while it is open.
+ *
+ * miag_nccl_unique_id: 128 bytes for rank 0 to share with the others
+ *   (ncclGetUniqueId); miag_nccl_comm_init: this rank's communicator on
+ *   `device` (ncclCommInitRank); miag_nccl_comm_destroy frees it (after
+ *   miag_ep_close).
+ * miag_ep_open: binds a context to a communicator.  Refuses ranks that
+ *   share a GPU (their flag waits could not both run).
+ * miag_moe_ep_async: x_dev a DEVICE pointer, enqueued on `stream` (NULL =
+ *   the context's stream); device errors (a peer that never stores its
+ *   rows: the bounded wait gives up after two seconds) reach the next
+ *   miag_sync.  miag_moe_ep: the same from a HOST pointer, returning when x
+ *   holds the result.
+ * miag_ep_rank: this rank, the number of ranks, and its experts: first,
+ *   count, and the step between them.  miag_ep_last_received: the rows and
+ *   pairs this rank's experts worked on in the last step. */
+typedef struct miag_ep miag_ep;
+int miag_nccl_unique_id(void *id, char *err, size_t errlen);
+int miag_nccl_comm_init(void **comm, int n_ranks, const void *id, int rank, int device,
+                        char *err, size_t errlen);
+void miag_nccl_comm_destroy(void *comm);
+int miag_ep_open(miag_ep **out, miag_ctx *c, void *nccl_comm, int strided, char *err,
+                 size_t errlen);
+void miag_ep_close(miag_ep *ep);
+int miag_moe_ep_async(miag_ep *ep, int layer, float *x_dev, int n_tokens, void *stream,
+                      char *err, size_t errlen);
+int miag_moe_ep(miag_ep *ep, int layer, float *x, int n_tokens, char *err, size_t errlen);
+int miag_ep_rank(const miag_ep *ep, int *rank, int *n_ranks, int *first_expert,
+                 int *n_experts_here, int *stride);
+int miag_ep_last_received(const miag_ep *ep, int *rows, int *pairs);
+
 /* Waits for the context's work on `stream` (NULL = own stream) and reports
  * any device-side error (a bounded wait that gave up, a bad index). */
 int miag_sync(miag_ctx *c, void *stream, char *err, size_t errlen);

@@ -83,6 +83,19 @@ SIGNATURES = {
     "miag_last_launch_count": (C.c_int, [C.c_void_p]),
     "miag_set_prefill_kernel": (C.c_int, [C.c_void_p, C.c_int, C.c_char_p, C.c_size_t]),
     "miag_prefill_kernel": (C.c_int, [C.c_void_p]),
+    "miag_nccl_unique_id": (C.c_int, [C.c_void_p, C.c_char_p, C.c_size_t]),
+    "miag_nccl_comm_init": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int,
+                                      C.c_char_p, C.c_size_t]),
+    "miag_nccl_comm_destroy": (None, [C.c_void_p]),
+    "miag_ep_open": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_char_p,
+                               C.c_size_t]),
+    "miag_ep_close": (None, [C.c_void_p]),
+    "miag_moe_ep_async": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p,
+                                    C.c_char_p, C.c_size_t]),
+    "miag_moe_ep": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_char_p, C.c_size_t]),
+    "miag_ep_rank": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                               C.c_void_p]),
+    "miag_ep_last_received": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p]),
     "miag_profile": (C.c_int, [C.c_void_p, C.c_int]),
     "miag_profile_stages": (C.c_int, []),
     "miag_profile_stage_name": (C.c_char_p, [C.c_int]),

@@ -74,3 +74,18 @@ def test_null_arguments_are_errors(lib):
     assert lib.miag_moe(None, 0, None, 1, err, len(err)) == -1
     assert lib.miag_quantize_row_q8(None, None, 32, None) == -1
     assert lib.miag_matvec(None, None, 1, None, None, 4, 32, None) == -1
+
+
+def test_nccl_loads_and_the_expert_parallel_block_rejects_bad_arguments(lib):
+    """libmiag finds NCCL at run time (an id needs no GPU) and its
+    expert-parallel entry points refuse null arguments with a message."""
+    buf = C.create_string_buffer(128)
+    err = N.errbuf()
+    assert lib.miag_nccl_unique_id(buf, err, len(err)) == 0, err.value
+    assert any(buf.raw)
+    ep = C.c_void_p()
+    assert lib.miag_ep_open(C.byref(ep), None, None, 0, err, len(err)) == -1
+    assert b"null" in err.value
+    assert lib.miag_moe_ep_async(None, 0, None, 0, None, err, len(err)) == -1
+    assert lib.miag_moe_ep(None, 0, None, 0, err, len(err)) == -1
+    lib.miag_ep_close(None)  # a no-op

@@ -152,3 +152,29 @@ def test_nccl_ranks_equal_the_block(torch_cuda, world, exchange, tokens, port):
     r = subprocess.run(cmd, capture_output=True, text=True, env=env, timeout=360)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
     assert "bit-exact" in r.stdout
+
+
+@pytest.mark.parametrize("world,placement,port", [(2, "contiguous", 29531), (2, "strided", 29532),
+                                                  (4, "contiguous", 29533), (8, "contiguous", 29534),
+                                                  (8, "strided", 29535)])
+def test_c_abi_expert_parallel_block_equals_the_block(torch_cuda, world, placement, port):
+    """libmiag's own expert-parallel block (NCCL inside the library, no torch
+    in the data path): bit for bit against the one-GPU block, ragged token
+    counts per rank, two layers sharing one exchange buffer."""
+    torch = torch_cuda
+    n = torch.cuda.device_count()
+    if n < world:
+        msg = (f"NOT CHECKED: the C-ABI expert-parallel block over {world} ranks needs {world} "
+               f"GPUs and {n} are visible")
+        warnings.warn(msg)
+        print(msg, file=sys.stderr)
+        pytest.skip(msg)
+    here = os.path.dirname(os.path.abspath(__file__))
+    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run",
+           "--nnodes=1", f"--nproc-per-node={world}", "--master-addr", "127.0.0.1",
+           "--master-port", str(port), os.path.join(here, "ep_worker_c.py")]
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", EP_PLACEMENT=placement, EP_TOKENS="300")
+    r = subprocess.run(cmd, capture_output=True, text=True, env=env, timeout=360)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+    assert "bit-exact" in r.stdout
+
