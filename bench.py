@@ -527,7 +527,7 @@ def make_ep(ctx, shape, lay, placement):
 
 def run_ours(args, T_desc, T, rms, zipf):
     ctx = Ctx()
-    from motoria_b200 import MoEEngine, build
+    from motoria_b200 import PREFILL_MMA, PREFILL_TCGEN05, MoEEngine, build
 
     build.build()
     shape = synth.QWEN3_30B_A3B
@@ -544,6 +544,7 @@ def run_ours(args, T_desc, T, rms, zipf):
         eng.load_layer(0, lay)
         runner = SingleRunner(eng, 0)
     engines.append(eng)
+    eng.set_prefill_kernel(PREFILL_TCGEN05 if args.prefill_kernel == "tcgen05" else PREFILL_MMA)
     m = measure(ctx, runner, x_host, args.steps, args.warmup, pageable=ctx.world == 1,
                 clocks=True)
     work = work_of(shape, T, m, eng, 0, experts_here=shape.n_experts // ctx.world)
@@ -554,6 +555,7 @@ def run_ours(args, T_desc, T, rms, zipf):
         other = "strided" if args.ep_placement == "contiguous" else "contiguous"
         r2, e2 = make_ep(ctx, shape, lay, other)
         engines.append(e2)
+        e2.set_prefill_kernel(eng.prefill_kernel())
         m2 = measure(ctx, r2, x_host, args.steps, args.warmup, e2e=False)
         extras[f"ep_{other}"] = {"value": ctx.world * T * args.steps / (m2["total_ms"] / 1e3),
                                  "ms_per_step": m2["total_ms"] / args.steps,
@@ -592,6 +594,7 @@ def run_ours(args, T_desc, T, rms, zipf):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": DTYPE,
             "data": "synthetic (seeded random-init Q8_0 weights and N(0,1) tokens)",
             "config": {"workload": f"{name}: {T_desc}", "tokens_per_gpu": T,
+                       "prefill_kernel": args.prefill_kernel,
                        "experts": shape.n_experts, "top_k": shape.n_active, "dim": shape.dim,
                        "expert_hidden": shape.expert_hidden,
                        "active_experts": main["active_experts"],
@@ -634,6 +637,9 @@ def main():
     ap.add_argument("--ep-placement", choices=["contiguous", "strided"], default="contiguous",
                     help="expert placement of the expert-parallel run (config5, N>1); the "
                          "other placement is reported beside it")
+    ap.add_argument("--prefill-kernel", choices=["mma", "tcgen05"], default="mma",
+                    help="expert kernels for prefill-size batches (miag_set_prefill_kernel); "
+                         "both give the same bits")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the decode figures (config2, config1) of the default run")

@@ -48,6 +48,28 @@ typedef int (*miag_expert_loader)(void *ctx, int layer, int expert, void *dst);
  * (tools/internal/mia/format.go:160-163, 16 KiB aligned). */
 size_t miag_blob_bytes(const miag_shape *shape);
 
+/* Writes a .mia model file (the converter's output, tools/internal/mia/
+ * format.go:200-263, as src/storage/mia_file.c:41-111 reads it) from a
+ * model held elsewhere, one tensor or expert at a time: for a machine where
+ * the reference's Go converter cannot run.  Dense tensors come as f32 by
+ * their canonical names (token_embd; blk.<l>.attn_norm, wq, wk, wv, wo,
+ * q_norm, k_norm, ffn_norm, router; output_norm, output) and matrices are
+ * quantized to Q8_0 as the reference quantizes (src/tensor/quant.c:11-27);
+ * experts come already in .mia blob layout through the loader port
+ * signature.  Weight type Q8_0.  Host code only: no GPU needed. */
+typedef struct {
+    uint32_t dim, n_layers, n_heads, n_kv_heads, head_dim, vocab;
+    uint32_t n_experts, n_active, expert_hidden, norm_topk;
+    float rope_theta, norm_eps;
+} miag_mia_config;
+/* Fills dst with the n f32 values (row-major) of the dense tensor `name`. */
+typedef int (*miag_mia_dense_source)(void *ctx, const char *name, float *dst, size_t n);
+int miag_mia_write(const char *path, const miag_mia_config *config,
+                   miag_mia_dense_source dense, miag_expert_loader expert, void *source_ctx,
+                   const void *tokenizer, size_t tokenizer_bytes, char *err, size_t errlen);
+/* The file's expert_blob_size for this config. */
+size_t miag_mia_expert_blob_bytes(const miag_mia_config *config);
+
 /* Creates a context on CUDA device `device`: validates the shape, allocates
  * HBM for every layer's experts and dense router tensors.  Replaces
  * mia_cache_init (include/mia/expert_cache.h:28-30) for the MoE path. */

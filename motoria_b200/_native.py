@@ -83,6 +83,9 @@ SIGNATURES = {
     "miag_last_launch_count": (C.c_int, [C.c_void_p]),
     "miag_set_prefill_kernel": (C.c_int, [C.c_void_p, C.c_int, C.c_char_p, C.c_size_t]),
     "miag_prefill_kernel": (C.c_int, [C.c_void_p]),
+    "miag_mia_write": (C.c_int, [C.c_char_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                 C.c_void_p, C.c_size_t, C.c_char_p, C.c_size_t]),
+    "miag_mia_expert_blob_bytes": (C.c_size_t, [C.c_void_p]),
     "miag_nccl_unique_id": (C.c_int, [C.c_void_p, C.c_char_p, C.c_size_t]),
     "miag_nccl_comm_init": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int,
                                       C.c_char_p, C.c_size_t]),

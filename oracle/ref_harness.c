@@ -249,3 +249,49 @@ void ref_rmsnorm(float *out, const float *x, const float *w, int n, float eps) {
 void ref_softmax(float *x, int n) { softmax(x, n); }
 void ref_top_k(const float *p, int n, int k, int *idx) { top_k(p, n, k, idx); }
 int ref_block_bytes(void) { return (int)sizeof(mia_block_q8); }
+
+/* The reference's .mia reader (src/storage/mia_file.c:41-126) behind opaque
+ * handles, for tests that check files written by libmiag's writer and load
+ * them through the loader port.  ref_mia_read_expert has the loader port's
+ * signature (it is mia_file_read_expert). */
+void *ref_mia_open(const char *path, char *err, size_t errlen) {
+    mia_file *f = calloc(1, sizeof(mia_file));
+    if (!f) return NULL;
+    if (mia_file_open(f, path, err, errlen) != 0) {
+        free(f);
+        return NULL;
+    }
+    return f;
+}
+void ref_mia_close(void *f) {
+    if (!f) return;
+    mia_file_close((mia_file *)f);
+    free(f);
+}
+int ref_mia_read_expert(void *f, int layer, int expert, void *dst) {
+    return mia_file_read_expert(f, layer, expert, dst);
+}
+/* header fields: dim, n_layers, n_heads, n_kv_heads, head_dim, vocab,
+ * n_experts, n_active, expert_hidden, norm_topk */
+void ref_mia_dims(void *fp, int32_t *out) {
+    const mia_header *h = &((mia_file *)fp)->h;
+    const uint32_t v[10] = {h->dim, h->n_layers, h->n_heads, h->n_kv_heads, h->head_dim,
+                            h->vocab, h->n_experts, h->n_active, h->expert_hidden, h->norm_topk};
+    for (int i = 0; i < 10; i++) out[i] = (int32_t)v[i];
+}
+float ref_mia_norm_eps(void *fp) { return ((mia_file *)fp)->h.norm_eps; }
+uint64_t ref_mia_blob_bytes(void *fp) { return ((mia_file *)fp)->h.expert_blob_size; }
+const float *ref_mia_ffn_norm(void *fp, int l) { return ((mia_file *)fp)->layers[l].ffn_norm; }
+const float *ref_mia_router(void *fp, int l) { return ((mia_file *)fp)->layers[l].router; }
+const void *ref_mia_tensor(void *fp, int l, int which) {
+    const mia_file *f = (const mia_file *)fp;
+    switch (which) {
+    case 0: return f->token_embd;
+    case 1: return f->output;
+    case 2: return f->output_norm;
+    case 3: return f->layers[l].wq;
+    case 4: return f->layers[l].attn_norm;
+    default: return NULL;
+    }
+}
+
