@@ -439,7 +439,7 @@ def measure(ctx: Ctx, runner, x_host, steps: int, warmup: int, e2e: bool = True,
     return out
 
 
-def roofline(kind, m, work, peaks, num_sms, workload):
+def roofline(kind, m, work, peaks, num_sms, workload, kernel_tag=""):
     """The dominant kernel's roofline.  kind "tensor" (prefill-size batches)
     or "hbm" (decode)."""
     nbytes, flops, fp32_ops, _ = work
@@ -457,7 +457,7 @@ def roofline(kind, m, work, peaks, num_sms, workload):
     ep = fp32_ops[top] / t / 1e12
     return {"bound": "tensor", "kernel": top, "achieved": tf, "peak": peaks["bf16_sustained"],
             "unit": "TFLOP/s", "frac": tf / peaks["bf16_sustained"],
-            "traffic": ncu_traffic(workload, top),
+            "traffic": ncu_traffic(workload, top + kernel_tag),
             "peak_source": f"{peaks['kind']} bf16_tflops_sustained (int8 MMA FLOPs of the "
                            "expert products)",
             "epilogue": {"achieved": ep, "peak": lane_rate, "unit": "T FP32 op/s",
@@ -475,7 +475,8 @@ def summarise(ctx, args, name, T, m, work, peaks, n_act, dim=2048, steps=None):
     block_bytes = sum(work[0].values())
     r = {"value": ctx.world * T * steps / (m["total_ms"] / 1e3),
          "ms_per_step": m["total_ms"] / steps,
-         "roofline": roofline(kind, m, work, peaks, ctx.num_sms, name),
+         "roofline": roofline(kind, m, work, peaks, ctx.num_sms, name,
+                              "_tcgen05" if args.prefill_kernel == "tcgen05" else ""),
          "block_achieved_gbs": block_bytes / (m["total_ms"] / steps / 1e3) / 1e9,
          "active_experts": n_act,
          "stages_ms": {k: round(v, 5) for k, v in m["stage_ms"].items()},
