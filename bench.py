@@ -526,6 +526,84 @@ def make_ep(ctx, shape, lay, placement):
     return EPRunner(block, eng), eng
 
 
+# config4: the whole Qwen3-30B-A3B decode step (miag_model_*), batch 1.
+MODEL_DESC = ("Qwen3-30B-A3B, 48 layers, all weights random-init Q8_0 in HBM; batch-1 decode of "
+              "256 tokens (positions 512..767, greedy) after a 512-token prompt of uniform-random "
+              "ids; f32 KV cache of 4096 positions")
+MODEL_PROMPT, MODEL_NEW, MODEL_CTX = 512, 256, 4096
+
+
+def model_config():
+    from motoria_b200.mia import MiaConfig
+    return MiaConfig(dim=2048, n_layers=48, n_heads=32, n_kv_heads=4, head_dim=128, vocab=151936,
+                     n_experts=128, n_active=8, expert_hidden=768, norm_topk=1, rope_theta=1e6,
+                     norm_eps=1e-6)
+
+
+def model_bytes_per_token(cfg, first_pos: int, n: int) -> float:
+    """HBM bytes one decode step reads, averaged over positions
+    first_pos .. first_pos + n - 1: per layer the attention matrices, the
+    router and 8 experts, the K and V rows up to the position; the LM head."""
+    d, qd, kvd = cfg.dim, cfg.n_heads * cfg.head_dim, cfg.n_kv_heads * cfg.head_dim
+    row = lambda cols: cols // 32 * 36  # noqa: E731
+    attn = (qd + 2 * kvd) * row(d) + d * row(qd)
+    router = cfg.n_experts * d * 4
+    experts = cfg.n_active * (2 * cfg.expert_hidden * row(d) + d * row(cfg.expert_hidden))
+    mean_len = first_pos + (n + 1) / 2  # positions 0..pos are read at pos
+    kv = 2 * mean_len * kvd * 4
+    return cfg.n_layers * (attn + router + experts + kv) + cfg.vocab * row(d) + row(d)
+
+
+def run_model_decode(ctx, args, peaks):
+    """config4 on one GPU: device-timed prompt and decode, and the host API
+    end to end (miag_model_generate: prompt in, tokens out)."""
+    import torch
+
+    from motoria_b200.model import Model
+
+    cfg = model_config()
+    P, NEW = MODEL_PROMPT, MODEL_NEW
+    prompt = np.random.default_rng(XSEED).integers(0, cfg.vocab, P).astype(np.int32)
+    with Model.synthetic(cfg, SEED, MODEL_CTX, device=ctx.local) as m:
+        s = torch.cuda.ExternalStream(m.stream)
+        for _ in range(max(1, args.warmup // 3)):  # captures the graph for this prompt length
+            m.generate(prompt, 1)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        with ClockSampler(ctx.local) as clk:
+            ev[0].record(s)
+            m.generate_async(prompt, 1)  # positions 0..511; the last yields the first new token
+            ev[1].record(s)
+            m.continue_async(NEW)        # positions 512..767
+            ev[2].record(s)
+            m.sync()
+        prompt_ms, decode_ms = ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2])
+        t0 = time.perf_counter()
+        toks = m.generate(prompt, NEW + 1)
+        e2e_s = time.perf_counter() - t0
+        launches = m.launches_per_step
+    tok_s = NEW / (decode_ms / 1e3)
+    bpt = model_bytes_per_token(cfg, P, NEW)
+    achieved = bpt * tok_s / 1e9
+    return {
+        "workload": f"config4: {MODEL_DESC}",
+        "metric": "Qwen3-30B-A3B decode tok/s", "value": tok_s, "unit": "tokens/s",
+        "ms_per_token": decode_ms / NEW,
+        "prompt_positions_per_s": P / (prompt_ms / 1e3),
+        "e2e": {"value": (P + NEW) / e2e_s, "unit": "positions/s",
+                "what": "miag_model_generate from a host prompt to host tokens: 512 prompt "
+                        "positions then 256 greedy ones, wall clock",
+                "h2d_bytes_per_step": P * 4 / (P + NEW), "d2h_bytes_per_step": (NEW + 1) * 4 / (P + NEW)},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": achieved / peaks["hbm_gbs"], "traffic": None,
+                     "basis": f"{bpt / 1e9:.3f} GB read per decode token (attention matrices, "
+                              "router and 8 experts per layer, K/V rows, LM head) x tokens/s; "
+                              f"peak: {peaks['kind']} copy bandwidth"},
+        "gpu_launches_per_step": launches,
+        "first_new_tokens": [int(t) for t in toks[:8]],
+        "clocks": clk.summary(),
+    }
+
+
 def run_ours(args, T_desc, T, rms, zipf):
     ctx = Ctx()
     from motoria_b200 import PREFILL_MMA, PREFILL_TCGEN05, MoEEngine, build
@@ -579,6 +657,7 @@ def run_ours(args, T_desc, T, rms, zipf):
             s["workload"] = f"{dn}: {ddesc}"
             decode[dn] = s
         extras["decode"] = decode
+        extras["decode_model"] = run_model_decode(ctx, args, peaks)
 
     if ctx.rank == 0:
         cpu = None

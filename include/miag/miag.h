@@ -98,6 +98,14 @@ int miag_upload_experts(miag_ctx *c, int layer, int first, int n,
 int miag_load_experts(miag_ctx *c, miag_expert_loader load, void *load_ctx,
                       char *err, size_t errlen);
 
+/* miag_upload_experts from DEVICE memory (no reference counterpart: for
+ * blobs that already sit in HBM, e.g. generated there).  Only enqueues on
+ * `stream` (NULL = the context's stream); blobs_dev must stay valid until
+ * the stream has passed this point. */
+int miag_upload_experts_device(miag_ctx *c, int layer, int first, int n,
+                               const void *blobs_dev, size_t stride, void *stream,
+                               char *err, size_t errlen);
+
 /* The MoE block, replacing forward.c:167-197 for n_tokens independent
  * tokens: x [n_tokens][dim] f32 is the residual stream, read and updated in
  * place (x += sum_j w_j * down_j(silu(gate_j xn) * up_j xn)).
@@ -328,6 +336,63 @@ int miag_last_launch_count(const miag_ctx *c);
 #define MIAG_PREFILL_TCGEN05 1
 int miag_set_prefill_kernel(miag_ctx *c, int kind, char *err, size_t errlen);
 int miag_prefill_kernel(const miag_ctx *c);
+
+/* ---- The whole decode step ---------------------------------------------
+ * A model in HBM: the .mia dense section (embedding, attention, norms,
+ * routers, LM head), an f32 KV cache of max_seq positions per layer, and the
+ * MoE blocks of a miag_ctx.  Replaces the reference's model state and step
+ * (mia_model_init / mia_model_step, include/mia/model.h:17-27,
+ * src/model/forward.c:36-62 and 199-217); the logits equal mia_model_step's
+ * bit for bit.  One step is one CUDA graph replay (captured on first use).
+ *
+ * miag_model_open: `moe` holds the experts (miag_load_experts) and must
+ *   have the model's MoE shape; it is not owned.  `dense` is the file's
+ *   dense section (mia_file.dense, mia_header.dense_size bytes) in host
+ *   memory, uploaded here, or NULL to fill it with miag_model_synth.
+ * miag_model_open_file: opens a Q8_0 .mia file (mia_file_open,
+ *   src/storage/mia_file.c:41-111) on `device`, experts and all; the model
+ *   owns its context.
+ * miag_model_synth: seeded random weights on the device (no reference
+ *   counterpart; benchmarks without a converted checkpoint): Q8_0 matrices
+ *   with q uniform on [-127, 127] and d = |N(0, 0.02)| / 127, routers
+ *   N(0, 0.02), norms 1.
+ * miag_model_step: one token at one position; returns the logits [vocab]
+ *   in host memory owned by the model (valid until the next call), or NULL
+ *   with a message (token or position out of range, as forward.c:202-203).
+ *   miag_model_step_async only enqueues; miag_model_logits_device holds the
+ *   result once miag_model_sync returns 0.
+ * miag_model_generate: the prompt one position at a time, then n_new
+ *   greedy tokens (argmax, the lowest index on ties), entirely on the device;
+ *   tokens_out receives the n_new tokens.  The _async form leaves them at
+ *   miag_model_tokens_device()[n_prompt ...].
+ * Not re-entrant; one host thread per model, as mia_model. */
+typedef struct miag_model miag_model;
+int miag_model_open(miag_model **out, miag_ctx *moe, const miag_mia_config *config,
+                    const void *dense, size_t dense_bytes, int max_seq, char *err,
+                    size_t errlen);
+int miag_model_open_file(miag_model **out, const char *path, int device, int max_seq,
+                         char *err, size_t errlen);
+void miag_model_close(miag_model *m);
+int miag_model_synth(miag_model *m, uint64_t seed, char *err, size_t errlen);
+const float *miag_model_step(miag_model *m, int token, int pos, char *err, size_t errlen);
+int miag_model_step_async(miag_model *m, int token, int pos, char *err, size_t errlen);
+int miag_model_generate(miag_model *m, const int32_t *prompt, int n_prompt, int n_new,
+                        int32_t *tokens_out, char *err, size_t errlen);
+int miag_model_generate_async(miag_model *m, const int32_t *prompt, int n_prompt, int n_new,
+                              char *err, size_t errlen);
+/* n_steps more greedy steps from where the last step left the model's
+ * device state (its next token and position); enqueues only.  A step whose
+ * position reaches max_seq fails at miag_model_sync. */
+int miag_model_continue_async(miag_model *m, int n_steps, char *err, size_t errlen);
+int miag_model_sync(miag_model *m, char *err, size_t errlen);
+const float *miag_model_logits_device(const miag_model *m);
+const int32_t *miag_model_tokens_device(const miag_model *m);
+void *miag_model_stream(const miag_model *m);  /* a cudaStream_t */
+miag_ctx *miag_model_moe(const miag_model *m);
+int miag_model_launches_per_step(const miag_model *m);
+/* 1 when steps run as CUDA graph replays, 0 when they are launched directly
+ * (the capture failed) or no step has run yet. */
+int miag_model_uses_graph(const miag_model *m);
 
 /* Per-kernel timing (no reference counterpart; the reference only has
  * wall-clock stats, src/app/main.c:146-158).  While enabled, every kernel of

@@ -40,6 +40,8 @@ SIGNATURES = {
     "miag_upload_experts": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p,
                                       C.c_size_t, C.c_char_p, C.c_size_t]),
     "miag_load_experts": (C.c_int, [C.c_void_p, LOADER, C.c_void_p, C.c_char_p, C.c_size_t]),
+    "miag_upload_experts_device": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p,
+                                             C.c_size_t, C.c_void_p, C.c_char_p, C.c_size_t]),
     "miag_moe": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_char_p, C.c_size_t]),
     "miag_moe_async": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p,
                                  C.c_char_p, C.c_size_t]),
@@ -99,6 +101,26 @@ SIGNATURES = {
     "miag_ep_rank": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                C.c_void_p]),
     "miag_ep_last_received": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p]),
+    "miag_model_open": (C.c_int, [C.POINTER(C.c_void_p), C.c_void_p, C.c_void_p, C.c_void_p,
+                                  C.c_size_t, C.c_int, C.c_char_p, C.c_size_t]),
+    "miag_model_open_file": (C.c_int, [C.POINTER(C.c_void_p), C.c_char_p, C.c_int, C.c_int,
+                                       C.c_char_p, C.c_size_t]),
+    "miag_model_close": (None, [C.c_void_p]),
+    "miag_model_synth": (C.c_int, [C.c_void_p, C.c_uint64, C.c_char_p, C.c_size_t]),
+    "miag_model_step": (C.c_void_p, [C.c_void_p, C.c_int, C.c_int, C.c_char_p, C.c_size_t]),
+    "miag_model_step_async": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_char_p, C.c_size_t]),
+    "miag_model_generate": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p,
+                                      C.c_char_p, C.c_size_t]),
+    "miag_model_generate_async": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int,
+                                            C.c_char_p, C.c_size_t]),
+    "miag_model_continue_async": (C.c_int, [C.c_void_p, C.c_int, C.c_char_p, C.c_size_t]),
+    "miag_model_sync": (C.c_int, [C.c_void_p, C.c_char_p, C.c_size_t]),
+    "miag_model_logits_device": (C.c_void_p, [C.c_void_p]),
+    "miag_model_tokens_device": (C.c_void_p, [C.c_void_p]),
+    "miag_model_stream": (C.c_void_p, [C.c_void_p]),
+    "miag_model_moe": (C.c_void_p, [C.c_void_p]),
+    "miag_model_launches_per_step": (C.c_int, [C.c_void_p]),
+    "miag_model_uses_graph": (C.c_int, [C.c_void_p]),
     "miag_profile": (C.c_int, [C.c_void_p, C.c_int]),
     "miag_profile_stages": (C.c_int, []),
     "miag_profile_stage_name": (C.c_char_p, [C.c_int]),

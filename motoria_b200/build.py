@@ -51,7 +51,7 @@ def _stale(target: Path, deps: list[Path]) -> bool:
 
 def build(force: bool = False, verbose: bool = False) -> Path:
     srcs = sources()
-    headers = list(CSRC.glob("*.cuh")) + list(INCLUDE.rglob("*.h"))
+    headers = list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h")) + list(INCLUDE.rglob("*.h"))
     if not force and not _stale(LIB, srcs + headers + [Path(__file__)]):
         return LIB
     OBJ_DIR.mkdir(exist_ok=True)

@@ -340,6 +340,29 @@ extern "C" int miag_upload_experts(miag_ctx *c, int layer, int first, int n, con
     return 0;
 }
 
+extern "C" int miag_upload_experts_device(miag_ctx *c, int layer, int first, int n,
+                                          const void *blobs_dev, size_t stride, void *stream,
+                                          char *err, size_t errlen) {
+    if (check_layer(c, layer, err, errlen)) return -1;
+    if (!blobs_dev || n < 0 || first < 0 || first + n > c->shape.n_experts) {
+        set_err(err, errlen, "bad expert range [%d, %d)", first, first + n);
+        return -1;
+    }
+    if (stride < mia_blob_content(&c->shape) || (stride & 3u) || ((uintptr_t)blobs_dev & 3u)) {
+        set_err(err, errlen, "blob stride %zu: at least the .mia blob (%zu), 4-byte aligned", stride,
+                mia_blob_content(&c->shape));
+        return -1;
+    }
+    if (n == 0) return 0;
+    CU(cudaSetDevice(c->device));
+    LayerState &L = c->layers[(size_t)layer];
+    launch_repack(c->dims, c->lay, (const uint8_t *)blobs_dev, stride, n,
+                  L.experts + (size_t)first * c->lay.expert_bytes,
+                  stream ? (cudaStream_t)stream : c->stream);
+    CU(cudaGetLastError());
+    return 0;
+}
+
 extern "C" int miag_load_experts(miag_ctx *c, miag_expert_loader load, void *load_ctx, char *err,
                                  size_t errlen) {
     if (!c || !load) {
@@ -803,6 +826,37 @@ void ctx_release_ep(miag_ctx *c, const void *owner) {
 int ctx_device(const miag_ctx *c) { return c->device; }
 const miag_shape *ctx_shape(const miag_ctx *c) { return &c->shape; }
 cudaStream_t ctx_stream(const miag_ctx *c) { return c->stream; }
+int ctx_num_sms(const miag_ctx *c) { return c->num_sms; }
+
+// Sizes the workspace for batches of up to T tokens now, so that later
+// calls of at most T tokens neither allocate nor synchronise (a captured
+// launch sequence needs that).  The returned address changes whenever the
+// workspace is re-allocated, which invalidates captured sequences.
+const void *ctx_reserve(miag_ctx *c, int T, char *err, size_t errlen) {
+    if (cudaSetDevice(c->device) != cudaSuccess) {
+        set_err(err, errlen, "cudaSetDevice failed");
+        return nullptr;
+    }
+    if (ensure_ws(c, T, err, errlen)) return nullptr;
+    return c->ws_mem;
+}
+const void *ctx_workspace(const miag_ctx *c) { return c->ws_mem; }
+
+// miag_set_layer from device memory (no bias): ffn_norm [d] and router
+// [E][d] f32 may be freed once the stream has passed this point.
+int ctx_set_layer_device(miag_ctx *c, int layer, const float *ffn_norm, const float *router,
+                         cudaStream_t s, char *err, size_t errlen) {
+    if (check_layer(c, layer, err, errlen)) return -1;
+    CU(cudaSetDevice(c->device));
+    LayerState &L = c->layers[(size_t)layer];
+    const size_t E = (size_t)c->shape.n_experts, d = (size_t)c->shape.dim;
+    launch_transpose_router(router, L.router_t, (int)E, (int)d, s);
+    CU(cudaGetLastError());
+    CU(cudaMemcpyAsync(L.ffn_norm, ffn_norm, d * 4, cudaMemcpyDeviceToDevice, s));
+    L.has_bias = false;
+    L.dense_set = true;
+    return 0;
+}
 }  // namespace miag
 
 extern "C" int miag_experts_to_ranks_async(miag_ctx *c, int layer, const int8_t *xq,

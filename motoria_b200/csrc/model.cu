@@ -1,0 +1,1224 @@
+// model.cu -- the whole decode step on the GPU: the reference's model state
+// and layer loop (mia_model_init / mia_model_step, src/model/forward.c:
+// 36-62 and 199-217) with every weight, the KV cache and the MoE experts
+// resident in HBM.
+//
+// One step = one token at one position, as mia_model_step:
+//   embed      x = dequant(token_embd[token])                   (:205-208)
+//   per layer  attention (:118-165), then the MoE block (:167-197) through
+//              the context's own launch sequence (miag_moe_async, T = 1)
+//   head       logits = output . rmsnorm(x, output_norm)         (:214-215)
+// Launches per step: 1 + n_layers * (3 + the MoE block's) + 1, each with
+// programmatic dependent launch, captured once into a CUDA graph and
+// replayed; the step's token and position live in device memory, so the
+// same graph serves every position.  The head's last CTA also picks the
+// next token (the next prompt token, else the greedy argmax) and advances
+// the position, so a whole prompt + generation runs as graph replays with
+// no host round trip.
+//
+// Arithmetic is the reference's, operation for operation (x86 scalar build,
+// no FMA contraction), so logits match mia_model_step bit for bit:
+//   * Q8_0 matvecs: the input quantized as mia_quantize_row_q8
+//     (src/tensor/quant.c:11-27), s = s + ((float)dot * w.d) * x.d over the
+//     row's blocks in order (matmul.c:19-28); block dots are exact int32;
+//   * rmsnorm (:75-81): the double sum of squares through the certified
+//     scale (common.cuh), then x * inv * w;
+//   * NeoX RoPE (:84-93): cos/sin of pos * pow(theta, -2i/hd) taken from a
+//     table the host fills with the same libm calls, the rotation in double;
+//   * attention (:142-161): serial float dot per position, softmax with the
+//     serial float sum, serial accumulation over positions per dimension.
+// The serial orders are kept where the reference's rounding depends on
+// them; the parallelism is across heads, positions, dimensions and rows.
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "kernels.cuh"
+#include "mia_layout.h"
+
+struct miag_ctx;
+
+namespace miag {
+// api.cu
+int ctx_device(const miag_ctx *c);
+const miag_shape *ctx_shape(const miag_ctx *c);
+int ctx_num_sms(const miag_ctx *c);
+const void *ctx_reserve(miag_ctx *c, int T, char *err, size_t errlen);
+const void *ctx_workspace(const miag_ctx *c);
+int ctx_set_layer_device(miag_ctx *c, int layer, const float *ffn_norm, const float *router,
+                         cudaStream_t s, char *err, size_t errlen);
+struct CtxView;
+}  // namespace miag
+
+namespace miag {
+namespace {
+
+constexpr int kErrStepArgs = 16;  // a step's token or position out of range (device check)
+constexpr int kErrModelWait = 17;  // a dense matvec gave up waiting for a staged tile
+
+void put_err(char *err, size_t errlen, const char *fmt, ...) {
+    if (!err || !errlen) return;
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(err, errlen, fmt, ap);
+    va_end(ap);
+}
+
+__device__ __forceinline__ uint32_t lds_u32(uint32_t addr) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+    return v;
+}
+
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// Embedding row: mia_dequantize_row (src/tensor/quant.c:29-38), x = d * q.
+
+__global__ void k_embed(float *x, const uint8_t *embd, const int32_t *args, int d, int vocab,
+                        int max_seq, int *err) {
+    pdl_launch_dependents();
+    pdl_wait();  // the previous step's head wrote args
+    const int token = args[0], pos = args[1];
+    if (token < 0 || token >= vocab || pos < 0 || pos >= max_seq) {
+        if (threadIdx.x == 0 && blockIdx.x == 0) set_error(err, kErrStepArgs);
+        return;
+    }
+    const uint8_t *row = embd + (size_t)token * (size_t)(d / MIAG_QK) * 36;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < d; i += gridDim.x * blockDim.x) {
+        const uint8_t *blk = row + (size_t)(i / MIAG_QK) * 36;
+        const float dq = *reinterpret_cast<const float *>(blk);
+        x[i] = __fmul_rn(dq, (float)(int8_t)blk[4 + i % MIAG_QK]);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Dense Q8_0 matvec of one token (mia_matvec, matmul.c:91-106), rows kept
+// in the file's layout: row r = nb consecutive 36-byte {f32 d; int8 q[32]}
+// blocks.  A CTA walks tiles of R consecutive rows, each one contiguous
+// bulk copy (kGemvStages in flight); the input is normalised and quantized
+// once per CTA while its first tiles land.  Warp roles per tile:
+//   8 term warps   the exact terms ((float)dot_b * w.d) * x.d of every
+//                  (row, block) of the tile into shared memory (a thread a
+//                  term: consecutive threads take consecutive blocks of a
+//                  row, so the 36-byte blocks fall in distinct banks);
+//   2 chain warps  a lane a row: s = s + term over the row's blocks in
+//                  order (matmul.c:23-26), from shared memory; lane 0 of the
+//                  first also refills each stage as soon as the term warps
+//                  are done with it.
+// The term buffer is double-buffered, so the chains of one tile overlap the
+// terms of the next.  Tiles are sized on the host so that a small matrix
+// spreads over every SM in one wave.  Up to three weight matrices that
+// share the input (wq, wk, wv) run as segments of one launch.
+
+constexpr int kGemvTermWarps = 8, kGemvChainWarps = 2;
+constexpr int kGemvThreads = (kGemvTermWarps + kGemvChainWarps) * 32;
+constexpr int kGemvStages = 2;
+constexpr int kGemvMaxRows = 32 * kGemvChainWarps;  // rows per tile
+constexpr size_t kGemvSmemBudget = 220 * 1024;
+
+struct GemvSeg {
+    const uint8_t *w;
+    float *out;
+    int rows, tile0;
+};
+
+struct GemvParams {
+    GemvSeg seg[3];
+    int nseg, ntiles, R, cols, nb, row_bytes, stage_bytes;
+    const float *in;    // [cols]
+    const float *norm;  // rmsnorm weight [cols], or null: the input is used as it is
+    float eps;
+    int resid;  // out[r] += s (the residual stream, forward.c:164) instead of out[r] = s
+    // next token (the head only): argmax over the rows of segment 0, then the
+    // step's arguments advance
+    unsigned long long *amax;
+    unsigned *ticket;
+    int32_t *args;
+    const int32_t *prompt;
+    int n_prompt;
+    int32_t *tokens;
+    int max_seq;
+    int *err;
+};
+
+struct GemvSmem {
+    size_t terms, xq, xin, red, bars, total;
+};
+
+__host__ __device__ inline GemvSmem gemv_smem(int stage_bytes, int R, int cols, int nb) {
+    GemvSmem g;
+    g.terms = (size_t)kGemvStages * stage_bytes;
+    g.xq = g.terms + (((size_t)2 * R * (nb + 1) * 4 + 15) & ~(size_t)15);
+    g.xin = g.xq + (((size_t)nb * 36 + 15) & ~(size_t)15);
+    g.red = g.xin + (size_t)cols * 4;
+    g.bars = g.red + 32 * 8;
+    g.total = g.bars + (kGemvStages + 4) * 8 + 16;
+    return g;
+}
+
+// Argmax key: larger value first, then the lower row (ties go to the first
+// row, as a strict > scan does).
+__device__ __forceinline__ unsigned long long argmax_key(float v, int row) {
+    uint32_t b = __float_as_uint(v);
+    b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    return ((unsigned long long)b << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)row);
+}
+
+__global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const __grid_constant__ GemvParams p) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const GemvSmem L = gemv_smem(p.stage_bytes, p.R, p.cols, p.nb);
+    float *terms = reinterpret_cast<float *>(smem + L.terms);  // [2][R][nb + 1]
+    uint8_t *xq = smem + L.xq;
+    float *xin = reinterpret_cast<float *>(smem + L.xin);
+    double *red = reinterpret_cast<double *>(smem + L.red);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.bars);  // [kGemvStages]
+    uint64_t *tfull = full + kGemvStages;                           // [2] terms written
+    uint64_t *tempty = tfull + 2;                                   // [2] terms consumed
+    __shared__ float s_inv;
+    __shared__ int s_abort;
+    __shared__ unsigned long long s_amax;
+    __shared__ int s_last;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int nb = p.nb, ts = nb + 1;  // term row stride (odd for even nb: no bank conflicts)
+    const int my_tiles = (int)blockIdx.x < p.ntiles
+                             ? (p.ntiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x
+                             : 0;
+    auto tile_rows = [&](int j, int &seg, int &r0) {
+        const int g = (int)blockIdx.x + j * (int)gridDim.x;
+        seg = (p.nseg > 2 && g >= p.seg[2].tile0) ? 2 : (p.nseg > 1 && g >= p.seg[1].tile0) ? 1 : 0;
+        r0 = (g - p.seg[seg].tile0) * p.R;
+        const int n = p.seg[seg].rows - r0;
+        return n < p.R ? n : p.R;
+    };
+    auto issue = [&](int j) {  // tile j of this CTA into stage j % kGemvStages
+        int seg, r0;
+        const int n = tile_rows(j, seg, r0);
+        const uint32_t bytes = ((uint32_t)n * (uint32_t)p.row_bytes + 15u) & ~15u;
+        uint64_t *bar = &full[j % kGemvStages];
+        mbar_arrive_expect_tx(bar, bytes);
+        bulk_g2s(smem + (size_t)(j % kGemvStages) * p.stage_bytes,
+                 p.seg[seg].w + (size_t)r0 * (size_t)p.row_bytes, bytes, bar);
+    };
+    const bool producer = warp == kGemvTermWarps && lane == 0;
+
+    if (tid == 0) {
+        for (int s = 0; s < kGemvStages; s++) mbar_init(&full[s], 1);
+        for (int b = 0; b < 2; b++) mbar_init(&tfull[b], kGemvTermWarps), mbar_init(&tempty[b], kGemvChainWarps);
+        fence_barrier_init();
+        s_abort = 0;
+        s_amax = 0ull;
+    }
+    __syncthreads();
+    int issued = 0;
+    if (producer)
+        for (; issued < kGemvStages && issued < my_tiles; issued++) issue(issued);  // weights: constant
+    pdl_launch_dependents();
+    pdl_wait();  // the input vector
+
+    // Input: rmsnorm (forward.c:75-81) when a weight is given, then Q8_0.
+    constexpr int kWarps = kGemvThreads / 32;
+    double ss = 0.0;
+    for (int i = tid; i < p.cols; i += kGemvThreads) {
+        const float v = p.in[i];
+        xin[i] = v;
+        ss = __dadd_rn(ss, __dmul_rn((double)v, (double)v));
+    }
+    if (p.norm) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss = __dadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+        if (lane == 0) red[warp] = ss;
+        __syncthreads();
+        if (warp == 0) {
+            const float inv = rms_scale_certified(lane < kWarps ? red[lane] : 0.0, xin, p.cols, p.eps, lane);
+            if (lane == 0) s_inv = inv;
+        }
+        __syncthreads();
+        const float inv = s_inv;
+        for (int i = tid; i < p.cols; i += kGemvThreads)
+            xin[i] = __fmul_rn(__fmul_rn(xin[i], inv), p.norm[i]);
+    }
+    __syncthreads();
+    for (int b = warp; b < nb; b += kWarps) {  // mia_quantize_row_q8, one warp a block
+        const float v = xin[b * MIAG_QK + lane];
+        float a = fabsf(v);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+        const float dq = __fdiv_rn(a, 127.0f);
+        const float id = dq != 0.0f ? __fdiv_rn(1.0f, dq) : 0.0f;
+        xq[b * 36 + 4 + lane] = (uint8_t)(int8_t)roundf(__fmul_rn(v, id));
+        if (lane == 0) *reinterpret_cast<float *>(xq + b * 36) = dq;
+    }
+    __syncthreads();
+
+    if (warp < kGemvTermWarps) {
+        // ---- term warps
+        const uint32_t xq_a = smem_addr(xq);
+        for (int j = 0; j < my_tiles; j++) {
+            const int s = j % kGemvStages, tb = j & 1;
+            if (*(volatile int *)&s_abort || !mbar_wait(&full[s], (uint32_t)(j / kGemvStages) & 1u) ||
+                (j >= 2 && !mbar_wait(&tempty[tb], (uint32_t)((j >> 1) - 1) & 1u))) {
+                set_error(p.err, kErrModelWait);
+                *(volatile int *)&s_abort = 1;
+                break;
+            }
+            int seg, r0;
+            const int n = tile_rows(j, seg, r0);
+            const uint32_t tile = smem_addr(smem) + (uint32_t)s * (uint32_t)p.stage_bytes;
+            float *tt = terms + (size_t)tb * p.R * ts;
+            for (int q = tid; q < n * nb; q += kGemvTermWarps * 32) {
+                const int r = q / nb, b = q - r * nb;
+                const uint32_t a = tile + (uint32_t)r * (uint32_t)p.row_bytes + (uint32_t)b * 36u;
+                const uint32_t xa = xq_a + (uint32_t)b * 36u;
+                int acc = 0;
+#pragma unroll
+                for (int k = 1; k < 9; k++) acc = __dp4a((int)lds_u32(a + 4u * k), (int)lds_u32(xa + 4u * k), acc);
+                tt[r * ts + b] = __fmul_rn(__fmul_rn(__int2float_rn(acc), lds32(a)), lds32(xa));
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tfull[tb]);
+        }
+    } else {
+        // ---- chain warps (lane = row) and the producer
+        const int cw = warp - kGemvTermWarps, r = cw * 32 + lane;
+        unsigned long long best = 0ull;
+        int j = 0;
+        for (; j < my_tiles; j++) {
+            const int tb = j & 1;
+            if (*(volatile int *)&s_abort || !mbar_wait(&tfull[tb], (uint32_t)(j >> 1) & 1u)) {
+                set_error(p.err, kErrModelWait);
+                *(volatile int *)&s_abort = 1;
+                break;
+            }
+            if (producer && issued < my_tiles) issue(issued++);  // the term warps left stage j's tile
+            int seg, r0;
+            const int n = tile_rows(j, seg, r0);
+            if (r < n) {
+                const float *tr = terms + (size_t)tb * p.R * ts + (size_t)r * ts;
+                float sum = 0.0f;
+#pragma unroll 8
+                for (int b = 0; b < nb; b++) sum = __fadd_rn(sum, tr[b]);
+                float *o = p.seg[seg].out + r0 + r;
+                *o = p.resid ? __fadd_rn(*o, sum) : sum;
+                if (p.amax && seg == 0) {
+                    const unsigned long long k = argmax_key(sum, r0 + r);
+                    best = k > best ? k : best;
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[tb]);
+        }
+        if (producer) {
+            // Nothing may still be landing in shared memory when the CTA
+            // leaves: after a failed wait, wait (bounded) for each stage's
+            // last copy.
+            for (int t = issued - kGemvStages < 0 ? 0 : issued - kGemvStages; t < issued; t++)
+                if (*(volatile int *)&s_abort) mbar_wait(&full[t % kGemvStages], (uint32_t)(t / kGemvStages) & 1u);
+        }
+        if (p.amax) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const unsigned long long v = __shfl_xor_sync(0xffffffffu, best, o);
+                best = v > best ? v : best;
+            }
+            if (lane == 0) atomicMax(&s_amax, best);
+        }
+    }
+    if (!p.amax) return;
+    __syncthreads();
+    if (tid == 0) {
+        atomicMax(p.amax, s_amax);
+        __threadfence();
+        s_last = atomicAdd(p.ticket, 1u) == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (!s_last || tid != 0) return;
+    // The last CTA: every row is in, the step's next token is known.
+    __threadfence();
+    const unsigned long long k = atomicAdd(p.amax, 0ull);
+    const int arg = (int)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
+    const int pos = p.args[1];
+    if (pos >= 0 && pos + 1 < p.max_seq) {
+        const int next = pos + 1;
+        const int token = next < p.n_prompt ? p.prompt[next] : arg;
+        p.tokens[next] = token;
+        p.args[0] = token;
+        p.args[1] = next;
+    } else {
+        p.args[1] = p.max_seq;  // the next step reports the position out of range
+    }
+    *p.amax = 0ull;
+    *p.ticket = 0u;
+}
+
+// ---------------------------------------------------------------------------
+// Attention of one layer at one position (forward.c:127-161), GQA.
+// Grid (n_heads, kAttnSplit).  Every CTA normalises and rotates its head's
+// q and its kv head's k (cheap, and bit-identical in each CTA); CTA y of
+// head h scores the position slices y, y + kAttnSplit, ... (a thread a
+// position: the reference's serial dot, then * scale) into a scratch row.
+// The last CTA of the head to finish (a ticket) runs the softmax -- max,
+// exp, the serial sum, the division -- and the accumulation over positions,
+// a thread a dimension in position order, V streamed through shared memory.
+// The new k and v rows are written to the cache by the first CTA of each
+// kv group; at position pos every CTA uses its own copies.
+
+constexpr int kAttnThreads = 256, kAttnSplit = 4, kAttnRows = 256, kAttnVRows = 64, kAttnVBufs = 4;
+
+struct AttnParams {
+    const float *qkv;  // q [qd] | k [kvd] | v [kvd]
+    const float *q_norm, *k_norm;
+    const double2 *rope;  // [max_seq][hd / 2] (cos, sin)
+    float *kc, *vc;       // this layer's cache, [max_seq][kvd]
+    float *scores;        // [n_heads][max_seq]
+    unsigned *ticket;     // [n_heads], zero between launches
+    float *att;           // [qd]
+    const int32_t *args;
+    int nh, nkv, hd, max_seq;
+    float eps, scale;
+    int *err;
+};
+
+// Probabilities are padded to 4 floats so the vectors after them stay
+// 16-byte aligned.
+__host__ __device__ inline int attn_prob_len(int max_seq) { return (max_seq + 3) & ~3; }
+
+__host__ __device__ inline size_t attn_smem_bytes(int hd, int max_seq) {
+    return (size_t)kAttnRows * (hd + 4) * 4   // K slice (V tiles reuse it)
+           + (size_t)attn_prob_len(max_seq) * 4  // probabilities
+           + (size_t)5 * hd * 4 + 64 * 4;     // qn, kn, vv, 2 x norm scratch, reductions
+}
+
+// rmsnorm of one head (forward.c:129/134, in place there) then NeoX RoPE
+// (:84-93), by one warp; tmp is scratch of hd floats.
+__device__ void head_norm_rope(const float *src, const float *w, float *dst, float *tmp, int hd,
+                               float eps, const double2 *cs, int lane) {
+    double ss = 0.0;
+    for (int i = lane; i < hd; i += 32) {
+        const float v = src[i];
+        ss = __dadd_rn(ss, __dmul_rn((double)v, (double)v));
+    }
+    const float inv = rms_scale_certified(ss, src, hd, eps, lane);
+    for (int i = lane; i < hd; i += 32) tmp[i] = __fmul_rn(__fmul_rn(src[i], inv), w[i]);
+    __syncwarp();
+    const int half = hd / 2;
+    for (int i = lane; i < half; i += 32) {
+        const double x0 = (double)tmp[i], x1 = (double)tmp[i + half];
+        const double c = cs[i].x, s = cs[i].y;
+        dst[i] = __double2float_rn(__dsub_rn(__dmul_rn(x0, c), __dmul_rn(x1, s)));
+        dst[i + half] = __double2float_rn(__dadd_rn(__dmul_rn(x0, s), __dmul_rn(x1, c)));
+    }
+}
+
+__global__ void __launch_bounds__(kAttnThreads, 1) k_attn(const __grid_constant__ AttnParams p) {
+    extern __shared__ __align__(16) float fsm[];
+    const int hd = p.hd, kvd = p.nkv * hd, qd = p.nh * hd, group = p.nh / p.nkv;
+    float *kt = fsm;                                  // [kAttnRows][hd + 4]
+    float *prob = kt + (size_t)kAttnRows * (hd + 4);  // [max_seq]
+    float *qn = prob + attn_prob_len(p.max_seq), *kn = qn + hd, *vv = kn + hd, *tmp = vv + hd;  // tmp: 2 x hd
+    float *red = tmp + 2 * hd;
+    __shared__ int s_last;
+    __shared__ float s_val;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int h = blockIdx.x, kvh = h / group;
+    pdl_launch_dependents();
+    pdl_wait();
+    const int pos = p.args[1];
+    if (pos < 0 || pos >= p.max_seq) {
+        if (tid == 0 && h == 0 && blockIdx.y == 0) set_error(p.err, kErrStepArgs);
+        return;
+    }
+    const float *qh = p.qkv + (size_t)h * hd;
+    const float *kh = p.qkv + qd + (size_t)kvh * hd;
+    const float *vh = p.qkv + qd + kvd + (size_t)kvh * hd;
+    const double2 *cs = p.rope + (size_t)pos * (hd / 2);
+    if (warp == 0) head_norm_rope(qh, p.q_norm, qn, tmp, hd, p.eps, cs, lane);
+    else if (warp == 1) head_norm_rope(kh, p.k_norm, kn, tmp + hd, hd, p.eps, cs, lane);
+    else if (warp == 2) for (int i = lane; i < hd; i += 32) vv[i] = vh[i];
+    __syncthreads();
+    if (h % group == 0 && blockIdx.y == 0)  // forward.c:139-140
+        for (int i = tid; i < hd; i += kAttnThreads) {
+            p.kc[(size_t)pos * kvd + (size_t)kvh * hd + i] = kn[i];
+            p.vc[(size_t)pos * kvd + (size_t)kvh * hd + i] = vv[i];
+        }
+
+    // Scores (forward.c:148-153).
+    const int c4 = hd / 4, n = pos + 1;
+    for (int sl = blockIdx.y; sl * kAttnRows < n; sl += gridDim.y) {
+        const int t0 = sl * kAttnRows, m = n - t0 < kAttnRows ? n - t0 : kAttnRows;
+        for (int i = tid; i < m * c4; i += kAttnThreads) {
+            const int r = i / c4, c = i % c4, t = t0 + r;
+            float *o = kt + (size_t)r * (hd + 4) + 4 * c;
+            if (t == pos)
+                *reinterpret_cast<float4 *>(o) = *reinterpret_cast<const float4 *>(kn + 4 * c);
+            else
+                cp_async16(o, p.kc + (size_t)t * kvd + (size_t)kvh * hd + 4 * c);
+        }
+        cp_async_commit();
+        cp_async_wait<0>();
+        __syncthreads();
+        if (tid < m) {
+            const float *kr = kt + (size_t)tid * (hd + 4);
+            float d = 0.0f;
+            for (int i = 0; i < hd; i += 4) {
+                const float4 k4 = *reinterpret_cast<const float4 *>(kr + i);
+                const float4 q4 = *reinterpret_cast<const float4 *>(qn + i);
+                d = __fadd_rn(d, __fmul_rn(q4.x, k4.x));
+                d = __fadd_rn(d, __fmul_rn(q4.y, k4.y));
+                d = __fadd_rn(d, __fmul_rn(q4.z, k4.z));
+                d = __fadd_rn(d, __fmul_rn(q4.w, k4.w));
+            }
+            p.scores[(size_t)h * p.max_seq + t0 + tid] = __fmul_rn(d, p.scale);
+        }
+        __syncthreads();
+    }
+
+    // The head's last CTA finishes it.
+    if (tid == 0) {
+        __threadfence();
+        s_last = atomicAdd(&p.ticket[h], 1u) == gridDim.y - 1;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+
+    // V rows stream through a ring of kAttnVBufs tiles of kAttnVRows rows in
+    // the K slice's space, kAttnVBufs - 1 tiles ahead of the accumulation;
+    // the first ones go out before the softmax, whose serial sum they overlap.
+    const int ntile = (n + kAttnVRows - 1) / kAttnVRows;
+    auto load_v = [&](int k) {  // always commits a group (empty past the end)
+        if (k < ntile) {
+            float *dst = kt + (size_t)(k % kAttnVBufs) * kAttnVRows * hd;
+            const int t0 = k * kAttnVRows, m = n - t0 < kAttnVRows ? n - t0 : kAttnVRows;
+            for (int i = tid; i < m * c4; i += kAttnThreads) {
+                const int r = i / c4, c = i % c4, t = t0 + r;
+                float *o = dst + (size_t)r * hd + 4 * c;
+                if (t == pos)
+                    *reinterpret_cast<float4 *>(o) = *reinterpret_cast<const float4 *>(vv + 4 * c);
+                else
+                    cp_async16(o, p.vc + (size_t)t * kvd + (size_t)kvh * hd + 4 * c);
+            }
+        }
+        cp_async_commit();
+    };
+    for (int k = 0; k < kAttnVBufs - 1; k++) load_v(k);
+
+    // softmax (forward.c:95-101)
+    float mx = -INFINITY;
+    for (int t = tid; t < n; t += kAttnThreads) {
+        const float v = __ldcg(p.scores + (size_t)h * p.max_seq + t);
+        prob[t] = v;
+        mx = fmaxf(mx, v);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) red[warp] = mx;
+    __syncthreads();
+    if (tid == 0) {
+        float m = red[0];
+        for (int w = 1; w < kAttnThreads / 32; w++) m = fmaxf(m, red[w]);
+        s_val = m;
+    }
+    __syncthreads();
+    mx = s_val;
+    for (int t = tid; t < n; t += kAttnThreads) prob[t] = expf_cr(__fsub_rn(prob[t], mx));
+    __syncthreads();
+    if (tid == 0) {
+        float sum = 0.0f;
+#pragma unroll 8
+        for (int t = 0; t < n; t++) sum = __fadd_rn(sum, prob[t]);
+        s_val = sum;
+        p.ticket[h] = 0u;
+    }
+    __syncthreads();
+    const float sum = s_val;
+    for (int t = tid; t < n; t += kAttnThreads) prob[t] = __fdiv_rn(prob[t], sum);
+
+    // out[i] = sum over t of p_t * v_t[i], t in order (forward.c:155-160).
+    float acc = 0.0f;
+    for (int k = 0; k < ntile; k++) {
+        load_v(k + kAttnVBufs - 1);  // into the buffer read at k - 1
+        cp_async_wait<kAttnVBufs - 1>();  // tile k has landed
+        __syncthreads();
+        if (tid < hd) {
+            const float *vt = kt + (size_t)(k % kAttnVBufs) * kAttnVRows * hd;
+            const int t0 = k * kAttnVRows, m = n - t0 < kAttnVRows ? n - t0 : kAttnVRows;
+#pragma unroll 8
+            for (int r = 0; r < m; r++) acc = __fadd_rn(acc, __fmul_rn(prob[t0 + r], vt[(size_t)r * hd + tid]));
+        }
+        __syncthreads();  // before the next load_v reuses a buffer
+    }
+    if (tid < hd) p.att[(size_t)h * hd + tid] = acc;
+}
+
+// ---------------------------------------------------------------------------
+// Synthetic weights (benchmarks): the counter-based splitmix64 streams of
+// motoria_b200/synth.py, generated on the device.  Q8_0 matrices get
+// q uniform on [-127, 127] and d = |N(0, 1)| * sigma / 127; f32 tensors
+// N(0, 1) * sigma, or ones.
+
+constexpr uint64_t kGamma = 0x9E3779B97F4A7C15ull;
+constexpr int kTagRouter = 1, kTagQw = 2, kTagDw = 3, kTagDense = 5;
+
+__host__ __device__ inline uint64_t sm_mix(uint64_t z) {
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+__host__ __device__ inline uint64_t sm_next(uint64_t z) { return sm_mix(z + kGamma); }
+inline uint64_t sm_key(uint64_t seed, std::initializer_list<uint64_t> ids) {
+    uint64_t k = sm_next(seed);
+    for (uint64_t i : ids) k = sm_next(k ^ i);
+    return k;
+}
+__device__ __forceinline__ uint64_t sm_stream(uint64_t k, uint64_t i) {
+    return sm_mix(k + (i + 1) * kGamma);
+}
+__device__ __forceinline__ double sm_uniform(uint64_t k, uint64_t i) {
+    return ((double)(sm_stream(k, i) >> 11) + 1.0) * 1.1102230246251565e-16;
+}
+__device__ __forceinline__ double sm_normal(uint64_t k, uint64_t i) {
+    const double u0 = sm_uniform(k, 2 * i), u1 = sm_uniform(k, 2 * i + 1);
+    return sqrt(-2.0 * log(u0)) * cos(6.283185307179586 * u1);
+}
+
+// nblocks Q8_0 blocks at dst (block b at dst + b * 36).
+__global__ void k_synth_q8(uint8_t *dst, size_t nblocks, uint64_t kq, uint64_t kd, double sigma) {
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    for (size_t b = (size_t)blockIdx.x * blockDim.x + threadIdx.x; b < nblocks; b += stride) {
+        uint8_t *blk = dst + b * 36;
+        const float dq = (float)(fabs(sm_normal(kd, b)) * sigma / 127.0);
+        memcpy(blk, &dq, 4);
+        for (int w = 0; w < 8; w++) {  // 16-bit chunks of the q stream, 4 per word
+            const uint64_t word = sm_stream(kq, b * 8 + w);
+            for (int c = 0; c < 4; c++) {
+                const uint32_t hbits = (uint32_t)(word >> (16 * c)) & 0xFFFFu;
+                blk[4 + w * 4 + c] = (uint8_t)(int8_t)((int)((hbits * 255u) >> 16) - 127);
+            }
+        }
+    }
+}
+
+__global__ void k_synth_f32(float *dst, size_t n, uint64_t k, double sigma, int ones) {
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+        dst[i] = ones ? 1.0f : (float)(sm_normal(k, i) * sigma);
+}
+
+}  // namespace
+}  // namespace miag
+
+using namespace miag;
+
+struct miag_model {
+    miag_ctx *moe = nullptr;
+    bool owns_moe = false;
+    miag_mia_config cfg{};
+    int device = 0, max_seq = 0, num_sms = 0;
+    int d = 0, qd = 0, kvd = 0, hd = 0;
+    cudaStream_t stream = nullptr;
+    std::vector<MiaTensor> layout;
+    size_t dense_bytes = 0;
+    uint8_t *dense = nullptr;  // the dense section, as in the file
+    double2 *rope = nullptr;
+    float *kc = nullptr, *vc = nullptr;
+    float *x = nullptr, *qkv = nullptr, *att = nullptr, *logits = nullptr, *scores = nullptr;
+    int32_t *args = nullptr, *prompt = nullptr, *tokens = nullptr;
+    int n_prompt = 0;
+    unsigned *tickets = nullptr;  // [n_heads] attention, [1] head
+    unsigned long long *amax = nullptr;
+    int *d_err = nullptr;
+    float *h_logits = nullptr;  // pinned
+    int32_t *h_args = nullptr;  // pinned
+    GemvParams qkv_p{}, wo_p{}, head_p{};
+    size_t qkv_smem = 0, wo_smem = 0, head_smem = 0, attn_smem = 0;
+    cudaGraphExec_t exec = nullptr;
+    const void *graph_ws = nullptr;
+    bool dense_set = false;
+    bool eager = false;  // the step could not be captured: launched directly
+    int last_launches = 0;
+};
+
+namespace {
+
+const uint8_t *tensor(const miag_model *m, size_t i) { return m->dense + m->layout[i].offset; }
+const float *tensor_f(const miag_model *m, size_t i) {
+    return reinterpret_cast<const float *>(tensor(m, i));
+}
+
+cudaError_t gemv_launch(const GemvParams &p, int grid, size_t smem, cudaStream_t s) {
+    if (!p.in || !p.err) return cudaErrorInvalidValue;
+    for (int i = 0; i < p.nseg; i++)
+        if (!p.seg[i].w || !p.seg[i].out) return cudaErrorInvalidValue;
+    return launch_dependent(k_gemv, dim3(grid), dim3(kGemvThreads), smem, s, p);
+}
+
+// Tiling of a matvec over `cols` inputs (segments' rows filled in by the
+// caller): the largest R (a multiple of 4, so every tile starts 16-byte
+// aligned) whose stages fit in shared memory, lowered to spread a small
+// matrix over the SMs in one wave.
+void gemv_plan(GemvParams &p, int cols, int num_sms, size_t *smem) {
+    p.cols = cols;
+    p.nb = cols / MIAG_QK;
+    p.row_bytes = p.nb * 36;
+    int rmax = kGemvMaxRows;
+    while (rmax > 4 && gemv_smem(rmax * p.row_bytes, rmax, cols, p.nb).total > kGemvSmemBudget) rmax -= 4;
+    int rows = 0;
+    for (int i = 0; i < p.nseg; i++) rows += p.seg[i].rows;
+    const int rbal = ((rows + num_sms - 1) / num_sms + 3) & ~3;
+    p.R = rbal < 4 ? 4 : rbal < rmax ? rbal : rmax;
+    p.stage_bytes = p.R * p.row_bytes;
+    int tiles = 0;
+    for (int i = 0; i < p.nseg; i++) {
+        p.seg[i].tile0 = tiles;
+        tiles += (p.seg[i].rows + p.R - 1) / p.R;
+    }
+    p.ntiles = tiles;
+    *smem = gemv_smem(p.stage_bytes, p.R, cols, p.nb).total;
+}
+
+int grid_of(const miag_model *m, const GemvParams &p) {
+    return p.ntiles < m->num_sms ? p.ntiles : m->num_sms;
+}
+
+#define MCU(x)                                                                    \
+    do {                                                                          \
+        cudaError_t e_ = (x);                                                     \
+        if (e_ != cudaSuccess) {                                                  \
+            put_err(err, errlen, "%s: %s", #x, cudaGetErrorString(e_));           \
+            return -1;                                                            \
+        }                                                                         \
+    } while (0)
+
+// The launch sequence of one step on stream s (captured into the graph).
+int enqueue_step(miag_model *m, cudaStream_t s, char *err, size_t errlen) {
+    const miag_mia_config &c = m->cfg;
+    int launches = 0;
+    MCU(launch_dependent(k_embed, dim3((m->d + 255) / 256), dim3(256), 0, s, m->x, tensor(m, 0),
+                         (const int32_t *)m->args, m->d, (int)c.vocab, m->max_seq, m->d_err));
+    launches++;
+    for (int l = 0; l < (int)c.n_layers; l++) {
+        GemvParams q = m->qkv_p;
+        q.seg[0].w = tensor(m, mia_layer_tensor(l, kWq));
+        q.seg[1].w = tensor(m, mia_layer_tensor(l, kWk));
+        q.seg[2].w = tensor(m, mia_layer_tensor(l, kWv));
+        q.norm = tensor_f(m, mia_layer_tensor(l, kAttnNorm));
+        MCU(gemv_launch(q, grid_of(m, q), m->qkv_smem, s));
+        AttnParams a{};
+        a.qkv = m->qkv;
+        a.q_norm = tensor_f(m, mia_layer_tensor(l, kQNorm));
+        a.k_norm = tensor_f(m, mia_layer_tensor(l, kKNorm));
+        a.rope = m->rope;
+        const size_t layer_off = (size_t)l * m->max_seq * m->kvd;
+        a.kc = m->kc + layer_off, a.vc = m->vc + layer_off;
+        a.scores = m->scores, a.ticket = m->tickets, a.att = m->att, a.args = m->args;
+        a.nh = (int)c.n_heads, a.nkv = (int)c.n_kv_heads, a.hd = m->hd, a.max_seq = m->max_seq;
+        a.eps = c.norm_eps;
+        a.scale = 1.0f / sqrtf((float)m->hd);  // forward.c:143
+        a.err = m->d_err;
+        MCU(launch_dependent(k_attn, dim3(c.n_heads, kAttnSplit), dim3(kAttnThreads), m->attn_smem, s, a));
+        GemvParams o = m->wo_p;
+        o.seg[0].w = tensor(m, mia_layer_tensor(l, kWo));
+        MCU(gemv_launch(o, grid_of(m, o), m->wo_smem, s));
+        launches += 3;
+        if (miag_moe_async(m->moe, l, m->x, 1, s, err, errlen) != 0) return -1;
+        launches += miag_last_launch_count(m->moe);
+    }
+    GemvParams hp = m->head_p;
+    const size_t nt = m->layout.size();  // ..., output_norm, output
+    hp.seg[0].w = tensor(m, nt - 1);
+    hp.norm = tensor_f(m, nt - 2);
+    MCU(gemv_launch(hp, grid_of(m, hp), m->head_smem, s));
+    launches++;
+    m->last_launches = launches;
+    return 0;
+}
+
+int capture(miag_model *m, char *err, size_t errlen) {
+    if (m->exec) {
+        cudaGraphExecDestroy(m->exec);
+        m->exec = nullptr;
+    }
+    const void *ws = ctx_reserve(m->moe, 1, err, errlen);
+    if (!ws) return -1;
+    cudaGraph_t g = nullptr;
+    MCU(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
+    const int rc = enqueue_step(m, m->stream, err, errlen);
+    const cudaError_t e = cudaStreamEndCapture(m->stream, &g);
+    if (rc != 0) {
+        if (g) cudaGraphDestroy(g);
+        return -1;
+    }
+    MCU(e);
+    const cudaError_t ie = cudaGraphInstantiate(&m->exec, g, 0);
+    cudaGraphDestroy(g);
+    MCU(ie);
+    m->graph_ws = ws;
+    return 0;
+}
+
+// Reads and clears the model's error word, then the MoE context's (after a
+// synchronisation of the model's stream).
+int check_errors(miag_model *m, char *err, size_t errlen) {
+    MCU(cudaStreamSynchronize(m->stream));
+    int code = 0;
+    MCU(cudaMemcpy(&code, m->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (code != 0) {
+        MCU(cudaMemset(m->d_err, 0, sizeof(int)));
+        // a step cut short may leave the tickets and the argmax set
+        MCU(cudaMemset(m->tickets, 0, ((size_t)m->cfg.n_heads + 1) * sizeof(unsigned)));
+        MCU(cudaMemset(m->amax, 0, sizeof(unsigned long long)));
+        put_err(err, errlen, "device error %d: %s", code,
+                code == kErrStepArgs ? "a step's token or position was out of range"
+                                     : "a dense matvec timed out waiting for a staged tile");
+        return -1;
+    }
+    return miag_sync(m->moe, m->stream, err, errlen);
+}
+
+// Steps as graph replays; where the capture fails (a driver without
+// programmatic edges in graphs, say) the same sequence is launched directly.
+int launch_steps(miag_model *m, int n, char *err, size_t errlen) {
+    if (!m->eager && (!m->exec || ctx_workspace(m->moe) != m->graph_ws)) {
+        char why[256] = "";
+        if (capture(m, why, sizeof why)) {
+            cudaGetLastError();
+            if (!ctx_reserve(m->moe, 1, err, errlen)) return -1;
+            m->eager = true;
+        }
+    }
+    for (int i = 0; i < n; i++) {
+        if (m->eager) {
+            if (enqueue_step(m, m->stream, err, errlen)) return -1;
+        } else {
+            MCU(cudaGraphLaunch(m->exec, m->stream));
+        }
+    }
+    return 0;
+}
+
+bool shape_matches(const miag_shape &s, const miag_mia_config &c) {
+    return s.dim == (int)c.dim && s.n_layers == (int)c.n_layers && s.n_experts == (int)c.n_experts &&
+           s.n_active == (int)c.n_active && s.expert_hidden == (int)c.expert_hidden &&
+           s.norm_topk == (int)c.norm_topk && s.norm_eps == c.norm_eps;
+}
+
+// Hands the dense section's routers and ffn norms to the MoE context.
+int set_moe_layers(miag_model *m, char *err, size_t errlen) {
+    for (int l = 0; l < (int)m->cfg.n_layers; l++)
+        if (ctx_set_layer_device(m->moe, l, tensor_f(m, mia_layer_tensor(l, kFfnNorm)),
+                                 tensor_f(m, mia_layer_tensor(l, kRouter)), m->stream, err, errlen))
+            return -1;
+    MCU(cudaStreamSynchronize(m->stream));
+    m->dense_set = true;
+    return 0;
+}
+
+}  // namespace
+
+extern "C" void miag_model_close(miag_model *m) {
+    if (!m) return;
+    cudaSetDevice(m->device);
+    if (m->stream) cudaStreamSynchronize(m->stream);
+    if (m->exec) cudaGraphExecDestroy(m->exec);
+    void *bufs[] = {m->dense, m->rope, m->kc, m->vc, m->x, m->qkv, m->att, m->logits, m->scores,
+                    m->args, m->prompt, m->tokens, m->tickets, m->amax, m->d_err};
+    for (void *b : bufs) cudaFree(b);
+    if (m->h_logits) cudaFreeHost(m->h_logits);
+    if (m->h_args) cudaFreeHost(m->h_args);
+    if (m->stream) cudaStreamDestroy(m->stream);
+    if (m->owns_moe) miag_close(m->moe);
+    delete m;
+}
+
+extern "C" int miag_model_open(miag_model **out, miag_ctx *moe, const miag_mia_config *config,
+                               const void *dense, size_t dense_bytes, int max_seq, char *err,
+                               size_t errlen) {
+    if (!out || !moe || !config) {
+        put_err(err, errlen, "null argument");
+        return -1;
+    }
+    *out = nullptr;
+    const miag_mia_config &c = *config;
+    if (!mia_config_ok(c) || c.head_dim % 4 || c.head_dim > 256) {
+        put_err(err, errlen, "unsupported model shape (head_dim a multiple of 4, at most 256)");
+        return -1;
+    }
+    if (!shape_matches(*ctx_shape(moe), c)) {
+        put_err(err, errlen, "the MoE context's shape differs from the model's");
+        return -1;
+    }
+    const int qd = (int)(c.n_heads * c.head_dim);
+    if (c.dim > 8192 || qd > 8192) {
+        put_err(err, errlen, "dim and n_heads * head_dim are limited to 8192");
+        return -1;
+    }
+    if (max_seq <= 0) {
+        put_err(err, errlen, "context length must be positive");
+        return -1;
+    }
+    if (attn_smem_bytes((int)c.head_dim, max_seq) > 227 * 1024) {
+        put_err(err, errlen, "context length %d too long for the attention kernel", max_seq);
+        return -1;
+    }
+    miag_model *m = new miag_model;
+    m->moe = moe;
+    m->cfg = c;
+    m->device = ctx_device(moe);
+    m->num_sms = ctx_num_sms(moe);
+    m->max_seq = max_seq;
+    m->d = (int)c.dim, m->qd = qd, m->hd = (int)c.head_dim, m->kvd = (int)(c.n_kv_heads * c.head_dim);
+    m->layout = mia_dense_layout(c, &m->dense_bytes);
+    if (dense && dense_bytes != m->dense_bytes) {
+        put_err(err, errlen, "dense section of %zu bytes, the layout needs %zu", dense_bytes,
+                m->dense_bytes);
+        delete m;
+        return -1;
+    }
+    auto fail = [&](const char *what, cudaError_t e) {
+        put_err(err, errlen, "%s: %s", what, cudaGetErrorString(e));
+        miag_model_close(m);
+        return -1;
+    };
+    cudaError_t e;
+    if ((e = cudaSetDevice(m->device)) != cudaSuccess) return fail("cudaSetDevice", e);
+    if ((e = cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking)) != cudaSuccess)
+        return fail("cudaStreamCreate", e);
+    const size_t L = c.n_layers, kv = L * (size_t)max_seq * m->kvd;
+    struct {
+        void **p;
+        size_t bytes;
+    } allocs[] = {
+        {(void **)&m->dense, m->dense_bytes + 256},  // tiles read up to 15 bytes past a matrix
+        {(void **)&m->rope, (size_t)max_seq * (m->hd / 2) * sizeof(double2)},
+        {(void **)&m->kc, kv * 4},
+        {(void **)&m->vc, kv * 4},
+        {(void **)&m->x, (size_t)m->d * 4},
+        {(void **)&m->qkv, (size_t)(qd + 2 * m->kvd) * 4},
+        {(void **)&m->att, (size_t)qd * 4},
+        {(void **)&m->logits, (size_t)c.vocab * 4},
+        {(void **)&m->scores, (size_t)c.n_heads * max_seq * 4},
+        {(void **)&m->args, 2 * sizeof(int32_t)},
+        {(void **)&m->prompt, (size_t)max_seq * sizeof(int32_t)},
+        {(void **)&m->tokens, (size_t)max_seq * sizeof(int32_t)},
+        {(void **)&m->tickets, (c.n_heads + 1) * sizeof(unsigned)},
+        {(void **)&m->amax, sizeof(unsigned long long)},
+        {(void **)&m->d_err, sizeof(int)},
+    };
+    for (auto &a : allocs) {
+        if ((e = cudaMalloc(a.p, a.bytes)) != cudaSuccess) return fail("cudaMalloc", e);
+        if ((e = cudaMemsetAsync(*a.p, 0, a.bytes, m->stream)) != cudaSuccess)
+            return fail("cudaMemset", e);
+    }
+    if ((e = cudaMallocHost(&m->h_logits, (size_t)c.vocab * 4)) != cudaSuccess)
+        return fail("cudaMallocHost", e);
+    if ((e = cudaMallocHost(&m->h_args, 2 * sizeof(int32_t))) != cudaSuccess)
+        return fail("cudaMallocHost", e);
+
+    // RoPE table: the reference's own libm calls (forward.c:87-88), here on
+    // the host, so the device rotates with the same cos and sin.
+    {
+        const int half = m->hd / 2;
+        std::vector<double2> tab((size_t)max_seq * half);
+        for (int i = 0; i < half; i++) {
+            const double freq = pow((double)c.rope_theta, -2.0 * i / m->hd);
+            for (int pos = 0; pos < max_seq; pos++) {
+                const double a = pos * freq;
+                tab[(size_t)pos * half + i] = make_double2(cos(a), sin(a));
+            }
+        }
+        if ((e = cudaMemcpyAsync(m->rope, tab.data(), tab.size() * sizeof(double2),
+                                 cudaMemcpyHostToDevice, m->stream)) != cudaSuccess)
+            return fail("rope upload", e);
+        if ((e = cudaStreamSynchronize(m->stream)) != cudaSuccess) return fail("rope upload", e);
+    }
+
+    // Matvec plans (weights bound per layer at launch).
+    GemvParams &q = m->qkv_p;
+    q.nseg = 3;
+    q.seg[0] = {nullptr, m->qkv, qd, 0};
+    q.seg[1] = {nullptr, m->qkv + qd, m->kvd, 0};
+    q.seg[2] = {nullptr, m->qkv + qd + m->kvd, m->kvd, 0};
+    q.in = m->x, q.eps = c.norm_eps, q.err = m->d_err;
+    gemv_plan(q, m->d, m->num_sms, &m->qkv_smem);
+    GemvParams &o = m->wo_p;
+    o.nseg = 1;
+    o.seg[0] = {nullptr, m->x, m->d, 0};
+    o.in = m->att, o.norm = nullptr, o.resid = 1, o.err = m->d_err;
+    gemv_plan(o, qd, m->num_sms, &m->wo_smem);
+    GemvParams &hp = m->head_p;
+    hp.nseg = 1;
+    hp.seg[0] = {nullptr, m->logits, (int)c.vocab, 0};
+    hp.in = m->x, hp.eps = c.norm_eps, hp.err = m->d_err;
+    hp.amax = m->amax, hp.ticket = m->tickets + c.n_heads, hp.args = m->args;
+    hp.prompt = m->prompt, hp.tokens = m->tokens, hp.max_seq = max_seq;
+    gemv_plan(hp, m->d, m->num_sms, &m->head_smem);
+    m->attn_smem = attn_smem_bytes(m->hd, max_seq);
+    {
+        size_t need = m->qkv_smem;
+        need = need > m->wo_smem ? need : m->wo_smem;
+        need = need > m->head_smem ? need : m->head_smem;
+        if ((e = cudaFuncSetAttribute(k_gemv, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)need)) !=
+                cudaSuccess ||
+            (e = cudaFuncSetAttribute(k_attn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)m->attn_smem)) != cudaSuccess)
+            return fail("kernel attributes", e);
+    }
+    *out = m;
+    if (dense) {
+        if ((e = cudaMemcpy(m->dense, dense, dense_bytes, cudaMemcpyHostToDevice)) != cudaSuccess) {
+            *out = nullptr;
+            return fail("dense upload", e);
+        }
+        if (set_moe_layers(m, err, errlen)) {
+            *out = nullptr;
+            miag_model_close(m);
+            return -1;
+        }
+    }
+    return 0;
+}
+
+// The loader port of the file: blob (layer, expert) by pread.
+namespace {
+struct FileSource {
+    FILE *f;
+    uint64_t off, blob, n_experts;
+};
+int file_expert(void *ctx, int layer, int expert, void *dst) {
+    FileSource *s = (FileSource *)ctx;
+    const uint64_t at = s->off + ((uint64_t)layer * s->n_experts + (uint64_t)expert) * s->blob;
+    if (fseeko(s->f, (off_t)at, SEEK_SET) != 0) return -1;
+    return fread(dst, 1, s->blob, s->f) == s->blob ? 0 : -1;
+}
+}  // namespace
+
+extern "C" int miag_model_open_file(miag_model **out, const char *path, int device, int max_seq,
+                                    char *err, size_t errlen) {
+    if (!out || !path) {
+        put_err(err, errlen, "null argument");
+        return -1;
+    }
+    *out = nullptr;
+    FILE *f = fopen(path, "rb");
+    if (!f) {
+        put_err(err, errlen, "open %s failed", path);
+        return -1;
+    }
+    MiaHeader h;
+    if (fread(&h, 1, sizeof h, f) != sizeof h || memcmp(h.magic, "MIA1", 4) != 0 || h.version != 1) {
+        fclose(f);
+        put_err(err, errlen, "%s: not a .mia v1 file", path);
+        return -1;
+    }
+    if (h.wtype != 1) {
+        fclose(f);
+        put_err(err, errlen, "%s: only Q8_0 models run on the GPU", path);
+        return -1;
+    }
+    miag_mia_config c{};
+    c.dim = h.dim, c.n_layers = h.n_layers, c.n_heads = h.n_heads, c.n_kv_heads = h.n_kv_heads;
+    c.head_dim = h.head_dim, c.vocab = h.vocab, c.n_experts = h.n_experts, c.n_active = h.n_active;
+    c.expert_hidden = h.expert_hidden, c.norm_topk = h.norm_topk, c.rope_theta = h.rope_theta;
+    c.norm_eps = h.norm_eps;
+    size_t dense_bytes = 0;
+    if (mia_config_ok(c)) mia_dense_layout(c, &dense_bytes);
+    if (!mia_config_ok(c) || h.dense_size != dense_bytes || h.expert_blob_size != miag_mia_expert_blob_bytes(&c)) {
+        fclose(f);
+        put_err(err, errlen, "%s: layout does not match its header", path);
+        return -1;
+    }
+    std::vector<uint8_t> dense(dense_bytes);
+    if (fseeko(f, (off_t)h.dense_offset, SEEK_SET) != 0 || fread(dense.data(), 1, dense_bytes, f) != dense_bytes) {
+        fclose(f);
+        put_err(err, errlen, "%s: short dense section", path);
+        return -1;
+    }
+    miag_shape s{(int32_t)c.dim, (int32_t)c.n_layers, (int32_t)c.n_experts, (int32_t)c.n_active,
+                 (int32_t)c.expert_hidden, (int32_t)c.norm_topk, c.norm_eps};
+    miag_ctx *ctx = nullptr;
+    if (miag_open(&ctx, &s, device, err, errlen)) {
+        fclose(f);
+        return -1;
+    }
+    FileSource src{f, h.experts_offset, h.expert_blob_size, h.n_experts};
+    miag_model *m = nullptr;
+    if (miag_load_experts(ctx, file_expert, &src, err, errlen) ||
+        miag_model_open(&m, ctx, &c, dense.data(), dense_bytes, max_seq, err, errlen)) {
+        fclose(f);
+        miag_close(ctx);
+        return -1;
+    }
+    fclose(f);
+    m->owns_moe = true;
+    *out = m;
+    return 0;
+}
+
+extern "C" int miag_model_synth(miag_model *m, uint64_t seed, char *err, size_t errlen) {
+    if (!m) {
+        put_err(err, errlen, "null model");
+        return -1;
+    }
+    MCU(cudaSetDevice(m->device));
+    const miag_mia_config &c = m->cfg;
+    const int grid = 4 * m->num_sms;
+    for (size_t i = 0; i < m->layout.size(); i++) {
+        const MiaTensor &t = m->layout[i];
+        uint8_t *p = m->dense + t.offset;
+        const bool is_router = t.name.size() > 6 && t.name.compare(t.name.size() - 6, 6, "router") == 0;
+        if (t.quantized) {
+            k_synth_q8<<<grid, 256, 0, m->stream>>>(p, t.rows * (t.cols / MIAG_QK),
+                                                     sm_key(seed, {kTagDense, i, 0}),
+                                                     sm_key(seed, {kTagDense, i, 1}), 0.02);
+        } else if (is_router) {
+            const int layer = (int)((i - 1) / kMiaLayerTensors);
+            k_synth_f32<<<grid, 256, 0, m->stream>>>((float *)p, t.rows * t.cols,
+                                                      sm_key(seed, {kTagRouter, (uint64_t)layer}),
+                                                      0.02, 0);
+        } else {
+            k_synth_f32<<<grid, 256, 0, m->stream>>>((float *)p, t.rows * t.cols, 0, 0.0, 1);
+        }
+        MCU(cudaGetLastError());
+    }
+    // Experts: .mia blobs generated in device staging, then stored.
+    const miag_shape &s = *ctx_shape(m->moe);
+    const size_t blob = miag_blob_bytes(&s);
+    const size_t nbg = (size_t)c.expert_hidden * (c.dim / MIAG_QK);   // gate / up blocks
+    const size_t nbd = (size_t)c.dim * (c.expert_hidden / MIAG_QK);   // down blocks
+    const size_t off_up = mia_align_up(nbg * 36, kMiaTensorAlign), off_down = 2 * off_up;
+    const int batch = 16;
+    uint8_t *stage = nullptr;
+    MCU(cudaMalloc(&stage, batch * blob));
+    int rc = 0;
+    for (int l = 0; l < (int)c.n_layers && rc == 0; l++)
+        for (int e0 = 0; e0 < (int)c.n_experts && rc == 0; e0 += batch) {
+            const int n = (int)c.n_experts - e0 < batch ? (int)c.n_experts - e0 : batch;
+            for (int k = 0; k < n; k++) {
+                uint8_t *b = stage + (size_t)k * blob;
+                const uint64_t e = (uint64_t)(e0 + k);
+                const size_t offs[3] = {0, off_up, off_down}, nbs[3] = {nbg, nbg, nbd};
+                for (int mat = 0; mat < 3; mat++)
+                    k_synth_q8<<<grid, 256, 0, m->stream>>>(
+                        b + offs[mat], nbs[mat], sm_key(seed, {kTagQw, (uint64_t)l, e, (uint64_t)mat}),
+                        sm_key(seed, {kTagDw, (uint64_t)l, e, (uint64_t)mat}), 0.02);
+            }
+            if (cudaGetLastError() != cudaSuccess ||
+                miag_upload_experts_device(m->moe, l, e0, n, stage, blob, m->stream, err, errlen))
+                rc = -1;
+        }
+    cudaStreamSynchronize(m->stream);
+    cudaFree(stage);
+    if (rc) return -1;
+    MCU(cudaStreamSynchronize(m->stream));
+    return set_moe_layers(m, err, errlen);
+}
+
+extern "C" int miag_model_step_async(miag_model *m, int token, int pos, char *err, size_t errlen) {
+    if (!m || !m->dense_set) {
+        put_err(err, errlen, m ? "the model has no weights (miag_model_synth)" : "null model");
+        return -1;
+    }
+    if (pos < 0 || pos >= m->max_seq || token < 0 || token >= (int)m->cfg.vocab) {  // forward.c:202-203
+        put_err(err, errlen, "token %d at position %d out of range", token, pos);
+        return -1;
+    }
+    MCU(cudaSetDevice(m->device));
+    const int32_t a[2] = {token, pos};
+    MCU(cudaStreamSynchronize(m->stream));  // the pinned arguments are free again
+    memcpy(m->h_args, a, sizeof a);
+    MCU(cudaMemcpyAsync(m->args, m->h_args, sizeof a, cudaMemcpyHostToDevice, m->stream));
+    return launch_steps(m, 1, err, errlen);
+}
+
+extern "C" const float *miag_model_step(miag_model *m, int token, int pos, char *err, size_t errlen) {
+    if (miag_model_step_async(m, token, pos, err, errlen)) return nullptr;
+    if (cudaMemcpyAsync(m->h_logits, m->logits, (size_t)m->cfg.vocab * 4, cudaMemcpyDeviceToHost,
+                        m->stream) != cudaSuccess) {
+        put_err(err, errlen, "logits copy failed");
+        return nullptr;
+    }
+    if (check_errors(m, err, errlen)) return nullptr;
+    return m->h_logits;
+}
+
+extern "C" int miag_model_generate_async(miag_model *m, const int32_t *prompt, int n_prompt,
+                                         int n_new, char *err, size_t errlen) {
+    if (!m || !m->dense_set || !prompt || n_prompt < 1 || n_new < 0 ||
+        (size_t)n_prompt + (size_t)n_new > (size_t)m->max_seq) {
+        put_err(err, errlen, "bad arguments (a prompt of >= 1 token; prompt + new <= context)");
+        return -1;
+    }
+    for (int i = 0; i < n_prompt; i++)
+        if (prompt[i] < 0 || prompt[i] >= (int)m->cfg.vocab) {
+            put_err(err, errlen, "prompt token %d out of range", i);
+            return -1;
+        }
+    MCU(cudaSetDevice(m->device));
+    MCU(cudaStreamSynchronize(m->stream));
+    MCU(cudaMemcpyAsync(m->prompt, prompt, (size_t)n_prompt * 4, cudaMemcpyHostToDevice, m->stream));
+    MCU(cudaMemcpyAsync(m->tokens, prompt, 4, cudaMemcpyHostToDevice, m->stream));
+    m->h_args[0] = prompt[0], m->h_args[1] = 0;
+    MCU(cudaMemcpyAsync(m->args, m->h_args, 8, cudaMemcpyHostToDevice, m->stream));
+    // the head reads n_prompt from its parameters: set it and re-capture
+    if (m->head_p.n_prompt != n_prompt) {
+        m->head_p.n_prompt = n_prompt;
+        if (m->exec) cudaGraphExecDestroy(m->exec);
+        m->exec = nullptr;
+    }
+    const int steps = n_prompt + n_new - 1;
+    return launch_steps(m, steps, err, errlen);
+}
+
+extern "C" int miag_model_continue_async(miag_model *m, int n_steps, char *err, size_t errlen) {
+    if (!m || !m->dense_set || n_steps < 0) {
+        put_err(err, errlen, "bad arguments");
+        return -1;
+    }
+    MCU(cudaSetDevice(m->device));
+    return launch_steps(m, n_steps, err, errlen);
+}
+
+extern "C" int miag_model_generate(miag_model *m, const int32_t *prompt, int n_prompt, int n_new,
+                                   int32_t *tokens_out, char *err, size_t errlen) {
+    if (!tokens_out && n_new > 0) {
+        put_err(err, errlen, "null output");
+        return -1;
+    }
+    if (miag_model_generate_async(m, prompt, n_prompt, n_new, err, errlen)) return -1;
+    if (n_new > 0 && cudaMemcpyAsync(tokens_out, m->tokens + n_prompt, (size_t)n_new * 4,
+                                     cudaMemcpyDeviceToHost, m->stream) != cudaSuccess) {
+        put_err(err, errlen, "token copy failed");
+        return -1;
+    }
+    return check_errors(m, err, errlen);
+}
+
+extern "C" int miag_model_sync(miag_model *m, char *err, size_t errlen) {
+    if (!m) {
+        put_err(err, errlen, "null model");
+        return -1;
+    }
+    MCU(cudaSetDevice(m->device));
+    return check_errors(m, err, errlen);
+}
+
+extern "C" const float *miag_model_logits_device(const miag_model *m) { return m ? m->logits : nullptr; }
+extern "C" const int32_t *miag_model_tokens_device(const miag_model *m) { return m ? m->tokens : nullptr; }
+extern "C" void *miag_model_stream(const miag_model *m) { return m ? (void *)m->stream : nullptr; }
+extern "C" miag_ctx *miag_model_moe(const miag_model *m) { return m ? m->moe : nullptr; }
+extern "C" int miag_model_launches_per_step(const miag_model *m) { return m ? m->last_launches : -1; }
+extern "C" int miag_model_uses_graph(const miag_model *m) { return m && m->exec && !m->eager ? 1 : 0; }

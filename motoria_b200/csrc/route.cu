@@ -25,39 +25,6 @@
 
 namespace miag {
 
-// (float)(1.0 / sqrt(ss / n + eps)) in IEEE double, as forward.c:79.
-__device__ __forceinline__ float rms_scale_of(double ss, int n, float eps) {
-    double q = __dadd_rn(__ddiv_rn(ss, (double)n), (double)eps);
-    return __double2float_rn(__ddiv_rn(1.0, __dsqrt_rn(q)));
-}
-
-// The reference sums x_i^2 serially in double (forward.c:78).  Each square is
-// exact in double and all terms are >= 0, so any summation order lands
-// within (n-1)*2^-53 relative of the exact sum, and so does the reference's.
-// The warp-parallel sum therefore brackets the reference's value; the scale
-// is monotone in the sum, so when both ends of the bracket give the same
-// float the reference's float is that one.  Otherwise (probability ~1e-5)
-// lane 0 repeats the serial sum over x (shared memory).
-__device__ float rms_scale_certified(double ss, const float *x, int n, float eps, int lane) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss = __dadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
-    const double rel = (2.02 * (double)n + 8.0) * 1.1102230246251565e-16;  // 2^-53
-    // lanes 0 and 1 evaluate the two ends of the bracket at the same time
-    const float end = rms_scale_of(ss * (lane == 0 ? 1.0 - rel : 1.0 + rel), n, eps);
-    const float a = __shfl_sync(0xffffffffu, end, 0), b = __shfl_sync(0xffffffffu, end, 1);
-    if (a == b) return a;
-    float r = 0.0f;
-    if (lane == 0) {
-        double s2 = 0.0;
-        for (int i = 0; i < n; i++) {
-            const double v = (double)x[i];
-            s2 = __dadd_rn(s2, __dmul_rn(v, v));
-        }
-        r = rms_scale_of(s2, n, eps);
-    }
-    return __shfl_sync(0xffffffffu, r, 0);
-}
-
 struct RouteParams {
     Dims m;
     LayerDev L;

@@ -2,7 +2,8 @@
 
 Loads ``oracle/lib/libmoe_oracle.so`` (the C restatement, moe_oracle.c) and,
 when it was built, ``oracle/_ref/libmia_ref.so`` (the reference engine's own
-sources driven by ref_harness.c).  Only tests/, the smoke check and the
+sources driven by ref_harness.c) and its diagnostic twin
+``oracle/_ref/libmia_ref_crexp.so`` (the same, with a correctly rounded expf).  Only tests/, the smoke check and the
 cpu_baseline leg of bench.py use this module, always as the checker.
 
 ``build()`` runs ``make -C oracle``; on a machine without the reference tree
@@ -20,6 +21,8 @@ import numpy as np
 HERE = Path(__file__).resolve().parent
 ORACLE_SO = HERE / "lib" / "libmoe_oracle.so"
 REF_SO = HERE / "_ref" / "libmia_ref.so"
+# the same reference build with expf correctly rounded (crexp.h): a diagnostic
+REF_CREXP_SO = HERE / "_ref" / "libmia_ref_crexp.so"
 
 
 class OShape(C.Structure):
@@ -161,8 +164,8 @@ class Oracle(_Lib):
 
 
 class Ref(_Lib):
-    def __init__(self):
-        super().__init__(REF_SO, "ref_")
+    def __init__(self, path: Path = REF_SO):
+        super().__init__(path, "ref_")
 
     def matvec(self, w, wtype, x, rows, cols, scalar=False):
         out = np.zeros(rows, np.float32)
@@ -192,3 +195,14 @@ def ref() -> Ref | None:
     if _ref is None and REF_SO.exists():
         _ref = Ref()
     return _ref
+
+
+_ref_crexp = None
+
+
+def ref_crexp() -> Ref | None:
+    """The reference build with expf correctly rounded, or None."""
+    global _ref_crexp
+    if _ref_crexp is None and REF_CREXP_SO.exists():
+        _ref_crexp = Ref(REF_CREXP_SO)
+    return _ref_crexp

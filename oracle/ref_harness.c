@@ -295,3 +295,42 @@ const void *ref_mia_tensor(void *fp, int l, int which) {
     }
 }
 
+
+/* The reference engine's whole model step (mia_model_step,
+ * src/model/forward.c:199-217) over a .mia file, every expert resident in
+ * its cache (src/storage/expert_cache.c), for the model-level parity tests. */
+typedef struct {
+    mia_file f;
+    mia_expert_cache cache;
+    mia_model m;
+} ref_model;
+
+void *ref_model_open(const char *path, int max_seq, char *err, size_t errlen) {
+    ref_model *r = calloc(1, sizeof(ref_model));
+    if (!r) return NULL;
+    if (mia_file_open(&r->f, path, err, errlen) != 0) {
+        free(r);
+        return NULL;
+    }
+    const int slots = (int)(r->f.h.n_layers * r->f.h.n_experts);
+    if (mia_cache_init(&r->cache, (int)r->f.h.n_layers, (int)r->f.h.n_experts,
+                       r->f.h.expert_blob_size, slots, mia_file_read_expert, &r->f) != 0 ||
+        mia_model_init(&r->m, &r->f, &r->cache, max_seq) != 0) {
+        snprintf(err, errlen, "reference model: out of memory");
+        mia_file_close(&r->f);
+        free(r);
+        return NULL;
+    }
+    return r;
+}
+const float *ref_model_step(void *h, int token, int pos) {
+    return mia_model_step(&((ref_model *)h)->m, token, pos);
+}
+void ref_model_close(void *h) {
+    ref_model *r = (ref_model *)h;
+    if (!r) return;
+    mia_model_free(&r->m);
+    mia_cache_free(&r->cache);
+    mia_file_close(&r->f);
+    free(r);
+}
