@@ -394,6 +394,31 @@ int miag_model_launches_per_step(const miag_model *m);
  * (the capture failed) or no step has run yet. */
 int miag_model_uses_graph(const miag_model *m);
 
+/* Batched prefill.  Replaces the reference's prompt loop, one
+ * mia_model_step per prompt token (src/app/main.c:119-124,
+ * src/app/serve.c:92-107), with one pass per layer over all n positions:
+ * each dense weight tile is staged once for 32 positions, the MoE block runs
+ * once per layer over the n tokens (the prefill-regime expert kernels), and
+ * the LM head runs for the last position only.  Every position's arithmetic
+ * is mia_model_step's, so the KV cache and the logits of position pos + n - 1
+ * (miag_model_logits_device) equal those of n single steps bit for bit.
+ * The head also picks the next token (greedy: argmax, lowest index on ties)
+ * into miag_model_tokens_device()[pos + n] and leaves the step arguments at
+ * (that token, pos + n), so miag_model_continue_async generates from there.
+ * Enqueues only; errors of the launches surface at miag_model_sync.
+ * miag_model_generate* run their prompt this way when it has more than one
+ * token, unless miag_model_set_batched_prefill(m, 0) asks for one step per
+ * position.  miag_model_prefill waits and returns the last position's
+ * logits in host memory owned by the model, or NULL with a message, as
+ * miag_model_step.  miag_model_prefill_launches: kernels the last prefill
+ * launched. */
+const float *miag_model_prefill(miag_model *m, const int32_t *tokens, int n, int pos, char *err,
+                                size_t errlen);
+int miag_model_prefill_async(miag_model *m, const int32_t *tokens, int n, int pos, char *err,
+                             size_t errlen);
+int miag_model_set_batched_prefill(miag_model *m, int on);
+int miag_model_prefill_launches(const miag_model *m);
+
 /* Per-kernel timing (no reference counterpart; the reference only has
  * wall-clock stats, src/app/main.c:146-158).  While enabled, every kernel of
  * the block is bracketed by CUDA events on the stream it is launched on.

@@ -121,6 +121,12 @@ SIGNATURES = {
     "miag_model_moe": (C.c_void_p, [C.c_void_p]),
     "miag_model_launches_per_step": (C.c_int, [C.c_void_p]),
     "miag_model_uses_graph": (C.c_int, [C.c_void_p]),
+    "miag_model_prefill_async": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_char_p,
+                                           C.c_size_t]),
+    "miag_model_prefill": (C.c_void_p, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_char_p,
+                                         C.c_size_t]),
+    "miag_model_set_batched_prefill": (C.c_int, [C.c_void_p, C.c_int]),
+    "miag_model_prefill_launches": (C.c_int, [C.c_void_p]),
     "miag_profile": (C.c_int, [C.c_void_p, C.c_int]),
     "miag_profile_stages": (C.c_int, []),
     "miag_profile_stage_name": (C.c_char_p, [C.c_int]),

@@ -29,6 +29,7 @@
 //     serial float sum, serial accumulation over positions per dimension.
 // The serial orders are kept where the reference's rounding depends on
 // them; the parallelism is across heads, positions, dimensions and rows.
+#include <algorithm>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -618,6 +619,293 @@ __global__ void k_synth_f32(float *dst, size_t n, uint64_t k, double sigma, int 
         dst[i] = ones ? 1.0f : (float)(sm_normal(k, i) * sigma);
 }
 
+// ---------------------------------------------------------------------------
+// Batched prefill: the positions pos0 .. pos0 + n - 1 of a prompt in one pass
+// per layer.  The reference prefills one position per mia_model_step
+// (src/app/main.c:119-124, serve.c:92-107); here every position's
+// arithmetic is still that step's, operation for operation (the same
+// kernels' arithmetic as the one-position path above), so the KV cache and
+// the last position's logits equal those of n single steps bit for bit.
+// What changes is the order of work: each dense weight tile is staged once
+// for 32 positions, the MoE block runs once per layer over all n tokens (the
+// grouped expert kernels of the prefill regime), and the head runs for the
+// last position only.
+
+constexpr int kPfTok = 32;       // positions per token tile: a lane each
+constexpr int kPfThreads = 256;  // 8 warps: rows of the weight tile
+constexpr int kPfAttnThreads = 256;
+
+// Bytes per position of the quantized inputs: the int8 values [cols], then
+// the block scales [cols / 32] f32, padded to an odd number of 16-byte units
+// so that the 16-byte loads of consecutive positions fall in distinct banks.
+__host__ __device__ inline int pf_pitch(int cols) {
+    int p = (cols + cols / MIAG_QK * 4 + 15) & ~15;
+    if (((p >> 4) & 1) == 0) p += 16;
+    return p;
+}
+
+// Rows of a weight tile: as many as fit beside one token tile of inputs.
+__host__ inline int pf_tile_rows(int cols) {
+    const int row_bytes = cols / MIAG_QK * 36;
+    const size_t budget = 200 * 1024 - (size_t)kPfTok * pf_pitch(cols);
+    int R = (int)(budget / row_bytes) & ~7;
+    return R < 8 ? 8 : R > 16 ? 16 : R;  // 16 rows: two CTAs an SM at 2048 columns
+}
+
+__host__ inline size_t pf_gemv_smem(int cols, int R) {
+    return (((size_t)R * (cols / MIAG_QK * 36) + 15) & ~(size_t)15) + (size_t)kPfTok * pf_pitch(cols) + 16;
+}
+
+// x[t] = dequant(token_embd[tokens[t]]) (forward.c:205-208, quant.c:29-38).
+__global__ void k_pf_embed(float *x, const uint8_t *embd, const int32_t *tokens, int d, int vocab,
+                           int *err) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int t = blockIdx.x, token = tokens[t];
+    if (token < 0 || token >= vocab) {
+        if (threadIdx.x == 0) set_error(err, kErrStepArgs);
+        return;
+    }
+    const uint8_t *row = embd + (size_t)token * (size_t)(d / MIAG_QK) * 36;
+    for (int i = threadIdx.x; i < d; i += blockDim.x) {
+        const uint8_t *blk = row + (size_t)(i / MIAG_QK) * 36;
+        x[(size_t)t * d + i] = __fmul_rn(*reinterpret_cast<const float *>(blk), (float)(int8_t)blk[4 + i % MIAG_QK]);
+    }
+}
+
+// One position's matvec input, as k_gemv prepares it: rmsnorm with `norm`
+// (forward.c:75-81, the certified scale) when given, then mia_quantize_row_q8
+// (quant.c:11-27) into xq[t]: int8 [cols], scales [cols / 32].  Grid: n.
+__global__ void __launch_bounds__(kPfThreads) k_pf_quant(const float *in, int in_stride, const float *norm,
+                                                         float eps, int cols, uint8_t *xq, int pitch) {
+    extern __shared__ __align__(16) float xin[];  // [cols]
+    __shared__ double red[kPfThreads / 32];
+    __shared__ float s_inv;
+    pdl_launch_dependents();
+    pdl_wait();
+    const int t = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const float *src = in + (size_t)t * in_stride;
+    double ss = 0.0;
+    for (int i = tid; i < cols; i += kPfThreads) {
+        const float v = src[i];
+        xin[i] = v;
+        ss = __dadd_rn(ss, __dmul_rn((double)v, (double)v));
+    }
+    if (norm) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss = __dadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+        if (lane == 0) red[warp] = ss;
+        __syncthreads();
+        if (warp == 0) {
+            const float inv = rms_scale_certified(lane < kPfThreads / 32 ? red[lane] : 0.0, xin, cols, eps, lane);
+            if (lane == 0) s_inv = inv;
+        }
+        __syncthreads();
+        const float inv = s_inv;
+        for (int i = tid; i < cols; i += kPfThreads) xin[i] = __fmul_rn(__fmul_rn(xin[i], inv), norm[i]);
+    }
+    __syncthreads();
+    uint8_t *dst = xq + (size_t)t * pitch;
+    const int nb = cols / MIAG_QK;
+    for (int b = warp; b < nb; b += kPfThreads / 32) {
+        const float v = xin[b * MIAG_QK + lane];
+        float a = fabsf(v);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+        const float dq = __fdiv_rn(a, 127.0f);
+        const float id = dq != 0.0f ? __fdiv_rn(1.0f, dq) : 0.0f;
+        dst[b * MIAG_QK + lane] = (uint8_t)(int8_t)roundf(__fmul_rn(v, id));
+        if (lane == 0) reinterpret_cast<float *>(dst + cols)[b] = dq;
+    }
+}
+
+struct PfGemvParams {
+    const uint8_t *w;   // [rows][cols / 32] 36-byte Q8_0 blocks (the file's layout)
+    int rows, cols, R;  // R rows per tile
+    const uint8_t *xq;  // [n][pitch] (k_pf_quant)
+    int pitch, n;
+    float *out;         // out[t * out_stride + r]
+    int out_stride, resid;
+    int *err;
+};
+
+// out[t][r] (+)= the Q8_0 dot of weight row r with position t's input: per
+// 32-block the exact int32 dot, ((float)dot * w.d) * x.d, added in block
+// order (matmul.c:19-28), each operation rounded on its own.  Grid (row
+// tiles, token tiles); a CTA stages its R weight rows and 32 positions'
+// inputs with two bulk copies, then warp w computes rows w, w + 8, ... for
+// the 32 positions, a lane a position.
+__global__ void __launch_bounds__(kPfThreads) k_pf_gemv(const __grid_constant__ PfGemvParams p) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int nb = p.cols / MIAG_QK, row_bytes = nb * 36;
+    uint8_t *wt = smem;
+    uint8_t *xt = smem + (((size_t)p.R * row_bytes + 15) & ~(size_t)15);
+    uint64_t *bar = reinterpret_cast<uint64_t *>(xt + (size_t)kPfTok * p.pitch);
+    const int r0 = blockIdx.x * p.R, t0 = blockIdx.y * kPfTok;
+    const int nr = min(p.R, p.rows - r0), nt = min(kPfTok, p.n - t0);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    // a ragged last tile may read up to 15 bytes past the matrix (the dense
+    // section is allocated with slack for that, as for k_gemv)
+    const uint32_t wbytes = ((uint32_t)(nr * row_bytes) + 15u) & ~15u, xbytes = (uint32_t)(nt * p.pitch);
+    if (tid == 0) {
+        mbar_init(bar, 1);
+        fence_barrier_init();
+        mbar_arrive_expect_tx(bar, wbytes + xbytes);
+        bulk_g2s(wt, p.w + (size_t)r0 * row_bytes, wbytes, bar);  // weights: constant
+    }
+    pdl_launch_dependents();
+    pdl_wait();  // the inputs (and, for a residual, the outputs) of earlier launches
+    if (tid == 0) bulk_g2s(xt, p.xq + (size_t)t0 * p.pitch, xbytes, bar);
+    __syncthreads();
+    if (!mbar_wait(bar, 0)) {
+        set_error(p.err, kErrModelWait);
+        if (tid == 0) mbar_wait(bar, 0);  // nothing may land after the CTA leaves
+        return;
+    }
+    if (lane >= nt) return;
+    const uint32_t xa = smem_addr(xt) + (uint32_t)(lane * p.pitch);
+    const uint32_t xsa = xa + (uint32_t)p.cols;
+    float *out = p.out + (size_t)(t0 + lane) * p.out_stride + r0;
+    for (int r = warp; r < nr; r += kPfThreads / 32) {
+        const uint32_t wa = smem_addr(wt) + (uint32_t)(r * row_bytes);
+        float s = 0.0f;
+        for (int b = 0; b < nb; b++) {
+            const uint32_t wb = wa + (uint32_t)(b * 36);
+            int4 xv0, xv1;
+            asm volatile("ld.shared.v4.s32 {%0, %1, %2, %3}, [%4];"
+                         : "=r"(xv0.x), "=r"(xv0.y), "=r"(xv0.z), "=r"(xv0.w) : "r"(xa + (uint32_t)(b * 32)));
+            asm volatile("ld.shared.v4.s32 {%0, %1, %2, %3}, [%4];"
+                         : "=r"(xv1.x), "=r"(xv1.y), "=r"(xv1.z), "=r"(xv1.w) : "r"(xa + (uint32_t)(b * 32 + 16)));
+            int acc = 0;
+            acc = __dp4a((int)lds_u32(wb + 4u), xv0.x, acc);
+            acc = __dp4a((int)lds_u32(wb + 8u), xv0.y, acc);
+            acc = __dp4a((int)lds_u32(wb + 12u), xv0.z, acc);
+            acc = __dp4a((int)lds_u32(wb + 16u), xv0.w, acc);
+            acc = __dp4a((int)lds_u32(wb + 20u), xv1.x, acc);
+            acc = __dp4a((int)lds_u32(wb + 24u), xv1.y, acc);
+            acc = __dp4a((int)lds_u32(wb + 28u), xv1.z, acc);
+            acc = __dp4a((int)lds_u32(wb + 32u), xv1.w, acc);
+            s = __fadd_rn(s, __fmul_rn(__fmul_rn(__int2float_rn(acc), lds32(wb)), lds32(xsa + 4u * b)));
+        }
+        out[r] = p.resid ? __fadd_rn(out[r], s) : s;
+    }
+}
+
+struct PfQkParams {
+    const float *qkv;  // [n][qd + 2 kvd]
+    const float *q_norm, *k_norm;
+    const double2 *rope;
+    float *q;          // [n][qd] normalised and rotated
+    float *kc, *vc;    // this layer's cache, [max_seq][kvd]
+    int nh, nkv, hd, pos0;
+    float eps;
+};
+
+// Per position: q and k head rmsnorm + NeoX RoPE (forward.c:127-136, the
+// arithmetic of head_norm_rope), k and v into the cache at pos0 + t
+// (:139-140).  Grid (n, n_heads + n_kv_heads), one warp.
+__global__ void k_pf_qk(const __grid_constant__ PfQkParams p) {
+    extern __shared__ __align__(16) float tmp[];  // [hd]
+    pdl_launch_dependents();
+    pdl_wait();
+    const int t = blockIdx.x, h = blockIdx.y, lane = threadIdx.x;
+    const int qd = p.nh * p.hd, kvd = p.nkv * p.hd, pos = p.pos0 + t;
+    const float *row = p.qkv + (size_t)t * (qd + 2 * kvd);
+    const double2 *cs = p.rope + (size_t)pos * (p.hd / 2);
+    if (h < p.nh) {
+        head_norm_rope(row + (size_t)h * p.hd, p.q_norm, p.q + (size_t)t * qd + (size_t)h * p.hd, tmp, p.hd,
+                       p.eps, cs, lane);
+    } else {
+        const int j = h - p.nh;
+        head_norm_rope(row + qd + (size_t)j * p.hd, p.k_norm, p.kc + (size_t)pos * kvd + (size_t)j * p.hd, tmp,
+                       p.hd, p.eps, cs, lane);
+        for (int i = lane; i < p.hd; i += 32)
+            p.vc[(size_t)pos * kvd + (size_t)j * p.hd + i] = row[qd + kvd + (size_t)j * p.hd + i];
+    }
+}
+
+struct PfAttnParams {
+    const float *q;            // [n][qd]
+    const float *kc, *vc;      // this layer's cache
+    float *att;                // [n][qd]
+    int nh, nkv, hd, pos0, max_seq;
+    float scale;
+};
+
+// Attention of position pos0 + t, head h, over positions 0 .. pos0 + t
+// (forward.c:142-161), the arithmetic of k_attn: serial float dot per
+// position, then * scale; max; exp; the serial sum; the division; the
+// accumulation over positions in order, a thread a dimension.  Grid
+// (n_heads, n).
+__global__ void __launch_bounds__(kPfAttnThreads) k_pf_attn(const __grid_constant__ PfAttnParams p) {
+    extern __shared__ __align__(16) float fsh[];
+    const int hd = p.hd, kvd = p.nkv * hd, qd = p.nh * hd, group = p.nh / p.nkv;
+    float *qs = fsh;                  // [hd]
+    float *prob = qs + hd;             // [max_seq]
+    __shared__ float red[kPfAttnThreads / 32];
+    __shared__ float s_val;
+    pdl_launch_dependents();
+    pdl_wait();
+    const int h = blockIdx.x, t = blockIdx.y, kvh = h / group, tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
+    const int n = p.pos0 + t + 1;
+    for (int i = tid; i < hd; i += kPfAttnThreads) qs[i] = p.q[(size_t)t * qd + (size_t)h * hd + i];
+    __syncthreads();
+    const float *kbase = p.kc + (size_t)kvh * hd;
+    float mx = -INFINITY;
+    for (int j = tid; j < n; j += kPfAttnThreads) {
+        const float *kr = kbase + (size_t)j * kvd;
+        float d = 0.0f;
+        for (int i = 0; i < hd; i += 4) {
+            const float4 k4 = *reinterpret_cast<const float4 *>(kr + i);
+            d = __fadd_rn(d, __fmul_rn(qs[i], k4.x));
+            d = __fadd_rn(d, __fmul_rn(qs[i + 1], k4.y));
+            d = __fadd_rn(d, __fmul_rn(qs[i + 2], k4.z));
+            d = __fadd_rn(d, __fmul_rn(qs[i + 3], k4.w));
+        }
+        const float v = __fmul_rn(d, p.scale);
+        prob[j] = v;
+        mx = fmaxf(mx, v);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) red[warp] = mx;
+    __syncthreads();
+    if (tid == 0) {
+        float m = red[0];
+        for (int w = 1; w < kPfAttnThreads / 32; w++) m = fmaxf(m, red[w]);
+        s_val = m;
+    }
+    __syncthreads();
+    mx = s_val;
+    for (int j = tid; j < n; j += kPfAttnThreads) prob[j] = expf_cr(__fsub_rn(prob[j], mx));
+    __syncthreads();
+    if (tid == 0) {
+        float sum = 0.0f;
+#pragma unroll 8
+        for (int j = 0; j < n; j++) sum = __fadd_rn(sum, prob[j]);
+        s_val = sum;
+    }
+    __syncthreads();
+    const float sum = s_val;
+    for (int j = tid; j < n; j += kPfAttnThreads) prob[j] = __fdiv_rn(prob[j], sum);
+    __syncthreads();
+    for (int i = tid; i < hd; i += kPfAttnThreads) {
+        const float *vb = p.vc + (size_t)kvh * hd + i;
+        float acc = 0.0f;
+        int j = 0;
+        for (; j + 8 <= n; j += 8) {  // eight loads in flight, the adds in order
+            float v[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) v[u] = vb[(size_t)(j + u) * kvd];
+#pragma unroll
+            for (int u = 0; u < 8; u++) acc = __fadd_rn(acc, __fmul_rn(prob[j + u], v[u]));
+        }
+        for (; j < n; j++) acc = __fadd_rn(acc, __fmul_rn(prob[j], vb[(size_t)j * kvd]));
+        p.att[(size_t)t * qd + (size_t)h * hd + i] = acc;
+    }
+}
+
 }  // namespace
 }  // namespace miag
 
@@ -650,6 +938,13 @@ struct miag_model {
     bool dense_set = false;
     bool eager = false;  // the step could not be captured: launched directly
     int last_launches = 0;
+    // batched prefill (miag_model_prefill_async): buffers for pf_cap positions
+    bool batched_prefill = true;
+    int pf_cap = 0, pf_last_launches = 0;
+    float *pf_x = nullptr, *pf_qkv = nullptr, *pf_q = nullptr, *pf_att = nullptr;
+    uint8_t *pf_xq = nullptr;
+    int32_t *pf_tok = nullptr;
+    int32_t *h_pf_tok = nullptr;  // pinned, pf_cap entries
 };
 
 namespace {
@@ -837,6 +1132,10 @@ extern "C" void miag_model_close(miag_model *m) {
     void *bufs[] = {m->dense, m->rope, m->kc, m->vc, m->x, m->qkv, m->att, m->logits, m->scores,
                     m->args, m->prompt, m->tokens, m->tickets, m->amax, m->d_err};
     for (void *b : bufs) cudaFree(b);
+    for (void *b : {(void *)m->pf_x, (void *)m->pf_qkv, (void *)m->pf_q, (void *)m->pf_att,
+                    (void *)m->pf_xq, (void *)m->pf_tok})
+        if (b) cudaFree(b);
+    if (m->h_pf_tok) cudaFreeHost(m->h_pf_tok);
     if (m->h_logits) cudaFreeHost(m->h_logits);
     if (m->h_args) cudaFreeHost(m->h_args);
     if (m->stream) cudaStreamDestroy(m->stream);
@@ -1127,6 +1426,172 @@ extern "C" int miag_model_synth(miag_model *m, uint64_t seed, char *err, size_t 
     return set_moe_layers(m, err, errlen);
 }
 
+// ---- batched prefill
+
+namespace {
+
+// Buffers for n positions (grown, never shrunk), and the MoE workspace for n
+// tokens, reserved here while the model's stream is idle: a workspace grown
+// by the MoE call itself would be freed under launches still queued on it.
+int ensure_prefill(miag_model *m, int n, char *err, size_t errlen) {
+    if (!ctx_reserve(m->moe, n, err, errlen)) return -1;
+    if (n <= m->pf_cap) return 0;
+    int cap = m->pf_cap ? m->pf_cap : 64;
+    while (cap < n) cap *= 2;
+    if (cap > m->max_seq) cap = m->max_seq;
+    for (void *b : {(void *)m->pf_x, (void *)m->pf_qkv, (void *)m->pf_q, (void *)m->pf_att,
+                    (void *)m->pf_xq, (void *)m->pf_tok})
+        if (b) cudaFree(b);
+    if (m->h_pf_tok) cudaFreeHost(m->h_pf_tok);
+    m->pf_x = m->pf_qkv = m->pf_q = m->pf_att = nullptr;
+    m->pf_xq = nullptr, m->pf_tok = nullptr, m->h_pf_tok = nullptr;
+    m->pf_cap = 0;
+    const size_t pitch = (size_t)(pf_pitch(m->d) > pf_pitch(m->qd) ? pf_pitch(m->d) : pf_pitch(m->qd));
+    struct {
+        void **p;
+        size_t bytes;
+    } allocs[] = {
+        {(void **)&m->pf_x, (size_t)cap * m->d * 4},
+        {(void **)&m->pf_qkv, (size_t)cap * (m->qd + 2 * m->kvd) * 4},
+        {(void **)&m->pf_q, (size_t)cap * m->qd * 4},
+        {(void **)&m->pf_att, (size_t)cap * m->qd * 4},
+        {(void **)&m->pf_xq, (size_t)cap * pitch},
+        {(void **)&m->pf_tok, (size_t)cap * 4},
+    };
+    for (auto &a : allocs) MCU(cudaMalloc(a.p, a.bytes));
+    MCU(cudaMallocHost(&m->h_pf_tok, (size_t)cap * 4));
+    const size_t gsm = std::max(pf_gemv_smem(m->d, pf_tile_rows(m->d)), pf_gemv_smem(m->qd, pf_tile_rows(m->qd)));
+    MCU(cudaFuncSetAttribute(k_pf_gemv, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gsm));
+    MCU(cudaFuncSetAttribute(k_pf_attn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)((m->hd + m->max_seq) * 4)));
+    MCU(cudaFuncSetAttribute(k_pf_quant, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)((m->d > m->qd ? m->d : m->qd) * 4)));
+    m->pf_cap = cap;
+    return 0;
+}
+
+int pf_gemv(miag_model *m, const uint8_t *w, int rows, int cols, float *out, int out_stride, int resid,
+            int n, cudaStream_t s, char *err, size_t errlen) {
+    PfGemvParams g{};
+    g.w = w, g.rows = rows, g.cols = cols, g.R = pf_tile_rows(cols);
+    g.xq = m->pf_xq, g.pitch = pf_pitch(cols), g.n = n;
+    g.out = out, g.out_stride = out_stride, g.resid = resid, g.err = m->d_err;
+    const dim3 grid((unsigned)((rows + g.R - 1) / g.R), (unsigned)((n + kPfTok - 1) / kPfTok));
+    MCU(launch_dependent(k_pf_gemv, grid, dim3(kPfThreads), pf_gemv_smem(cols, g.R), s, g));
+    return 0;
+}
+
+// The launch sequence of a prefill of n positions from pos0 (tokens in
+// pf_tok): per layer 8 launches and the MoE block's, then the head.
+int enqueue_prefill(miag_model *m, int n, int pos0, cudaStream_t s, char *err, size_t errlen) {
+    const miag_mia_config &c = m->cfg;
+    const int d = m->d, qd = m->qd, kvd = m->kvd, hd = m->hd, qkv_w = qd + 2 * kvd;
+    int launches = 0;
+    MCU(launch_dependent(k_pf_embed, dim3((unsigned)n), dim3(256), 0, s, m->pf_x, tensor(m, 0),
+                         (const int32_t *)m->pf_tok, d, (int)c.vocab, m->d_err));
+    launches++;
+    for (int l = 0; l < (int)c.n_layers; l++) {
+        MCU(launch_dependent(k_pf_quant, dim3((unsigned)n), dim3(kPfThreads), (size_t)d * 4, s,
+                             (const float *)m->pf_x, d, tensor_f(m, mia_layer_tensor(l, kAttnNorm)),
+                             c.norm_eps, d, m->pf_xq, pf_pitch(d)));
+        if (pf_gemv(m, tensor(m, mia_layer_tensor(l, kWq)), qd, d, m->pf_qkv, qkv_w, 0, n, s, err, errlen) ||
+            pf_gemv(m, tensor(m, mia_layer_tensor(l, kWk)), kvd, d, m->pf_qkv + qd, qkv_w, 0, n, s, err,
+                    errlen) ||
+            pf_gemv(m, tensor(m, mia_layer_tensor(l, kWv)), kvd, d, m->pf_qkv + qd + kvd, qkv_w, 0, n, s, err,
+                    errlen))
+            return -1;
+        const size_t layer_off = (size_t)l * m->max_seq * kvd;
+        PfQkParams qk{};
+        qk.qkv = m->pf_qkv;
+        qk.q_norm = tensor_f(m, mia_layer_tensor(l, kQNorm));
+        qk.k_norm = tensor_f(m, mia_layer_tensor(l, kKNorm));
+        qk.rope = m->rope, qk.q = m->pf_q;
+        qk.kc = m->kc + layer_off, qk.vc = m->vc + layer_off;
+        qk.nh = (int)c.n_heads, qk.nkv = (int)c.n_kv_heads, qk.hd = hd, qk.pos0 = pos0;
+        qk.eps = c.norm_eps;
+        MCU(launch_dependent(k_pf_qk, dim3((unsigned)n, c.n_heads + c.n_kv_heads), dim3(32), (size_t)hd * 4, s,
+                             qk));
+        PfAttnParams at{};
+        at.q = m->pf_q, at.kc = m->kc + layer_off, at.vc = m->vc + layer_off, at.att = m->pf_att;
+        at.nh = (int)c.n_heads, at.nkv = (int)c.n_kv_heads, at.hd = hd, at.pos0 = pos0, at.max_seq = m->max_seq;
+        at.scale = 1.0f / sqrtf((float)hd);  // forward.c:143
+        MCU(launch_dependent(k_pf_attn, dim3(c.n_heads, (unsigned)n), dim3(kPfAttnThreads),
+                             (size_t)(hd + pos0 + n) * 4, s, at));
+        MCU(launch_dependent(k_pf_quant, dim3((unsigned)n), dim3(kPfThreads), (size_t)qd * 4, s,
+                             (const float *)m->pf_att, qd, (const float *)nullptr, c.norm_eps, qd, m->pf_xq,
+                             pf_pitch(qd)));
+        if (pf_gemv(m, tensor(m, mia_layer_tensor(l, kWo)), d, qd, m->pf_x, d, 1, n, s, err, errlen)) return -1;
+        launches += 8;
+        if (miag_moe_async(m->moe, l, m->pf_x, n, s, err, errlen) != 0) return -1;
+        launches += miag_last_launch_count(m->moe);
+    }
+    GemvParams hp = m->head_p;
+    const size_t nt = m->layout.size();
+    hp.seg[0].w = tensor(m, nt - 1);
+    hp.norm = tensor_f(m, nt - 2);
+    hp.in = m->pf_x + (size_t)(n - 1) * d;
+    MCU(gemv_launch(hp, grid_of(m, hp), m->head_smem, s));
+    launches++;
+    m->pf_last_launches = launches;
+    return 0;
+}
+
+// Checks and stages a prefill of tokens[0 .. n) at positions pos0 .. :
+// the tokens into pf_tok and the sequence record, the step arguments as the
+// one-position path leaves them before the last position's head.
+int stage_prefill(miag_model *m, const int32_t *tokens, int n, int pos0, char *err, size_t errlen) {
+    if (!m || !m->dense_set) {
+        put_err(err, errlen, m ? "the model has no weights (miag_model_synth)" : "null model");
+        return -1;
+    }
+    if (!tokens || n < 1 || pos0 < 0 || (size_t)pos0 + (size_t)n > (size_t)m->max_seq) {
+        put_err(err, errlen, "bad prefill: %d tokens from position %d (context %d)", n, pos0, m->max_seq);
+        return -1;
+    }
+    for (int i = 0; i < n; i++)
+        if (tokens[i] < 0 || tokens[i] >= (int)m->cfg.vocab) {
+            put_err(err, errlen, "prompt token %d out of range", i);
+            return -1;
+        }
+    MCU(cudaSetDevice(m->device));
+    MCU(cudaStreamSynchronize(m->stream));  // pinned staging free; no launch uses the workspace
+    if (ensure_prefill(m, n, err, errlen)) return -1;
+    memcpy(m->h_pf_tok, tokens, (size_t)n * 4);
+    MCU(cudaMemcpyAsync(m->pf_tok, m->h_pf_tok, (size_t)n * 4, cudaMemcpyHostToDevice, m->stream));
+    MCU(cudaMemcpyAsync(m->tokens + pos0, m->pf_tok, (size_t)n * 4, cudaMemcpyDeviceToDevice, m->stream));
+    m->h_args[0] = tokens[n - 1], m->h_args[1] = pos0 + n - 1;
+    MCU(cudaMemcpyAsync(m->args, m->h_args, 8, cudaMemcpyHostToDevice, m->stream));
+    return 0;
+}
+
+}  // namespace
+
+extern "C" int miag_model_prefill_async(miag_model *m, const int32_t *tokens, int n, int pos, char *err,
+                                        size_t errlen) {
+    if (stage_prefill(m, tokens, n, pos, err, errlen)) return -1;
+    return enqueue_prefill(m, n, pos, m->stream, err, errlen);
+}
+
+extern "C" const float *miag_model_prefill(miag_model *m, const int32_t *tokens, int n, int pos, char *err,
+                                           size_t errlen) {
+    if (miag_model_prefill_async(m, tokens, n, pos, err, errlen)) return nullptr;
+    if (cudaMemcpyAsync(m->h_logits, m->logits, (size_t)m->cfg.vocab * 4, cudaMemcpyDeviceToHost,
+                        m->stream) != cudaSuccess) {
+        put_err(err, errlen, "logits copy failed");
+        return nullptr;
+    }
+    if (check_errors(m, err, errlen)) return nullptr;
+    return m->h_logits;
+}
+
+extern "C" int miag_model_set_batched_prefill(miag_model *m, int on) {
+    if (!m) return -1;
+    m->batched_prefill = on != 0;
+    return 0;
+}
+
+extern "C" int miag_model_prefill_launches(const miag_model *m) { return m ? m->pf_last_launches : -1; }
+
 extern "C" int miag_model_step_async(miag_model *m, int token, int pos, char *err, size_t errlen) {
     if (!m || !m->dense_set) {
         put_err(err, errlen, m ? "the model has no weights (miag_model_synth)" : "null model");
@@ -1178,6 +1643,14 @@ extern "C" int miag_model_generate_async(miag_model *m, const int32_t *prompt, i
         m->head_p.n_prompt = n_prompt;
         if (m->exec) cudaGraphExecDestroy(m->exec);
         m->exec = nullptr;
+    }
+    if (m->batched_prefill && n_prompt > 1) {
+        // the prompt in one batched pass: its head leaves the first new
+        // token and the position n_prompt in the step arguments
+        if (stage_prefill(m, prompt, n_prompt, 0, err, errlen) ||
+            enqueue_prefill(m, n_prompt, 0, m->stream, err, errlen))
+            return -1;
+        return launch_steps(m, n_new > 0 ? n_new - 1 : 0, err, errlen);
     }
     const int steps = n_prompt + n_new - 1;
     return launch_steps(m, steps, err, errlen);

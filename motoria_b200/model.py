@@ -117,6 +117,32 @@ class Model:
         err = N.errbuf()
         N.check(N.lib().miag_model_sync(self._m, err, len(err)), err, "miag_model_sync")
 
+    def prefill_async(self, tokens, pos: int = 0) -> None:
+        """Positions pos .. pos + len(tokens) - 1 in one batched pass; the
+        last position's logits and the next (greedy) token stay on the
+        device (miag_model_prefill_async)."""
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        err = N.errbuf()
+        N.check(N.lib().miag_model_prefill_async(self._m, t.ctypes.data, t.size, int(pos), err,
+                                                 len(err)), err, "miag_model_prefill_async")
+
+    def prefill(self, tokens, pos: int = 0) -> np.ndarray:
+        """The positions in one batched pass; the last position's logits
+        [vocab] (a copy), as miag_model_step returns one position's."""
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        err = N.errbuf()
+        p = N.lib().miag_model_prefill(self._m, t.ctypes.data, t.size, int(pos), err, len(err))
+        if not p:
+            raise N.MiagError(f"miag_model_prefill: {err.value.decode(errors='replace')}")
+        return np.ctypeslib.as_array(C.cast(p, C.POINTER(C.c_float)), (self.vocab,)).copy()
+
+    def set_batched_prefill(self, on: bool) -> None:
+        N.lib().miag_model_set_batched_prefill(self._m, int(bool(on)))
+
+    @property
+    def prefill_launches(self) -> int:
+        return N.lib().miag_model_prefill_launches(self._m)
+
     @property
     def stream(self) -> int:
         return N.lib().miag_model_stream(self._m) or 0

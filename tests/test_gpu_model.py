@@ -153,6 +153,64 @@ def test_greedy_generation_equals_the_reference_loop(models):
     assert got.tolist() == want
 
 
+PREFILL = {"tiny": (70, 37), "qwen_heads": (33, 5)}  # prompt length, second chunk
+
+
+def test_prefill_equals_single_steps(models):
+    """A prompt in one batched pass (miag_model_prefill) leaves the logits of
+    its last position, and the KV cache the next steps read, equal bit for
+    bit to the reference's one step per position; a second chunk prefilled
+    from a later position likewise."""
+    name, case, cfg, _, ref, gpu = models
+    n1, n2 = PREFILL[name]
+    rng = np.random.default_rng(23)
+    toks = rng.integers(0, cfg.vocab, size=n1 + 1 + n2).astype(np.int32)
+    want = None
+    for pos in range(n1):
+        want = ref.step(int(toks[pos]), pos)
+    got = gpu.prefill(toks[:n1], 0)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), \
+        f"{name}: prefill logits differ, rel-max {rel_max(got, want):.2e}"
+    # one ordinary step after the prefill reads the prefilled cache
+    want = ref.step(int(toks[n1]), n1)
+    got = gpu.step(int(toks[n1]), n1)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    # a second chunk from position n1 + 1
+    for pos in range(n1 + 1, n1 + 1 + n2):
+        want = ref.step(int(toks[pos]), pos)
+    got = gpu.prefill(toks[n1 + 1:], n1 + 1)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+def test_generation_with_and_without_batched_prefill(models):
+    """generate() runs its prompt batched by default; one step per position
+    gives the same tokens."""
+    name, case, cfg, _, ref, gpu = models
+    rng = np.random.default_rng(31)
+    prompt = rng.integers(0, cfg.vocab, size=PREFILL[name][0]).astype(np.int32)
+    a = gpu.generate(prompt, 6)
+    gpu.set_batched_prefill(False)
+    try:
+        b = gpu.generate(prompt, 6)
+    finally:
+        gpu.set_batched_prefill(True)
+    assert a.tolist() == b.tolist()
+    assert gpu.prefill_launches >= 2 + cfg.n_layers * 8
+
+
+def test_prefill_rejects_bad_arguments(models):
+    name, case, cfg, _, ref, gpu = models
+    with pytest.raises(N.MiagError):
+        gpu.prefill(np.array([0, cfg.vocab], np.int32), 0)  # token out of range
+    with pytest.raises(N.MiagError):
+        gpu.prefill(np.zeros(4, np.int32), case["max_seq"] - 3)  # past the context
+    with pytest.raises(N.MiagError):
+        gpu.prefill(np.zeros(0, np.int32), 0)
+    want = ref.step(3, 0)
+    got = gpu.step(3, 0)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
 def test_out_of_range_steps_fail_and_leave_the_model_usable(models):
     name, case, cfg, _, ref, gpu = models
     for tok, pos in ((-1, 0), (cfg.vocab, 0), (0, -1), (0, case["max_seq"])):
