@@ -417,6 +417,20 @@ const float *miag_model_prefill(miag_model *m, const int32_t *tokens, int n, int
 int miag_model_prefill_async(miag_model *m, const int32_t *tokens, int n, int pos, char *err,
                              size_t errlen);
 int miag_model_set_batched_prefill(miag_model *m, int on);
+
+/* The next-token choice on the device.  Replaces mia_sampler_init /
+ * mia_sample (include/mia/sampler.h, src/tokenizer/sampler.c:5-66) in the
+ * generation loops of src/app/main.c:126-141 and serve.c:115-133: with
+ * temperature > 0 every step (and a prefill) draws its next token as
+ * mia_sample does -- e = expf((l - max) / temperature) with the serial sum,
+ * the candidates p >= (1 - top_p) / (n - 1) in the order of glibc's stable
+ * qsort (p descending, then index), the smallest prefix reaching top_p, and
+ * the xorshift64* draw from `seed` (0: the reference's fixed default) -- so
+ * a generation equals the reference loop's token for token.  Temperature
+ * <= 0: the greedy argmax of the head (the default).  Waits for the model's
+ * stream; the next step re-captures its graph. */
+int miag_model_set_sampler(miag_model *m, float temperature, float top_p, uint64_t seed, char *err,
+                           size_t errlen);
 int miag_model_prefill_launches(const miag_model *m);
 
 /* Per-kernel timing (no reference counterpart; the reference only has

@@ -126,6 +126,8 @@ SIGNATURES = {
     "miag_model_prefill": (C.c_void_p, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_char_p,
                                          C.c_size_t]),
     "miag_model_set_batched_prefill": (C.c_int, [C.c_void_p, C.c_int]),
+    "miag_model_set_sampler": (C.c_int, [C.c_void_p, C.c_float, C.c_float, C.c_uint64, C.c_char_p,
+                                         C.c_size_t]),
     "miag_model_prefill_launches": (C.c_int, [C.c_void_p]),
     "miag_profile": (C.c_int, [C.c_void_p, C.c_int]),
     "miag_profile_stages": (C.c_int, []),

@@ -37,6 +37,8 @@
 #include <string>
 #include <vector>
 
+#include <cub/device/device_radix_sort.cuh>
+
 #include "kernels.cuh"
 #include "mia_layout.h"
 
@@ -151,6 +153,7 @@ struct GemvParams {
     int n_prompt;
     int32_t *tokens;
     int max_seq;
+    int32_t *best;  // sampling: the argmax goes here and the sampler advances the step
     int *err;
 };
 
@@ -351,7 +354,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const __grid_constant_
     const unsigned long long k = atomicAdd(p.amax, 0ull);
     const int arg = (int)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
     const int pos = p.args[1];
-    if (pos >= 0 && pos + 1 < p.max_seq) {
+    if (p.best) {
+        *p.best = arg;
+    } else if (pos >= 0 && pos + 1 < p.max_seq) {
         const int next = pos + 1;
         const int token = next < p.n_prompt ? p.prompt[next] : arg;
         p.tokens[next] = token;
@@ -906,6 +911,182 @@ __global__ void __launch_bounds__(kPfAttnThreads) k_pf_attn(const __grid_constan
     }
 }
 
+// ---------------------------------------------------------------------------
+// Sampling on the device: mia_sample (src/tokenizer/sampler.c:33-66) with a
+// temperature above zero, after the head has found the argmax (:34-37).
+//   e_i = expf((l_i - l_best) / temperature), sum = e_0 + e_1 + ... serially
+//   p_i = e_i / sum; the candidates p_i >= (1 - top_p) / (n - 1), sorted by
+//   p descending -- glibc's qsort is a merge sort, stable, so equal p keep
+//   the index order: the sort key (~bits(p), i) gives the same order;
+//   the smallest prefix whose serial cumulative sum reaches top_p, then
+//   r = rand01() * cum and the first candidate whose running sum exceeds r.
+// The serial sums are the reference's, in its order; one thread adds while
+// the CTA stages the next tile of values in shared memory.
+
+constexpr int kSmpThreads = 256, kSmpTile = 4096, kSmpPickTile = 2048;
+
+struct SmpState {
+    unsigned long long rng;  // xorshift64* state (sampler.c:24-29)
+    float sum, cum;
+    int best, last, m;
+};
+
+// xorshift64*: the next state and its float in [0, 1) (sampler.c:24-29).
+__device__ __forceinline__ float smp_rand01(unsigned long long &s) {
+    s ^= s >> 12;
+    s ^= s << 25;
+    s ^= s >> 27;
+    return __fdiv_rn((float)((s * 0x2545F4914F6CDD1DULL) >> 40), 16777216.0f);
+}
+
+// e_i and their serial sum.  One CTA: tile k + 1's exponentials are formed
+// while thread 0 adds tile k's.
+__global__ void __launch_bounds__(kSmpThreads) k_smp_sum(const float *logits, int n, float temp, float *e,
+                                                         SmpState *st) {
+    __shared__ float buf[2][kSmpTile];
+    const int tid = threadIdx.x;
+    const float mx = logits[st->best];
+    const int ntile = (n + kSmpTile - 1) / kSmpTile;
+    auto fill = [&](int k) {
+        for (int j = tid; j < kSmpTile; j += kSmpThreads) {
+            const int i = k * kSmpTile + j;
+            if (i < n) {
+                const float v = expf_cr(__fdiv_rn(__fsub_rn(logits[i], mx), temp));
+                buf[k & 1][j] = v;
+                e[i] = v;
+            }
+        }
+    };
+    fill(0);
+    __syncthreads();
+    float sum = 0.0f;
+    for (int k = 0; k < ntile; k++) {
+        if (k + 1 < ntile) fill(k + 1);
+        if (tid == 0) {
+            const int m = min(kSmpTile, n - k * kSmpTile);
+            const float *b = buf[k & 1];
+#pragma unroll 8
+            for (int j = 0; j < m; j++) sum = __fadd_rn(sum, b[j]);
+        }
+        __syncthreads();
+    }
+    if (tid == 0) st->sum = sum;
+}
+
+// p_i and the sort keys: (~bits(p_i)) << 32 | i for the candidates (p >= 0,
+// so its bits order like its value), all ones for the rest.
+__global__ void k_smp_keys(const float *e, int n, float top_p, SmpState *st, float *p,
+                           unsigned long long *keys) {
+    const float sum = st->sum;
+    const float cutoff = __fdiv_rn(__fsub_rn(1.0f, top_p), (float)(n > 1 ? n - 1 : 1));
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const float v = __fdiv_rn(e[i], sum);
+        p[i] = v;
+        keys[i] = v >= cutoff ? ((unsigned long long)(~__float_as_uint(v)) << 32) | (unsigned)i : ~0ull;
+    }
+}
+
+// The nucleus and the draw over the sorted candidates; then the step
+// advances as the head's greedy path does (the prompt's own next token while
+// the prompt lasts, without drawing).
+__global__ void __launch_bounds__(kSmpThreads) k_smp_pick(const unsigned long long *keys, const float *p, int n,
+                                                          float top_p, SmpState *st, int32_t *args,
+                                                          const int32_t *prompt, int n_prompt, int32_t *tokens,
+                                                          int max_seq) {
+    __shared__ float buf[2][kSmpPickTile];
+    __shared__ int ibuf[2][kSmpPickTile];
+    __shared__ int s_stop, s_m;
+    const int tid = threadIdx.x;
+    const int pos = args[1];
+    if (pos < 0 || pos + 1 >= max_seq) {
+        if (tid == 0) args[1] = max_seq;  // the next step reports the position out of range
+        return;
+    }
+    const int next = pos + 1;
+    if (next < n_prompt) {
+        if (tid == 0) {
+            tokens[next] = prompt[next];
+            args[0] = prompt[next];
+            args[1] = next;
+        }
+        return;
+    }
+    // pass 0: the cumulative sum up to top_p; pass 1: the draw
+    int token = st->best;
+    float cum = 0.0f, r = 0.0f, acc = 0.0f;
+    int last = -1, m = n;
+    if (tid == 0) s_m = n;
+    for (int pass = 0; pass < 2; pass++) {
+        const int end = pass == 0 ? n : last + 1;
+        const int ntile = (end + kSmpPickTile - 1) / kSmpPickTile;
+        auto fill = [&](int k) {
+            for (int j = tid; j < kSmpPickTile; j += kSmpThreads) {
+                const int q = k * kSmpPickTile + j;
+                const unsigned long long key = q < end ? keys[q] : ~0ull;
+                const int i = key == ~0ull ? -1 : (int)(key & 0xFFFFFFFFull);
+                ibuf[k & 1][j] = i;
+                buf[k & 1][j] = i >= 0 ? p[i] : 0.0f;
+            }
+        };
+        if (tid == 0) s_stop = 0;
+        if (ntile > 0) fill(0);
+        __syncthreads();
+        for (int k = 0; k < ntile && !s_stop; k++) {
+            if (k + 1 < ntile) fill(k + 1);
+            if (tid == 0) {
+                const int cnt = min(kSmpPickTile, end - k * kSmpPickTile);
+                for (int j = 0; j < cnt; j++) {
+                    const int i = ibuf[k & 1][j];
+                    const int q = k * kSmpPickTile + j;
+                    if (pass == 0) {
+                        if (i < 0) {  // past the candidates
+                            s_m = q;
+                            s_stop = 1;
+                            break;
+                        }
+                        cum = __fadd_rn(cum, buf[k & 1][j]);
+                        if (cum >= top_p) {
+                            last = q;
+                            s_stop = 1;
+                            break;
+                        }
+                    } else {
+                        acc = __fadd_rn(acc, buf[k & 1][j]);
+                        if (r < acc) {
+                            token = i;
+                            s_stop = 1;
+                            break;
+                        }
+                        if (q == last) token = i;  // no candidate passed r: the last one
+                    }
+                }
+            }
+            __syncthreads();
+        }
+        if (pass == 0) {
+            if (tid == 0) {
+                m = s_m;
+                if (last < 0) last = m - 1;
+                if (last >= 0) {
+                    unsigned long long s = st->rng;
+                    r = __fmul_rn(smp_rand01(s), cum);
+                    st->rng = s;
+                }
+                s_m = last;  // broadcast
+            }
+            __syncthreads();
+            last = s_m;
+            if (last < 0) break;  // no candidate: the argmax
+        }
+    }
+    if (tid == 0) {
+        st->cum = cum, st->last = last;
+        tokens[next] = token;
+        args[0] = token;
+        args[1] = next;
+    }
+}
+
 }  // namespace
 }  // namespace miag
 
@@ -945,6 +1126,13 @@ struct miag_model {
     uint8_t *pf_xq = nullptr;
     int32_t *pf_tok = nullptr;
     int32_t *h_pf_tok = nullptr;  // pinned, pf_cap entries
+    // sampling (miag_model_set_sampler): temperature 0 = greedy in the head
+    float smp_temp = 0.0f, smp_top_p = 1.0f;
+    SmpState *smp = nullptr;
+    float *smp_e = nullptr, *smp_p = nullptr;
+    unsigned long long *smp_k0 = nullptr, *smp_k1 = nullptr;
+    void *smp_tmp = nullptr;
+    size_t smp_tmp_bytes = 0;
 };
 
 namespace {
@@ -998,6 +1186,22 @@ int grid_of(const miag_model *m, const GemvParams &p) {
         }                                                                         \
     } while (0)
 
+// The draw after the head (temperature > 0): the exponentials and their
+// serial sum, the candidates' keys, their sort, the nucleus and the draw.
+int enqueue_sample(miag_model *m, cudaStream_t s, char *err, size_t errlen) {
+    const int n = (int)m->cfg.vocab;
+    k_smp_sum<<<1, kSmpThreads, 0, s>>>(m->logits, n, m->smp_temp, m->smp_e, m->smp);
+    MCU(cudaGetLastError());
+    k_smp_keys<<<(n + 255) / 256, 256, 0, s>>>(m->smp_e, n, m->smp_top_p, m->smp, m->smp_p, m->smp_k0);
+    MCU(cudaGetLastError());
+    size_t bytes = m->smp_tmp_bytes;
+    MCU(cub::DeviceRadixSort::SortKeys(m->smp_tmp, bytes, m->smp_k0, m->smp_k1, n, 0, 64, s));
+    k_smp_pick<<<1, kSmpThreads, 0, s>>>(m->smp_k1, m->smp_p, n, m->smp_top_p, m->smp, m->args, m->prompt,
+                                          m->head_p.n_prompt, m->tokens, m->max_seq);
+    MCU(cudaGetLastError());
+    return 0;
+}
+
 // The launch sequence of one step on stream s (captured into the graph).
 int enqueue_step(miag_model *m, cudaStream_t s, char *err, size_t errlen) {
     const miag_mia_config &c = m->cfg;
@@ -1036,8 +1240,13 @@ int enqueue_step(miag_model *m, cudaStream_t s, char *err, size_t errlen) {
     const size_t nt = m->layout.size();  // ..., output_norm, output
     hp.seg[0].w = tensor(m, nt - 1);
     hp.norm = tensor_f(m, nt - 2);
+    hp.best = m->smp_temp > 0.0f ? &m->smp->best : nullptr;
     MCU(gemv_launch(hp, grid_of(m, hp), m->head_smem, s));
     launches++;
+    if (m->smp_temp > 0.0f) {
+        if (enqueue_sample(m, s, err, errlen)) return -1;
+        launches += 3;
+    }
     m->last_launches = launches;
     return 0;
 }
@@ -1136,6 +1345,9 @@ extern "C" void miag_model_close(miag_model *m) {
                     (void *)m->pf_xq, (void *)m->pf_tok})
         if (b) cudaFree(b);
     if (m->h_pf_tok) cudaFreeHost(m->h_pf_tok);
+    for (void *b : {(void *)m->smp, (void *)m->smp_e, (void *)m->smp_p, (void *)m->smp_k0, (void *)m->smp_k1,
+                    m->smp_tmp})
+        if (b) cudaFree(b);
     if (m->h_logits) cudaFreeHost(m->h_logits);
     if (m->h_args) cudaFreeHost(m->h_args);
     if (m->stream) cudaStreamDestroy(m->stream);
@@ -1530,8 +1742,13 @@ int enqueue_prefill(miag_model *m, int n, int pos0, cudaStream_t s, char *err, s
     hp.seg[0].w = tensor(m, nt - 1);
     hp.norm = tensor_f(m, nt - 2);
     hp.in = m->pf_x + (size_t)(n - 1) * d;
+    hp.best = m->smp_temp > 0.0f ? &m->smp->best : nullptr;
     MCU(gemv_launch(hp, grid_of(m, hp), m->head_smem, s));
     launches++;
+    if (m->smp_temp > 0.0f) {
+        if (enqueue_sample(m, s, err, errlen)) return -1;
+        launches += 3;
+    }
     m->pf_last_launches = launches;
     return 0;
 }
@@ -1582,6 +1799,38 @@ extern "C" const float *miag_model_prefill(miag_model *m, const int32_t *tokens,
     }
     if (check_errors(m, err, errlen)) return nullptr;
     return m->h_logits;
+}
+
+extern "C" int miag_model_set_sampler(miag_model *m, float temperature, float top_p, uint64_t seed, char *err,
+                                      size_t errlen) {
+    if (!m) {
+        put_err(err, errlen, "null model");
+        return -1;
+    }
+    MCU(cudaSetDevice(m->device));
+    MCU(cudaStreamSynchronize(m->stream));
+    const int n = (int)m->cfg.vocab;
+    if (!m->smp) {
+        MCU(cudaMalloc(&m->smp, sizeof(SmpState)));
+        MCU(cudaMemset(m->smp, 0, sizeof(SmpState)));
+        MCU(cudaMalloc(&m->smp_e, (size_t)n * 4));
+        MCU(cudaMalloc(&m->smp_p, (size_t)n * 4));
+        MCU(cudaMalloc(&m->smp_k0, (size_t)n * 8));
+        MCU(cudaMalloc(&m->smp_k1, (size_t)n * 8));
+        size_t bytes = 0;
+        MCU(cub::DeviceRadixSort::SortKeys(nullptr, bytes, m->smp_k0, m->smp_k1, n, 0, 64, m->stream));
+        MCU(cudaMalloc(&m->smp_tmp, bytes));
+        m->smp_tmp_bytes = bytes;
+    }
+    // sampler.c:7-10: top_p outside (0, 1] means 1; a zero seed a fixed one
+    SmpState st{};
+    st.rng = seed ? seed : 0x2545F4914F6CDD1DULL;
+    MCU(cudaMemcpy(m->smp, &st, sizeof st, cudaMemcpyHostToDevice));
+    m->smp_temp = temperature > 0.0f ? temperature : 0.0f;
+    m->smp_top_p = top_p > 0.0f && top_p <= 1.0f ? top_p : 1.0f;
+    if (m->exec) cudaGraphExecDestroy(m->exec);  // the step's launches change
+    m->exec = nullptr;
+    return 0;
 }
 
 extern "C" int miag_model_set_batched_prefill(miag_model *m, int on) {

@@ -136,6 +136,13 @@ class Model:
             raise N.MiagError(f"miag_model_prefill: {err.value.decode(errors='replace')}")
         return np.ctypeslib.as_array(C.cast(p, C.POINTER(C.c_float)), (self.vocab,)).copy()
 
+    def set_sampler(self, temperature: float, top_p: float = 1.0, seed: int = 0) -> None:
+        """Draw each next token as mia_sample does (temperature > 0), or take
+        the greedy argmax (temperature <= 0, the default)."""
+        err = N.errbuf()
+        N.check(N.lib().miag_model_set_sampler(self._m, float(temperature), float(top_p), int(seed),
+                                               err, len(err)), err, "miag_model_set_sampler")
+
     def set_batched_prefill(self, on: bool) -> None:
         N.lib().miag_model_set_batched_prefill(self._m, int(bool(on)))
 

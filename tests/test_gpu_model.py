@@ -198,6 +198,59 @@ def test_generation_with_and_without_batched_prefill(models):
     assert gpu.prefill_launches >= 2 + cfg.n_layers * 8
 
 
+class MiaSampler(C.Structure):
+    """mia_sampler (include/mia/sampler.h)."""
+
+    _fields_ = [("temperature", C.c_float), ("top_p", C.c_float), ("n", C.c_int),
+                ("rng", C.c_uint64), ("buf", C.c_void_p)]
+
+
+def reference_sampled_loop(ref: RefModel, prompt, n_new, temp, top_p, seed, vocab):
+    """The generation loop of src/app/main.c:118-141: the prompt one step a
+    position, then mia_sample on a copy of the logits and a step with the
+    drawn token."""
+    lib = ref.lib
+    lib.mia_sampler_init.argtypes = [C.POINTER(MiaSampler), C.c_float, C.c_float, C.c_int, C.c_uint64]
+    lib.mia_sample.argtypes = [C.POINTER(MiaSampler), C.POINTER(C.c_float)]
+    lib.mia_sample.restype = C.c_int
+    lib.mia_sampler_free.argtypes = [C.POINTER(MiaSampler)]
+    smp = MiaSampler()
+    assert lib.mia_sampler_init(C.byref(smp), temp, top_p, vocab, seed) == 0
+    logits = None
+    for p, t in enumerate(prompt):
+        logits = ref.step(int(t), p)
+    out = []
+    for i in range(n_new):
+        work = np.ascontiguousarray(logits, dtype=np.float32).copy()
+        t = lib.mia_sample(C.byref(smp), work.ctypes.data_as(C.POINTER(C.c_float)))
+        out.append(int(t))
+        if i + 1 < n_new:
+            logits = ref.step(t, len(prompt) + i)
+    lib.mia_sampler_free(C.byref(smp))
+    return out
+
+
+@pytest.mark.parametrize("temp,top_p,seed,batched", [(0.7, 0.8, 42, True), (1.3, 1.0, 0, True),
+                                                     (0.9, 0.5, 7, False)])
+def test_sampled_generation_equals_the_reference_sampler(models, temp, top_p, seed, batched):
+    """Temperature / top-p sampling on the device draws the same tokens as
+    the reference's mia_sample (sampler.c:33-66) in its generation loop,
+    with the same seed; the prompt batched or one step a position."""
+    name, case, cfg, _, ref, gpu = models
+    rng = np.random.default_rng(41)
+    prompt = rng.integers(0, cfg.vocab, size=7).astype(np.int32)
+    n_new = 12
+    want = reference_sampled_loop(ref, prompt, n_new, temp, top_p, seed, cfg.vocab)
+    gpu.set_sampler(temp, top_p, seed)
+    gpu.set_batched_prefill(batched)
+    try:
+        got = gpu.generate(prompt, n_new)
+    finally:
+        gpu.set_sampler(0.0)
+        gpu.set_batched_prefill(True)
+    assert got.tolist() == want, f"{name}: {got.tolist()} vs {want}"
+
+
 def test_prefill_rejects_bad_arguments(models):
     name, case, cfg, _, ref, gpu = models
     with pytest.raises(N.MiagError):
