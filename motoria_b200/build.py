@@ -79,6 +79,41 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     return LIB
 
 
+ENGINE = PKG / "engine"
+
+
+def reference_tree() -> Path | None:
+    """The motorIa source tree the engine applications build from:
+    $MIA_REFERENCE, else the reference_path of BASELINE.json beside the
+    package; None when neither names a tree."""
+    import json
+
+    cand = os.environ.get("MIA_REFERENCE")
+    if not cand:
+        try:
+            cand = json.loads((PKG.parent / "BASELINE.json").read_text()).get("reference_path")
+        except (OSError, ValueError):
+            cand = None
+    if cand and (Path(cand) / "src" / "app" / "serve.c").exists():
+        return Path(cand)
+    return None
+
+
+def build_engine() -> Path | None:
+    """The engine's applications (mia, mia-serve, mia-dump) with the model
+    layer on the GPU (engine/mia_model_gpu.c over libmiag), built from the
+    reference tree where one exists (engine/Makefile); returns their
+    directory, or None without a tree (they may have been built elsewhere)."""
+    build()
+    tree = reference_tree()
+    if tree is None:
+        return None
+    r = subprocess.run(["make", "-s", "-C", str(ENGINE), f"REF={tree}"], capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"engine build failed:\n{r.stdout}\n{r.stderr}")
+    return ENGINE / "_bin"
+
+
 if __name__ == "__main__":
     import sys
 
