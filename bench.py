@@ -555,14 +555,15 @@ def model_bytes_per_token(cfg, first_pos: int, n: int) -> float:
 
 
 def run_model_decode(ctx, args, peaks):
-    """config4 on one GPU: device-timed prompt and decode, and the host API
-    end to end (miag_model_generate: prompt in, tokens out)."""
+    """config4 on one GPU: device-timed prompt (one batched prefill) and
+    decode, and the host API end to end (miag_model_generate: prompt in,
+    tokens out)."""
     import torch
 
     from motoria_b200.model import Model
 
     cfg = model_config()
-    P, NEW = MODEL_PROMPT, MODEL_NEW
+    P, NEW = MODEL_PROMPT, getattr(args, "model_new", MODEL_NEW)
     prompt = np.random.default_rng(XSEED).integers(0, cfg.vocab, P).astype(np.int32)
     with Model.synthetic(cfg, SEED, MODEL_CTX, device=ctx.local) as m:
         s = torch.cuda.ExternalStream(m.stream)
@@ -589,9 +590,10 @@ def run_model_decode(ctx, args, peaks):
         "metric": "Qwen3-30B-A3B decode tok/s", "value": tok_s, "unit": "tokens/s",
         "ms_per_token": decode_ms / NEW,
         "prompt_positions_per_s": P / (prompt_ms / 1e3),
+        "prompt": f"{P} positions in one batched prefill (miag_model_prefill)",
         "e2e": {"value": (P + NEW) / e2e_s, "unit": "positions/s",
-                "what": "miag_model_generate from a host prompt to host tokens: 512 prompt "
-                        "positions then 256 greedy ones, wall clock",
+                "what": f"miag_model_generate from a host prompt to host tokens: {P} prompt "
+                        f"positions (one batched prefill) then {NEW} greedy ones, wall clock",
                 "h2d_bytes_per_step": P * 4 / (P + NEW), "d2h_bytes_per_step": (NEW + 1) * 4 / (P + NEW)},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": achieved / peaks["hbm_gbs"], "traffic": None,
@@ -723,7 +725,19 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the decode figures (config2, config1) of the default run")
+    ap.add_argument("--model-only", action="store_true",
+                    help="only the whole-model decode (config4); prints its own JSON line")
+    ap.add_argument("--model-new", type=int, default=MODEL_NEW,
+                    help="decode steps of the whole-model run (after its 512-position prompt)")
     args = ap.parse_args()
+    if args.model_only:
+        from motoria_b200 import build
+        build.build()
+        ctx = Ctx()
+        line = run_model_decode(ctx, args, load_peaks())
+        if ctx.rank == 0:
+            print(json.dumps(line), flush=True)
+        return
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     desc, T, rms, zipf = WORKLOADS[args.workload]

@@ -51,6 +51,13 @@ static gpu_model *find_model(const mia_model *m) {
     return NULL;
 }
 
+/* The GPU model behind an engine model (NULL if none): for the loops that
+ * call libmiag directly, e.g. a prompt through miag_model_prefill. */
+miag_model *mia_model_gpu(const mia_model *m) {
+    gpu_model *p = find_model(m);
+    return p ? p->g : NULL;
+}
+
 size_t mia_model_state_bytes(const mia_file *f, int max_seq) {
     (void)max_seq; /* activations and the KV cache live in HBM */
     return (size_t)f->h.vocab * sizeof(float); /* the host copy of the logits */
