@@ -436,6 +436,11 @@ def measure(ctx: Ctx, runner, x_host, steps: int, warmup: int, e2e: bool = True,
     out["e2e_s"], out["e2e_own_buffers"] = e2e_pass(True)
     if pageable:
         out["e2e_pageable_s"], _ = e2e_pass(False)
+    # one more (untimed) call over the whole batch on the device: the host
+    # API moves large batches through in chunks, and the routing readback
+    # (work_of) describes the last call
+    one_step()
+    runner.eng.sync(sp)
     return out
 
 

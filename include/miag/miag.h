@@ -116,6 +116,14 @@ int miag_moe(miag_ctx *c, int layer, float *x, int n_tokens, char *err,
              size_t errlen);
 int miag_moe_async(miag_ctx *c, int layer, float *x_dev, int n_tokens,
                    void *stream, char *err, size_t errlen);
+/* miag_moe with at least 2048 tokens moves them through in `chunks` pieces
+ * (default 4; 1: one piece): a copy stream brings piece k + 1 in and takes
+ * piece k - 1 out while the block runs on piece k, so most of the host
+ * transfers hide behind the kernels.  Tokens are independent in the block,
+ * so the results equal one pass over all of them bit for bit; the
+ * inspection calls (miag_routing, miag_router_logits) then describe the
+ * last piece.  No reference counterpart (the reference has no device). */
+int miag_set_transfer_chunks(miag_ctx *c, int chunks);
 
 /* The MoE block with nothing allocated during the call.  No counterpart in
  * the reference (motorIa sizes all scratch once, from its RAM budget).  For

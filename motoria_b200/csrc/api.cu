@@ -7,6 +7,8 @@
 #include <vector>
 
 #include "../../include/miag/miag.h"
+#include <algorithm>
+
 #include "kernels.cuh"
 
 using namespace miag;
@@ -38,6 +40,10 @@ struct miag_ctx {
     int ws_cap = 0;
     Work ws{};
     float *x_dev = nullptr;
+    // miag_moe's transfer pipeline: a copy stream and per-chunk events
+    cudaStream_t copy_stream = nullptr;
+    std::vector<cudaEvent_t> pipe_events;
+    int transfer_chunks = 4;  // miag_set_transfer_chunks
     int *d_err = nullptr;
     int *h_err = nullptr;  // pinned: the error word, read back with a call's results
     // expert parallelism: this rank's exchange buffer (flags | CTA counter |
@@ -250,6 +256,11 @@ extern "C" void miag_close(miag_ctx *c) {
     if (c->h_err) cudaFreeHost(c->h_err);
     cudaFree(c->stage_dev);
     if (c->stage_host) cudaFreeHost(c->stage_host);
+    if (c->copy_stream) {
+        cudaStreamSynchronize(c->copy_stream);
+        cudaStreamDestroy(c->copy_stream);
+    }
+    for (cudaEvent_t e : c->pipe_events) cudaEventDestroy(e);
     if (c->stream) cudaStreamDestroy(c->stream);
     delete c;
 }
@@ -607,6 +618,54 @@ extern "C" int miag_sync(miag_ctx *c, void *stream, char *err, size_t errlen) {
     return read_device_error(c, err, errlen);
 }
 
+// Batches of at least kPipeMin tokens move through miag_moe in
+// transfer_chunks chunks (miag_set_transfer_chunks): the copy stream brings chunk k + 1 in and takes chunk k - 1 out
+// while the block runs on chunk k.  Tokens are independent in the block
+// (forward.c:167-197 is a per-token loop), so the results are those of one
+// call over all of them, bit for bit.  Chunks are enqueued in the order
+// in(0), block(0), in(1), block(1), ... and the copies out last, so that
+// with pageable host memory, whose copies hold the calling thread, the
+// device still works on the chunks already enqueued.
+constexpr int kPipeMin = 2048, kPipeMaxChunks = 16;
+
+static int moe_pipelined(miag_ctx *c, int layer, float *x, int n_tokens, char *err, size_t errlen) {
+    if (!c->copy_stream) {
+        CU(cudaStreamCreateWithFlags(&c->copy_stream, cudaStreamNonBlocking));
+        for (int i = 0; i < 2 * kPipeMaxChunks; i++) {
+            cudaEvent_t e;
+            CU(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+            c->pipe_events.push_back(e);
+        }
+    }
+    const size_t row = (size_t)c->shape.dim * sizeof(float);
+    const int chunks = c->transfer_chunks;
+    const int per = ((n_tokens + chunks - 1) / chunks + 31) & ~31;
+    int launches = 0, n_chunks = 0;
+    for (int k = 0; k < chunks && k * per < n_tokens; k++, n_chunks++) {
+        const int t0 = k * per, tk = std::min(per, n_tokens - t0);
+        CU(cudaMemcpyAsync(c->x_dev + (size_t)t0 * c->shape.dim, x + (size_t)t0 * c->shape.dim,
+                           (size_t)tk * row, cudaMemcpyHostToDevice, c->copy_stream));
+        CU(cudaEventRecord(c->pipe_events[k], c->copy_stream));
+        CU(cudaStreamWaitEvent(c->stream, c->pipe_events[k], 0));
+        if (ensure_ws(c, tk, err, errlen)) return -1;  // counts only: the buffers hold n_tokens
+        if (enqueue_moe(c, layer, c->x_dev + (size_t)t0 * c->shape.dim, tk, c->stream, err, errlen))
+            return -1;
+        launches += c->last_launches;
+        CU(cudaEventRecord(c->pipe_events[kPipeMaxChunks + k], c->stream));
+    }
+    for (int k = 0; k < n_chunks; k++) {
+        const int t0 = k * per, tk = std::min(per, n_tokens - t0);
+        CU(cudaStreamWaitEvent(c->copy_stream, c->pipe_events[kPipeMaxChunks + k], 0));
+        CU(cudaMemcpyAsync(x + (size_t)t0 * c->shape.dim, c->x_dev + (size_t)t0 * c->shape.dim,
+                           (size_t)tk * row, cudaMemcpyDeviceToHost, c->copy_stream));
+    }
+    // after the last chunk's block: the error word with the results
+    CU(cudaMemcpyAsync(c->h_err, c->d_err, sizeof(int), cudaMemcpyDeviceToHost, c->copy_stream));
+    CU(cudaStreamSynchronize(c->copy_stream));
+    c->last_launches = launches;
+    return read_device_error(c, err, errlen, *c->h_err);
+}
+
 extern "C" int miag_moe(miag_ctx *c, int layer, float *x, int n_tokens, char *err, size_t errlen) {
     if (check_layer(c, layer, err, errlen)) return -1;
     if (n_tokens < 0 || (n_tokens > 0 && !x)) {
@@ -619,6 +678,8 @@ extern "C" int miag_moe(miag_ctx *c, int layer, float *x, int n_tokens, char *er
     }
     CU(cudaSetDevice(c->device));
     if (ensure_ws(c, n_tokens, err, errlen)) return -1;
+    if (n_tokens >= kPipeMin && c->transfer_chunks > 1)
+        return moe_pipelined(c, layer, x, n_tokens, err, errlen);
     const size_t bytes = (size_t)n_tokens * c->shape.dim * sizeof(float);
     CU(cudaMemcpyAsync(c->x_dev, x, bytes, cudaMemcpyHostToDevice, c->stream));
     if (enqueue_moe(c, layer, c->x_dev, n_tokens, c->stream, err, errlen)) return -1;
@@ -1039,6 +1100,12 @@ extern "C" int miag_set_prefill_kernel(miag_ctx *c, int kind, char *err, size_t 
     }
     CU(cudaStreamSynchronize(c->stream));
     c->prefill_tc = kind == MIAG_PREFILL_TCGEN05;
+    return 0;
+}
+
+extern "C" int miag_set_transfer_chunks(miag_ctx *c, int chunks) {
+    if (!c || chunks < 1 || chunks > kPipeMaxChunks) return -1;
+    c->transfer_chunks = chunks;
     return 0;
 }
 

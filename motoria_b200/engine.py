@@ -293,6 +293,11 @@ class MoEEngine:
         N.check(self._lib.miag_set_prefill_kernel(self._ctx, kind, err, len(err)), err,
                 "miag_set_prefill_kernel")
 
+    def set_transfer_chunks(self, chunks: int) -> None:
+        """Pieces a host-API call of >= 2048 tokens moves through (1: one)."""
+        if self._lib.miag_set_transfer_chunks(self._ctx, int(chunks)) != 0:
+            raise N.MiagError(f"miag_set_transfer_chunks: bad count {chunks}")
+
     def prefill_kernel(self) -> int:
         return int(self._lib.miag_prefill_kernel(self._ctx))
 

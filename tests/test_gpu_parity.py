@@ -56,6 +56,9 @@ def qwen(torch_cuda):
     zipf = get_layer(QWEN, True)
     eng.set_layer(1, zipf.ffn_norm, zipf.router, zipf.bias)
     eng.upload_experts(1, zipf.blobs)
+    # host calls in one pass, so that the routing readbacks cover every token
+    # (test_host_call_in_pieces_equals_one_pass covers the piecewise calls)
+    eng.set_transfer_chunks(1)
     yield eng, plain, zipf
     eng.close()
 
@@ -237,6 +240,28 @@ def test_prefill_kernels_agree_bit_for_bit(qwen, T, layer):
         eng.set_prefill_kernel(default)
     same = np.all(got.view(np.uint32) == want.view(np.uint32), axis=1)
     assert same.all(), f"{int((~same).sum())} of {T} tokens differ"
+
+
+@pytest.mark.parametrize("T,chunks", [(2048, 4), (4096, 4), (3001, 3), (4096, 16)])
+def test_host_call_in_pieces_equals_one_pass(qwen, T, chunks):
+    """miag_moe of >= 2048 host tokens moves them through in pieces while the
+    block runs (copy stream): every output bit equals one pass, from pinned
+    and from pageable host memory."""
+    import torch
+    eng, _, _ = qwen
+    x = synth.tokens(QWEN, 900 + T, T, rms_normalise=False)
+    eng.set_transfer_chunks(1)
+    want = eng.moe(x, layer=1)
+    eng.set_transfer_chunks(chunks)
+    try:
+        got = eng.moe(x, layer=1)
+        pinned = torch.from_numpy(x.copy()).pin_memory()
+        arr = pinned.numpy()
+        eng.moe_inplace(arr, layer=1)
+    finally:
+        eng.set_transfer_chunks(1)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    assert np.array_equal(arr.view(np.uint32), want.view(np.uint32))
 
 
 # ---- size-independent properties -------------------------------------------
