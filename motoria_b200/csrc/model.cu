@@ -158,7 +158,7 @@ struct GemvParams {
 };
 
 struct GemvSmem {
-    size_t terms, xq, xin, red, bars, total;
+    size_t terms, xq, xin, nrm, red, bars, total;
 };
 
 __host__ __device__ inline GemvSmem gemv_smem(int stage_bytes, int R, int cols, int nb) {
@@ -166,7 +166,8 @@ __host__ __device__ inline GemvSmem gemv_smem(int stage_bytes, int R, int cols, 
     g.terms = (size_t)kGemvStages * stage_bytes;
     g.xq = g.terms + (((size_t)2 * R * (nb + 1) * 4 + 15) & ~(size_t)15);
     g.xin = g.xq + (((size_t)nb * 36 + 15) & ~(size_t)15);
-    g.red = g.xin + (size_t)cols * 4;
+    g.nrm = g.xin + (size_t)cols * 4;
+    g.red = g.nrm + (size_t)cols * 4;
     g.bars = g.red + 32 * 8;
     g.total = g.bars + (kGemvStages + 4) * 8 + 16;
     return g;
@@ -186,6 +187,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const __grid_constant_
     float *terms = reinterpret_cast<float *>(smem + L.terms);  // [2][R][nb + 1]
     uint8_t *xq = smem + L.xq;
     float *xin = reinterpret_cast<float *>(smem + L.xin);
+    float *nrm = reinterpret_cast<float *>(smem + L.nrm);
     double *red = reinterpret_cast<double *>(smem + L.red);
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.bars);  // [kGemvStages]
     uint64_t *tfull = full + kGemvStages;                           // [2] terms written
@@ -229,15 +231,23 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const __grid_constant_
     int issued = 0;
     if (producer)
         for (; issued < kGemvStages && issued < my_tiles; issued++) issue(issued);  // weights: constant
+    // the norm weight is constant too: on its way before the wait
+    if (p.norm)
+        for (int i = 4 * tid; i < p.cols; i += 4 * kGemvThreads) cp_async16(nrm + i, p.norm + i);
+    cp_async_commit();
     pdl_launch_dependents();
     pdl_wait();  // the input vector
+    // the input row in one round trip (every copy in flight before one wait)
+    for (int i = 4 * tid; i < p.cols; i += 4 * kGemvThreads) cp_async16(xin + i, p.in + i);
+    cp_async_commit();
+    cp_async_wait<0>();
+    __syncthreads();
 
     // Input: rmsnorm (forward.c:75-81) when a weight is given, then Q8_0.
     constexpr int kWarps = kGemvThreads / 32;
     double ss = 0.0;
     for (int i = tid; i < p.cols; i += kGemvThreads) {
-        const float v = p.in[i];
-        xin[i] = v;
+        const float v = xin[i];
         ss = __dadd_rn(ss, __dmul_rn((double)v, (double)v));
     }
     if (p.norm) {
@@ -252,7 +262,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const __grid_constant_
         __syncthreads();
         const float inv = s_inv;
         for (int i = tid; i < p.cols; i += kGemvThreads)
-            xin[i] = __fmul_rn(__fmul_rn(xin[i], inv), p.norm[i]);
+            xin[i] = __fmul_rn(__fmul_rn(xin[i], inv), nrm[i]);
     }
     __syncthreads();
     for (int b = warp; b < nb; b += kWarps) {  // mia_quantize_row_q8, one warp a block
@@ -404,7 +414,7 @@ __host__ __device__ inline int attn_prob_len(int max_seq) { return (max_seq + 3)
 __host__ __device__ inline size_t attn_smem_bytes(int hd, int max_seq) {
     return (size_t)kAttnRows * (hd + 4) * 4   // K slice (V tiles reuse it)
            + (size_t)attn_prob_len(max_seq) * 4  // probabilities
-           + (size_t)5 * hd * 4 + 64 * 4;     // qn, kn, vv, 2 x norm scratch, reductions
+           + (size_t)7 * hd * 4 + 64 * 4;     // qn, kn, vv, 2 x norm scratch, q/k norm weights, reductions
 }
 
 // rmsnorm of one head (forward.c:129/134, in place there) then NeoX RoPE
@@ -434,12 +444,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn(const __grid_constant_
     float *kt = fsm;                                  // [kAttnRows][hd + 4]
     float *prob = kt + (size_t)kAttnRows * (hd + 4);  // [max_seq]
     float *qn = prob + attn_prob_len(p.max_seq), *kn = qn + hd, *vv = kn + hd, *tmp = vv + hd;  // tmp: 2 x hd
-    float *red = tmp + 2 * hd;
+    float *wqn = tmp + 2 * hd, *wkn = wqn + hd;  // the q and k norm weights
+    float *red = wkn + hd;
     __shared__ int s_last;
     __shared__ float s_val;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int h = blockIdx.x, kvh = h / group;
+    // the layer's norm weights are constant: on their way before the wait
+    for (int i = tid; i < hd; i += kAttnThreads) {
+        wqn[i] = p.q_norm[i];
+        wkn[i] = p.k_norm[i];
+    }
     pdl_launch_dependents();
     pdl_wait();
     const int pos = p.args[1];
@@ -451,8 +467,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn(const __grid_constant_
     const float *kh = p.qkv + qd + (size_t)kvh * hd;
     const float *vh = p.qkv + qd + kvd + (size_t)kvh * hd;
     const double2 *cs = p.rope + (size_t)pos * (hd / 2);
-    if (warp == 0) head_norm_rope(qh, p.q_norm, qn, tmp, hd, p.eps, cs, lane);
-    else if (warp == 1) head_norm_rope(kh, p.k_norm, kn, tmp + hd, hd, p.eps, cs, lane);
+    __syncthreads();  // the norm weights
+    if (warp == 0) head_norm_rope(qh, wqn, qn, tmp, hd, p.eps, cs, lane);
+    else if (warp == 1) head_norm_rope(kh, wkn, kn, tmp + hd, hd, p.eps, cs, lane);
     else if (warp == 2) for (int i = lane; i < hd; i += 32) vv[i] = vh[i];
     __syncthreads();
     if (h % group == 0 && blockIdx.y == 0)  // forward.c:139-140

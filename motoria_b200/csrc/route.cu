@@ -155,6 +155,22 @@ __global__ void __launch_bounds__(9 * 32, 1) k_route(RouteParams p, int W, int s
         return;
     }
 
+    // the layer's ffn_norm is constant: loaded before the wait (shared by the
+    // consumer warps)
+    {
+        const float4 *src = reinterpret_cast<const float4 *>(p.L.ffn_norm);
+        float4 *dst = reinterpret_cast<float4 *>(norm);
+        const int stride = 32 * W;
+        for (int i0 = warp * 32 + lane; i0 < d / 4; i0 += 4 * stride) {
+            float4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++)
+                if (i0 + stride * u < d / 4) v[u] = __ldg(src + i0 + stride * u);
+#pragma unroll
+            for (int u = 0; u < 4; u++)
+                if (i0 + stride * u < d / 4) dst[i0 + stride * u] = v[u];
+        }
+    }
     pdl_wait();  // x, and the counters and outputs the previous call used
     const int tw0 = tg0 + warp * R;  // this warp's first token
     const int nt = max(0, min(R, p.T - tw0));
@@ -176,20 +192,6 @@ __global__ void __launch_bounds__(9 * 32, 1) k_route(RouteParams p, int W, int s
 #pragma unroll
             for (int u = 0; u < 16; u++)
                 if (i0 + 32 * u < d / 4) dst[i0 + 32 * u] = v[u];
-        }
-    }
-    {
-        const float4 *src = reinterpret_cast<const float4 *>(p.L.ffn_norm);
-        float4 *dst = reinterpret_cast<float4 *>(norm);
-        const int stride = 32 * W;
-        for (int i0 = warp * 32 + lane; i0 < d / 4; i0 += 4 * stride) {
-            float4 v[4];
-#pragma unroll
-            for (int u = 0; u < 4; u++)
-                if (i0 + stride * u < d / 4) v[u] = __ldg(src + i0 + stride * u);
-#pragma unroll
-            for (int u = 0; u < 4; u++)
-                if (i0 + stride * u < d / 4) dst[i0 + stride * u] = v[u];
         }
     }
     named_barrier_sync(1, W * 32);  // consumer warps only
