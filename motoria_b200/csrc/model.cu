@@ -619,19 +619,48 @@ __device__ __forceinline__ double sm_normal(uint64_t k, uint64_t i) {
 }
 
 // nblocks Q8_0 blocks at dst (block b at dst + b * 36).
+// Q8_0 block b of a matrix: d = |N(0, 1)| * sigma / 127 from stream kd,
+// q uniform on [-127, 127] from 16-bit chunks of stream kq.
+__device__ __forceinline__ void synth_q8_block(uint8_t *blk, size_t b, uint64_t kq, uint64_t kd,
+                                               double sigma) {
+    const float dq = (float)(fabs(sm_normal(kd, b)) * sigma / 127.0);
+    memcpy(blk, &dq, 4);
+    for (int w = 0; w < 8; w++) {  // 16-bit chunks of the q stream, 4 per word
+        const uint64_t word = sm_stream(kq, b * 8 + w);
+        for (int c = 0; c < 4; c++) {
+            const uint32_t hbits = (uint32_t)(word >> (16 * c)) & 0xFFFFu;
+            blk[4 + w * 4 + c] = (uint8_t)(int8_t)((int)((hbits * 255u) >> 16) - 127);
+        }
+    }
+}
+
 __global__ void k_synth_q8(uint8_t *dst, size_t nblocks, uint64_t kq, uint64_t kd, double sigma) {
     const size_t stride = (size_t)gridDim.x * blockDim.x;
-    for (size_t b = (size_t)blockIdx.x * blockDim.x + threadIdx.x; b < nblocks; b += stride) {
-        uint8_t *blk = dst + b * 36;
-        const float dq = (float)(fabs(sm_normal(kd, b)) * sigma / 127.0);
-        memcpy(blk, &dq, 4);
-        for (int w = 0; w < 8; w++) {  // 16-bit chunks of the q stream, 4 per word
-            const uint64_t word = sm_stream(kq, b * 8 + w);
-            for (int c = 0; c < 4; c++) {
-                const uint32_t hbits = (uint32_t)(word >> (16 * c)) & 0xFFFFu;
-                blk[4 + w * 4 + c] = (uint8_t)(int8_t)((int)((hbits * 255u) >> 16) - 127);
-            }
-        }
+    for (size_t b = (size_t)blockIdx.x * blockDim.x + threadIdx.x; b < nblocks; b += stride)
+        synth_q8_block(dst + b * 36, b, kq, kd, sigma);
+}
+
+// The experts of one staging batch in one launch: expert k's matrix mat
+// (gate, up, down) at dst + k * blob + off[mat], nb[mat] blocks, keys
+// key[k][mat] -- the values k_synth_q8 gives each matrix on its own.
+constexpr int kSynthBatch = 16;
+struct SynthExperts {
+    uint8_t *dst;
+    size_t blob, off[3], nb[3];
+    int n;
+    uint64_t kq[kSynthBatch][3], kd[kSynthBatch][3];
+    double sigma;
+};
+__global__ void k_synth_experts(const __grid_constant__ SynthExperts p) {
+    const size_t per = p.nb[0] + p.nb[1] + p.nb[2];
+    const size_t total = per * (size_t)p.n, stride = (size_t)gridDim.x * blockDim.x;
+    for (size_t g = (size_t)blockIdx.x * blockDim.x + threadIdx.x; g < total; g += stride) {
+        const int k = (int)(g / per);
+        size_t b = g - (size_t)k * per;
+        int mat = 0;
+        while (mat < 2 && b >= p.nb[mat]) b -= p.nb[mat++];
+        synth_q8_block(p.dst + (size_t)k * p.blob + p.off[mat] + b * 36, b, p.kq[k][mat], p.kd[k][mat],
+                       p.sigma);
     }
 }
 
@@ -850,7 +879,7 @@ struct PfAttnParams {
     const float *q;            // [n][qd]
     const float *kc, *vc;      // this layer's cache
     float *att;                // [n][qd]
-    int nh, nkv, hd, pos0, max_seq;
+    int nh, nkv, hd, pos0, max_seq, n;
     float scale;
 };
 
@@ -925,6 +954,137 @@ __global__ void __launch_bounds__(kPfAttnThreads) k_pf_attn(const __grid_constan
         }
         for (; j < n; j++) acc = __fadd_rn(acc, __fmul_rn(prob[j], vb[(size_t)j * kvd]));
         p.att[(size_t)t * qd + (size_t)h * hd + i] = acc;
+    }
+}
+
+// The same attention for prompts that fit: a CTA takes one kv head and TQ
+// positions, i.e. the QN = group * TQ queries that read the same K and V
+// rows, and streams those rows through shared memory once for all of them.
+// Arithmetic as k_pf_attn (and k_attn), query by query: each score a serial
+// dot over the head dimensions, the softmax's serial sum over positions in
+// order, each output dimension a serial sum over positions in order.
+// Threads: four per query (a quarter of the positions for the scores and
+// the exponentials, a quarter of the dimensions for the accumulation).
+constexpr int kPfQ = 64, kPfTJ = 32;  // queries a CTA, positions a K/V tile
+constexpr int kPfTiledMaxPos = 640;   // scores of every query stay in shared memory
+constexpr int kPfTiledMaxHd = 128;
+
+__host__ __device__ inline int pf_tq(int group) { return group >= kPfQ ? 1 : kPfQ / group; }
+__host__ __device__ inline size_t pf_attn_tiled_smem(int hd, int npos) {
+    return ((size_t)(kPfQ + kPfTJ) * (hd + 4) + (size_t)kPfQ * ((npos + 3) & ~3)) * 4;
+}
+
+__global__ void __launch_bounds__(4 * kPfQ) k_pf_attn_tiled(const __grid_constant__ PfAttnParams p) {
+    extern __shared__ __align__(16) float fsh[];
+    const int hd = p.hd, kvd = p.nkv * hd, qd = p.nh * hd, group = p.nh / p.nkv;
+    const int TQ = pf_tq(group), g = blockIdx.x, t0 = blockIdx.y * TQ;
+    const int tid = threadIdx.x, q = tid >> 2, part = tid & 3;
+    const int rs = hd + 4;  // padded row stride: four rows' 16-byte loads in distinct banks
+    const int n_cta = p.pos0 + min(t0 + TQ, p.n);  // positions any query of the CTA reads
+    const int npad = (n_cta + 3) & ~3;
+    float *qs = fsh, *kv = qs + (size_t)kPfQ * rs, *sc = kv + (size_t)kPfTJ * rs;
+    const int hg = q / TQ, tt = q - hg * TQ;
+    const int h = g * group + hg, t = t0 + tt;
+    const bool live = hg < group && t < p.n;
+    const int pq = p.pos0 + t;  // this query's position: it reads positions 0 .. pq
+    pdl_launch_dependents();
+    pdl_wait();
+    for (int v = tid; v < kPfQ * (hd / 4); v += 4 * kPfQ) {
+        const int r = v / (hd / 4), c = v - r * (hd / 4);
+        const int rhg = r / TQ, rt = t0 + (r - rhg * TQ);
+        if (rhg < group && rt < p.n)
+            cp_async16(qs + (size_t)r * rs + 4 * c, p.q + (size_t)rt * qd + (size_t)(g * group + rhg) * hd + 4 * c);
+    }
+    const float *kb = p.kc + (size_t)g * hd, *vb = p.vc + (size_t)g * hd;
+    auto load_tile = [&](const float *base, int j0) {
+        const int m = min(kPfTJ, n_cta - j0);
+        for (int v = tid; v < m * (hd / 4); v += 4 * kPfQ) {
+            const int r = v / (hd / 4), c = v - r * (hd / 4);
+            cp_async16(kv + (size_t)r * rs + 4 * c, base + (size_t)(j0 + r) * kvd + 4 * c);
+        }
+        cp_async_commit();
+        cp_async_wait<0>();
+        __syncthreads();
+    };
+    // scores: positions part, part + 4, ... of each tile
+    for (int j0 = 0; j0 < n_cta; j0 += kPfTJ) {
+        load_tile(kb, j0);
+        if (live) {
+            float acc[kPfTJ / 4];
+#pragma unroll
+            for (int m = 0; m < kPfTJ / 4; m++) acc[m] = 0.0f;
+            const float *qr = qs + (size_t)q * rs;
+            for (int i = 0; i < hd; i += 4) {
+                const float4 q4 = *reinterpret_cast<const float4 *>(qr + i);
+#pragma unroll
+                for (int m = 0; m < kPfTJ / 4; m++) {
+                    const float4 k4 = *reinterpret_cast<const float4 *>(kv + (size_t)(part + 4 * m) * rs + i);
+                    acc[m] = __fadd_rn(acc[m], __fmul_rn(q4.x, k4.x));
+                    acc[m] = __fadd_rn(acc[m], __fmul_rn(q4.y, k4.y));
+                    acc[m] = __fadd_rn(acc[m], __fmul_rn(q4.z, k4.z));
+                    acc[m] = __fadd_rn(acc[m], __fmul_rn(q4.w, k4.w));
+                }
+            }
+#pragma unroll
+            for (int m = 0; m < kPfTJ / 4; m++) {
+                const int j = j0 + part + 4 * m;
+                if (j <= pq) sc[(size_t)q * npad + j] = __fmul_rn(acc[m], p.scale);
+            }
+        }
+        __syncthreads();  // before the next tile overwrites this one
+    }
+    // softmax of each query's row (forward.c:95-101)
+    float *row = sc + (size_t)q * npad;
+    float mx = -INFINITY;
+    if (live)
+        for (int j = part; j <= pq; j += 4) mx = fmaxf(mx, row[j]);
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    if (live)
+        for (int j = part; j <= pq; j += 4) row[j] = expf_cr(__fsub_rn(row[j], mx));
+    __syncwarp();
+    float sum = 0.0f;
+    if (live && part == 0) {
+#pragma unroll 8
+        for (int j = 0; j <= pq; j++) sum = __fadd_rn(sum, row[j]);
+    }
+    sum = __shfl_sync(0xffffffffu, sum, (tid & 31) & ~3);
+    if (live)
+        for (int j = part; j <= pq; j += 4) row[j] = __fdiv_rn(row[j], sum);
+    __syncthreads();
+    // out[i] = sum over positions of p_j * v_j[i], positions in order
+    // (:155-160).  This thread's dimensions: the 16-byte chunks part,
+    // part + 4, ... (the four threads of a query read distinct banks).
+    const int nch = hd / 16;  // chunks a thread
+    float acc[kPfTiledMaxHd / 4];
+#pragma unroll
+    for (int u = 0; u < kPfTiledMaxHd / 4; u++) acc[u] = 0.0f;
+    for (int j0 = 0; j0 < n_cta; j0 += kPfTJ) {
+        load_tile(vb, j0);
+        if (live) {
+            const int m = min(kPfTJ, pq + 1 - j0);
+            for (int jj = 0; jj < m; jj++) {
+                const float pj = row[j0 + jj];
+                const float *vr = kv + (size_t)jj * rs + 4 * part;
+#pragma unroll
+                for (int k = 0; k < kPfTiledMaxHd / 16; k++) {
+                    if (k < nch) {
+                        const float4 v4 = *reinterpret_cast<const float4 *>(vr + 16 * k);
+                        acc[4 * k] = __fadd_rn(acc[4 * k], __fmul_rn(pj, v4.x));
+                        acc[4 * k + 1] = __fadd_rn(acc[4 * k + 1], __fmul_rn(pj, v4.y));
+                        acc[4 * k + 2] = __fadd_rn(acc[4 * k + 2], __fmul_rn(pj, v4.z));
+                        acc[4 * k + 3] = __fadd_rn(acc[4 * k + 3], __fmul_rn(pj, v4.w));
+                    }
+                }
+            }
+        }
+        __syncthreads();
+    }
+    if (live) {
+        float *out = p.att + (size_t)t * qd + (size_t)h * hd + 4 * part;
+#pragma unroll
+        for (int k = 0; k < kPfTiledMaxHd / 16; k++)
+            if (k < nch) *reinterpret_cast<float4 *>(out + 16 * k) = make_float4(acc[4 * k], acc[4 * k + 1], acc[4 * k + 2], acc[4 * k + 3]);
     }
 }
 
@@ -1628,22 +1788,24 @@ extern "C" int miag_model_synth(miag_model *m, uint64_t seed, char *err, size_t 
     const size_t nbg = (size_t)c.expert_hidden * (c.dim / MIAG_QK);   // gate / up blocks
     const size_t nbd = (size_t)c.dim * (c.expert_hidden / MIAG_QK);   // down blocks
     const size_t off_up = mia_align_up(nbg * 36, kMiaTensorAlign), off_down = 2 * off_up;
-    const int batch = 16;
+    const int batch = kSynthBatch;
     uint8_t *stage = nullptr;
     MCU(cudaMalloc(&stage, batch * blob));
     int rc = 0;
     for (int l = 0; l < (int)c.n_layers && rc == 0; l++)
         for (int e0 = 0; e0 < (int)c.n_experts && rc == 0; e0 += batch) {
             const int n = (int)c.n_experts - e0 < batch ? (int)c.n_experts - e0 : batch;
-            for (int k = 0; k < n; k++) {
-                uint8_t *b = stage + (size_t)k * blob;
-                const uint64_t e = (uint64_t)(e0 + k);
-                const size_t offs[3] = {0, off_up, off_down}, nbs[3] = {nbg, nbg, nbd};
-                for (int mat = 0; mat < 3; mat++)
-                    k_synth_q8<<<grid, 256, 0, m->stream>>>(
-                        b + offs[mat], nbs[mat], sm_key(seed, {kTagQw, (uint64_t)l, e, (uint64_t)mat}),
-                        sm_key(seed, {kTagDw, (uint64_t)l, e, (uint64_t)mat}), 0.02);
-            }
+            SynthExperts se{};
+            se.dst = stage, se.blob = blob, se.n = n, se.sigma = 0.02;
+            se.off[0] = 0, se.off[1] = off_up, se.off[2] = off_down;
+            se.nb[0] = nbg, se.nb[1] = nbg, se.nb[2] = nbd;
+            for (int k = 0; k < n; k++)
+                for (int mat = 0; mat < 3; mat++) {
+                    const uint64_t e = (uint64_t)(e0 + k);
+                    se.kq[k][mat] = sm_key(seed, {kTagQw, (uint64_t)l, e, (uint64_t)mat});
+                    se.kd[k][mat] = sm_key(seed, {kTagDw, (uint64_t)l, e, (uint64_t)mat});
+                }
+            k_synth_experts<<<grid, 256, 0, m->stream>>>(se);
             if (cudaGetLastError() != cudaSuccess ||
                 miag_upload_experts_device(m->moe, l, e0, n, stage, blob, m->stream, err, errlen))
                 rc = -1;
@@ -1693,6 +1855,9 @@ int ensure_prefill(miag_model *m, int n, char *err, size_t errlen) {
     MCU(cudaFuncSetAttribute(k_pf_gemv, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gsm));
     MCU(cudaFuncSetAttribute(k_pf_attn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)((m->hd + m->max_seq) * 4)));
+    if (m->hd <= kPfTiledMaxHd)
+        MCU(cudaFuncSetAttribute(k_pf_attn_tiled, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)pf_attn_tiled_smem(m->hd, kPfTiledMaxPos)));
     MCU(cudaFuncSetAttribute(k_pf_quant, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)((m->d > m->qd ? m->d : m->qd) * 4)));
     m->pf_cap = cap;
@@ -1744,8 +1909,16 @@ int enqueue_prefill(miag_model *m, int n, int pos0, cudaStream_t s, char *err, s
         at.q = m->pf_q, at.kc = m->kc + layer_off, at.vc = m->vc + layer_off, at.att = m->pf_att;
         at.nh = (int)c.n_heads, at.nkv = (int)c.n_kv_heads, at.hd = hd, at.pos0 = pos0, at.max_seq = m->max_seq;
         at.scale = 1.0f / sqrtf((float)hd);  // forward.c:143
-        MCU(launch_dependent(k_pf_attn, dim3(c.n_heads, (unsigned)n), dim3(kPfAttnThreads),
-                             (size_t)(hd + pos0 + n) * 4, s, at));
+        at.n = n;
+        const int group = (int)(c.n_heads / c.n_kv_heads);
+        if (pos0 + n <= kPfTiledMaxPos && hd <= kPfTiledMaxHd && hd % 16 == 0 && group <= kPfQ) {
+            const int TQ = pf_tq(group);
+            MCU(launch_dependent(k_pf_attn_tiled, dim3(c.n_kv_heads, (unsigned)((n + TQ - 1) / TQ)),
+                                 dim3(4 * kPfQ), pf_attn_tiled_smem(hd, pos0 + n), s, at));
+        } else {
+            MCU(launch_dependent(k_pf_attn, dim3(c.n_heads, (unsigned)n), dim3(kPfAttnThreads),
+                                 (size_t)(hd + pos0 + n) * 4, s, at));
+        }
         MCU(launch_dependent(k_pf_quant, dim3((unsigned)n), dim3(kPfThreads), (size_t)qd * 4, s,
                              (const float *)m->pf_att, qd, (const float *)nullptr, c.norm_eps, qd, m->pf_xq,
                              pf_pitch(qd)));
