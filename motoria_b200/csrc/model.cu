@@ -682,8 +682,8 @@ __global__ void k_synth_f32(float *dst, size_t n, uint64_t k, double sigma, int 
 // grouped expert kernels of the prefill regime), and the head runs for the
 // last position only.
 
-constexpr int kPfTok = 32;       // positions per token tile: a lane each
-constexpr int kPfThreads = 256;  // 8 warps: rows of the weight tile
+constexpr int kPfTok = 32;       // positions per token tile
+constexpr int kPfThreads = 128;  // 4 warps: 8 positions each
 constexpr int kPfAttnThreads = 256;
 
 // Bytes per position of the quantized inputs: the int8 values [cols], then
@@ -695,16 +695,15 @@ __host__ __device__ inline int pf_pitch(int cols) {
     return p;
 }
 
-// Rows of a weight tile: as many as fit beside one token tile of inputs.
-__host__ inline int pf_tile_rows(int cols) {
-    const int row_bytes = cols / MIAG_QK * 36;
-    const size_t budget = 200 * 1024 - (size_t)kPfTok * pf_pitch(cols);
-    int R = (int)(budget / row_bytes) & ~7;
-    return R < 8 ? 8 : R > 16 ? 16 : R;  // 16 rows: two CTAs an SM at 2048 columns
+// A weight tile is 16 rows (one int8 MMA's M), staged with a 16-byte pad per
+// row where the row length allows (rows land in distinct banks).
+constexpr int kPfRows = 16;
+__host__ __device__ inline int pf_wstride(int cols) {
+    const int rb = cols / MIAG_QK * 36;
+    return rb % 16 == 0 ? rb + 16 : rb;
 }
-
-__host__ inline size_t pf_gemv_smem(int cols, int R) {
-    return (((size_t)R * (cols / MIAG_QK * 36) + 15) & ~(size_t)15) + (size_t)kPfTok * pf_pitch(cols) + 16;
+__host__ inline size_t pf_gemv_smem(int cols) {
+    return (((size_t)kPfRows * pf_wstride(cols) + 15) & ~(size_t)15) + (size_t)kPfTok * pf_pitch(cols);
 }
 
 // x[t] = dequant(token_embd[tokens[t]]) (forward.c:205-208, quant.c:29-38).
@@ -772,7 +771,7 @@ __global__ void __launch_bounds__(kPfThreads) k_pf_quant(const float *in, int in
 
 struct PfGemvParams {
     const uint8_t *w;   // [rows][cols / 32] 36-byte Q8_0 blocks (the file's layout)
-    int rows, cols, R;  // R rows per tile
+    int rows, cols;
     const uint8_t *xq;  // [n][pitch] (k_pf_quant)
     int pitch, n;
     float *out;         // out[t * out_stride + r]
@@ -780,65 +779,90 @@ struct PfGemvParams {
     int *err;
 };
 
+__device__ __forceinline__ void pf_mma_s8(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+    // D = A * B + kMagicBits: the int32 dot of each (row, position), exact,
+    // read as a float it is 12582912 + dot (|dot| < 2^22)
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+        "{%8, %9}, {%10, %10, %10, %10};"
+        : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(kMagicBits));
+}
+
 // out[t][r] (+)= the Q8_0 dot of weight row r with position t's input: per
-// 32-block the exact int32 dot, ((float)dot * w.d) * x.d, added in block
-// order (matmul.c:19-28), each operation rounded on its own.  Grid (row
-// tiles, token tiles); a CTA stages its R weight rows and 32 positions'
-// inputs with two bulk copies, then warp w computes rows w, w + 8, ... for
-// the 32 positions, a lane a position.
+// 32-block the exact int32 dot (one int8 tensor-core MMA, m16n8k32, for 16
+// rows x 8 positions), then ((float)dot * w.d) * x.d added in block order
+// (matmul.c:19-28), each operation rounded on its own.  Grid (row tiles of
+// 16, position tiles of 32); a CTA stages its rows (cp.async, padded) and 32
+// positions' inputs, then warp w takes positions 8w .. 8w + 7; each lane
+// holds the sums of rows (g, g + 8) x positions (2tq, 2tq + 1).
 __global__ void __launch_bounds__(kPfThreads) k_pf_gemv(const __grid_constant__ PfGemvParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
-    const int nb = p.cols / MIAG_QK, row_bytes = nb * 36;
+    const int nb = p.cols / MIAG_QK, row_bytes = nb * 36, ws = pf_wstride(p.cols);
     uint8_t *wt = smem;
-    uint8_t *xt = smem + (((size_t)p.R * row_bytes + 15) & ~(size_t)15);
-    uint64_t *bar = reinterpret_cast<uint64_t *>(xt + (size_t)kPfTok * p.pitch);
-    const int r0 = blockIdx.x * p.R, t0 = blockIdx.y * kPfTok;
-    const int nr = min(p.R, p.rows - r0), nt = min(kPfTok, p.n - t0);
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    // a ragged last tile may read up to 15 bytes past the matrix (the dense
-    // section is allocated with slack for that, as for k_gemv)
-    const uint32_t wbytes = ((uint32_t)(nr * row_bytes) + 15u) & ~15u, xbytes = (uint32_t)(nt * p.pitch);
-    if (tid == 0) {
-        mbar_init(bar, 1);
-        fence_barrier_init();
-        mbar_arrive_expect_tx(bar, wbytes + xbytes);
-        bulk_g2s(wt, p.w + (size_t)r0 * row_bytes, wbytes, bar);  // weights: constant
+    uint8_t *xt = smem + (((size_t)kPfRows * ws + 15) & ~(size_t)15);
+    const int r0 = blockIdx.x * kPfRows, t0 = blockIdx.y * kPfTok;
+    const int nr = min(kPfRows, p.rows - r0), nt = min(kPfTok, p.n - t0);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, tq = lane & 3;
+    // weights are constant: their copies go out before the wait
+    if (ws != row_bytes) {
+        const int cpr = row_bytes / 16;  // 16-byte chunks a row
+        for (int v = tid; v < nr * cpr; v += kPfThreads) {
+            const int r = v / cpr, c = v - r * cpr;
+            cp_async16(wt + (size_t)r * ws + 16 * c, p.w + (size_t)(r0 + r) * row_bytes + 16 * c);
+        }
+    } else {  // rows of a length that is no multiple of 16: the tile as it lies
+        const int chunks = (nr * row_bytes + 15) / 16;  // may read 15 bytes past (the section has slack)
+        for (int v = tid; v < chunks; v += kPfThreads)
+            cp_async16(wt + 16 * v, p.w + (size_t)r0 * row_bytes + 16 * v);
     }
     pdl_launch_dependents();
     pdl_wait();  // the inputs (and, for a residual, the outputs) of earlier launches
-    if (tid == 0) bulk_g2s(xt, p.xq + (size_t)t0 * p.pitch, xbytes, bar);
-    __syncthreads();
-    if (!mbar_wait(bar, 0)) {
-        set_error(p.err, kErrModelWait);
-        if (tid == 0) mbar_wait(bar, 0);  // nothing may land after the CTA leaves
-        return;
+    {
+        const int cpt = p.pitch / 16;
+        for (int v = tid; v < nt * cpt; v += kPfThreads)
+            cp_async16(xt + 16 * v, p.xq + (size_t)t0 * p.pitch + 16 * v);
     }
-    if (lane >= nt) return;
-    const uint32_t xa = smem_addr(xt) + (uint32_t)(lane * p.pitch);
-    const uint32_t xsa = xa + (uint32_t)p.cols;
-    float *out = p.out + (size_t)(t0 + lane) * p.out_stride + r0;
-    for (int r = warp; r < nr; r += kPfThreads / 32) {
-        const uint32_t wa = smem_addr(wt) + (uint32_t)(r * row_bytes);
-        float s = 0.0f;
-        for (int b = 0; b < nb; b++) {
-            const uint32_t wb = wa + (uint32_t)(b * 36);
-            int4 xv0, xv1;
-            asm volatile("ld.shared.v4.s32 {%0, %1, %2, %3}, [%4];"
-                         : "=r"(xv0.x), "=r"(xv0.y), "=r"(xv0.z), "=r"(xv0.w) : "r"(xa + (uint32_t)(b * 32)));
-            asm volatile("ld.shared.v4.s32 {%0, %1, %2, %3}, [%4];"
-                         : "=r"(xv1.x), "=r"(xv1.y), "=r"(xv1.z), "=r"(xv1.w) : "r"(xa + (uint32_t)(b * 32 + 16)));
-            int acc = 0;
-            acc = __dp4a((int)lds_u32(wb + 4u), xv0.x, acc);
-            acc = __dp4a((int)lds_u32(wb + 8u), xv0.y, acc);
-            acc = __dp4a((int)lds_u32(wb + 12u), xv0.z, acc);
-            acc = __dp4a((int)lds_u32(wb + 16u), xv0.w, acc);
-            acc = __dp4a((int)lds_u32(wb + 20u), xv1.x, acc);
-            acc = __dp4a((int)lds_u32(wb + 24u), xv1.y, acc);
-            acc = __dp4a((int)lds_u32(wb + 28u), xv1.z, acc);
-            acc = __dp4a((int)lds_u32(wb + 32u), xv1.w, acc);
-            s = __fadd_rn(s, __fmul_rn(__fmul_rn(__int2float_rn(acc), lds32(wb)), lds32(xsa + 4u * b)));
+    cp_async_commit();
+    cp_async_wait<0>();
+    __syncthreads();
+    const int tw = 8 * warp;  // this warp's first position in the tile
+    if (tw >= nt) return;
+    // rows g and g + 8 (clamped into the tile: a row past the matrix is read,
+    // never stored), positions tw + g (B operand) and tw + 2tq, + 1 (sums)
+    const int ra = min(g, nr - 1), rb = min(g + 8, nr - 1);
+    const uint32_t wa = smem_addr(wt) + (uint32_t)(ra * ws), wb = smem_addr(wt) + (uint32_t)(rb * ws);
+    const int tb = min(tw + g, nt - 1);
+    const uint32_t xb = smem_addr(xt) + (uint32_t)(tb * p.pitch);
+    const int t_lo = min(tw + 2 * tq, nt - 1), t_hi = min(tw + 2 * tq + 1, nt - 1);
+    const uint32_t xs_lo = smem_addr(xt) + (uint32_t)(t_lo * p.pitch + p.cols);
+    const uint32_t xs_hi = smem_addr(xt) + (uint32_t)(t_hi * p.pitch + p.cols);
+    float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    for (int b = 0; b < nb; b++) {
+        const uint32_t ba = wa + (uint32_t)(b * 36), bb = wb + (uint32_t)(b * 36);
+        const uint32_t a0 = lds_u32(ba + 4u + 4u * tq), a1 = lds_u32(bb + 4u + 4u * tq);
+        const uint32_t a2 = lds_u32(ba + 20u + 4u * tq), a3 = lds_u32(bb + 20u + 4u * tq);
+        const uint32_t xq0 = xb + (uint32_t)(b * 32);
+        const uint32_t b0 = lds_u32(xq0 + 4u * tq), b1 = lds_u32(xq0 + 16u + 4u * tq);
+        int c[4];
+        pf_mma_s8(c, a0, a1, a2, a3, b0, b1);
+        const float wd_a = lds32(ba), wd_b = lds32(bb);
+        const float xd_lo = lds32(xs_lo + 4u * b), xd_hi = lds32(xs_hi + 4u * b);
+        const float d0 = __fadd_rn(__int_as_float(c[0]), -kMagic), d1 = __fadd_rn(__int_as_float(c[1]), -kMagic);
+        const float d2 = __fadd_rn(__int_as_float(c[2]), -kMagic), d3 = __fadd_rn(__int_as_float(c[3]), -kMagic);
+        s[0] = __fadd_rn(s[0], __fmul_rn(__fmul_rn(d0, wd_a), xd_lo));
+        s[1] = __fadd_rn(s[1], __fmul_rn(__fmul_rn(d1, wd_a), xd_hi));
+        s[2] = __fadd_rn(s[2], __fmul_rn(__fmul_rn(d2, wd_b), xd_lo));
+        s[3] = __fadd_rn(s[3], __fmul_rn(__fmul_rn(d3, wd_b), xd_hi));
+    }
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        const int r = (k < 2 ? g : g + 8), t = tw + 2 * tq + (k & 1);
+        if (r < nr && t < nt) {
+            float *o = p.out + (size_t)(t0 + t) * p.out_stride + r0 + r;
+            *o = p.resid ? __fadd_rn(*o, s[k]) : s[k];
         }
-        out[r] = p.resid ? __fadd_rn(out[r], s) : s;
     }
 }
 
@@ -1851,7 +1875,7 @@ int ensure_prefill(miag_model *m, int n, char *err, size_t errlen) {
     };
     for (auto &a : allocs) MCU(cudaMalloc(a.p, a.bytes));
     MCU(cudaMallocHost(&m->h_pf_tok, (size_t)cap * 4));
-    const size_t gsm = std::max(pf_gemv_smem(m->d, pf_tile_rows(m->d)), pf_gemv_smem(m->qd, pf_tile_rows(m->qd)));
+    const size_t gsm = std::max(pf_gemv_smem(m->d), pf_gemv_smem(m->qd));
     MCU(cudaFuncSetAttribute(k_pf_gemv, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gsm));
     MCU(cudaFuncSetAttribute(k_pf_attn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)((m->hd + m->max_seq) * 4)));
@@ -1867,11 +1891,11 @@ int ensure_prefill(miag_model *m, int n, char *err, size_t errlen) {
 int pf_gemv(miag_model *m, const uint8_t *w, int rows, int cols, float *out, int out_stride, int resid,
             int n, cudaStream_t s, char *err, size_t errlen) {
     PfGemvParams g{};
-    g.w = w, g.rows = rows, g.cols = cols, g.R = pf_tile_rows(cols);
+    g.w = w, g.rows = rows, g.cols = cols;
     g.xq = m->pf_xq, g.pitch = pf_pitch(cols), g.n = n;
     g.out = out, g.out_stride = out_stride, g.resid = resid, g.err = m->d_err;
-    const dim3 grid((unsigned)((rows + g.R - 1) / g.R), (unsigned)((n + kPfTok - 1) / kPfTok));
-    MCU(launch_dependent(k_pf_gemv, grid, dim3(kPfThreads), pf_gemv_smem(cols, g.R), s, g));
+    const dim3 grid((unsigned)((rows + kPfRows - 1) / kPfRows), (unsigned)((n + kPfTok - 1) / kPfTok));
+    MCU(launch_dependent(k_pf_gemv, grid, dim3(kPfThreads), pf_gemv_smem(cols), s, g));
     return 0;
 }
 
