@@ -989,8 +989,8 @@ __global__ void __launch_bounds__(kPfAttnThreads) k_pf_attn(const __grid_constan
 // order, each output dimension a serial sum over positions in order.
 // Threads: four per query (a quarter of the positions for the scores and
 // the exponentials, a quarter of the dimensions for the accumulation).
-constexpr int kPfQ = 64, kPfTJ = 32;  // queries a CTA, positions a K/V tile
-constexpr int kPfTiledMaxPos = 640;   // scores of every query stay in shared memory
+constexpr int kPfQ = 32, kPfTJ = 32;  // queries a CTA, positions a K/V tile
+constexpr int kPfTiledMaxPos = 1280;  // scores of every query stay in shared memory
 constexpr int kPfTiledMaxHd = 128;
 
 __host__ __device__ inline int pf_tq(int group) { return group >= kPfQ ? 1 : kPfQ / group; }
@@ -1001,7 +1001,9 @@ __host__ __device__ inline size_t pf_attn_tiled_smem(int hd, int npos) {
 __global__ void __launch_bounds__(4 * kPfQ) k_pf_attn_tiled(const __grid_constant__ PfAttnParams p) {
     extern __shared__ __align__(16) float fsh[];
     const int hd = p.hd, kvd = p.nkv * hd, qd = p.nh * hd, group = p.nh / p.nkv;
-    const int TQ = pf_tq(group), g = blockIdx.x, t0 = blockIdx.y * TQ;
+    // the longest (last) positions first, so that the short ones fill the
+    // last wave
+    const int TQ = pf_tq(group), g = blockIdx.x, t0 = ((int)gridDim.y - 1 - (int)blockIdx.y) * TQ;
     const int tid = threadIdx.x, q = tid >> 2, part = tid & 3;
     const int rs = hd + 4;  // padded row stride: four rows' 16-byte loads in distinct banks
     const int n_cta = p.pos0 + min(t0 + TQ, p.n);  // positions any query of the CTA reads
