@@ -384,14 +384,12 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const __grid_constant_
 // Grid (n_heads, kAttnSplit).  Every CTA normalises and rotates its head's
 // q and its kv head's k (cheap, and bit-identical in each CTA); CTA y of
 // head h scores the position slices y, y + kAttnSplit, ... (a thread a
-// position: the reference's serial dot, then * scale) into a scratch row.
-// The last CTA of the head to finish (a ticket) runs the softmax -- max,
-// exp, the serial sum, the division -- and the accumulation over positions,
-// a thread a dimension in position order, V streamed through shared memory.
+// position: the reference's serial dot, then * scale) into a scratch row;
+// k_attn_out then forms the softmax and the accumulation over positions.
 // The new k and v rows are written to the cache by the first CTA of each
 // kv group; at position pos every CTA uses its own copies.
 
-constexpr int kAttnThreads = 256, kAttnSplit = 4, kAttnRows = 256, kAttnVRows = 64, kAttnVBufs = 4;
+constexpr int kAttnThreads = 256, kAttnSplit = 4, kAttnRows = 256;
 
 struct AttnParams {
     const float *qkv;  // q [qd] | k [kvd] | v [kvd]
@@ -414,7 +412,7 @@ __host__ __device__ inline int attn_prob_len(int max_seq) { return (max_seq + 3)
 __host__ __device__ inline size_t attn_smem_bytes(int hd, int max_seq) {
     return (size_t)kAttnRows * (hd + 4) * 4   // K slice (V tiles reuse it)
            + (size_t)attn_prob_len(max_seq) * 4  // probabilities
-           + (size_t)7 * hd * 4 + 64 * 4;     // qn, kn, vv, 2 x norm scratch, q/k norm weights, reductions
+           + (size_t)7 * hd * 4;              // qn, kn, vv, 2 x norm scratch, q/k norm weights
 }
 
 // rmsnorm of one head (forward.c:129/134, in place there) then NeoX RoPE
@@ -445,10 +443,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn(const __grid_constant_
     float *prob = kt + (size_t)kAttnRows * (hd + 4);  // [max_seq]
     float *qn = prob + attn_prob_len(p.max_seq), *kn = qn + hd, *vv = kn + hd, *tmp = vv + hd;  // tmp: 2 x hd
     float *wqn = tmp + 2 * hd, *wkn = wqn + hd;  // the q and k norm weights
-    float *red = wkn + hd;
-    __shared__ int s_last;
-    __shared__ float s_val;
-
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int h = blockIdx.x, kvh = h / group;
     // the layer's norm weights are constant: on their way before the wait
@@ -509,35 +503,52 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn(const __grid_constant_
         __syncthreads();
     }
 
-    // The head's last CTA finishes it.
-    if (tid == 0) {
-        __threadfence();
-        s_last = atomicAdd(&p.ticket[h], 1u) == gridDim.y - 1;
-    }
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
+}
 
-    // V rows stream through a ring of kAttnVBufs tiles of kAttnVRows rows in
-    // the K slice's space, kAttnVBufs - 1 tiles ahead of the accumulation;
-    // the first ones go out before the softmax, whose serial sum they overlap.
-    const int ntile = (n + kAttnVRows - 1) / kAttnVRows;
+// The rest of the attention (forward.c:154-161), a launch of its own so that
+// the V rows of a head are read by several CTAs: grid (n_heads,
+// kAttnOutSplit), CTA y the output dimensions [y hd / S, (y + 1) hd / S).
+// Every CTA forms the head's softmax from the scores (max, exp, the serial
+// sum, the division: the same operations on the same values, so the same
+// probabilities), then accumulates its dimensions over the positions in
+// order, V streamed through shared memory.
+constexpr int kAttnOutSplit = 4, kAttnOutRows = 64, kAttnOutBufs = 4;
+
+// Dimension slices a head's output is split into: four where a slice stays
+// a whole number of 16-byte chunks, else one.
+__host__ __device__ inline int attn_out_split(int hd) { return hd % 16 == 0 ? kAttnOutSplit : 1; }
+__host__ __device__ inline size_t attn_out_smem_bytes(int hd, int max_seq) {
+    return (size_t)attn_prob_len(max_seq) * 4 + (size_t)kAttnOutBufs * kAttnOutRows * (hd / attn_out_split(hd)) * 4;
+}
+
+__global__ void __launch_bounds__(kAttnThreads, 1) k_attn_out(const __grid_constant__ AttnParams p) {
+    extern __shared__ __align__(16) float fsm[];
+    const int hd = p.hd, kvd = p.nkv * hd, group = p.nh / p.nkv;
+    const int dq = hd / (int)gridDim.y, d0 = blockIdx.y * dq, c4 = dq / 4;
+    float *prob = fsm;                                   // [max_seq]
+    float *vt = prob + attn_prob_len(p.max_seq);         // [bufs][rows][dq]
+    __shared__ float red[kAttnThreads / 32];
+    __shared__ float s_val;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int h = blockIdx.x, kvh = h / group;
+    pdl_launch_dependents();
+    pdl_wait();  // the scores, and the cache rows of this position
+    const int pos = p.args[1];
+    if (pos < 0 || pos >= p.max_seq) return;  // reported by k_attn
+    const int n = pos + 1;
+    const int ntile = (n + kAttnOutRows - 1) / kAttnOutRows;
     auto load_v = [&](int k) {  // always commits a group (empty past the end)
         if (k < ntile) {
-            float *dst = kt + (size_t)(k % kAttnVBufs) * kAttnVRows * hd;
-            const int t0 = k * kAttnVRows, m = n - t0 < kAttnVRows ? n - t0 : kAttnVRows;
+            float *dst = vt + (size_t)(k % kAttnOutBufs) * kAttnOutRows * dq;
+            const int t0 = k * kAttnOutRows, m = n - t0 < kAttnOutRows ? n - t0 : kAttnOutRows;
             for (int i = tid; i < m * c4; i += kAttnThreads) {
-                const int r = i / c4, c = i % c4, t = t0 + r;
-                float *o = dst + (size_t)r * hd + 4 * c;
-                if (t == pos)
-                    *reinterpret_cast<float4 *>(o) = *reinterpret_cast<const float4 *>(vv + 4 * c);
-                else
-                    cp_async16(o, p.vc + (size_t)t * kvd + (size_t)kvh * hd + 4 * c);
+                const int r = i / c4, c = i % c4;
+                cp_async16(dst + (size_t)r * dq + 4 * c, p.vc + (size_t)(t0 + r) * kvd + (size_t)kvh * hd + d0 + 4 * c);
             }
         }
         cp_async_commit();
     };
-    for (int k = 0; k < kAttnVBufs - 1; k++) load_v(k);
+    for (int k = 0; k < kAttnOutBufs - 1; k++) load_v(k);
 
     // softmax (forward.c:95-101)
     float mx = -INFINITY;
@@ -564,7 +575,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn(const __grid_constant_
 #pragma unroll 8
         for (int t = 0; t < n; t++) sum = __fadd_rn(sum, prob[t]);
         s_val = sum;
-        p.ticket[h] = 0u;
     }
     __syncthreads();
     const float sum = s_val;
@@ -573,18 +583,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn(const __grid_constant_
     // out[i] = sum over t of p_t * v_t[i], t in order (forward.c:155-160).
     float acc = 0.0f;
     for (int k = 0; k < ntile; k++) {
-        load_v(k + kAttnVBufs - 1);  // into the buffer read at k - 1
-        cp_async_wait<kAttnVBufs - 1>();  // tile k has landed
+        load_v(k + kAttnOutBufs - 1);  // into the buffer read at k - 1
+        cp_async_wait<kAttnOutBufs - 1>();  // tile k has landed
         __syncthreads();
-        if (tid < hd) {
-            const float *vt = kt + (size_t)(k % kAttnVBufs) * kAttnVRows * hd;
-            const int t0 = k * kAttnVRows, m = n - t0 < kAttnVRows ? n - t0 : kAttnVRows;
+        if (tid < dq) {
+            const float *v = vt + (size_t)(k % kAttnOutBufs) * kAttnOutRows * dq;
+            const int t0 = k * kAttnOutRows, m = n - t0 < kAttnOutRows ? n - t0 : kAttnOutRows;
 #pragma unroll 8
-            for (int r = 0; r < m; r++) acc = __fadd_rn(acc, __fmul_rn(prob[t0 + r], vt[(size_t)r * hd + tid]));
+            for (int r = 0; r < m; r++) acc = __fadd_rn(acc, __fmul_rn(prob[t0 + r], v[(size_t)r * dq + tid]));
         }
         __syncthreads();  // before the next load_v reuses a buffer
     }
-    if (tid < hd) p.att[(size_t)h * hd + tid] = acc;
+    if (tid < dq) p.att[(size_t)h * hd + d0 + tid] = acc;
 }
 
 // ---------------------------------------------------------------------------
@@ -1432,10 +1442,12 @@ int enqueue_step(miag_model *m, cudaStream_t s, char *err, size_t errlen) {
         a.scale = 1.0f / sqrtf((float)m->hd);  // forward.c:143
         a.err = m->d_err;
         MCU(launch_dependent(k_attn, dim3(c.n_heads, kAttnSplit), dim3(kAttnThreads), m->attn_smem, s, a));
+        MCU(launch_dependent(k_attn_out, dim3(c.n_heads, attn_out_split(m->hd)), dim3(kAttnThreads),
+                             attn_out_smem_bytes(m->hd, m->max_seq), s, a));
         GemvParams o = m->wo_p;
         o.seg[0].w = tensor(m, mia_layer_tensor(l, kWo));
         MCU(gemv_launch(o, grid_of(m, o), m->wo_smem, s));
-        launches += 3;
+        launches += 4;
         if (miag_moe_async(m->moe, l, m->x, 1, s, err, errlen) != 0) return -1;
         launches += miag_last_launch_count(m->moe);
     }
@@ -1688,7 +1700,9 @@ extern "C" int miag_model_open(miag_model **out, miag_ctx *moe, const miag_mia_c
         if ((e = cudaFuncSetAttribute(k_gemv, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)need)) !=
                 cudaSuccess ||
             (e = cudaFuncSetAttribute(k_attn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)m->attn_smem)) != cudaSuccess)
+                                      (int)m->attn_smem)) != cudaSuccess ||
+            (e = cudaFuncSetAttribute(k_attn_out, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)attn_out_smem_bytes(m->hd, max_seq))) != cudaSuccess)
             return fail("kernel attributes", e);
     }
     *out = m;
