@@ -251,6 +251,31 @@ def test_sampled_generation_equals_the_reference_sampler(models, temp, top_p, se
     assert got.tolist() == want, f"{name}: {got.tolist()} vs {want}"
 
 
+def test_long_prefill_equals_single_steps(tmp_path, torch_cuda):
+    """A prompt past the tiled prefill attention's 1280 positions (the
+    kernel with one CTA per head and position takes it) and one below it,
+    on the tiny shapes: the last logits equal the reference's step loop."""
+    build.build()
+    if O.ref_crexp() is None:
+        pytest.skip("the reference builds (oracle/_ref) are absent")
+    cfg = MiaConfig(**CASES["tiny"]["cfg"])
+    path = str(tmp_path / "tiny_long.mia")
+    write_model(path, cfg, seed=515)
+    max_seq = 1400
+    ref = RefModel(O.ref_crexp(), path, max_seq, cfg.vocab)
+    toks = np.random.default_rng(3).integers(0, cfg.vocab, size=1330).astype(np.int32)
+    want = {}
+    for pos, t in enumerate(toks):
+        logits = ref.step(int(t), pos)
+        if pos + 1 in (1000, 1330):
+            want[pos + 1] = logits
+    ref.close()
+    with Model.open_file(path, device=0, max_seq=max_seq) as gpu:
+        for n in (1000, 1330):
+            got = gpu.prefill(toks[:n], 0)
+            assert np.array_equal(got.view(np.uint32), want[n].view(np.uint32)), n
+
+
 def test_prefill_rejects_bad_arguments(models):
     name, case, cfg, _, ref, gpu = models
     with pytest.raises(N.MiagError):
