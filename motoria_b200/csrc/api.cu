@@ -641,26 +641,36 @@ static int moe_pipelined(miag_ctx *c, int layer, float *x, int n_tokens, char *e
     const int chunks = c->transfer_chunks;
     const int per = ((n_tokens + chunks - 1) / chunks + 31) & ~31;
     int launches = 0, n_chunks = 0;
-    for (int k = 0; k < chunks && k * per < n_tokens; k++, n_chunks++) {
-        const int t0 = k * per, tk = std::min(per, n_tokens - t0);
-        CU(cudaMemcpyAsync(c->x_dev + (size_t)t0 * c->shape.dim, x + (size_t)t0 * c->shape.dim,
-                           (size_t)tk * row, cudaMemcpyHostToDevice, c->copy_stream));
-        CU(cudaEventRecord(c->pipe_events[k], c->copy_stream));
-        CU(cudaStreamWaitEvent(c->stream, c->pipe_events[k], 0));
-        if (ensure_ws(c, tk, err, errlen)) return -1;  // counts only: the buffers hold n_tokens
-        if (enqueue_moe(c, layer, c->x_dev + (size_t)t0 * c->shape.dim, tk, c->stream, err, errlen))
-            return -1;
-        launches += c->last_launches;
-        CU(cudaEventRecord(c->pipe_events[kPipeMaxChunks + k], c->stream));
+    auto enqueue = [&]() -> int {
+        for (int k = 0; k < chunks && k * per < n_tokens; k++, n_chunks++) {
+            const int t0 = k * per, tk = std::min(per, n_tokens - t0);
+            CU(cudaMemcpyAsync(c->x_dev + (size_t)t0 * c->shape.dim, x + (size_t)t0 * c->shape.dim,
+                               (size_t)tk * row, cudaMemcpyHostToDevice, c->copy_stream));
+            CU(cudaEventRecord(c->pipe_events[k], c->copy_stream));
+            CU(cudaStreamWaitEvent(c->stream, c->pipe_events[k], 0));
+            if (ensure_ws(c, tk, err, errlen)) return -1;  // counts only: the buffers hold n_tokens
+            if (enqueue_moe(c, layer, c->x_dev + (size_t)t0 * c->shape.dim, tk, c->stream, err, errlen))
+                return -1;
+            launches += c->last_launches;
+            CU(cudaEventRecord(c->pipe_events[kPipeMaxChunks + k], c->stream));
+        }
+        for (int k = 0; k < n_chunks; k++) {
+            const int t0 = k * per, tk = std::min(per, n_tokens - t0);
+            CU(cudaStreamWaitEvent(c->copy_stream, c->pipe_events[kPipeMaxChunks + k], 0));
+            CU(cudaMemcpyAsync(x + (size_t)t0 * c->shape.dim, c->x_dev + (size_t)t0 * c->shape.dim,
+                               (size_t)tk * row, cudaMemcpyDeviceToHost, c->copy_stream));
+        }
+        // after the last chunk's block: the error word with the results
+        CU(cudaMemcpyAsync(c->h_err, c->d_err, sizeof(int), cudaMemcpyDeviceToHost, c->copy_stream));
+        return 0;
+    };
+    if (enqueue() != 0) {
+        // nothing enqueued may still write into the caller's buffer once the
+        // call has returned
+        cudaStreamSynchronize(c->copy_stream);
+        cudaStreamSynchronize(c->stream);
+        return -1;
     }
-    for (int k = 0; k < n_chunks; k++) {
-        const int t0 = k * per, tk = std::min(per, n_tokens - t0);
-        CU(cudaStreamWaitEvent(c->copy_stream, c->pipe_events[kPipeMaxChunks + k], 0));
-        CU(cudaMemcpyAsync(x + (size_t)t0 * c->shape.dim, c->x_dev + (size_t)t0 * c->shape.dim,
-                           (size_t)tk * row, cudaMemcpyDeviceToHost, c->copy_stream));
-    }
-    // after the last chunk's block: the error word with the results
-    CU(cudaMemcpyAsync(c->h_err, c->d_err, sizeof(int), cudaMemcpyDeviceToHost, c->copy_stream));
     CU(cudaStreamSynchronize(c->copy_stream));
     c->last_launches = launches;
     return read_device_error(c, err, errlen, *c->h_err);
