@@ -85,6 +85,7 @@ SIGNATURES = {
     "miag_last_launch_count": (C.c_int, [C.c_void_p]),
     "miag_set_prefill_kernel": (C.c_int, [C.c_void_p, C.c_int, C.c_char_p, C.c_size_t]),
     "miag_set_transfer_chunks": (C.c_int, [C.c_void_p, C.c_int]),
+    "miag_set_host_copy_threads": (C.c_int, [C.c_void_p, C.c_int]),
     "miag_prefill_kernel": (C.c_int, [C.c_void_p]),
     "miag_mia_write": (C.c_int, [C.c_char_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                  C.c_void_p, C.c_size_t, C.c_char_p, C.c_size_t]),

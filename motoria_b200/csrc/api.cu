@@ -1,9 +1,13 @@
 // api.cu -- the libmiag C ABI (include/miag/miag.h): context, HBM expert
 // store, workspace and the MoE block launch sequence.
+#include <condition_variable>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <memory>
+#include <mutex>
 #include <new>
+#include <thread>
 #include <vector>
 
 #include "../../include/miag/miag.h"
@@ -14,6 +18,75 @@
 using namespace miag;
 
 namespace {
+
+// Host threads that split one memcpy between them: miag_moe's copies between
+// the caller's pageable buffer and the context's pinned staging buffer.  The
+// calling thread copies the first part; copy() returns when every part is
+// done, so a worker never misses a generation.
+class CopyPool {
+  public:
+    explicit CopyPool(int workers) {
+        for (int i = 0; i < workers; i++) threads_.emplace_back([this, i] { run(i + 1); });
+    }
+    ~CopyPool() {
+        {
+            std::lock_guard<std::mutex> g(m_);
+            stop_ = true;
+        }
+        wake_.notify_all();
+        for (std::thread &t : threads_) t.join();
+    }
+    int workers() const { return (int)threads_.size(); }
+    void copy(void *dst, const void *src, size_t bytes) {
+        const int parts = workers() + 1;
+        if (parts == 1 || bytes < ((size_t)256 << 10)) {
+            memcpy(dst, src, bytes);
+            return;
+        }
+        {
+            std::lock_guard<std::mutex> g(m_);
+            dst_ = (char *)dst;
+            src_ = (const char *)src;
+            bytes_ = bytes;
+            parts_ = parts;
+            left_ = parts - 1;
+            gen_++;
+        }
+        wake_.notify_all();
+        part(0);
+        std::unique_lock<std::mutex> l(m_);
+        done_.wait(l, [this] { return left_ == 0; });
+    }
+
+  private:
+    void part(int i) const {
+        const size_t per = ((bytes_ + parts_ - 1) / parts_ + 63) & ~(size_t)63;
+        const size_t b = std::min(bytes_, (size_t)i * per), e = std::min(bytes_, b + per);
+        if (e > b) memcpy(dst_ + b, src_ + b, e - b);
+    }
+    void run(int i) {
+        uint64_t seen = 0;
+        std::unique_lock<std::mutex> l(m_);
+        for (;;) {
+            wake_.wait(l, [&] { return stop_ || gen_ != seen; });
+            if (stop_) return;
+            seen = gen_;
+            l.unlock();
+            part(i);
+            l.lock();
+            if (--left_ == 0) done_.notify_one();
+        }
+    }
+    std::vector<std::thread> threads_;
+    std::mutex m_;
+    std::condition_variable wake_, done_;
+    bool stop_ = false;
+    uint64_t gen_ = 0;
+    int parts_ = 1, left_ = 0;
+    char *dst_ = nullptr;
+    const char *src_ = nullptr;
+    size_t bytes_ = 0;
+};
 
 struct LayerState {
     float *ffn_norm = nullptr;
@@ -44,6 +117,12 @@ struct miag_ctx {
     cudaStream_t copy_stream = nullptr;
     std::vector<cudaEvent_t> pipe_events;
     int transfer_chunks = 4;  // miag_set_transfer_chunks
+    // pageable callers: host threads copy through a pinned staging buffer
+    // (miag_set_host_copy_threads; 0 = the driver's own pageable copies)
+    int host_threads = -1;  // -1: not chosen yet (min(8, cores - 1))
+    std::unique_ptr<CopyPool> copy_pool;
+    float *pipe_host = nullptr;
+    size_t pipe_host_bytes = 0;
     int *d_err = nullptr;
     int *h_err = nullptr;  // pinned: the error word, read back with a call's results
     // expert parallelism: this rank's exchange buffer (flags | CTA counter |
@@ -261,6 +340,8 @@ extern "C" void miag_close(miag_ctx *c) {
         cudaStreamDestroy(c->copy_stream);
     }
     for (cudaEvent_t e : c->pipe_events) cudaEventDestroy(e);
+    c->copy_pool.reset();
+    if (c->pipe_host) cudaFreeHost(c->pipe_host);
     if (c->stream) cudaStreamDestroy(c->stream);
     delete c;
 }
@@ -619,54 +700,98 @@ extern "C" int miag_sync(miag_ctx *c, void *stream, char *err, size_t errlen) {
 }
 
 // Batches of at least kPipeMin tokens move through miag_moe in
-// transfer_chunks chunks (miag_set_transfer_chunks): the copy stream brings chunk k + 1 in and takes chunk k - 1 out
-// while the block runs on chunk k.  Tokens are independent in the block
-// (forward.c:167-197 is a per-token loop), so the results are those of one
-// call over all of them, bit for bit.  Chunks are enqueued in the order
-// in(0), block(0), in(1), block(1), ... and the copies out last, so that
-// with pageable host memory, whose copies hold the calling thread, the
-// device still works on the chunks already enqueued.
+// transfer_chunks pieces (miag_set_transfer_chunks): the copy stream brings
+// piece k + 1 in and takes piece k - 1 out while the block runs on piece k.
+// Tokens are independent in the block (forward.c:167-197 is a per-token
+// loop), so the results are those of one call over all of them, bit for bit.
+// Pieces are enqueued in the order in(0), block(0), in(1), block(1), ... and
+// the copies out last.
+//
+// A pageable caller buffer (the reference's m->x is malloc'd) goes through a
+// pinned staging buffer: host threads copy piece k + 1 into it while piece k
+// crosses PCIe and the block runs, and copy each piece's results back out as
+// soon as its device-to-host copy has landed.  Piece k's staging region holds
+// its inputs and then its results: the results are copied in only after the
+// block, which follows the inputs' copy out of the region.
 constexpr int kPipeMin = 2048, kPipeMaxChunks = 16;
+constexpr size_t kStageMin = (size_t)1 << 20;  // smaller pageable buffers: the driver's copies
 
-static int moe_pipelined(miag_ctx *c, int layer, float *x, int n_tokens, char *err, size_t errlen) {
+static bool host_pageable(const void *p) {
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return true;
+    }
+    return a.type == cudaMemoryTypeUnregistered;
+}
+
+static int ensure_host_staging(miag_ctx *c, size_t bytes, char *err, size_t errlen) {
+    if (!c->copy_pool) {
+        if (c->host_threads < 0) {
+            const int cores = (int)std::thread::hardware_concurrency();
+            c->host_threads = std::max(1, std::min(8, cores - 1));
+        }
+        c->copy_pool.reset(new CopyPool(c->host_threads - 1));
+    }
+    if (c->pipe_host_bytes >= bytes) return 0;
+    if (c->pipe_host) cudaFreeHost(c->pipe_host);
+    c->pipe_host = nullptr;
+    c->pipe_host_bytes = 0;
+    CU(cudaHostAlloc((void **)&c->pipe_host, bytes, cudaHostAllocDefault));
+    c->pipe_host_bytes = bytes;
+    return 0;
+}
+
+static int moe_pipelined(miag_ctx *c, int layer, float *x, int n_tokens, int chunks, bool staged,
+                         char *err, size_t errlen) {
     if (!c->copy_stream) {
         CU(cudaStreamCreateWithFlags(&c->copy_stream, cudaStreamNonBlocking));
-        for (int i = 0; i < 2 * kPipeMaxChunks; i++) {
+        for (int i = 0; i < 3 * kPipeMaxChunks; i++) {
             cudaEvent_t e;
             CU(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
             c->pipe_events.push_back(e);
         }
     }
-    const size_t row = (size_t)c->shape.dim * sizeof(float);
-    const int chunks = c->transfer_chunks;
+    const size_t dim = (size_t)c->shape.dim, row = dim * sizeof(float);
+    if (staged && ensure_host_staging(c, (size_t)n_tokens * row, err, errlen)) return -1;
+    float *const src = staged ? c->pipe_host : x;  // what the copy engines read and write
+    cudaEvent_t *const ev_in = c->pipe_events.data(), *const ev_block = ev_in + kPipeMaxChunks,
+                       *const ev_out = ev_block + kPipeMaxChunks;
     const int per = ((n_tokens + chunks - 1) / chunks + 31) & ~31;
     int launches = 0, n_chunks = 0;
     auto enqueue = [&]() -> int {
         for (int k = 0; k < chunks && k * per < n_tokens; k++, n_chunks++) {
             const int t0 = k * per, tk = std::min(per, n_tokens - t0);
-            CU(cudaMemcpyAsync(c->x_dev + (size_t)t0 * c->shape.dim, x + (size_t)t0 * c->shape.dim,
-                               (size_t)tk * row, cudaMemcpyHostToDevice, c->copy_stream));
-            CU(cudaEventRecord(c->pipe_events[k], c->copy_stream));
-            CU(cudaStreamWaitEvent(c->stream, c->pipe_events[k], 0));
+            if (staged) c->copy_pool->copy(src + t0 * dim, x + t0 * dim, (size_t)tk * row);
+            CU(cudaMemcpyAsync(c->x_dev + t0 * dim, src + t0 * dim, (size_t)tk * row,
+                               cudaMemcpyHostToDevice, c->copy_stream));
+            CU(cudaEventRecord(ev_in[k], c->copy_stream));
+            CU(cudaStreamWaitEvent(c->stream, ev_in[k], 0));
             if (ensure_ws(c, tk, err, errlen)) return -1;  // counts only: the buffers hold n_tokens
-            if (enqueue_moe(c, layer, c->x_dev + (size_t)t0 * c->shape.dim, tk, c->stream, err, errlen))
-                return -1;
+            if (enqueue_moe(c, layer, c->x_dev + t0 * dim, tk, c->stream, err, errlen)) return -1;
             launches += c->last_launches;
-            CU(cudaEventRecord(c->pipe_events[kPipeMaxChunks + k], c->stream));
+            CU(cudaEventRecord(ev_block[k], c->stream));
         }
         for (int k = 0; k < n_chunks; k++) {
             const int t0 = k * per, tk = std::min(per, n_tokens - t0);
-            CU(cudaStreamWaitEvent(c->copy_stream, c->pipe_events[kPipeMaxChunks + k], 0));
-            CU(cudaMemcpyAsync(x + (size_t)t0 * c->shape.dim, c->x_dev + (size_t)t0 * c->shape.dim,
-                               (size_t)tk * row, cudaMemcpyDeviceToHost, c->copy_stream));
+            CU(cudaStreamWaitEvent(c->copy_stream, ev_block[k], 0));
+            CU(cudaMemcpyAsync(src + t0 * dim, c->x_dev + t0 * dim, (size_t)tk * row,
+                               cudaMemcpyDeviceToHost, c->copy_stream));
+            CU(cudaEventRecord(ev_out[k], c->copy_stream));
         }
-        // after the last chunk's block: the error word with the results
+        // after the last piece's block: the error word with the results
         CU(cudaMemcpyAsync(c->h_err, c->d_err, sizeof(int), cudaMemcpyDeviceToHost, c->copy_stream));
+        if (staged) {
+            for (int k = 0; k < n_chunks; k++) {
+                const int t0 = k * per, tk = std::min(per, n_tokens - t0);
+                CU(cudaEventSynchronize(ev_out[k]));
+                c->copy_pool->copy(x + t0 * dim, src + t0 * dim, (size_t)tk * row);
+            }
+        }
         return 0;
     };
     if (enqueue() != 0) {
-        // nothing enqueued may still write into the caller's buffer once the
-        // call has returned
+        // no copy enqueued may still land once the call has returned
         cudaStreamSynchronize(c->copy_stream);
         cudaStreamSynchronize(c->stream);
         return -1;
@@ -688,9 +813,10 @@ extern "C" int miag_moe(miag_ctx *c, int layer, float *x, int n_tokens, char *er
     }
     CU(cudaSetDevice(c->device));
     if (ensure_ws(c, n_tokens, err, errlen)) return -1;
-    if (n_tokens >= kPipeMin && c->transfer_chunks > 1)
-        return moe_pipelined(c, layer, x, n_tokens, err, errlen);
     const size_t bytes = (size_t)n_tokens * c->shape.dim * sizeof(float);
+    const bool staged = c->host_threads != 0 && bytes >= kStageMin && host_pageable(x);
+    const int chunks = n_tokens >= kPipeMin ? c->transfer_chunks : 1;
+    if (staged || chunks > 1) return moe_pipelined(c, layer, x, n_tokens, chunks, staged, err, errlen);
     CU(cudaMemcpyAsync(c->x_dev, x, bytes, cudaMemcpyHostToDevice, c->stream));
     if (enqueue_moe(c, layer, c->x_dev, n_tokens, c->stream, err, errlen)) return -1;
     CU(cudaMemcpyAsync(x, c->x_dev, bytes, cudaMemcpyDeviceToHost, c->stream));
@@ -1116,6 +1242,13 @@ extern "C" int miag_set_prefill_kernel(miag_ctx *c, int kind, char *err, size_t 
 extern "C" int miag_set_transfer_chunks(miag_ctx *c, int chunks) {
     if (!c || chunks < 1 || chunks > kPipeMaxChunks) return -1;
     c->transfer_chunks = chunks;
+    return 0;
+}
+
+extern "C" int miag_set_host_copy_threads(miag_ctx *c, int threads) {
+    if (!c || threads < 0 || threads > 64) return -1;
+    if (threads != c->host_threads) c->copy_pool.reset();  // the next staged call makes the pool
+    c->host_threads = threads;
     return 0;
 }
 

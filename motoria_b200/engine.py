@@ -298,6 +298,12 @@ class MoEEngine:
         if self._lib.miag_set_transfer_chunks(self._ctx, int(chunks)) != 0:
             raise N.MiagError(f"miag_set_transfer_chunks: bad count {chunks}")
 
+    def set_host_copy_threads(self, threads: int) -> None:
+        """Host threads that copy a pageable buffer of >= 1 MiB through the
+        context's pinned staging buffer (0: the driver's pageable copies)."""
+        if self._lib.miag_set_host_copy_threads(self._ctx, int(threads)) != 0:
+            raise N.MiagError(f"miag_set_host_copy_threads: bad count {threads}")
+
     def prefill_kernel(self) -> int:
         return int(self._lib.miag_prefill_kernel(self._ctx))
 

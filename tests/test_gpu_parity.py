@@ -264,6 +264,34 @@ def test_host_call_in_pieces_equals_one_pass(qwen, T, chunks):
     assert np.array_equal(arr.view(np.uint32), want.view(np.uint32))
 
 
+@pytest.mark.parametrize("T,chunks", [(300, 4), (2048, 4), (4097, 8)])
+def test_pageable_staging_equals_direct_copies(qwen, T, chunks):
+    """A pageable host buffer of >= 1 MiB goes through the context's pinned
+    staging buffer, copied by host threads piece by piece: every output bit
+    equals the driver's own pageable copies (0 threads), one copying thread,
+    and a pinned buffer."""
+    import torch
+    eng, _, _ = qwen
+    x = synth.tokens(QWEN, 1300 + T, T, rms_normalise=False)
+    eng.set_transfer_chunks(chunks)
+    try:
+        eng.set_host_copy_threads(0)
+        want = eng.moe(x, layer=0)
+        outs = {}
+        for threads in (1, 3, 8):
+            eng.set_host_copy_threads(threads)
+            outs[threads] = eng.moe(x, layer=0)
+        pinned = torch.from_numpy(x.copy()).pin_memory()
+        arr = pinned.numpy()
+        eng.moe_inplace(arr, layer=0)
+        outs["pinned"] = arr
+    finally:
+        eng.set_host_copy_threads(8)
+        eng.set_transfer_chunks(1)
+    for k, got in outs.items():
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), k
+
+
 # ---- size-independent properties -------------------------------------------
 
 def test_batch_invariance_and_determinism(qwen):
