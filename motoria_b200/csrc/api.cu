@@ -1,5 +1,7 @@
 // api.cu -- the libmiag C ABI (include/miag/miag.h): context, HBM expert
 // store, workspace and the MoE block launch sequence.
+#include <atomic>
+#include <chrono>
 #include <condition_variable>
 #include <cstdarg>
 #include <cstdio>
@@ -21,8 +23,10 @@ namespace {
 
 // Host threads that split one memcpy between them: miag_moe's copies between
 // the caller's pageable buffer and the context's pinned staging buffer.  The
-// calling thread copies the first part; copy() returns when every part is
-// done, so a worker never misses a generation.
+// calling thread copies the first part and returns when every part is done,
+// so a worker never misses a generation.  A worker spins for a while after
+// its part (one call issues its copies a few microseconds apart) and then
+// sleeps until the next one.
 class CopyPool {
   public:
     explicit CopyPool(int workers) {
@@ -43,19 +47,16 @@ class CopyPool {
             memcpy(dst, src, bytes);
             return;
         }
-        {
-            std::lock_guard<std::mutex> g(m_);
-            dst_ = (char *)dst;
-            src_ = (const char *)src;
-            bytes_ = bytes;
-            parts_ = parts;
-            left_ = parts - 1;
-            gen_++;
-        }
+        dst_ = (char *)dst;
+        src_ = (const char *)src;
+        bytes_ = bytes;
+        parts_ = parts;
+        left_.store(parts - 1, std::memory_order_relaxed);
+        gen_.fetch_add(1, std::memory_order_release);
+        { std::lock_guard<std::mutex> g(m_); }  // a worker going to sleep sees the new generation
         wake_.notify_all();
         part(0);
-        std::unique_lock<std::mutex> l(m_);
-        done_.wait(l, [this] { return left_ == 0; });
+        while (left_.load(std::memory_order_acquire) != 0) std::this_thread::yield();
     }
 
   private:
@@ -66,23 +67,31 @@ class CopyPool {
     }
     void run(int i) {
         uint64_t seen = 0;
-        std::unique_lock<std::mutex> l(m_);
         for (;;) {
-            wake_.wait(l, [&] { return stop_ || gen_ != seen; });
-            if (stop_) return;
-            seen = gen_;
-            l.unlock();
+            const auto t0 = std::chrono::steady_clock::now();
+            for (int n = 0; gen_.load(std::memory_order_acquire) == seen; n++) {
+                if ((n & 255) == 255 &&
+                    std::chrono::steady_clock::now() - t0 > std::chrono::microseconds(200)) {
+                    std::unique_lock<std::mutex> l(m_);
+                    wake_.wait(l, [&] {
+                        return stop_ || gen_.load(std::memory_order_acquire) != seen;
+                    });
+                    if (stop_) return;
+                    break;
+                }
+            }
+            seen = gen_.load(std::memory_order_acquire);
             part(i);
-            l.lock();
-            if (--left_ == 0) done_.notify_one();
+            left_.fetch_sub(1, std::memory_order_acq_rel);
         }
     }
     std::vector<std::thread> threads_;
     std::mutex m_;
-    std::condition_variable wake_, done_;
+    std::condition_variable wake_;
     bool stop_ = false;
-    uint64_t gen_ = 0;
-    int parts_ = 1, left_ = 0;
+    std::atomic<uint64_t> gen_{0};
+    std::atomic<int> left_{0};
+    int parts_ = 1;
     char *dst_ = nullptr;
     const char *src_ = nullptr;
     size_t bytes_ = 0;
@@ -708,13 +717,15 @@ extern "C" int miag_sync(miag_ctx *c, void *stream, char *err, size_t errlen) {
 // the copies out last.
 //
 // A pageable caller buffer (the reference's m->x is malloc'd) goes through a
-// pinned staging buffer: host threads copy piece k + 1 into it while piece k
-// crosses PCIe and the block runs, and copy each piece's results back out as
-// soon as its device-to-host copy has landed.  Piece k's staging region holds
-// its inputs and then its results: the results are copied in only after the
-// block, which follows the inputs' copy out of the region.
+// pinned staging buffer in slices of about 2 MiB: host threads copy slice
+// i + 1 into it while slice i crosses PCIe, and each piece's block waits for
+// its last slice.  Results come back the same way: the host copies a slice
+// out as soon as its device-to-host copy has landed.  A slice's staging
+// region holds its inputs and then its results; the results are copied in
+// only after the block, which follows the inputs' copy out of the region.
 constexpr int kPipeMin = 2048, kPipeMaxChunks = 16;
-constexpr size_t kStageMin = (size_t)1 << 20;  // smaller pageable buffers: the driver's copies
+constexpr size_t kStageMin = (size_t)1 << 20;    // smaller pageable buffers: the driver's copies
+constexpr size_t kStageSlice = (size_t)2 << 20;  // bytes per staged slice
 
 static bool host_pageable(const void *p) {
     cudaPointerAttributes a;
@@ -746,7 +757,7 @@ static int moe_pipelined(miag_ctx *c, int layer, float *x, int n_tokens, int chu
                          char *err, size_t errlen) {
     if (!c->copy_stream) {
         CU(cudaStreamCreateWithFlags(&c->copy_stream, cudaStreamNonBlocking));
-        for (int i = 0; i < 3 * kPipeMaxChunks; i++) {
+        for (int i = 0; i < 2 * kPipeMaxChunks; i++) {
             cudaEvent_t e;
             CU(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
             c->pipe_events.push_back(e);
@@ -755,16 +766,28 @@ static int moe_pipelined(miag_ctx *c, int layer, float *x, int n_tokens, int chu
     const size_t dim = (size_t)c->shape.dim, row = dim * sizeof(float);
     if (staged && ensure_host_staging(c, (size_t)n_tokens * row, err, errlen)) return -1;
     float *const src = staged ? c->pipe_host : x;  // what the copy engines read and write
+    const int per = ((n_tokens + chunks - 1) / chunks + 31) & ~31;
+    // tokens per transfer: a slice of the staging buffer, or the whole piece
+    const int slice = staged ? (int)std::max<size_t>(1, kStageSlice / row) : per;
+    int n_slices = 0;
+    for (int t0 = 0; t0 < n_tokens; t0 += per) n_slices += (std::min(per, n_tokens - t0) + slice - 1) / slice;
+    while ((int)c->pipe_events.size() < 2 * kPipeMaxChunks + n_slices) {
+        cudaEvent_t e;
+        CU(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+        c->pipe_events.push_back(e);
+    }
     cudaEvent_t *const ev_in = c->pipe_events.data(), *const ev_block = ev_in + kPipeMaxChunks,
                        *const ev_out = ev_block + kPipeMaxChunks;
-    const int per = ((n_tokens + chunks - 1) / chunks + 31) & ~31;
     int launches = 0, n_chunks = 0;
     auto enqueue = [&]() -> int {
         for (int k = 0; k < chunks && k * per < n_tokens; k++, n_chunks++) {
             const int t0 = k * per, tk = std::min(per, n_tokens - t0);
-            if (staged) c->copy_pool->copy(src + t0 * dim, x + t0 * dim, (size_t)tk * row);
-            CU(cudaMemcpyAsync(c->x_dev + t0 * dim, src + t0 * dim, (size_t)tk * row,
-                               cudaMemcpyHostToDevice, c->copy_stream));
+            for (int s0 = t0; s0 < t0 + tk; s0 += slice) {
+                const size_t bytes = (size_t)std::min(slice, t0 + tk - s0) * row;
+                if (staged) c->copy_pool->copy(src + s0 * dim, x + s0 * dim, bytes);
+                CU(cudaMemcpyAsync(c->x_dev + s0 * dim, src + s0 * dim, bytes, cudaMemcpyHostToDevice,
+                                   c->copy_stream));
+            }
             CU(cudaEventRecord(ev_in[k], c->copy_stream));
             CU(cudaStreamWaitEvent(c->stream, ev_in[k], 0));
             if (ensure_ws(c, tk, err, errlen)) return -1;  // counts only: the buffers hold n_tokens
@@ -772,20 +795,27 @@ static int moe_pipelined(miag_ctx *c, int layer, float *x, int n_tokens, int chu
             launches += c->last_launches;
             CU(cudaEventRecord(ev_block[k], c->stream));
         }
+        int j = 0;
         for (int k = 0; k < n_chunks; k++) {
             const int t0 = k * per, tk = std::min(per, n_tokens - t0);
             CU(cudaStreamWaitEvent(c->copy_stream, ev_block[k], 0));
-            CU(cudaMemcpyAsync(src + t0 * dim, c->x_dev + t0 * dim, (size_t)tk * row,
-                               cudaMemcpyDeviceToHost, c->copy_stream));
-            CU(cudaEventRecord(ev_out[k], c->copy_stream));
+            for (int s0 = t0; s0 < t0 + tk; s0 += slice) {
+                CU(cudaMemcpyAsync(src + s0 * dim, c->x_dev + s0 * dim,
+                                   (size_t)std::min(slice, t0 + tk - s0) * row, cudaMemcpyDeviceToHost,
+                                   c->copy_stream));
+                CU(cudaEventRecord(ev_out[j++], c->copy_stream));
+            }
         }
         // after the last piece's block: the error word with the results
         CU(cudaMemcpyAsync(c->h_err, c->d_err, sizeof(int), cudaMemcpyDeviceToHost, c->copy_stream));
         if (staged) {
+            j = 0;
             for (int k = 0; k < n_chunks; k++) {
-                const int t0 = k * per, tk = std::min(per, n_tokens - t0);
-                CU(cudaEventSynchronize(ev_out[k]));
-                c->copy_pool->copy(x + t0 * dim, src + t0 * dim, (size_t)tk * row);
+                const int t0 = k * per, t1 = std::min(t0 + per, n_tokens);
+                for (int s0 = t0; s0 < t1; s0 += slice) {
+                    CU(cudaEventSynchronize(ev_out[j++]));
+                    c->copy_pool->copy(x + s0 * dim, src + s0 * dim, (size_t)std::min(slice, t1 - s0) * row);
+                }
             }
         }
         return 0;
