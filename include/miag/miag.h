@@ -119,7 +119,9 @@ int miag_moe_async(miag_ctx *c, int layer, float *x_dev, int n_tokens,
 /* miag_moe with at least 2048 tokens moves them through in `chunks` pieces
  * (default 4; 1: one piece): a copy stream brings piece k + 1 in and takes
  * piece k - 1 out while the block runs on piece k, so most of the host
- * transfers hide behind the kernels.  Tokens are independent in the block,
+ * transfers hide behind the kernels.  With three or more pieces the first
+ * and the last hold n / (2 chunks) tokens, which shortens the exposed
+ * copies; the others split the rest.  Tokens are independent in the block,
  * so the results equal one pass over all of them bit for bit; the
  * inspection calls (miag_routing, miag_router_logits) then describe the
  * last piece.  No reference counterpart (the reference has no device). */

@@ -753,6 +753,27 @@ static int ensure_host_staging(miag_ctx *c, size_t bytes, char *err, size_t errl
     return 0;
 }
 
+// Piece boundaries: with three or more pieces, a first and a last piece of
+// n / (2 chunks) tokens and equal pieces between them, else equal pieces
+// (multiples of 32 tokens).  Only the first piece's copy in and the last
+// piece's copy out are exposed, while every piece costs one stream of the
+// layer's expert weights: at config 5 (4096 tokens, 4 pieces) edges of 512
+// tokens took 2.55 ms a pinned call against 2.66 with equal pieces.
+static std::vector<int> piece_bounds(int n, int chunks) {
+    int edge = (n / (2 * chunks) + 31) & ~31;
+    if (chunks < 3 || 2 * edge >= n) edge = 0;
+    const int m = edge ? chunks - 2 : chunks, mid = n - 2 * edge;  // m equal pieces over mid
+    std::vector<int> b{0};
+    if (edge) b.push_back(edge);
+    for (int i = 1; i < m; i++) {
+        const int t = edge + ((int)((long long)mid * i / m) & ~31);
+        if (t > b.back()) b.push_back(t);
+    }
+    if (edge) b.push_back(n - edge);
+    b.push_back(n);
+    return b;
+}
+
 static int moe_pipelined(miag_ctx *c, int layer, float *x, int n_tokens, int chunks, bool staged,
                          char *err, size_t errlen) {
     if (!c->copy_stream) {
@@ -766,11 +787,12 @@ static int moe_pipelined(miag_ctx *c, int layer, float *x, int n_tokens, int chu
     const size_t dim = (size_t)c->shape.dim, row = dim * sizeof(float);
     if (staged && ensure_host_staging(c, (size_t)n_tokens * row, err, errlen)) return -1;
     float *const src = staged ? c->pipe_host : x;  // what the copy engines read and write
-    const int per = ((n_tokens + chunks - 1) / chunks + 31) & ~31;
+    const std::vector<int> bound = piece_bounds(n_tokens, chunks);
+    const int n_chunks = (int)bound.size() - 1;  // piece k: tokens [bound[k], bound[k + 1])
     // tokens per transfer: a slice of the staging buffer, or the whole piece
-    const int slice = staged ? (int)std::max<size_t>(1, kStageSlice / row) : per;
+    const int slice = staged ? (int)std::max<size_t>(1, kStageSlice / row) : n_tokens;
     int n_slices = 0;
-    for (int t0 = 0; t0 < n_tokens; t0 += per) n_slices += (std::min(per, n_tokens - t0) + slice - 1) / slice;
+    for (int k = 0; k < n_chunks; k++) n_slices += (bound[k + 1] - bound[k] + slice - 1) / slice;
     while ((int)c->pipe_events.size() < 2 * kPipeMaxChunks + n_slices) {
         cudaEvent_t e;
         CU(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
@@ -778,10 +800,10 @@ static int moe_pipelined(miag_ctx *c, int layer, float *x, int n_tokens, int chu
     }
     cudaEvent_t *const ev_in = c->pipe_events.data(), *const ev_block = ev_in + kPipeMaxChunks,
                        *const ev_out = ev_block + kPipeMaxChunks;
-    int launches = 0, n_chunks = 0;
+    int launches = 0;
     auto enqueue = [&]() -> int {
-        for (int k = 0; k < chunks && k * per < n_tokens; k++, n_chunks++) {
-            const int t0 = k * per, tk = std::min(per, n_tokens - t0);
+        for (int k = 0; k < n_chunks; k++) {
+            const int t0 = bound[k], tk = bound[k + 1] - t0;
             for (int s0 = t0; s0 < t0 + tk; s0 += slice) {
                 const size_t bytes = (size_t)std::min(slice, t0 + tk - s0) * row;
                 if (staged) c->copy_pool->copy(src + s0 * dim, x + s0 * dim, bytes);
@@ -797,7 +819,7 @@ static int moe_pipelined(miag_ctx *c, int layer, float *x, int n_tokens, int chu
         }
         int j = 0;
         for (int k = 0; k < n_chunks; k++) {
-            const int t0 = k * per, tk = std::min(per, n_tokens - t0);
+            const int t0 = bound[k], tk = bound[k + 1] - t0;
             CU(cudaStreamWaitEvent(c->copy_stream, ev_block[k], 0));
             for (int s0 = t0; s0 < t0 + tk; s0 += slice) {
                 CU(cudaMemcpyAsync(src + s0 * dim, c->x_dev + s0 * dim,
@@ -811,7 +833,7 @@ static int moe_pipelined(miag_ctx *c, int layer, float *x, int n_tokens, int chu
         if (staged) {
             j = 0;
             for (int k = 0; k < n_chunks; k++) {
-                const int t0 = k * per, t1 = std::min(t0 + per, n_tokens);
+                const int t0 = bound[k], t1 = bound[k + 1];
                 for (int s0 = t0; s0 < t1; s0 += slice) {
                     CU(cudaEventSynchronize(ev_out[j++]));
                     c->copy_pool->copy(x + s0 * dim, src + s0 * dim, (size_t)std::min(slice, t1 - s0) * row);
