@@ -126,12 +126,13 @@ int miag_moe_async(miag_ctx *c, int layer, float *x_dev, int n_tokens,
  * inspection calls (miag_routing, miag_router_logits) then describe the
  * last piece.  No reference counterpart (the reference has no device). */
 int miag_set_transfer_chunks(miag_ctx *c, int chunks);
-/* miag_moe with a pageable host buffer of at least 1 MiB (malloc'd, like
+/* miag_moe with a pageable host buffer of 1 MiB to 1 GiB (malloc'd, like
  * the reference's m->x) copies it through a pinned staging buffer of the
  * context with `threads` host threads (the calling one included), piece by
  * piece, so that the host copies overlap the transfers and the block.
  * Default min(8, cores - 1); 0 leaves pageable buffers to the CUDA driver's
- * own staged copies.  Pinned (registered) buffers are always copied
+ * own staged copies, and so does a call whose pinned staging buffer or
+ * threads cannot be had.  Pinned (registered) buffers are always copied
  * directly.  Results are the same bits either way.  No reference
  * counterpart. */
 int miag_set_host_copy_threads(miag_ctx *c, int threads);

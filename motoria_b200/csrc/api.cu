@@ -645,6 +645,7 @@ extern "C" int miag_sync(miag_ctx *c, void *stream, char *err, size_t errlen) {
 // only after the block, which follows the inputs' copy out of the region.
 constexpr int kPipeMin = 2048, kPipeMaxChunks = 16;
 constexpr size_t kStageMin = (size_t)1 << 20;    // smaller pageable buffers: the driver's copies
+constexpr size_t kStageMax = (size_t)1 << 30;    // larger ones too (no staging buffer that big)
 constexpr size_t kStageSlice = (size_t)2 << 20;  // bytes per staged slice
 
 static bool host_pageable(const void *p) {
@@ -656,21 +657,31 @@ static bool host_pageable(const void *p) {
     return a.type == cudaMemoryTypeUnregistered;
 }
 
-static int ensure_host_staging(miag_ctx *c, size_t bytes, char *err, size_t errlen) {
+// The copy threads and a pinned staging buffer of `bytes`; false when either
+// cannot be had, and the call then leaves its copies to the CUDA runtime.
+static bool ensure_host_staging(miag_ctx *c, size_t bytes) {
     if (!c->copy_pool) {
         if (c->host_threads < 0) {
             const int cores = (int)std::thread::hardware_concurrency();
             c->host_threads = std::max(1, std::min(8, cores - 1));
         }
-        c->copy_pool.reset(new CopyPool(c->host_threads - 1));
+        try {
+            c->copy_pool.reset(new CopyPool(c->host_threads - 1));
+        } catch (...) {  // no threads to be had
+            return false;
+        }
     }
-    if (c->pipe_host_bytes >= bytes) return 0;
+    if (c->pipe_host_bytes >= bytes) return true;
     if (c->pipe_host) cudaFreeHost(c->pipe_host);
     c->pipe_host = nullptr;
     c->pipe_host_bytes = 0;
-    CU(cudaHostAlloc((void **)&c->pipe_host, bytes, cudaHostAllocDefault));
+    if (cudaHostAlloc((void **)&c->pipe_host, bytes, cudaHostAllocDefault) != cudaSuccess) {
+        cudaGetLastError();
+        c->pipe_host = nullptr;
+        return false;
+    }
     c->pipe_host_bytes = bytes;
-    return 0;
+    return true;
 }
 
 static int moe_pipelined(miag_ctx *c, int layer, float *x, int n_tokens, int chunks, bool staged,
@@ -684,7 +695,7 @@ static int moe_pipelined(miag_ctx *c, int layer, float *x, int n_tokens, int chu
         }
     }
     const size_t dim = (size_t)c->shape.dim, row = dim * sizeof(float);
-    if (staged && ensure_host_staging(c, (size_t)n_tokens * row, err, errlen)) return -1;
+    if (staged && !ensure_host_staging(c, (size_t)n_tokens * row)) staged = false;
     float *const src = staged ? c->pipe_host : x;  // what the copy engines read and write
     const std::vector<int> bound = piece_bounds(n_tokens, chunks);
     const int n_chunks = (int)bound.size() - 1;  // piece k: tokens [bound[k], bound[k + 1])
@@ -765,7 +776,8 @@ extern "C" int miag_moe(miag_ctx *c, int layer, float *x, int n_tokens, char *er
     CU(cudaSetDevice(c->device));
     if (ensure_ws(c, n_tokens, err, errlen)) return -1;
     const size_t bytes = (size_t)n_tokens * c->shape.dim * sizeof(float);
-    const bool staged = c->host_threads != 0 && bytes >= kStageMin && host_pageable(x);
+    const bool staged =
+        c->host_threads != 0 && bytes >= kStageMin && bytes <= kStageMax && host_pageable(x);
     const int chunks = n_tokens >= kPipeMin ? c->transfer_chunks : 1;
     if (staged || chunks > 1) return moe_pipelined(c, layer, x, n_tokens, chunks, staged, err, errlen);
     CU(cudaMemcpyAsync(c->x_dev, x, bytes, cudaMemcpyHostToDevice, c->stream));
