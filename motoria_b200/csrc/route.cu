@@ -10,7 +10,8 @@
 //   1. each warp rmsnorms its tokens into shared memory, certified to equal
 //      the reference's serial double sum (see rms_scale);
 //   2. the expert groups' CTAs quantize xn to Q8_0 for the expert GEMVs,
-//      each a share of the blocks;
+//      each a share of the blocks, once the router logits (3.) are out: a
+//      warp quantizes the rows of the warp half a CTA away;
 //   3. lane e computes the router logit of expert 32*eg + e for the warp's
 //      tokens as the reference's serial fp32 sum (rounded multiply, then
 //      rounded add, i = 0..d-1 in order).  The group's router slice, stored
@@ -195,9 +196,9 @@ __global__ void __launch_bounds__(9 * 32, 1) k_route(RouteParams p, int W, int s
         }
     }
     named_barrier_sync(1, W * 32);  // consumer warps only
-    // 1.+2. rmsnorm (forward.c:75-81) and Q8_0 of xn (quant.c:11-27).  Lane l
-    // holds elements 4l + 128k (k < d/128) of a token: eight lanes cover one
-    // 32-block, so block maxima take three shuffles.
+    // 1. rmsnorm (forward.c:75-81).  Lane l holds elements 4l + 128k
+    // (k < d/128) of a token: eight lanes cover one 32-block, so the Q8_0
+    // block maxima of phase 2 take three shuffles.
     const int nq4 = d / 128;  // float4 per lane (d is a multiple of 32; see tail)
     for (int r = 0; r < nt; r++) {
         float *xr = xw + (size_t)r * d;
@@ -216,9 +217,8 @@ __global__ void __launch_bounds__(9 * 32, 1) k_route(RouteParams p, int W, int s
         }
         const double ss = __dadd_rn(__dadd_rn(s4[0], s4[1]), __dadd_rn(s4[2], s4[3]));
         const float inv = rms_scale_certified(ss, xr, d, p.m.eps, lane);
-        const int t = tw0 + r;
-        // xn in place; then Q8_0 in groups of four float4 (sixteen values
-        // per lane) so the block maxima, divisions and roundings overlap.
+        // xn in place (its Q8_0 comes after the router logits)
+#pragma unroll 4
         for (int k = 0; k < nq4; k++) {
             const int i = 4 * lane + 128 * k;
             float4 v = *reinterpret_cast<const float4 *>(xr + i);
@@ -229,57 +229,8 @@ __global__ void __launch_bounds__(9 * 32, 1) k_route(RouteParams p, int W, int s
             v.w = __fmul_rn(__fmul_rn(v.w, inv), w.w);
             *reinterpret_cast<float4 *>(xr + i) = v;
         }
-        {
-            // the expert-group CTAs of a token share the quantization: group
-            // g takes every G-th run of four float4 per lane (16 blocks)
-            const int xs = scale_pad(d / MIAG_QK);
-            for (int k0 = 4 * (int)blockIdx.y; k0 < nq4; k0 += 4 * (int)gridDim.y) {
-                float4 v[4];
-                float a[4], dq[4], id[4];
-#pragma unroll
-                for (int u = 0; u < 4; u++) {
-                    v[u] = k0 + u < nq4 ? *reinterpret_cast<const float4 *>(xr + 4 * lane + 128 * (k0 + u))
-                                        : make_float4(0.f, 0.f, 0.f, 0.f);
-                    a[u] = fmaxf(fmaxf(fabsf(v[u].x), fabsf(v[u].y)), fmaxf(fabsf(v[u].z), fabsf(v[u].w)));
-                }
-#pragma unroll
-                for (int o = 1; o < 8; o <<= 1)
-#pragma unroll
-                    for (int u = 0; u < 4; u++) a[u] = fmaxf(a[u], __shfl_xor_sync(0xffffffffu, a[u], o));
-#pragma unroll
-                for (int u = 0; u < 4; u++) {
-                    dq[u] = __fdiv_rn(a[u], 127.0f);
-                    id[u] = dq[u] != 0.0f ? __fdiv_rn(1.0f, dq[u]) : 0.0f;
-                }
-#pragma unroll
-                for (int u = 0; u < 4; u++) {
-                    if (k0 + u >= nq4) break;
-                    const int i = 4 * lane + 128 * (k0 + u);
-                    const uint32_t q0 = (uint8_t)(int8_t)roundf(__fmul_rn(v[u].x, id[u]));
-                    const uint32_t q1 = (uint8_t)(int8_t)roundf(__fmul_rn(v[u].y, id[u]));
-                    const uint32_t q2 = (uint8_t)(int8_t)roundf(__fmul_rn(v[u].z, id[u]));
-                    const uint32_t q3 = (uint8_t)(int8_t)roundf(__fmul_rn(v[u].w, id[u]));
-                    *reinterpret_cast<uint32_t *>(p.xq + (size_t)t * d + i) =
-                        q0 | (q1 << 8) | (q2 << 16) | (q3 << 24);
-                    if ((lane & 7) == 0) p.dx[(size_t)t * xs + i / MIAG_QK] = dq[u];
-                }
-            }
-        }
         for (int i = 128 * nq4 + lane; i < d; i += 32) {  // tail (d % 128 == 32, 64, 96)
             xr[i] = __fmul_rn(__fmul_rn(xr[i], inv), norm[i]);
-        }
-        if (blockIdx.y == 0 && 128 * nq4 < d) {
-            // tail blocks: one warp-wide pass per 32-block
-            for (int b = 4 * nq4; b < d / MIAG_QK; b++) {
-                const float v = xr[b * MIAG_QK + lane];
-                float a = fabsf(v);
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
-                const float dq = __fdiv_rn(a, 127.0f);
-                const float id = dq != 0.0f ? __fdiv_rn(1.0f, dq) : 0.0f;
-                p.xq[(size_t)t * d + b * MIAG_QK + lane] = (int8_t)roundf(__fmul_rn(v, id));
-                if (lane == 0) p.dx[(size_t)t * scale_pad(d / MIAG_QK) + b] = dq;
-            }
         }
     }
     __syncwarp();
@@ -331,6 +282,66 @@ __global__ void __launch_bounds__(9 * 32, 1) k_route(RouteParams p, int W, int s
         *last_flag = last;
     }
     named_barrier_sync(1, W * 32);
+    // 2. Q8_0 of xn (quant.c:11-27) for the expert products, which read it
+    // only after this launch: each warp quantizes the rows of the warp half a
+    // CTA away, so that with one token (the other warp idle) the quantization
+    // runs beside the last CTA's top-k instead of before the router adds.
+    // The expert-group CTAs of a token share it: group g takes every G-th run
+    // of four float4 per lane (16 blocks); the d % 128 tail blocks go to
+    // group 0, one warp-wide pass per 32-block.
+    {
+        const int qw = (warp + (W + 1) / 2) % W;
+        const int tq0 = tg0 + qw * R;
+        const int nqt = max(0, min(R, p.T - tq0));
+        const int xs = scale_pad(d / MIAG_QK);
+        for (int r = 0; r < nqt; r++) {
+            const int t = tq0 + r;
+            const float *xr = xs_all + ((size_t)qw * R + r) * d;
+            for (int k0 = 4 * (int)blockIdx.y; k0 < nq4; k0 += 4 * (int)gridDim.y) {
+                float4 v[4];
+                float a[4], dq[4], id[4];
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    v[u] = k0 + u < nq4 ? *reinterpret_cast<const float4 *>(xr + 4 * lane + 128 * (k0 + u))
+                                        : make_float4(0.f, 0.f, 0.f, 0.f);
+                    a[u] = fmaxf(fmaxf(fabsf(v[u].x), fabsf(v[u].y)), fmaxf(fabsf(v[u].z), fabsf(v[u].w)));
+                }
+#pragma unroll
+                for (int o = 1; o < 8; o <<= 1)
+#pragma unroll
+                    for (int u = 0; u < 4; u++) a[u] = fmaxf(a[u], __shfl_xor_sync(0xffffffffu, a[u], o));
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    dq[u] = __fdiv_rn(a[u], 127.0f);
+                    id[u] = dq[u] != 0.0f ? __fdiv_rn(1.0f, dq[u]) : 0.0f;
+                }
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    if (k0 + u >= nq4) break;
+                    const int i = 4 * lane + 128 * (k0 + u);
+                    const uint32_t q0 = (uint8_t)(int8_t)roundf(__fmul_rn(v[u].x, id[u]));
+                    const uint32_t q1 = (uint8_t)(int8_t)roundf(__fmul_rn(v[u].y, id[u]));
+                    const uint32_t q2 = (uint8_t)(int8_t)roundf(__fmul_rn(v[u].z, id[u]));
+                    const uint32_t q3 = (uint8_t)(int8_t)roundf(__fmul_rn(v[u].w, id[u]));
+                    *reinterpret_cast<uint32_t *>(p.xq + (size_t)t * d + i) =
+                        q0 | (q1 << 8) | (q2 << 16) | (q3 << 24);
+                    if ((lane & 7) == 0) p.dx[(size_t)t * xs + i / MIAG_QK] = dq[u];
+                }
+            }
+            if (blockIdx.y == 0 && 128 * nq4 < d) {
+                for (int b = 4 * nq4; b < d / MIAG_QK; b++) {
+                    const float v = xr[b * MIAG_QK + lane];
+                    float a = fabsf(v);
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+                    const float dq = __fdiv_rn(a, 127.0f);
+                    const float id = dq != 0.0f ? __fdiv_rn(1.0f, dq) : 0.0f;
+                    p.xq[(size_t)t * d + b * MIAG_QK + lane] = (int8_t)roundf(__fmul_rn(v, id));
+                    if (lane == 0) p.dx[(size_t)t * xs + b] = dq;
+                }
+            }
+        }
+    }
     if (!*last_flag) return;
     __threadfence();
     float *buf = ring + (size_t)warp * E;  // the ring is idle now: every chunk was consumed
